@@ -1,0 +1,418 @@
+"""Benchmark of the B200 VoxCPM2 per-patch path (one JSON line on rank 0).
+
+    python bench.py [--gpus N] [--steps K] [--warmup W] [--impl ours|reference]
+
+Workload (the headline metric's configuration): one
+Q8_0 x bf16 skinny product, M = 22 activation rows, K = 2048, N = 6144,
+fp32 accumulation, bf16 output. A step is one product on one of 16 rotating
+seeded weight copies (214 MB, larger than the 126 MB L2, so every step reads
+its weights from HBM). Steps are replayed from CUDA graphs of 100 launches so
+the host's launch rate does not bound the device. With N > 1 (torchrun, one
+process per GPU) every rank runs its own products (replicas, weak scaling);
+the value is all ranks' bytes over the slowest rank's time.
+
+`value` is HBM-resident throughput in GB/s of algorithmic bytes (weights +
+activations + bf16 output). `e2e` is the same metric through the C ABI with
+host buffers: each step copies x from pinned memory, runs the product and
+reads y back. `--impl reference` times the reference's arithmetic on the host
+cores: the reference (HIP, AMD-only) cannot be built here, so the CPU oracle
+port (oracle/, a float32 transcription of its product kernel) stands in.
+"""
+
+from __future__ import annotations
+
+import argparse
+import json
+import math
+import os
+import statistics
+import subprocess
+import sys
+import threading
+import time
+from pathlib import Path
+
+ROOT = Path(__file__).resolve().parent
+sys.path.insert(0, str(ROOT))
+
+ROWS, IN, OUT = 22, 2048, 6144
+WEIGHT_BYTES = OUT * IN * 34 // 32          # 13,369,344
+X_BYTES = ROWS * IN * 2                     # 90,112
+Y_BYTES = ROWS * OUT * 2                    # 270,336 (bf16 output)
+STEP_BYTES = WEIGHT_BYTES + X_BYTES + Y_BYTES  # 13,729,792
+COPIES = 16
+GRAPH_LAUNCHES = 100
+METRIC = "Q8_0 skinny-product HBM GB/s (M=22, K=2048, N=6144, bf16 out)"
+
+
+def parse():
+    p = argparse.ArgumentParser()
+    p.add_argument("--gpus", type=int, default=1)
+    p.add_argument("--steps", type=int, default=400_000)
+    p.add_argument("--warmup", type=int, default=20_000)
+    p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    return p.parse_args()
+
+
+# ---------------------------------------------------------------- distributed
+
+def init_dist(n_gpus: int):
+    world = int(os.environ.get("WORLD_SIZE", "1"))
+    rank = int(os.environ.get("RANK", "0"))
+    local = int(os.environ.get("LOCAL_RANK", "0"))
+    if world > 1:
+        import datetime
+
+        import torch
+        import torch.distributed as dist
+
+        torch.cuda.set_device(local)
+        dist.init_process_group("nccl", timeout=datetime.timedelta(seconds=120),
+                                device_id=torch.device("cuda", local))
+    return world, rank, local
+
+
+def barrier(world):
+    if world > 1:
+        import torch.distributed as dist
+
+        dist.barrier()
+
+
+def max_over_ranks(world, value: float) -> float:
+    if world == 1:
+        return value
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    return float(t.item())
+
+
+def sum_over_ranks(world, value: float) -> float:
+    if world == 1:
+        return value
+    import torch
+    import torch.distributed as dist
+
+    t = torch.tensor([value], dtype=torch.float64, device="cuda")
+    dist.all_reduce(t, op=dist.ReduceOp.SUM)
+    return float(t.item())
+
+
+# ---------------------------------------------------------------- clocks
+
+class ClockSampler:
+    """nvidia-smi samples of SM clock and throttle reasons while running."""
+
+    FIELDS = ("index,clocks.sm,clocks.max.sm,power.draw,clocks_event_reasons.active,"
+              "clocks_event_reasons.hw_slowdown,clocks_event_reasons.hw_thermal_slowdown,"
+              "clocks_event_reasons.sw_thermal_slowdown,clocks_event_reasons.sw_power_cap")
+
+    def __init__(self, gpu_index: int):
+        self.gpu_index = gpu_index
+        self.proc = None
+        self.lines: list[str] = []
+        self.thread = None
+
+    def __enter__(self):
+        try:
+            self.proc = subprocess.Popen(
+                ["nvidia-smi", "-i", str(self.gpu_index), f"--query-gpu={self.FIELDS}",
+                 "--format=csv,noheader,nounits", "-lms", "50"],
+                stdout=subprocess.PIPE, stderr=subprocess.DEVNULL, text=True)
+            self.thread = threading.Thread(target=self._read, daemon=True)
+            self.thread.start()
+            time.sleep(0.15)
+        except (OSError, FileNotFoundError):
+            self.proc = None
+        return self
+
+    def _read(self):
+        for line in self.proc.stdout:
+            self.lines.append(line.strip())
+
+    def __exit__(self, *exc):
+        if self.proc is not None:
+            self.proc.terminate()
+            try:
+                self.proc.wait(timeout=5)
+            except subprocess.TimeoutExpired:
+                self.proc.kill()
+
+    def summary(self) -> dict:
+        sm, mx, reasons = [], [], set()
+        names = ["hw_slowdown", "hw_thermal_slowdown", "sw_thermal_slowdown", "sw_power_cap"]
+        for line in self.lines:
+            parts = [p.strip() for p in line.split(",")]
+            if len(parts) < 9:
+                continue
+            try:
+                sm.append(float(parts[1]))
+                mx.append(float(parts[2]))
+            except ValueError:
+                continue
+            for name, flag in zip(names, parts[5:9]):
+                if flag.lower() == "active":
+                    reasons.add(name)
+        if not sm:
+            return {"sm_mhz": None, "sm_max_mhz": None, "reasons": [], "samples": 0}
+        return {"sm_mhz": statistics.median(sm), "sm_max_mhz": max(mx), "reasons": sorted(reasons),
+                "samples": len(sm)}
+
+
+# ---------------------------------------------------------------- shared
+
+def measured_peak():
+    path = ROOT / "MEASURED_PEAKS.json"
+    if path.exists():
+        data = json.loads(path.read_text())
+        return float(data["hbm_gbs"]), "measured"
+    return 6650.0, "fallback"
+
+
+def profiled_traffic():
+    """DRAM bytes per launch of the product kernel from the committed ncu
+    summary (profiles/traffic.json), or None."""
+    path = ROOT / "profiles" / "traffic.json"
+    if not path.exists():
+        return None
+    data = json.loads(path.read_text())
+    return data.get("q8_product_m22_k2048_n6144", {}).get("dram_bytes_per_launch")
+
+
+def cpu_sample(threads: int, budget_s: float):
+    """The oracle's float32 product transcription on a slice of config 0,
+    repeated for about `budget_s` seconds; returns (GB/s, description)."""
+    import numpy as np
+
+    import oracle
+
+    rows_out = 1024
+    blocks = oracle.random_q8_0(1, 0, rows_out, IN)
+    rng = np.random.default_rng(0)
+    x = oracle.bf16_bits(rng.normal(0, 1, (ROWS, IN)).astype(np.float32))
+    y = np.zeros((ROWS, rows_out), np.float32)
+    oracle.linear(x, oracle.Q8_0, blocks, ROWS, IN, rows_out, y=y, threads=threads)
+    start = time.perf_counter()
+    reps = 0
+    while True:
+        oracle.linear(x, oracle.Q8_0, blocks, ROWS, IN, rows_out, y=y, threads=threads)
+        reps += 1
+        elapsed = time.perf_counter() - start
+        if elapsed >= budget_s:
+            break
+    bytes_per = rows_out * IN * 34 // 32 + X_BYTES + ROWS * rows_out * 2
+    return bytes_per * reps / elapsed / 1e9, (
+        f"{reps} x (M={ROWS}, K={IN}, N={rows_out} of {OUT}) fp32 per-block transcription, "
+        f"{elapsed:.1f} s")
+
+
+# ---------------------------------------------------------------- reference arm
+
+def run_reference(args, world, rank):
+    if rank != 0:
+        return
+    import numpy as np
+
+    import oracle
+
+    threads = os.cpu_count() or 1
+    # One step = the product on a slice of the output rows, sized so that the
+    # whole --warmup + --steps run stays within about a minute.
+    probe_rows = 256
+    blocks_probe = oracle.random_q8_0(1, 0, probe_rows, IN)
+    rng = np.random.default_rng(0)
+    x = oracle.bf16_bits(rng.normal(0, 1, (ROWS, IN)).astype(np.float32))
+    y = np.zeros((ROWS, probe_rows), np.float32)
+    t0 = time.perf_counter()
+    oracle.linear(x, oracle.Q8_0, blocks_probe, ROWS, IN, probe_rows, y=y, threads=threads)
+    per_row = max((time.perf_counter() - t0) / probe_rows, 1e-9)
+    total = max(args.steps + args.warmup, 1)
+    rows_out = int(max(16, min(OUT, 60.0 / total / per_row)) // 16 * 16)
+    blocks = oracle.random_q8_0(1, 0, rows_out, IN)
+    y = np.zeros((ROWS, rows_out), np.float32)
+    for _ in range(args.warmup):
+        oracle.linear(x, oracle.Q8_0, blocks, ROWS, IN, rows_out, y=y, threads=threads)
+    t0 = time.perf_counter()
+    for _ in range(args.steps):
+        oracle.linear(x, oracle.Q8_0, blocks, ROWS, IN, rows_out, y=y, threads=threads)
+    elapsed = time.perf_counter() - t0
+    step_bytes = rows_out * IN * 34 // 32 + X_BYTES + ROWS * rows_out * 2
+    value = step_bytes * args.steps / elapsed / 1e9
+    sample = (f"each step: M={ROWS}, K={IN}, N={rows_out} of {OUT} output rows "
+              f"(float32 per-block transcription of the reference's Q8_0 product)")
+    line = {
+        "impl": "reference", "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world,
+        "steps": args.steps, "warmup": args.warmup,
+        "ms_per_step": elapsed / max(args.steps, 1) * 1e3, "higher_is_better": True,
+        "scaling": "weak", "vs_baseline": None, "dtype": "f32", "data": "synthetic (seeded)",
+        "config": {"workload": "q8_product_m22_k2048_n6144", "rows": ROWS, "in": IN, "out": OUT},
+        "cpu_baseline": {"value": value, "unit": "GB/s", "cores": threads, "kind": "port",
+                         "sample": sample},
+        "e2e": {"value": value, "unit": "GB/s", "h2d_bytes_per_step": 0, "d2h_bytes_per_step": 0},
+        "note": "the reference is HIP for AMD gfx1151 and cannot be built here (no hipcc/ROCm, no "
+                "Gufo SDK); this arm times the CPU oracle port of its product on the host cores",
+    }
+    print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------- our arm
+
+def run_ours(args, world, rank, local):
+    import numpy as np
+    import torch
+
+    from voxcpm_b200 import _lib
+    from voxcpm_b200 import kernels as K
+
+    device = torch.device("cuda", local)
+    torch.cuda.set_device(device)
+    lib = _lib.load()
+    stream = torch.cuda.Stream(device)
+
+    # Seeded weight copies (distinct per copy and rank), repacked into tiles.
+    tiles = []
+    for c in range(COPIES):
+        blocks = torch.from_numpy(K.RandomQ8_0(1000 + rank, c, OUT, IN)).to(device)
+        t = torch.empty(K.Q8TilesBytes(OUT, IN), dtype=torch.uint8, device=device)
+        K.Q8_0ToTiles(blocks, OUT, IN, t, stream=stream)
+        tiles.append(t)
+        del blocks
+    rng = np.random.default_rng(rank)
+    x_host = torch.from_numpy(rng.normal(0, 1, (ROWS, IN)).astype(np.float32)).to(torch.bfloat16)
+    x = x_host.to(device)
+    y = torch.empty(ROWS, OUT, dtype=torch.bfloat16, device=device)
+    torch.cuda.synchronize()
+
+    s = stream.cuda_stream
+    x_ptr, y_ptr = x.data_ptr(), y.data_ptr()
+    tile_ptrs = [t.data_ptr() for t in tiles]
+
+    def launch(i):
+        st = lib.vx_product(_lib.WEIGHTS_Q8_TILES, x_ptr, tile_ptrs[i % COPIES], y_ptr, _lib.OUT_BF16,
+                            ROWS, IN, OUT, 0, None, s)
+        if st != 0:
+            raise RuntimeError(lib.vx_last_error().decode())
+
+    # A graph of GRAPH_LAUNCHES products over the rotating copies.
+    graph = torch.cuda.CUDAGraph()
+    with torch.cuda.stream(stream):
+        for i in range(3):
+            launch(i)
+        stream.synchronize()
+        with torch.cuda.graph(graph, stream=stream):
+            for i in range(GRAPH_LAUNCHES):
+                launch(i)
+    torch.cuda.synchronize()
+
+    def run_steps(n):
+        with torch.cuda.stream(stream):
+            for _ in range(n // GRAPH_LAUNCHES):
+                graph.replay()
+            for i in range(n % GRAPH_LAUNCHES):
+                launch(i)
+
+    run_steps(max(args.warmup, 3))
+    torch.cuda.synchronize()
+
+    start = torch.cuda.Event(enable_timing=True)
+    stop = torch.cuda.Event(enable_timing=True)
+    visible = os.environ.get("CUDA_VISIBLE_DEVICES")
+    sampler = ClockSampler(int(visible.split(",")[local]) if visible else local)
+    barrier(world)
+    torch.cuda.synchronize()
+    with sampler:
+        start.record(stream)
+        run_steps(args.steps)
+        stop.record(stream)
+        torch.cuda.synchronize()
+    barrier(world)
+    ms = start.elapsed_time(stop)
+    ms_max = max_over_ranks(world, ms)
+    total_bytes = sum_over_ranks(world, STEP_BYTES * args.steps)
+    value = total_bytes / (ms_max / 1e3) / 1e9
+    per_launch_s = ms / 1e3 / max(args.steps, 1)
+    achieved = STEP_BYTES / per_launch_s / 1e9
+    bits = K.DeviceError()
+    if bits:
+        raise RuntimeError(f"device wait timed out: bits {bits:#x}")
+
+    # e2e through the C ABI with host buffers: H2D x, product, D2H y per step.
+    x_pinned = x_host.pin_memory()
+    y_pinned = torch.empty(ROWS, OUT, dtype=torch.bfloat16).pin_memory()
+    e2e_steps = min(max(args.steps // 100, 50), 5000)
+
+    def e2e_step(i):
+        x.copy_(x_pinned, non_blocking=True)
+        launch(i)
+        y_pinned.copy_(y, non_blocking=True)
+
+    with torch.cuda.stream(stream):
+        for i in range(10):
+            e2e_step(i)
+        stream.synchronize()
+        barrier(world)
+        e_start = torch.cuda.Event(enable_timing=True)
+        e_stop = torch.cuda.Event(enable_timing=True)
+        e_start.record(stream)
+        for i in range(e2e_steps):
+            e2e_step(i)
+        e_stop.record(stream)
+        stream.synchronize()
+    e_ms = max_over_ranks(world, e_start.elapsed_time(e_stop))
+    e2e_value = sum_over_ranks(world, STEP_BYTES * e2e_steps) / (e_ms / 1e3) / 1e9
+
+    clocks = sampler.summary()
+    if rank != 0:
+        return
+    peak, peak_kind = measured_peak()
+    cpu_value, cpu_desc = cpu_sample(os.cpu_count() or 1, 10.0)
+    plan = K.PlanWmma(ROWS, IN, OUT, 0)
+    line = {
+        "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
+        "warmup": args.warmup, "ms_per_step": ms_max / max(args.steps, 1),
+        "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "bf16",
+        "data": "synthetic (seeded Q8_0 weights: q uniform [-127,127], fp16 scales |N(0,0.02)|/127; "
+                "x ~ N(0,1) bf16)",
+        "config": {"workload": "q8_product_m22_k2048_n6144_bf16out", "rows": ROWS, "in": IN,
+                   "out": OUT, "accumulate": "fp32", "weight_copies": COPIES,
+                   "l2": f"inputs larger than L2: {COPIES} rotating weight copies "
+                         f"({COPIES * WEIGHT_BYTES / 1e6:.0f} MB)",
+                   "launch": f"CUDA graphs of {GRAPH_LAUNCHES} products, programmatic dependent launch",
+                   "plan": {"splits": plan.splits, "blocks_per_split": plan.blocks_per_split,
+                            "variant": plan.variant},
+                   "parallelism": f"replicas x{world}"},
+        "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
+                     "frac": achieved / peak, "traffic": profiled_traffic(),
+                     "peak_source": f"{peak_kind} hbm_gbs (copy rate)",
+                     "frac_of_8TBps": achieved / 8000.0,
+                     "algorithmic_bytes_per_launch": STEP_BYTES},
+        "cpu_baseline": {"value": cpu_value, "unit": "GB/s", "cores": os.cpu_count() or 1,
+                         "kind": "port", "sample": cpu_desc},
+        "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": X_BYTES,
+                "d2h_bytes_per_step": Y_BYTES, "steps": e2e_steps},
+        "gpu_launches": args.steps,
+        "clocks": clocks,
+    }
+    print(json.dumps(line), flush=True)
+
+
+def main():
+    args = parse()
+    world, rank, local = init_dist(args.gpus)
+    try:
+        if args.impl == "reference":
+            run_reference(args, world, rank)
+        else:
+            run_ours(args, world, rank, local)
+    finally:
+        if world > 1:
+            import torch.distributed as dist
+
+            dist.destroy_process_group()
+
+
+if __name__ == "__main__":
+    main()

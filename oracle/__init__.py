@@ -1,0 +1,199 @@
+"""CPU oracle of the VoxCPM2 per-patch path — TEST INFRASTRUCTURE ONLY.
+
+Only tests/, __graft_entry__.smoke() and bench.py's cpu_baseline / reference
+legs use it, as the checker or the timed CPU baseline. The product
+(voxcpm_b200, libvoxcpm_b200.so) never imports or links it.
+
+The arithmetic lives in vxoracle.c (plain C, one function per reference
+kernel, each citing the reference file:line it restates); this module loads
+it with ctypes and wraps numpy arrays. model.py composes the primitives into
+the reference's ForwardStack / DiT evaluation / generation step.
+
+Parity status: UNPINNED against OpenBMB's outputs (the golden tensors need the
+absent checkpoint); pinned on the weight-free pieces (see vxoracle.h).
+"""
+
+from __future__ import annotations
+
+import ctypes
+import subprocess
+from ctypes import POINTER, c_double, c_float, c_int, c_int32, c_size_t, c_uint16, c_uint64, c_void_p
+from pathlib import Path
+
+import numpy as np
+
+HERE = Path(__file__).resolve().parent
+LIBRARY = HERE / "libvxoracle.so"
+
+BF16_ROWS = 0
+Q8_0 = 2
+
+
+def build(force: bool = False) -> Path:
+    """Compiles vxoracle.c with gcc (oracle/Makefile)."""
+    if force or not LIBRARY.exists() or LIBRARY.stat().st_mtime < (HERE / "vxoracle.c").stat().st_mtime:
+        subprocess.run(["make", "-C", str(HERE), "-B" if force else "libvxoracle.so"], check=True,
+                       stdout=subprocess.DEVNULL)
+    return LIBRARY
+
+
+_lib = None
+
+
+def lib():
+    global _lib
+    if _lib is None:
+        build()
+        L = ctypes.CDLL(str(LIBRARY))
+        P = c_void_p
+        sig = {
+            "vxo_bf16_bits": (c_uint16, [c_float]),
+            "vxo_bf16_value": (c_float, [c_uint16]),
+            "vxo_half_value": (c_float, [c_uint16]),
+            "vxo_half_bits": (c_uint16, [c_float]),
+            "vxo_to_bf16_array": (None, [P, P, c_size_t]),
+            "vxo_hash": (c_uint64, [c_uint64, c_uint64, c_uint64]),
+            "vxo_random_q8_0": (None, [c_uint64, c_uint64, c_size_t, c_size_t, c_float, P]),
+            "vxo_random_bf16": (None, [c_uint64, c_uint64, c_size_t, c_float, c_float, P]),
+            "vxo_q8_0_to_tiles": (None, [P, c_size_t, c_size_t, P]),
+            "vxo_bf16_to_tiles": (None, [P, c_size_t, c_size_t, P]),
+            "vxo_q8_0_dequant": (None, [P, c_size_t, c_size_t, P]),
+            "vxo_product_exact": (None, [P, c_int, P, P, P, P, c_size_t, c_size_t, c_size_t, c_int]),
+            "vxo_linear": (None, [P, c_int, P, P, c_size_t, c_size_t, c_size_t, c_int, c_int]),
+            "vxo_rms_norm": (None, [P, P, P, P, c_size_t, c_size_t, c_float]),
+            "vxo_rope_table": (None, [c_double, c_size_t, P, c_double, c_size_t, P]),
+            "vxo_qkv_rope": (None, [P, P, P, P, P, P, P, c_size_t, c_size_t, c_size_t, c_size_t, c_size_t]),
+            "vxo_attention": (None, [P, P, P, P, c_size_t, c_size_t, c_size_t, c_size_t, c_int,
+                                     c_size_t, c_size_t, c_size_t, c_size_t]),
+            "vxo_swiglu": (None, [P, P, c_size_t, c_size_t]),
+            "vxo_add_bias": (None, [P, P, c_size_t, c_size_t]),
+            "vxo_to_bf16": (None, [P, P, c_size_t, c_int]),
+            "vxo_concat_rows": (None, [P, P, c_size_t, P, P, c_size_t, P, c_size_t]),
+            "vxo_quantize": (None, [P, P, c_size_t, c_float]),
+            "vxo_prepend_special": (None, [P, P, P, c_size_t, c_size_t, c_size_t]),
+            "vxo_assemble_dit": (None, [P, P, P, P, P, c_size_t, c_size_t]),
+            "vxo_gather_rows": (None, [P, P, P, c_size_t, c_size_t]),
+            "vxo_guided_euler": (None, [P, P, c_size_t, c_float, c_float]),
+            "vxo_euler_schedule": (c_size_t, [c_size_t, c_float, P, P, P, c_size_t]),
+            "vxo_linspace": (None, [c_float, c_float, c_size_t, P]),
+            "vxo_sinusoid": (None, [c_float, c_size_t, P]),
+        }
+        for name, (res, args) in sig.items():
+            fn = getattr(L, name)
+            fn.restype = res
+            fn.argtypes = args
+        _lib = L
+    return _lib
+
+
+def _p(a: np.ndarray | None):
+    if a is None:
+        return None
+    assert a.flags["C_CONTIGUOUS"], "contiguous array expected"
+    return a.ctypes.data
+
+
+# ---------------------------------------------------------------- numerics
+
+def bf16_bits(values: np.ndarray) -> np.ndarray:
+    values = np.ascontiguousarray(values, dtype=np.float32)
+    out = np.empty(values.shape, dtype=np.uint16)
+    lib().vxo_to_bf16_array(_p(values), _p(out), values.size)
+    return out
+
+
+def bf16_value(bits: np.ndarray) -> np.ndarray:
+    bits = np.ascontiguousarray(bits, dtype=np.uint16)
+    return (bits.astype(np.uint32) << 16).view(np.float32)
+
+
+def half_value(bits: int) -> float:
+    return lib().vxo_half_value(bits)
+
+
+def half_bits(value: float) -> int:
+    return lib().vxo_half_bits(value)
+
+
+# ---------------------------------------------------------------- weights
+
+def random_q8_0(seed: int, tensor: int, rows: int, columns: int, scale_std: float = 0.02 / 127) -> np.ndarray:
+    out = np.empty(rows * (columns // 32) * 34, dtype=np.uint8)
+    lib().vxo_random_q8_0(seed, tensor, rows, columns, scale_std, _p(out))
+    return out
+
+
+def random_bf16(seed: int, tensor: int, count: int, mean: float = 0.0, std: float = 0.02) -> np.ndarray:
+    out = np.empty(count, dtype=np.uint16)
+    lib().vxo_random_bf16(seed, tensor, count, mean, std, _p(out))
+    return out
+
+
+def q8_0_to_tiles(blocks: np.ndarray, rows: int, columns: int) -> np.ndarray:
+    out = np.empty((rows + 15) // 16 * (columns // 32) * 544, dtype=np.uint8)
+    lib().vxo_q8_0_to_tiles(_p(blocks), rows, columns, _p(out))
+    return out
+
+
+def bf16_to_tiles(w: np.ndarray, rows: int, columns: int) -> np.ndarray:
+    out = np.empty((rows + 15) // 16 * (columns // 32) * 512, dtype=np.uint16)
+    lib().vxo_bf16_to_tiles(_p(np.ascontiguousarray(w)), rows, columns, _p(out))
+    return out
+
+
+def q8_0_dequant(blocks: np.ndarray, rows: int, columns: int) -> np.ndarray:
+    out = np.empty(rows * columns, dtype=np.float64)
+    lib().vxo_q8_0_dequant(_p(blocks), rows, columns, _p(out))
+    return out.reshape(rows, columns)
+
+
+# ---------------------------------------------------------------- products
+
+def product_exact(x: np.ndarray, fmt: int, w: np.ndarray, rows: int, columns: int, out: int,
+                  before: np.ndarray | None = None, threads: int = 0):
+    """(exact, magnitude) in double: tests/products_test.cpp:115-145."""
+    exact = np.empty(rows * out, dtype=np.float64)
+    magnitude = np.empty(rows * out, dtype=np.float64)
+    b = None if before is None else np.ascontiguousarray(before, dtype=np.float32)
+    lib().vxo_product_exact(_p(np.ascontiguousarray(x, dtype=np.uint16)), fmt, _p(w), _p(b), _p(exact),
+                            _p(magnitude), rows, columns, out, threads)
+    return exact.reshape(rows, out), magnitude.reshape(rows, out)
+
+
+def linear(x: np.ndarray, fmt: int, w: np.ndarray, rows: int, columns: int, out: int,
+           y: np.ndarray | None = None, accumulate: bool = False, threads: int = 0) -> np.ndarray:
+    """float32 transcription of the device products (y (+)= x W^T)."""
+    if y is None:
+        y = np.zeros((rows, out), dtype=np.float32)
+    assert y.dtype == np.float32 and y.flags["C_CONTIGUOUS"]
+    lib().vxo_linear(_p(np.ascontiguousarray(x, dtype=np.uint16)), fmt, _p(w), _p(y), rows, columns, out,
+                     int(accumulate), threads)
+    return y
+
+
+def relative_error(y: np.ndarray, exact: np.ndarray, magnitude: np.ndarray) -> float:
+    """max |y - exact| / sum |x w| (tests/products_test.cpp:115-145)."""
+    return float(np.max(np.abs(y.astype(np.float64) - exact) / np.maximum(magnitude, 1e-30)))
+
+
+# ---------------------------------------------------------------- schedule / time
+
+def linspace(start: float, end: float, steps: int) -> np.ndarray:
+    out = np.empty(steps, dtype=np.float32)
+    lib().vxo_linspace(start, end, steps, _p(out))
+    return out
+
+
+def euler_schedule(timesteps: int, sway: float = 1.0):
+    cap = timesteps + 1
+    t = np.empty(cap, np.float32)
+    dt = np.empty(cap, np.float32)
+    ev = np.empty(cap, np.int32)
+    n = lib().vxo_euler_schedule(timesteps, sway, _p(t), _p(dt), _p(ev), cap)
+    return t[:n].copy(), dt[:n].copy(), ev[:n].astype(bool)
+
+
+def sinusoid(t: float, width: int) -> np.ndarray:
+    out = np.empty(width, np.float32)
+    lib().vxo_sinusoid(t, width, _p(out))
+    return out

@@ -1,0 +1,92 @@
+"""The C ABI without a GPU: the library loads, exports every function that
+include/*.h declares, its ctypes table covers them, and its host-side parts
+(planning, tile sizes, seeded weights) behave."""
+
+import re
+import subprocess
+from pathlib import Path
+
+import numpy as np
+
+import oracle
+from voxcpm_b200 import _lib
+from voxcpm_b200 import kernels as K
+
+ROOT = Path(__file__).resolve().parent.parent
+
+
+def declared_functions() -> set[str]:
+    names = set()
+    for header in (ROOT / "include").glob("*.h"):
+        text = header.read_text()
+        names |= set(re.findall(r"^VX_API\s+[^(;]*?\b(vx_\w+)\s*\(", text, re.MULTILINE))
+    return names
+
+
+def exported_symbols() -> set[str]:
+    out = subprocess.run(["nm", "-D", "--defined-only", str(_lib.LIBRARY)], check=True,
+                         capture_output=True, text=True).stdout
+    return {line.split()[-1] for line in out.splitlines() if line.split()}
+
+
+def test_library_exports_every_declared_function():
+    declared = declared_functions()
+    assert len(declared) > 20
+    exported = exported_symbols()
+    missing = declared - exported
+    assert not missing, f"declared but not exported: {sorted(missing)}"
+    # Nothing else leaks: the C ABI is the whole interface.
+    extra = {s for s in exported if s.startswith("vx_")} - declared
+    assert not extra, f"exported but not declared: {sorted(extra)}"
+
+
+def test_ctypes_table_covers_the_header():
+    assert declared_functions() <= set(_lib.SIGNATURES)
+    lib = _lib.load()
+    for name in _lib.SIGNATURES:
+        getattr(lib, name)
+
+
+def test_host_queries():
+    lib = _lib.load()
+    assert lib.vx_version().startswith(b"voxcpm_b200")
+    # kernels/wmma_products.hpp:29-38: rows padded to 16.
+    assert K.Q8TilesBytes(6144, 2048) == 6144 // 16 * 64 * 544 == 13_369_344
+    assert K.Q8TilesBytes(72, 1024) == 5 * 32 * 544
+    assert K.Bf16TilesBytes(2, 2048) == 1 * 64 * 1024
+
+
+def test_planner():
+    # Every plan covers the reduction with nonempty splits of at most 1024
+    # columns and at most 8 CTAs per cluster.
+    for rows in (1, 2, 5, 8, 11, 22, 32):
+        for columns, out in ((1024, 2560), (2048, 1024), (4096, 1024), (1024, 8192), (6144, 2048),
+                             (2048, 6144), (8192, 512), (64, 1024), (2048, 2)):
+            for target in (0, 1, 4096):
+                plan = K.PlanWmma(rows, columns, out, target)
+                kb = columns // 32
+                assert 1 <= plan.splits <= 8
+                assert plan.blocks_per_split * 32 <= 1024
+                assert plan.splits * plan.blocks_per_split >= kb
+                assert (plan.splits - 1) * plan.blocks_per_split < kb
+                assert plan.partial_floats == 0 and plan.counters == 0
+    assert K.PlanWmma(22, 2048, 6144, 1).splits == 2  # fewest allowed splits
+    assert K.PlanWmma(22, 48, 16).splits == 0          # in not a multiple of 32
+
+
+def test_library_weights_match_the_oracle_restatement():
+    """vx_random_* (product) and the oracle's restatement give identical bytes."""
+    for seed, tensor, rows, columns in ((0, 0, 48, 256), (123456789, 77, 16, 2048), (5, 3, 1, 32)):
+        assert np.array_equal(K.RandomQ8_0(seed, tensor, rows, columns),
+                              oracle.random_q8_0(seed, tensor, rows, columns))
+    for mean, std in ((0.0, 0.02), (1.0, 0.05)):
+        assert np.array_equal(K.RandomBf16(9, 4, 100_000, mean, std), oracle.random_bf16(9, 4, 100_000, mean, std))
+    # Large enough to use the library's worker threads.
+    assert np.array_equal(K.RandomQ8_0(1, 2, 512, 8192), oracle.random_q8_0(1, 2, 512, 8192))
+
+
+def test_invalid_arguments_fail_without_a_gpu():
+    lib = _lib.load()
+    status = lib.vx_random_q8_0(0, 0, 4, 33, 0.01, None)
+    assert status == _lib.VX_INVALID
+    assert b"vx_random_q8_0" in lib.vx_last_error()

@@ -1,0 +1,235 @@
+"""The products and their weight tiles against the CPU oracle, on a B200.
+
+Mirrors the reference's tests/products_test.cpp: random GGML Q8_0 blocks
+(q uniform in [-128, 127], fp16 scale bits uniform in [0x1000, 0x1C00]) and
+bf16 activations ~N(0, 2) at VoxCPM2's shapes and odd ones, every row count
+the reference tests, plans of one, the planner's and many splits, plain and
+accumulating products, compared with a double-precision sum of the same
+operands. Metric: max |y - exact| / sum |x w| per output, limit 1e-5
+(products_test.cpp:115-145, :229-237). Every call goes through the C ABI.
+"""
+
+import numpy as np
+import pytest
+import torch
+
+import oracle
+from voxcpm_b200 import kernels as K
+from voxcpm_b200 import _lib
+from voxcpm_b200.gemm import Bf16Gemm, Matrix
+
+pytestmark = pytest.mark.gpu
+
+LIMIT = 1e-5
+
+ALL_ROWS = [1, 2, 4, 5, 8, 11, 16, 22, 32]
+# products_test.cpp:326-338: VoxCPM2's shapes and odd ones.
+SHAPES = [
+    (64, 1024, [4, 8]),
+    (512, 1024, [1, 4]),
+    (1024, 2560, ALL_ROWS),
+    (2048, 1024, [1, 5, 22]),
+    (4096, 1024, [1, 5, 22]),
+    (2048, 2048, [1, 5]),
+    (6144, 2048, [1, 3]),
+    (8192, 512, [1, 22]),
+    (1024, 72, [3, 22]),  # rows not a multiple of 16
+    (2048, 2, [1]),
+]
+
+
+def make_q8_blocks(out, columns, rng):
+    """GGML Q8_0 blocks as products_test.cpp:59-84 draws them."""
+    blocks = out * columns // 32
+    raw = np.empty((blocks, 34), dtype=np.uint8)
+    scale_bits = rng.integers(0x1000, 0x1C01, size=blocks).astype(np.uint16)
+    raw[:, 0] = scale_bits & 0xFF
+    raw[:, 1] = scale_bits >> 8
+    raw[:, 2:] = rng.integers(-128, 128, size=(blocks, 32)).astype(np.int8).view(np.uint8)
+    return raw.reshape(-1)
+
+
+def make_activations(rows, columns, rng, std=2.0):
+    return oracle.bf16_bits(rng.normal(0.0, std, size=(rows, columns)).astype(np.float32))
+
+
+def to_dev(a: np.ndarray) -> torch.Tensor:
+    t = torch.from_numpy(np.ascontiguousarray(a))
+    if t.dtype == torch.uint16:
+        t = t.view(torch.int16)
+    return t.cuda()
+
+
+def from_dev_u16(t: torch.Tensor) -> np.ndarray:
+    return t.cpu().view(torch.int16).numpy().view(np.uint16)
+
+
+def prepare(out, columns, rng):
+    blocks = make_q8_blocks(out, columns, rng)
+    q8_tiles = torch.zeros(K.Q8TilesBytes(out, columns), dtype=torch.uint8, device="cuda")
+    K.Q8_0ToTiles(to_dev(blocks), out, columns, q8_tiles)
+    dequant = torch.empty(out * columns, dtype=torch.int16, device="cuda")
+    K.Q8TilesToBf16(q8_tiles, out, columns, dequant)
+    bf16_tiles = torch.zeros(K.Bf16TilesBytes(out, columns) // 2, dtype=torch.int16, device="cuda")
+    K.Bf16ToTiles(dequant, out, columns, bf16_tiles)
+    return blocks, q8_tiles, dequant, bf16_tiles
+
+
+@pytest.mark.parametrize("columns,out,row_counts", SHAPES)
+def test_shape(cuda, columns, out, row_counts):
+    rng = np.random.default_rng(1234 + columns * 7 + out)
+    blocks, q8_tiles, dequant, bf16_tiles = prepare(out, columns, rng)
+    torch.cuda.synchronize()
+
+    # The repack writes exactly the oracle's tiles (bit for bit).
+    assert np.array_equal(q8_tiles.cpu().numpy(), oracle.q8_0_to_tiles(blocks, out, columns))
+    # Exact dequantization: bf16(scale * q) (products_test.cpp:175-185).
+    values = oracle.q8_0_dequant(blocks, out, columns)
+    host_dequant = from_dev_u16(dequant)
+    assert np.array_equal(host_dequant, oracle.bf16_bits(values.astype(np.float32).reshape(-1)))
+    # bf16 tiles round trip (products_test.cpp:186-190).
+    unpacked = torch.empty_like(dequant)
+    K.Bf16TilesToRows(bf16_tiles, out, columns, unpacked)
+    assert torch.equal(unpacked, dequant)
+    assert np.array_equal(bf16_tiles.cpu().view(torch.int16).numpy().view(np.uint16),
+                          oracle.bf16_to_tiles(host_dequant, out, columns))
+
+    worst = {}
+    for rows in row_counts:
+        x = make_activations(rows, columns, rng)
+        before = rng.normal(0.0, 1.0, size=(rows, out)).astype(np.float32)
+        x_dev = to_dev(x)
+        exact_q8 = {a: oracle.product_exact(x, oracle.Q8_0, blocks, rows, columns, out,
+                                            before if a else None) for a in (False, True)}
+        exact_bf16 = {a: oracle.product_exact(x, oracle.BF16_ROWS, host_dequant, rows, columns, out,
+                                              before if a else None) for a in (False, True)}
+        y = torch.empty(rows, out, dtype=torch.float32, device="cuda")
+        for accumulate in (False, True):
+            for target in (1, 0, 4096):
+                plan = K.PlanWmma(rows, columns, out, target)
+                assert plan.splits > 0
+                for name, fn, weights, exact in (
+                    ("q8", K.WmmaQ8, q8_tiles, exact_q8[accumulate]),
+                    ("bf16 tiles", K.WmmaBf16, bf16_tiles, exact_bf16[accumulate]),
+                ):
+                    y.copy_(torch.from_numpy(before))
+                    assert fn(x_dev, weights, y, rows, columns, out, accumulate, plan), name
+                    torch.cuda.synchronize()
+                    err = oracle.relative_error(y.cpu().numpy(), *exact)
+                    key = (name, rows, plan.splits, accumulate)
+                    worst[key] = err
+                    assert err <= LIMIT, f"{name} rows {rows} splits {plan.splits}: {err:.3e}"
+            # bf16 rows (SkinnyGemm) on the dequantized weights.
+            y.copy_(torch.from_numpy(before))
+            assert K.SkinnyGemm(x_dev, dequant, y, rows, columns, out, accumulate)
+            torch.cuda.synchronize()
+            err = oracle.relative_error(y.cpu().numpy(), *exact_bf16[accumulate])
+            assert err <= LIMIT, f"skinny rows {rows}: {err:.3e}"
+    assert K.DeviceError() == 0
+    print(f"in {columns} out {out}: worst {max(worst.values()):.3e}")
+
+
+def test_every_variant(cuda):
+    """Each kernel shape on each format gives the same sums (config-0 shape)."""
+    rng = np.random.default_rng(7)
+    rows, columns, out = 22, 2048, 6144
+    blocks, q8_tiles, dequant, bf16_tiles = prepare(out, columns, rng)
+    x = make_activations(rows, columns, rng)
+    x_dev = to_dev(x)
+    exact = oracle.product_exact(x, oracle.Q8_0, blocks, rows, columns, out)
+    exact_rows = oracle.product_exact(x, oracle.BF16_ROWS, from_dev_u16(dequant), rows, columns, out)
+    y = torch.empty(rows, out, dtype=torch.float32, device="cuda")
+    ran = {fmt: 0 for fmt in (_lib.WEIGHTS_Q8_TILES, _lib.WEIGHTS_BF16_TILES, _lib.WEIGHTS_BF16)}
+    for variant in range(len(K.ProductVariants())):
+        for splits in (2, 3, 4, 8):
+            bps = -(-columns // 32 // splits)
+            if -(-(columns // 32) // bps) != splits:
+                continue
+            plan = _lib.WmmaPlan(splits, bps, 0, 0, variant)
+            for fmt, w, ex in ((_lib.WEIGHTS_Q8_TILES, q8_tiles, exact),
+                               (_lib.WEIGHTS_BF16_TILES, bf16_tiles, exact_rows),
+                               (_lib.WEIGHTS_BF16, dequant, exact_rows)):
+                y.zero_()
+                if not K.Product(fmt, x_dev, w, y, rows, columns, out, False, plan):
+                    continue  # this shape's shared memory exceeds the kernels' limit
+                ran[fmt] += 1
+                torch.cuda.synchronize()
+                err = oracle.relative_error(y.cpu().numpy(), *ex)
+                assert err <= LIMIT, f"variant {variant} splits {splits} format {fmt}: {err:.3e}"
+    assert all(count >= 8 for count in ran.values()), ran
+
+
+def test_bf16_output(cuda):
+    """The bf16-output epilogue: bf16(fp32 sum)."""
+    rng = np.random.default_rng(11)
+    rows, columns, out = 22, 2048, 6144
+    blocks, q8_tiles, _, _ = prepare(out, columns, rng)
+    x = make_activations(rows, columns, rng, std=1.0)
+    x_dev = to_dev(x)
+    y32 = torch.empty(rows, out, dtype=torch.float32, device="cuda")
+    y16 = torch.empty(rows, out, dtype=torch.bfloat16, device="cuda")
+    assert K.Product(_lib.WEIGHTS_Q8_TILES, x_dev, q8_tiles, y32, rows, columns, out)
+    assert K.Product(_lib.WEIGHTS_Q8_TILES, x_dev, q8_tiles, y16, rows, columns, out)
+    torch.cuda.synchronize()
+    # Same fp32 sums, rounded once to bf16 (RNE): bit-equal to rounding y32.
+    expect = oracle.bf16_bits(y32.cpu().numpy())
+    got = y16.cpu().view(torch.int16).numpy().view(np.uint16)
+    assert np.array_equal(got, expect)
+    exact, mag = oracle.product_exact(x, oracle.Q8_0, blocks, rows, columns, out)
+    rel = np.abs(y16.float().cpu().numpy() - exact) / np.maximum(np.abs(exact), 1e-30)
+    assert float(np.max(rel)) <= 2.0 ** -8  # one bf16 rounding
+
+
+def test_fp32_transcription_agrees(cuda):
+    """The device sums agree with the oracle's fp32 per-block transcription
+    (wmma_products.hip:201-214) to float32 summation-order noise."""
+    rng = np.random.default_rng(5)
+    rows, columns, out = 22, 1024, 2560
+    blocks, q8_tiles, _, _ = prepare(out, columns, rng)
+    x = make_activations(rows, columns, rng)
+    y = torch.empty(rows, out, dtype=torch.float32, device="cuda")
+    assert K.WmmaQ8(to_dev(x), q8_tiles, y, rows, columns, out, False)
+    torch.cuda.synchronize()
+    ref = oracle.linear(x, oracle.Q8_0, blocks, rows, columns, out)
+    exact, mag = oracle.product_exact(x, oracle.Q8_0, blocks, rows, columns, out)
+    assert float(np.max(np.abs(y.cpu().numpy() - ref) / mag)) <= 2e-6
+
+
+@pytest.mark.parametrize("columns,out", [(1024, 2560), (4096, 1024)])
+def test_linear(cuda, columns, out):
+    """Bf16Gemm::Linear on Q8 and bf16 tiles, chunks of 32 rows up to and
+    beyond 128 (products_test.cpp:256-313)."""
+    rng = np.random.default_rng(99 + columns)
+    blocks, q8_tiles, dequant, bf16_tiles = prepare(out, columns, rng)
+    host_dequant = from_dev_u16(dequant)
+    gemm = Bf16Gemm()
+    for rows in (1, 22, 40, 130):
+        x = make_activations(rows, columns, rng)
+        before = rng.normal(0.0, 1.0, size=(rows, out)).astype(np.float32)
+        x_dev = to_dev(x)
+        y = torch.empty(rows, out, dtype=torch.float32, device="cuda")
+        for accumulate in (False, True):
+            for fmt, w, ref_fmt, ref_w in (
+                (_lib.WEIGHTS_Q8_TILES, q8_tiles, oracle.Q8_0, blocks),
+                (_lib.WEIGHTS_BF16_TILES, bf16_tiles, oracle.BF16_ROWS, host_dequant),
+                (_lib.WEIGHTS_BF16, dequant, oracle.BF16_ROWS, host_dequant),
+            ):
+                y.copy_(torch.from_numpy(before))
+                gemm.Linear(x_dev, Matrix(fmt, w), y, rows, columns, out, accumulate)
+                torch.cuda.synchronize()
+                exact = oracle.product_exact(x, ref_fmt, ref_w, rows, columns, out,
+                                             before if accumulate else None)
+                err = oracle.relative_error(y.cpu().numpy(), *exact)
+                assert err <= LIMIT, f"linear fmt {fmt} rows {rows}: {err:.3e}"
+    gemm.close()
+
+
+def test_unsupported_shapes(cuda):
+    """Launchers return False (nothing launched) for shapes they do not take."""
+    x = torch.zeros(64 * 48, dtype=torch.int16, device="cuda")
+    w = torch.zeros(4096, dtype=torch.uint8, device="cuda")
+    y = torch.zeros(64 * 64, dtype=torch.float32, device="cuda")
+    assert not K.WmmaQ8(x, w, y, 33, 32, 16, False)      # more than 32 rows
+    assert not K.WmmaQ8(x, w, y, 1, 48, 16, False)       # in not a multiple of 32
+    assert not K.WmmaQ8(x, w, y, 0, 32, 16, False)       # no rows
+    assert not K.SkinnyGemm(x, x, y, 1, 16384, 2, False)  # in > 8192

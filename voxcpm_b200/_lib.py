@@ -1,0 +1,141 @@
+"""ctypes binding of libvoxcpm_b200.so (the C ABI in include/voxcpm_b200.h).
+
+The shared library is the product: every kernel runs from it. This module
+only declares argument types. It raises at import when the library is
+missing; there is no fallback path.
+"""
+
+from __future__ import annotations
+
+import ctypes
+import os
+from ctypes import POINTER, c_char_p, c_float, c_int, c_size_t, c_uint, c_uint64, c_void_p
+from pathlib import Path
+
+LIBRARY = Path(__file__).resolve().parent / "libvoxcpm_b200.so"
+
+VX_OK = 0
+VX_UNSUPPORTED = 1
+VX_INVALID = 2
+VX_CUDA_ERROR = 3
+VX_DEVICE_TIMEOUT = 4
+
+WEIGHTS_BF16 = 0
+WEIGHTS_BF16_TILES = 1
+WEIGHTS_Q8_TILES = 2
+
+OUT_F32 = 0
+OUT_BF16 = 1
+
+
+class WmmaPlan(ctypes.Structure):
+    """vx_wmma_plan (replaces WmmaPlan, kernels/wmma_products.hpp:74-81)."""
+
+    _fields_ = [
+        ("splits", c_size_t),
+        ("blocks_per_split", c_size_t),
+        ("partial_floats", c_size_t),
+        ("counters", c_size_t),
+        ("variant", c_int),
+    ]
+
+
+class SplitScratch(ctypes.Structure):
+    """vx_split_scratch (kernels/wmma_products.hpp:62-68)."""
+
+    _fields_ = [
+        ("partials", c_void_p),
+        ("partial_floats", c_size_t),
+        ("counters", c_void_p),
+        ("counter_count", c_size_t),
+    ]
+
+
+# name -> (restype, argtypes)
+SIGNATURES: dict[str, tuple] = {
+    "vx_last_error": (c_char_p, []),
+    "vx_device_error": (c_int, [POINTER(c_uint)]),
+    "vx_version": (c_char_p, []),
+    "vx_q8_tiles_bytes": (c_size_t, [c_size_t, c_size_t]),
+    "vx_bf16_tiles_bytes": (c_size_t, [c_size_t, c_size_t]),
+    "vx_q8_0_to_tiles": (c_int, [c_void_p, c_size_t, c_size_t, c_void_p, c_void_p]),
+    "vx_bf16_to_tiles": (c_int, [c_void_p, c_size_t, c_size_t, c_void_p, c_void_p]),
+    "vx_q8_tiles_to_bf16": (c_int, [c_void_p, c_size_t, c_size_t, c_void_p, c_void_p]),
+    "vx_bf16_tiles_to_rows": (c_int, [c_void_p, c_size_t, c_size_t, c_void_p, c_void_p]),
+    "vx_plan_wmma": (WmmaPlan, [c_size_t, c_size_t, c_size_t, c_size_t]),
+    "vx_wmma_q8": (
+        c_int,
+        [c_void_p, c_void_p, c_void_p, c_size_t, c_size_t, c_size_t, c_int,
+         POINTER(WmmaPlan), POINTER(SplitScratch), c_void_p],
+    ),
+    "vx_wmma_bf16": (
+        c_int,
+        [c_void_p, c_void_p, c_void_p, c_size_t, c_size_t, c_size_t, c_int,
+         POINTER(WmmaPlan), POINTER(SplitScratch), c_void_p],
+    ),
+    "vx_skinny_gemm": (
+        c_int,
+        [c_void_p, c_void_p, c_void_p, c_size_t, c_size_t, c_size_t, c_int, c_void_p],
+    ),
+    "vx_skinny_gemm_with": (
+        c_int,
+        [c_int, c_void_p, c_void_p, c_void_p, c_size_t, c_size_t, c_size_t, c_int, c_void_p],
+    ),
+    "vx_read_probe": (c_int, [c_void_p, c_size_t, c_uint, c_void_p, c_void_p]),
+    "vx_product": (
+        c_int,
+        [c_int, c_void_p, c_void_p, c_void_p, c_int, c_size_t, c_size_t, c_size_t,
+         c_int, POINTER(WmmaPlan), c_void_p],
+    ),
+    "vx_set_programmatic_launch": (None, [c_int]),
+    "vx_product_variants": (c_int, []),
+    "vx_product_variant_shape": (
+        None, [c_int, POINTER(c_int), POINTER(c_int), POINTER(c_int), POINTER(c_int)]
+    ),
+    "vx_random_q8_0": (c_int, [c_uint64, c_uint64, c_size_t, c_size_t, c_float, c_void_p]),
+    "vx_random_bf16": (c_int, [c_uint64, c_uint64, c_size_t, c_float, c_float, c_void_p]),
+    "vx_gemm_create": (c_void_p, [c_void_p]),
+    "vx_gemm_destroy": (None, [c_void_p]),
+    "vx_gemm_linear": (
+        c_int,
+        [c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_size_t, c_size_t, c_size_t, c_int],
+    ),
+}
+
+_lib: ctypes.CDLL | None = None
+
+
+def load() -> ctypes.CDLL:
+    """The loaded library with argument types declared (raises if absent)."""
+    global _lib
+    if _lib is not None:
+        return _lib
+    if not LIBRARY.exists():
+        raise ImportError(
+            f"{LIBRARY} is missing: build it with `python -m voxcpm_b200.build` "
+            "(the CUDA library is the only implementation; there is no fallback)"
+        )
+    lib = ctypes.CDLL(str(LIBRARY), mode=os.RTLD_NOW | ctypes.RTLD_GLOBAL)
+    for name, (restype, argtypes) in SIGNATURES.items():
+        fn = getattr(lib, name)
+        fn.restype = restype
+        fn.argtypes = argtypes
+    _lib = lib
+    return lib
+
+
+class VxError(RuntimeError):
+    """A failed library call (the reference throws GpuError, device.hpp:16-30)."""
+
+    def __init__(self, status: int, message: str):
+        super().__init__(f"status {status}: {message}")
+        self.status = status
+
+
+def check(status: int, unsupported_ok: bool = False) -> bool:
+    """Maps a vx_status to True / False (unsupported) / an exception."""
+    if status == VX_OK:
+        return True
+    if status == VX_UNSUPPORTED and unsupported_ok:
+        return False
+    raise VxError(status, load().vx_last_error().decode(errors="replace"))

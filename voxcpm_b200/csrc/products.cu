@@ -1,0 +1,830 @@
+// Skinny products on sm_100a (see products.cuh).
+//
+// Design (B200-first, not a translation of the reference's WMMA kernel):
+// - Weights stream from HBM into shared memory with 1-D TMA bulk copies
+//   (cp.async.bulk + mbarrier transaction counts), one ring of stages per
+//   warp, so a warp never waits on another warp for its weights. Copies
+//   carry an L2 evict-first hint: weights are read once per product.
+// - Each warp owns 16-row groups of weights for the CTA's slice of the
+//   reduction and runs mma.sync m16n8k16 (bf16 in, fp32 accumulate) with the
+//   weights as the 16-row A operand and the activation rows as 8-column B
+//   tiles (22 rows -> 3 tiles). The k index is permuted identically in A and
+//   B so that every lane reads contiguous bytes (8 int8 or 8 bf16 of a row):
+//   no ldmatrix, no bank conflicts.
+// - Q8_0 stays exact (kernels/wmma_products.hip:29-55): the int8 values are
+//   stored biased (q + 128) and become bf16 through the float bit pattern
+//   0x4B0000uu - (2^23 + 128) (exact); every 32-column block is summed in
+//   fp32 by its own pair of MMAs and then scaled by its fp16 scale into the
+//   fp32 accumulator with one fused multiply-add (the reference's
+//   fmaf(scale, sum, acc), kernels/wmma_products.hip:201-209).
+// - Split-K runs inside one thread-block cluster: the CTAs of a cluster take
+//   consecutive slices of the reduction of the same weight rows, and CTA 0
+//   adds the others' partial sums from their shared memory (DSMEM) in
+//   cluster-rank order, so results never depend on timing (the reference's
+//   ordered split sum, kernels/wmma_products.hip:249-295) and no global
+//   scratch or counters are needed.
+// - Launched with programmatic dependent launch: a product issues its
+//   weight copies before waiting for the previous kernel, so consecutive
+//   products keep HBM busy across kernel boundaries.
+#include "products.cuh"
+#include "vx_common.cuh"
+
+#include <algorithm>
+#include <atomic>
+#include <mutex>
+
+namespace vx {
+
+__device__ unsigned g_vx_device_error = 0;
+
+unsigned* DeviceErrorWord() {
+  void* address = nullptr;
+  if (cudaGetSymbolAddress(&address, g_vx_device_error) != cudaSuccess)
+    return nullptr;
+  return static_cast<unsigned*>(address);
+}
+
+int ReadDeviceError(unsigned* bits) {
+  if (cudaDeviceSynchronize() != cudaSuccess)
+    return kCudaError;
+  unsigned value = 0;
+  if (cudaMemcpyFromSymbol(&value, g_vx_device_error, sizeof(unsigned)) !=
+      cudaSuccess)
+    return kCudaError;
+  const unsigned zero = 0;
+  if (cudaMemcpyToSymbol(g_vx_device_error, &zero, sizeof(unsigned)) !=
+      cudaSuccess)
+    return kCudaError;
+  *bits = value;
+  return kOk;
+}
+
+namespace {
+
+// ------------------------------------------------------------ kernel shapes
+
+struct VariantShape {
+  int warps;   // consumer warps per CTA
+  int groups;  // 16-row weight groups per warp
+  int stage;   // 32-column blocks per pipeline stage
+  int depth;   // stages in flight per warp
+};
+
+constexpr VariantShape kVariants[] = {
+    {8, 1, 4, 4},  // 128 rows per CTA
+    {4, 1, 4, 4},  // 64 rows per CTA
+    {4, 2, 2, 4},  // 128 rows per CTA, two groups per warp
+    {2, 1, 4, 6},  // 32 rows per CTA
+    {8, 1, 2, 6},  // 128 rows per CTA, shorter stages
+};
+constexpr int kNumVariants = sizeof(kVariants) / sizeof(kVariants[0]);
+
+__host__ __device__ constexpr int RowStrideBytes(int stage) {
+  // Rows of a bf16-rows stage are padded so that 8 lanes reading 16 bytes at
+  // the same column of consecutive rows hit distinct banks (stride = 64 mod
+  // 128).
+  return stage * 64 + ((stage % 2 == 0) ? 64 : 0);
+}
+
+__host__ __device__ constexpr int GroupStageBytes(int format, int stage) {
+  return format == static_cast<int>(WeightFormat::kQ8Tiles)
+             ? stage * kQ8TileBytes
+             : (format == static_cast<int>(WeightFormat::kBf16Tiles)
+                    ? stage * kBf16TileBytes
+                    : 16 * RowStrideBytes(stage));
+}
+
+inline std::size_t Align128(std::size_t v) { return (v + 127) / 128 * 128; }
+
+/// x rows in shared memory: `columns` bf16 per row, padded to 64 mod 128
+/// bytes (conflict-free 16-byte reads of 8 consecutive rows).
+inline int XStrideBytes(int columns) {
+  const int bytes = columns * 2;
+  return (bytes % 128 == 64) ? bytes : (bytes + 127) / 128 * 128 + 64;
+}
+
+struct ProductArgs {
+  const Bf16* x;
+  const unsigned char* w;
+  float* y;
+  Bf16* y_bf16;
+  int m;  // activation rows
+  int k;  // reduction size (in)
+  int n;  // output columns (out)
+  int k_blocks;
+  int splits;
+  int blocks_per_split;
+  int accumulate;
+  int x_stride;     // bytes per activation row in shared memory
+  int rings_bytes;  // bytes of all warps' rings (>= the reduction buffer)
+};
+
+// ------------------------------------------------------------ math pieces
+
+__device__ inline void Mma16816(float (&d)[4], std::uint32_t a0,
+                                std::uint32_t a1, std::uint32_t a2,
+                                std::uint32_t a3, std::uint32_t b0,
+                                std::uint32_t b1, const float (&c)[4]) {
+  asm volatile(
+      "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, "
+      "{%4,%5,%6,%7}, {%8,%9}, {%10,%11,%12,%13};"
+      : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(c[0]),
+        "f"(c[1]), "f"(c[2]), "f"(c[3]));
+}
+
+/// Four biased int8 values (q + 128) -> two bf16 pairs (bytes 0,1 and 2,3),
+/// exactly: 0x4B0000uu is 2^23 + u as a float; subtracting 2^23 + 128
+/// leaves q, whose float has at most 8 significant bits, so its upper half
+/// is its bf16.
+__device__ inline void DequantWord(std::uint32_t w, std::uint32_t& pair01,
+                                   std::uint32_t& pair23) {
+  const float f0 = __uint_as_float(Prmt(w, 0x4B000000u, 0x7540u));
+  const float f1 = __uint_as_float(Prmt(w, 0x4B000000u, 0x7541u));
+  const float f2 = __uint_as_float(Prmt(w, 0x4B000000u, 0x7542u));
+  const float f3 = __uint_as_float(Prmt(w, 0x4B000000u, 0x7543u));
+  const float2 bias = make_float2(-8388736.0f, -8388736.0f);
+  const float2 a = Add2(make_float2(f0, f1), bias);
+  const float2 b = Add2(make_float2(f2, f3), bias);
+  pair01 = Prmt(__float_as_uint(a.x), __float_as_uint(a.y), 0x7632u);
+  pair23 = Prmt(__float_as_uint(b.x), __float_as_uint(b.y), 0x7632u);
+}
+
+// ------------------------------------------------------------ the kernel
+
+template <int kFormat, int kWarps, int kGroups, int kNTiles, int kStage,
+          int kDepth>
+__global__ void __launch_bounds__(kWarps * 32)
+    ProductKernel(const ProductArgs p) {
+  constexpr int kGroupBytes = GroupStageBytes(kFormat, kStage);
+  constexpr int kRingBytes = kDepth * kGroups * kGroupBytes;
+  constexpr bool kQ8 = kFormat == static_cast<int>(WeightFormat::kQ8Tiles);
+  constexpr bool kRows = kFormat == static_cast<int>(WeightFormat::kBf16);
+  constexpr int kTileBytes = kQ8 ? kQ8TileBytes : kBf16TileBytes;
+  constexpr int kRowStride = RowStrideBytes(kStage);
+
+  extern __shared__ __align__(128) unsigned char smem[];
+  const int lane = threadIdx.x & 31;
+  const int warp = threadIdx.x >> 5;
+  const int gid = lane >> 2;
+  const int tig = lane & 3;
+  const int split = static_cast<int>(blockIdx.x) % p.splits;
+  const int panel = static_cast<int>(blockIdx.x) / p.splits;
+  const int first = split * p.blocks_per_split;
+  const int last = min(first + p.blocks_per_split, p.k_blocks);
+  const int nblocks = max(last - first, 0);
+  const int x_rows = kNTiles * 8;
+  const int groups_total = (p.n + 15) / 16;
+  const int group0 = (panel * kWarps + warp) * kGroups;
+  const int my_groups = max(0, min(kGroups, groups_total - group0));
+
+  unsigned char* xs = smem;
+  unsigned char* rings = smem + ((x_rows * p.x_stride + 127) / 128) * 128;
+  std::uint64_t* bars =
+      reinterpret_cast<std::uint64_t*>(rings + p.rings_bytes);
+  std::uint64_t* xbar = bars + kWarps * kDepth;
+  unsigned char* ring = rings + warp * kRingBytes;
+  std::uint64_t* full = bars + warp * kDepth;
+
+  if (threadIdx.x == 0) {
+    for (int i = 0; i < kWarps * kDepth + 1; ++i)
+      MbarInit(&bars[i], 1);
+    FenceMbarInit();
+  }
+  // Activation rows past `m` read as zeros.
+  {
+    uint4* pad = reinterpret_cast<uint4*>(xs + p.m * p.x_stride);
+    const int count = (x_rows - p.m) * p.x_stride / 16;
+    for (int i = threadIdx.x; i < count; i += blockDim.x)
+      pad[i] = make_uint4(0, 0, 0, 0);
+  }
+  __syncthreads();
+
+  const std::uint64_t evict_first = PolicyEvictFirst();
+  const int nstages = (nblocks + kStage - 1) / kStage;
+
+  // Issues stage `st` of this warp's weights into its ring slot.
+  auto issue = [&](int st) {
+    const int slot = st % kDepth;
+    const int b0 = first + st * kStage;
+    const int nb = min(kStage, last - b0);
+    std::uint64_t* bar = &full[slot];
+    unsigned char* dst = ring + slot * kGroups * kGroupBytes;
+    if constexpr (!kRows) {
+      if (lane == 0) {
+        MbarArriveExpectTx(bar, my_groups * nb * kTileBytes);
+        for (int g = 0; g < my_groups; ++g) {
+          const unsigned char* src =
+              p.w + (static_cast<std::size_t>(group0 + g) * p.k_blocks + b0) *
+                        kTileBytes;
+          BulkLoad(dst + g * kGroupBytes, src, nb * kTileBytes, bar,
+                   evict_first);
+        }
+      }
+    } else {
+      int valid = 0;
+      for (int g = 0; g < my_groups; ++g)
+        valid += min(16, p.n - (group0 + g) * 16);
+      if (lane == 0)
+        MbarArriveExpectTx(bar, valid * nb * 64);
+      __syncwarp();
+      if (lane < 16) {
+        for (int g = 0; g < my_groups; ++g) {
+          const int row = (group0 + g) * 16 + lane;
+          if (row < p.n) {
+            const unsigned char* src =
+                p.w + (static_cast<std::size_t>(row) * p.k + b0 * 32) * 2;
+            BulkLoad(dst + g * kGroupBytes + lane * kRowStride, src, nb * 64,
+                     bar, evict_first);
+          }
+        }
+      }
+    }
+  };
+
+  const bool active = my_groups > 0 && nblocks > 0;
+  int issued = 0;
+  if (active) {
+    for (; issued < min(kDepth, nstages); ++issued)
+      issue(issued);
+  }
+  // Weights do not depend on earlier kernels; activations (and y) may.
+  GridLaunchDependents();
+  GridDependencyWait();
+  if (threadIdx.x == 0 && nblocks > 0) {
+    const std::uint64_t evict_last = PolicyEvictLast();
+    MbarArriveExpectTx(xbar, p.m * nblocks * 64);
+    for (int row = 0; row < p.m; ++row)
+      BulkLoad(xs + row * p.x_stride,
+               p.x + static_cast<std::size_t>(row) * p.k + first * 32,
+               nblocks * 64, xbar, evict_last);
+  }
+
+  float acc[kGroups][kNTiles][4];
+#pragma unroll
+  for (int g = 0; g < kGroups; ++g)
+#pragma unroll
+    for (int j = 0; j < kNTiles; ++j)
+#pragma unroll
+      for (int c = 0; c < 4; ++c)
+        acc[g][j][c] = 0.0f;
+
+  bool failed = false;
+  int waited = 0;
+  if (active) {
+    if (!MbarWaitBounded(xbar, 0, &g_vx_device_error, kErrActivationWait))
+      failed = true;
+    for (int st = 0; st < nstages && !failed; ++st) {
+      const int slot = st % kDepth;
+      if (!MbarWaitBounded(&full[slot], (st / kDepth) & 1,
+                           &g_vx_device_error, kErrWeightWait)) {
+        failed = true;
+        break;
+      }
+      ++waited;
+      const int nb = min(kStage, last - (first + st * kStage));
+      const unsigned char* stage_base = ring + slot * kGroups * kGroupBytes;
+#pragma unroll 1
+      for (int kb = 0; kb < nb; ++kb) {
+        // B: 8 consecutive reduction columns of activation row 8j + gid.
+        uint4 b[kNTiles];
+        const int column = (st * kStage + kb) * 32 + 8 * tig;
+#pragma unroll
+        for (int j = 0; j < kNTiles; ++j)
+          b[j] = *reinterpret_cast<const uint4*>(
+              xs + (8 * j + gid) * p.x_stride + column * 2);
+#pragma unroll
+        for (int g = 0; g < kGroups; ++g) {
+          if (g >= my_groups)
+            break;
+          const unsigned char* base = stage_base + g * kGroupBytes;
+          if constexpr (kQ8) {
+            const unsigned char* tile = base + kb * kQ8TileBytes;
+            const uint2 lo =
+                *reinterpret_cast<const uint2*>(tile + gid * 32 + 8 * tig);
+            const uint2 hi = *reinterpret_cast<const uint2*>(
+                tile + (gid + 8) * 32 + 8 * tig);
+            const std::uint32_t sc =
+                *reinterpret_cast<const std::uint32_t*>(tile + 512 + 4 * gid);
+            const float s_lo = HalfBitsToFloat(
+                static_cast<std::uint16_t>(sc & 0xFFFFu));
+            const float s_hi =
+                HalfBitsToFloat(static_cast<std::uint16_t>(sc >> 16));
+            std::uint32_t a00, a02, a01, a03, a10, a12, a11, a13;
+            DequantWord(lo.x, a00, a02);
+            DequantWord(hi.x, a01, a03);
+            DequantWord(lo.y, a10, a12);
+            DequantWord(hi.y, a11, a13);
+            const float zero[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+            for (int j = 0; j < kNTiles; ++j) {
+              float part[4];
+              Mma16816(part, a00, a01, a02, a03, b[j].x, b[j].y, zero);
+              Mma16816(part, a10, a11, a12, a13, b[j].z, b[j].w, part);
+              const float2 lo2 = Fma2(make_float2(s_lo, s_lo),
+                                      make_float2(part[0], part[1]),
+                                      make_float2(acc[g][j][0], acc[g][j][1]));
+              const float2 hi2 = Fma2(make_float2(s_hi, s_hi),
+                                      make_float2(part[2], part[3]),
+                                      make_float2(acc[g][j][2], acc[g][j][3]));
+              acc[g][j][0] = lo2.x;
+              acc[g][j][1] = lo2.y;
+              acc[g][j][2] = hi2.x;
+              acc[g][j][3] = hi2.y;
+            }
+          } else {
+            const unsigned char* row_lo;
+            const unsigned char* row_hi;
+            if constexpr (kRows) {
+              row_lo = base + gid * kRowStride + kb * 64;
+              row_hi = base + (gid + 8) * kRowStride + kb * 64;
+            } else {
+              const unsigned char* tile = base + kb * kBf16TileBytes;
+              row_lo = tile + gid * 64;
+              row_hi = tile + (gid + 8) * 64;
+            }
+            const uint4 lo = *reinterpret_cast<const uint4*>(row_lo + 16 * tig);
+            const uint4 hi = *reinterpret_cast<const uint4*>(row_hi + 16 * tig);
+#pragma unroll
+            for (int j = 0; j < kNTiles; ++j) {
+              Mma16816(acc[g][j], lo.x, hi.x, lo.y, hi.y, b[j].x, b[j].y,
+                       acc[g][j]);
+              Mma16816(acc[g][j], lo.z, hi.z, lo.w, hi.w, b[j].z, b[j].w,
+                       acc[g][j]);
+            }
+          }
+        }
+      }
+      __syncwarp();
+      if (issued < nstages) {
+        // The slot's generic-proxy reads are done; order them before the
+        // async-proxy writes of the next copy.
+        FenceProxyAsync();
+        issue(issued);
+        ++issued;
+      }
+    }
+    if (failed) {
+      // Give copies still in flight a bounded chance to land before the
+      // shared memory is released.
+      for (int st = waited; st < issued; ++st)
+        (void)MbarWaitBounded(&full[st % kDepth], (st / kDepth) & 1,
+                              &g_vx_device_error, kErrDrainWait,
+                              100000000ull);
+    }
+  }
+
+  const int lanes_groups = kWarps * kGroups * kNTiles;
+  if (p.splits > 1) {
+    float4* red = reinterpret_cast<float4*>(rings);
+    __syncthreads();  // every warp is done with its ring
+    if (split != 0) {
+#pragma unroll
+      for (int g = 0; g < kGroups; ++g)
+#pragma unroll
+        for (int j = 0; j < kNTiles; ++j)
+          red[((warp * kGroups + g) * kNTiles + j) * 32 + lane] =
+              make_float4(acc[g][j][0], acc[g][j][1], acc[g][j][2],
+                          acc[g][j][3]);
+    }
+    ClusterSync();
+    if (split == 0) {
+      for (int r = 1; r < p.splits; ++r) {
+#pragma unroll
+        for (int g = 0; g < kGroups; ++g)
+#pragma unroll
+          for (int j = 0; j < kNTiles; ++j) {
+            const float4 v = LoadSharedCluster4(MapShared(
+                &red[((warp * kGroups + g) * kNTiles + j) * 32 + lane], r));
+            acc[g][j][0] += v.x;
+            acc[g][j][1] += v.y;
+            acc[g][j][2] += v.z;
+            acc[g][j][3] += v.w;
+          }
+      }
+    }
+    ClusterSync();  // the others keep their shared memory until CTA 0 read it
+  }
+  (void)lanes_groups;
+  if (split != 0)
+    return;
+#pragma unroll
+  for (int g = 0; g < kGroups; ++g) {
+    if (g >= my_groups)
+      break;
+#pragma unroll
+    for (int j = 0; j < kNTiles; ++j)
+#pragma unroll
+      for (int c = 0; c < 4; ++c) {
+        const int n = (group0 + g) * 16 + gid + 8 * (c >> 1);
+        const int m = 8 * j + 2 * tig + (c & 1);
+        if (m < p.m && n < p.n) {
+          const std::size_t index = static_cast<std::size_t>(m) * p.n + n;
+          float value = acc[g][j][c];
+          if (p.y != nullptr) {
+            if (p.accumulate)
+              value = p.y[index] + value;
+            p.y[index] = value;
+          } else {
+            if (p.accumulate)
+              value = Bf16ToFloat(p.y_bf16[index]) + value;
+            p.y_bf16[index] = FloatToBf16(value);
+          }
+        }
+      }
+  }
+}
+
+// ------------------------------------------------------------ dispatch table
+
+using KernelFn = void (*)(const ProductArgs);
+
+template <int kFormat, int kNTiles, int kVariant>
+constexpr KernelFn KernelFor() {
+  return ProductKernel<kFormat, kVariants[kVariant].warps,
+                       kVariants[kVariant].groups, kNTiles,
+                       kVariants[kVariant].stage, kVariants[kVariant].depth>;
+}
+
+template <int kFormat, int kNTiles, int... kV>
+struct VariantRow {
+  static constexpr KernelFn table[] = {KernelFor<kFormat, kNTiles, kV>()...};
+};
+
+template <int kFormat, int kNTiles>
+using Row = VariantRow<kFormat, kNTiles, 0, 1, 2, 3, 4>;
+
+KernelFn Lookup(int format, int ntiles, int variant) {
+  static const KernelFn* table[3][4] = {
+      {Row<0, 1>::table, Row<0, 2>::table, Row<0, 3>::table, Row<0, 4>::table},
+      {Row<1, 1>::table, Row<1, 2>::table, Row<1, 3>::table, Row<1, 4>::table},
+      {Row<2, 1>::table, Row<2, 2>::table, Row<2, 3>::table, Row<2, 4>::table},
+  };
+  return table[format][ntiles - 1][variant];
+}
+
+std::atomic<bool> g_programmatic{true};
+
+int SmCount() {
+  static int count = [] {
+    int device = 0;
+    int sms = 148;
+    if (cudaGetDevice(&device) == cudaSuccess)
+      cudaDeviceGetAttribute(&sms, cudaDevAttrMultiProcessorCount, device);
+    return sms;
+  }();
+  return count;
+}
+
+struct Footprint {
+  int x_stride;
+  int rings_bytes;
+  std::size_t smem;
+};
+
+Footprint FootprintOf(int format, int variant, int ntiles,
+                      int blocks_per_split) {
+  const VariantShape& v = kVariants[variant];
+  Footprint f;
+  f.x_stride = XStrideBytes(blocks_per_split * 32);
+  const int rings =
+      v.warps * v.depth * v.groups * GroupStageBytes(format, v.stage);
+  const int reduction = v.warps * v.groups * ntiles * 32 * 16;
+  f.rings_bytes = static_cast<int>(Align128(std::max(rings, reduction)));
+  f.smem = Align128(static_cast<std::size_t>(ntiles) * 8 * f.x_stride) +
+           f.rings_bytes + (v.warps * v.depth + 1) * 8;
+  return f;
+}
+
+}  // namespace
+
+void SetProgrammaticLaunch(bool enabled) { g_programmatic = enabled; }
+bool ProgrammaticLaunch() { return g_programmatic; }
+
+int NumProductVariants() { return kNumVariants; }
+
+void ProductVariantShape(int variant, int* warps, int* groups, int* stage,
+                         int* depth) {
+  const VariantShape& v = kVariants[variant];
+  *warps = v.warps;
+  *groups = v.groups;
+  *stage = v.stage;
+  *depth = v.depth;
+}
+
+ProductPlan PlanProduct(WeightFormat format, std::size_t rows, std::size_t in,
+                        std::size_t out, std::size_t target_ctas) {
+  ProductPlan best;
+  if (rows == 0 || in == 0 || out == 0 || in % kTileColumns != 0)
+    return best;
+  const int k_blocks = static_cast<int>(in / kTileColumns);
+  const int groups_total = static_cast<int>((out + 15) / 16);
+  const int min_splits =
+      (k_blocks * kTileColumns + kMaxSliceColumns - 1) / kMaxSliceColumns;
+  const int sms = SmCount();
+  const int ntiles = static_cast<int>((std::min<std::size_t>(rows, 32) + 7) / 8);
+  // Candidates: every variant and split count; cost = the largest number of
+  // weight blocks a CTA streams (one wave of CTAs), plus a small charge per
+  // split for the activation slice and the cluster reduction.
+  double best_cost = 1e30;
+  for (int variant = 0; variant < kNumVariants; ++variant) {
+    const VariantShape& v = kVariants[variant];
+    const int rows_per_cta = 16 * v.groups * v.warps;
+    const int panels = (groups_total * 16 + rows_per_cta - 1) / rows_per_cta;
+    for (int splits = std::max(1, min_splits); splits <= 8; ++splits) {
+      if (splits > k_blocks)
+        break;
+      const int bps = (k_blocks + splits - 1) / splits;
+      const int used = (k_blocks + bps - 1) / bps;
+      if (used != splits)
+        continue;
+      const Footprint f =
+          FootprintOf(static_cast<int>(format), variant, ntiles, bps);
+      if (f.smem > 200 * 1024)
+        continue;
+      const int ctas = panels * splits;
+      double cost;
+      if (target_ctas != 0) {
+        cost = std::abs(static_cast<double>(ctas) -
+                        static_cast<double>(target_ctas)) +
+               0.01 * variant;
+      } else {
+        const int waves = (ctas + sms - 1) / sms;
+        const double per_cta = static_cast<double>(rows_per_cta) / 16.0 * bps;
+        cost = waves * (per_cta + 2.0) + 1.5 * splits +
+               (v.warps < 4 ? 2.0 : 0.0);
+      }
+      if (cost < best_cost) {
+        best_cost = cost;
+        best.variant = variant;
+        best.splits = splits;
+        best.blocks_per_split = bps;
+      }
+    }
+  }
+  return best;
+}
+
+int LaunchProduct(WeightFormat format, const std::uint16_t* x, const void* w,
+                  float* y, std::uint16_t* y_bf16, std::size_t rows,
+                  std::size_t in, std::size_t out, bool accumulate,
+                  const ProductPlan* plan_in, cudaStream_t stream) {
+  if (rows == 0 || rows > kMaxProductRows || in == 0 || out == 0 ||
+      in % kTileColumns != 0)
+    return kUnsupported;
+  if (x == nullptr || w == nullptr || (y == nullptr && y_bf16 == nullptr))
+    return kInvalid;
+  if (reinterpret_cast<std::uintptr_t>(x) % 16 != 0 ||
+      reinterpret_cast<std::uintptr_t>(w) % 16 != 0)
+    return kInvalid;
+  const int f = static_cast<int>(format);
+  if (f < 0 || f > 2)
+    return kInvalid;
+  const int k_blocks = static_cast<int>(in / kTileColumns);
+  ProductPlan plan = plan_in != nullptr && plan_in->variant >= 0
+                         ? *plan_in
+                         : PlanProduct(format, rows, in, out, 0);
+  if (plan.variant < 0 || plan.variant >= kNumVariants || plan.splits < 1 ||
+      plan.splits > 8 || plan.blocks_per_split < 1 ||
+      plan.blocks_per_split * 32 > kMaxSliceColumns ||
+      static_cast<long>(plan.splits) * plan.blocks_per_split < k_blocks ||
+      (k_blocks + plan.blocks_per_split - 1) / plan.blocks_per_split !=
+          plan.splits)
+    return kUnsupported;
+  const int ntiles = static_cast<int>((rows + 7) / 8);
+  const Footprint fp =
+      FootprintOf(f, plan.variant, ntiles, plan.blocks_per_split);
+  if (fp.smem > 200 * 1024)
+    return kUnsupported;
+  const VariantShape& v = kVariants[plan.variant];
+  const int rows_per_cta = 16 * v.groups * v.warps;
+  const int panels =
+      static_cast<int>((out + rows_per_cta - 1) / rows_per_cta);
+  KernelFn kernel = Lookup(f, ntiles, plan.variant);
+
+  // The dynamic shared-memory limit is per function and device.
+  {
+    static std::mutex mutex;
+    static std::size_t configured[8][3][4][kNumVariants] = {};
+    int device = 0;
+    if (cudaGetDevice(&device) != cudaSuccess)
+      return kCudaError;
+    std::lock_guard<std::mutex> lock(mutex);
+    std::size_t& have = configured[device & 7][f][ntiles - 1][plan.variant];
+    if (have < fp.smem) {
+      if (cudaFuncSetAttribute(kernel,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               static_cast<int>(200 * 1024)) != cudaSuccess)
+        return kCudaError;
+      have = 200 * 1024;
+    }
+  }
+
+  ProductArgs args;
+  args.x = x;
+  args.w = static_cast<const unsigned char*>(w);
+  args.y = y;
+  args.y_bf16 = y != nullptr ? nullptr : y_bf16;
+  args.m = static_cast<int>(rows);
+  args.k = static_cast<int>(in);
+  args.n = static_cast<int>(out);
+  args.k_blocks = k_blocks;
+  args.splits = plan.splits;
+  args.blocks_per_split = plan.blocks_per_split;
+  args.accumulate = accumulate ? 1 : 0;
+  args.x_stride = fp.x_stride;
+  args.rings_bytes = fp.rings_bytes;
+
+  cudaLaunchConfig_t config = {};
+  config.gridDim = dim3(static_cast<unsigned>(panels * plan.splits));
+  config.blockDim = dim3(static_cast<unsigned>(v.warps * 32));
+  config.dynamicSmemBytes = fp.smem;
+  config.stream = stream;
+  cudaLaunchAttribute attributes[2];
+  int count = 0;
+  if (plan.splits > 1) {
+    attributes[count].id = cudaLaunchAttributeClusterDimension;
+    attributes[count].val.clusterDim.x = static_cast<unsigned>(plan.splits);
+    attributes[count].val.clusterDim.y = 1;
+    attributes[count].val.clusterDim.z = 1;
+    ++count;
+  }
+  if (g_programmatic) {
+    attributes[count].id = cudaLaunchAttributeProgrammaticStreamSerialization;
+    attributes[count].val.programmaticStreamSerializationAllowed = 1;
+    ++count;
+  }
+  config.attrs = attributes;
+  config.numAttrs = count;
+  if (cudaLaunchKernelEx(&config, kernel, args) != cudaSuccess)
+    return kCudaError;
+  return kOk;
+}
+
+// ------------------------------------------------------------ repacks
+
+namespace {
+
+/// GGML Q8_0 blocks ([rows][in/32] of {fp16 d, int8 q[32]}) -> tiles of 16
+/// rows x 32 columns: 512 bytes of q + 128 (row-major within the tile), then
+/// the 16 rows' fp16 scales in the order (0,8), (1,9), ..., (7,15). Rows past
+/// `rows` (up to the tile) hold q = 0 and scale 0. Follows the tile order of
+/// kernels/wmma_products.hip:62-79 (16-row groups, blocks along the columns).
+__global__ void Q8_0ToTilesKernel(const std::uint8_t* blocks, int rows,
+                                  int in, std::uint8_t* tiles) {
+  const int per_row = in / 32;
+  const int padded = (rows + 15) / 16 * 16;
+  const long index = static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (index >= static_cast<long>(padded) * per_row)
+    return;
+  const int row = static_cast<int>(index / per_row);
+  const int block = static_cast<int>(index % per_row);
+  std::uint8_t* tile =
+      tiles + (static_cast<std::size_t>(row / 16) * per_row + block) *
+                  kQ8TileBytes;
+  const int r = row % 16;
+  const int scale_slot = r < 8 ? 2 * r : 2 * (r - 8) + 1;
+  if (row < rows) {
+    const std::uint8_t* source = blocks + static_cast<std::size_t>(index) * 34;
+    tile[512 + 2 * scale_slot] = source[0];
+    tile[512 + 2 * scale_slot + 1] = source[1];
+    for (int i = 0; i < 32; ++i)
+      tile[32 * r + i] = static_cast<std::uint8_t>(source[2 + i] ^ 0x80u);
+  } else {
+    tile[512 + 2 * scale_slot] = 0;
+    tile[512 + 2 * scale_slot + 1] = 0;
+    for (int i = 0; i < 32; ++i)
+      tile[32 * r + i] = 0x80u;
+  }
+}
+
+/// bf16 rows -> tiles [16 rows][32] (kernels/wmma_products.hip:81-92);
+/// padding rows are zero.
+__global__ void Bf16ToTilesKernel(const Bf16* w, int rows, int in,
+                                  Bf16* tiles) {
+  const int padded = (rows + 15) / 16 * 16;
+  const long index = static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (index >= static_cast<long>(padded) * in)
+    return;
+  const int row = static_cast<int>(index / in);
+  const int k = static_cast<int>(index % in);
+  const int per_row = in / 32;
+  tiles[(static_cast<std::size_t>(row / 16) * per_row + k / 32) * 512 +
+        (row % 16) * 32 + k % 32] = row < rows ? w[index] : Bf16{0};
+}
+
+/// Q8 tiles -> bf16(scale * q) rows, the rounding of a load-time expansion
+/// (kernels/wmma_products.hip:94-112).
+__global__ void Q8TilesToBf16Kernel(const std::uint8_t* tiles, int rows,
+                                    int in, Bf16* out) {
+  const long index = static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (index >= static_cast<long>(rows) * in)
+    return;
+  const int row = static_cast<int>(index / in);
+  const int k = static_cast<int>(index % in);
+  const int per_row = in / 32;
+  const std::uint8_t* tile =
+      tiles + (static_cast<std::size_t>(row / 16) * per_row + k / 32) *
+                  kQ8TileBytes;
+  const int r = row % 16;
+  const int scale_slot = r < 8 ? 2 * r : 2 * (r - 8) + 1;
+  const auto bits = static_cast<std::uint16_t>(
+      tile[512 + 2 * scale_slot] | (tile[513 + 2 * scale_slot] << 8));
+  const int q = static_cast<int>(tile[32 * r + k % 32]) - 128;
+  out[index] = FloatToBf16(HalfBitsToFloat(bits) * static_cast<float>(q));
+}
+
+__global__ void Bf16TilesToRowsKernel(const Bf16* tiles, int rows, int in,
+                                      Bf16* out) {
+  const long index = static_cast<long>(blockIdx.x) * blockDim.x + threadIdx.x;
+  if (index >= static_cast<long>(rows) * in)
+    return;
+  const int row = static_cast<int>(index / in);
+  const int k = static_cast<int>(index % in);
+  const int per_row = in / 32;
+  out[index] = tiles[(static_cast<std::size_t>(row / 16) * per_row + k / 32) *
+                         512 +
+                     (row % 16) * 32 + k % 32];
+}
+
+__global__ void ReadProbeKernel(const uint4* data, std::size_t count,
+                                unsigned* sink) {
+  unsigned value = 0;
+  for (std::size_t i = blockIdx.x * static_cast<std::size_t>(blockDim.x) +
+                       threadIdx.x;
+       i < count; i += static_cast<std::size_t>(gridDim.x) * blockDim.x) {
+    const uint4 v = __ldcs(data + i);
+    value ^= v.x ^ v.y ^ v.z ^ v.w;
+  }
+  if (value == 0x12345678u)
+    *sink = value;
+}
+
+unsigned BlocksFor(std::size_t count) {
+  return static_cast<unsigned>((count + 255) / 256);
+}
+
+int LaunchStatus() {
+  return cudaGetLastError() == cudaSuccess ? kOk : kCudaError;
+}
+
+}  // namespace
+
+int Q8_0ToTiles(const std::uint8_t* blocks, std::size_t rows, std::size_t in,
+                std::uint8_t* tiles, cudaStream_t stream) {
+  if (in % 32 != 0 || blocks == nullptr || tiles == nullptr)
+    return kInvalid;
+  const std::size_t count = (rows + 15) / 16 * 16 * (in / 32);
+  if (count == 0)
+    return kOk;
+  Q8_0ToTilesKernel<<<BlocksFor(count), 256, 0, stream>>>(
+      blocks, static_cast<int>(rows), static_cast<int>(in), tiles);
+  return LaunchStatus();
+}
+
+int Bf16ToTiles(const std::uint16_t* w, std::size_t rows, std::size_t in,
+                std::uint16_t* tiles, cudaStream_t stream) {
+  if (in % 32 != 0 || w == nullptr || tiles == nullptr)
+    return kInvalid;
+  const std::size_t count = (rows + 15) / 16 * 16 * in;
+  if (count == 0)
+    return kOk;
+  Bf16ToTilesKernel<<<BlocksFor(count), 256, 0, stream>>>(
+      w, static_cast<int>(rows), static_cast<int>(in), tiles);
+  return LaunchStatus();
+}
+
+int Q8TilesToBf16(const std::uint8_t* tiles, std::size_t rows, std::size_t in,
+                  std::uint16_t* out, cudaStream_t stream) {
+  if (in % 32 != 0 || tiles == nullptr || out == nullptr)
+    return kInvalid;
+  const std::size_t count = rows * in;
+  if (count == 0)
+    return kOk;
+  Q8TilesToBf16Kernel<<<BlocksFor(count), 256, 0, stream>>>(
+      tiles, static_cast<int>(rows), static_cast<int>(in), out);
+  return LaunchStatus();
+}
+
+int Bf16TilesToRows(const std::uint16_t* tiles, std::size_t rows,
+                    std::size_t in, std::uint16_t* out, cudaStream_t stream) {
+  if (in % 32 != 0 || tiles == nullptr || out == nullptr)
+    return kInvalid;
+  const std::size_t count = rows * in;
+  if (count == 0)
+    return kOk;
+  Bf16TilesToRowsKernel<<<BlocksFor(count), 256, 0, stream>>>(
+      tiles, static_cast<int>(rows), static_cast<int>(in), out);
+  return LaunchStatus();
+}
+
+int ReadProbe(const void* data, std::size_t pieces, unsigned blocks,
+              unsigned* sink, cudaStream_t stream) {
+  if (data == nullptr || sink == nullptr || blocks == 0)
+    return kInvalid;
+  ReadProbeKernel<<<blocks, 256, 0, stream>>>(static_cast<const uint4*>(data),
+                                              pieces, sink);
+  return LaunchStatus();
+}
+
+}  // namespace vx

@@ -1,0 +1,86 @@
+// Skinny products y[rows][out] (+)= x[rows][in] * W[out][in]^T on sm_100a:
+// bf16 activations, weights as Q8_0 tiles, bf16 tiles or bf16 rows, fp32
+// accumulation, fp32 or bf16 output.
+//
+// Replaces the reference's product kernels: kernels/wmma_products.hip
+// (WmmaQ8 / WmmaBf16, :139-296, :386-400), kernels/skinny_gemm.hip
+// (SkinnyGemm, :42-253, :360-389) and their repack kernels
+// (kernels/wmma_products.hip:62-126).
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstddef>
+#include <cstdint>
+
+namespace vx {
+
+/// Weight storage, matrix.hpp:9-13 (same order).
+enum class WeightFormat : int {
+  kBf16 = 0,       // bfloat16 [out][in], row-major
+  kBf16Tiles = 1,  // bfloat16 tiles of 16 rows x 32 columns
+  kQ8Tiles = 2,    // Q8_0 tiles of 16 rows x 32 columns plus 16 fp16 scales
+};
+
+constexpr int kTileRows = 16;
+constexpr int kTileColumns = 32;
+constexpr int kQ8TileBytes = 16 * 32 + 16 * 2;
+constexpr int kBf16TileBytes = 16 * 32 * 2;
+/// Most activation rows one launch takes (4 MMA column tiles of 8).
+constexpr int kMaxProductRows = 32;
+/// Longest reduction slice one CTA holds in shared memory.
+constexpr int kMaxSliceColumns = 1024;
+
+inline std::size_t Q8TilesBytes(std::size_t rows, std::size_t in) {
+  return (rows + kTileRows - 1) / kTileRows * (in / kTileColumns) *
+         kQ8TileBytes;
+}
+inline std::size_t Bf16TilesBytes(std::size_t rows, std::size_t in) {
+  return (rows + kTileRows - 1) / kTileRows * (in / kTileColumns) *
+         kBf16TileBytes;
+}
+
+/// How one product launch is cut: `splits` CTAs (one thread-block
+/// cluster) share each panel of weight rows, each taking
+/// `blocks_per_split` 32-column blocks of the reduction; `variant` picks
+/// the kernel shape (warps per CTA, row groups per warp, pipeline).
+struct ProductPlan {
+  int variant = -1;
+  int splits = 1;
+  int blocks_per_split = 0;
+};
+
+/// The plan for a product (target_ctas 0: the planner's choice; otherwise
+/// about that many CTAs).
+ProductPlan PlanProduct(WeightFormat format, std::size_t rows, std::size_t in,
+                        std::size_t out, std::size_t target_ctas = 0);
+
+/// Launches one product of at most kMaxProductRows rows. Returns kOk,
+/// kUnsupported (nothing launched) or kInvalid / kCudaError.
+int LaunchProduct(WeightFormat format, const std::uint16_t* x, const void* w,
+                  float* y, std::uint16_t* y_bf16, std::size_t rows,
+                  std::size_t in, std::size_t out, bool accumulate,
+                  const ProductPlan* plan, cudaStream_t stream);
+
+/// Whether kernels are launched with programmatic dependent launch.
+void SetProgrammaticLaunch(bool enabled);
+bool ProgrammaticLaunch();
+
+int NumProductVariants();
+/// Warps, row groups per warp, blocks per stage, stages of a variant.
+void ProductVariantShape(int variant, int* warps, int* groups, int* stage,
+                         int* depth);
+
+// Repacks (load time).
+int Q8_0ToTiles(const std::uint8_t* blocks, std::size_t rows, std::size_t in,
+                std::uint8_t* tiles, cudaStream_t stream);
+int Bf16ToTiles(const std::uint16_t* w, std::size_t rows, std::size_t in,
+                std::uint16_t* tiles, cudaStream_t stream);
+int Q8TilesToBf16(const std::uint8_t* tiles, std::size_t rows, std::size_t in,
+                  std::uint16_t* out, cudaStream_t stream);
+int Bf16TilesToRows(const std::uint16_t* tiles, std::size_t rows,
+                    std::size_t in, std::uint16_t* out, cudaStream_t stream);
+int ReadProbe(const void* data, std::size_t pieces, unsigned blocks,
+              unsigned* sink, cudaStream_t stream);
+
+}  // namespace vx

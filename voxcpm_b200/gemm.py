@@ -1,0 +1,44 @@
+"""Bf16Gemm: product dispatch by weight format and row count (gemm.hpp:49-72),
+over the C ABI (vx_gemm_*)."""
+
+from __future__ import annotations
+
+import torch
+
+from ._lib import check, load
+from .kernels import _ptr, _stream
+
+
+class Matrix:
+    """A weight matrix on the device (matrix.hpp:15-19): format + data."""
+
+    def __init__(self, fmt: int, data: torch.Tensor):
+        self.format = fmt
+        self.data = data
+
+
+class Bf16Gemm:
+    """One instance per stream (gemm.hpp:49-72)."""
+
+    def __init__(self, stream=None):
+        self._lib = load()
+        self._handle = self._lib.vx_gemm_create(_stream(stream))
+        if not self._handle:
+            raise RuntimeError("vx_gemm_create failed")
+
+    def Linear(self, x: torch.Tensor, w: Matrix, y: torch.Tensor, rows: int, columns: int, out: int,
+               accumulate: bool) -> None:
+        """y[rows][out] (+)= x[rows][columns] * w^T (gemm.hpp:51-58)."""
+        check(self._lib.vx_gemm_linear(self._handle, _ptr(x), w.format, _ptr(w.data), _ptr(y),
+                                       rows, columns, out, int(accumulate)))
+
+    def close(self) -> None:
+        if self._handle:
+            self._lib.vx_gemm_destroy(self._handle)
+            self._handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
