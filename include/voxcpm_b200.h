@@ -166,6 +166,117 @@ VX_API int vx_product_variants(void);
 VX_API void vx_product_variant_shape(int variant, int* warps, int* groups,
                               int* stage, int* depth);
 
+/* ------------------------------------------------------------ stack kernels */
+
+/* KV cache element type: float32 (the reference's, transformer.hpp:17-36)
+ * or bf16. Caches are [kv_head][capacity][head_dim] per layer. */
+#define VX_CACHE_F32 0
+#define VX_CACHE_BF16 1
+
+/* Text rows take embedding[ids[row]] * scale, others zero. Replaces Embed
+ * (kernels/generator_kernels.hpp:18-22). */
+VX_API vx_status vx_embed(const uint16_t* table, const int32_t* ids,
+                          const int32_t* text_mask, float* output, size_t rows,
+                          size_t width, float scale, cudaStream_t stream);
+/* output[indices[i]] = input[i]. Replaces ScatterRows
+ * (kernels/generator_kernels.hpp:24-26). */
+VX_API vx_status vx_scatter_rows(const float* input, const int32_t* indices,
+                                 float* output, size_t rows, size_t width,
+                                 cudaStream_t stream);
+/* output[i] = input[indices[i]]. Replaces GatherRows
+ * (kernels/generator_kernels.hpp:28-30). */
+VX_API vx_status vx_gather_rows(const float* input, const int32_t* indices,
+                                float* output, size_t rows, size_t width,
+                                cudaStream_t stream);
+/* bf16(weight * x * rsqrt(mean(x^2) + eps)) per row, optional fp32 copy.
+ * Replaces RmsNorm (kernels/generator_kernels.hpp:32-36). */
+VX_API vx_status vx_rms_norm(const float* input, const uint16_t* weight,
+                             uint16_t* output, float* output_f32, size_t rows,
+                             size_t width, float epsilon, cudaStream_t stream);
+/* Splits [q | k | v] heads, rotates q and k by the cos/sin table row
+ * positions[row] (no rotation when cos_sin is null), writes q
+ * [rows][heads][head_dim] and appends k, v at cache_rows[row]. Replaces
+ * QkvRope (kernels/generator_kernels.hpp:38-47). */
+VX_API vx_status vx_qkv_rope(const float* qkv, const float* cos_sin,
+                             const int32_t* positions,
+                             const int32_t* cache_rows, float* q,
+                             void* k_cache, void* v_cache, int cache_type,
+                             size_t rows, size_t heads, size_t kv_heads,
+                             size_t head_dim, size_t capacity,
+                             cudaStream_t stream);
+/* Softmax attention (head_dim 128, GQA) of each row over `past` cached keys
+ * plus its sequence's rows (up to itself when causal); bf16 output
+ * [rows][heads * 128]. With `past_device` non-null the kernel reads `past`
+ * from device memory (graph replays) and `max_keys` bounds the keys per row.
+ * Replaces Attention (kernels/generator_kernels.hpp:49-58). */
+VX_API vx_status vx_attention(const float* q, const void* k_cache,
+                              const void* v_cache, int cache_type,
+                              uint16_t* output, size_t rows,
+                              size_t rows_per_sequence,
+                              size_t keys_per_sequence, size_t past,
+                              const int32_t* past_device, int causal,
+                              size_t heads, size_t kv_heads, size_t head_dim,
+                              size_t capacity, size_t max_keys,
+                              cudaStream_t stream);
+/* bf16(silu(g) * u) of [rows][gate | up]. Replaces SwiGlu
+ * (kernels/generator_kernels.hpp:60-62). */
+VX_API vx_status vx_swiglu(const float* gate_up, uint16_t* output, size_t rows,
+                           size_t width, cudaStream_t stream);
+/* data[row][i] += bias[i]. Replaces AddBias
+ * (kernels/generator_kernels.hpp:64-66). */
+VX_API vx_status vx_add_bias(float* data, const uint16_t* bias, size_t rows,
+                             size_t width, cudaStream_t stream);
+/* bf16(x) or bf16(silu(x)). Replaces ToBf16
+ * (kernels/generator_kernels.hpp:68-70). */
+VX_API vx_status vx_to_bf16(const float* input, uint16_t* output, size_t count,
+                            int silu, cudaStream_t stream);
+/* bf16 rows [a * a_scale | b * b_scale] (null scales are 1). Replaces
+ * ConcatRows (kernels/generator_kernels.hpp:72-76). */
+VX_API vx_status vx_concat_rows(const float* a, const float* a_scale,
+                                size_t a_width, const float* b,
+                                const float* b_scale, size_t b_width,
+                                uint16_t* output, size_t rows,
+                                cudaStream_t stream);
+/* FSQ: bf16(rint(tanh(x) * scale) / scale). Replaces Quantize
+ * (kernels/generator_kernels.hpp:78-81). */
+VX_API vx_status vx_quantize(const float* input, uint16_t* output, size_t count,
+                             float scale, cudaStream_t stream);
+/* mask ? quantized : plain, per row. Replaces SelectRows
+ * (kernels/generator_kernels.hpp:83-86). */
+VX_API vx_status vx_select_rows(const float* quantized, const float* plain,
+                                const int32_t* mask, float* output,
+                                size_t rows, size_t width,
+                                cudaStream_t stream);
+/* The local encoder's input: per patch a special row, then the projected
+ * rows. Replaces PrependSpecial (kernels/generator_kernels.hpp:88-92). */
+VX_API vx_status vx_prepend_special(const float* rows_in,
+                                    const uint16_t* special, float* output,
+                                    size_t patches, size_t patch_size,
+                                    size_t width, cudaStream_t stream);
+/* The DiT's CFG pair [mu_a, mu_b, time, cond x P, x x P] (unconditional mu
+ * zero). Replaces AssembleDit (kernels/generator_kernels.hpp:94-99). */
+VX_API vx_status vx_assemble_dit(const float* mu, const float* time,
+                                 const float* cond, const float* x,
+                                 float* output, size_t patch_size,
+                                 size_t width, cudaStream_t stream);
+/* CFG-Zero* guidance and the Euler step. Replaces GuidedEuler
+ * (kernels/generator_kernels.hpp:101-107). */
+VX_API vx_status vx_guided_euler(const float* velocity, float* x,
+                                 size_t count, float cfg, float dt,
+                                 cudaStream_t stream);
+
+/* Host: the LongRoPE cos/sin table [positions][cos dim/2 | sin dim/2] in
+ * float32. Replaces RopeTable (transformer.hpp:63-66, transformer.cpp:20-45). */
+VX_API vx_status vx_rope_table(double theta, size_t dim, const double* factors,
+                               double scaling, size_t positions, float* table);
+/* Host: the Euler steps (t, dt, evaluate) of `timesteps` sway-sampled steps;
+ * writes at most `capacity`, returns the count. Replaces EulerSchedule
+ * (generator.hpp:43-44, generator.cpp:63-80). */
+VX_API size_t vx_euler_schedule(size_t timesteps, float sway, float* t,
+                                float* dt, int32_t* evaluate, size_t capacity);
+/* Host: SinusoidalPosEmb(width)(t), scale 1000 (generator.cpp:39-53). */
+VX_API vx_status vx_sinusoid(float t, size_t width, float* out);
+
 /* ------------------------------------------------------------ synthetic weights */
 
 /* Host: GGML Q8_0 blocks [rows][in/32] of seeded random weights, a pure

@@ -90,3 +90,30 @@ def test_invalid_arguments_fail_without_a_gpu():
     status = lib.vx_random_q8_0(0, 0, 4, 33, 0.01, None)
     assert status == _lib.VX_INVALID
     assert b"vx_random_q8_0" in lib.vx_last_error()
+
+
+def test_host_math_matches_the_oracle():
+    """The library's host-side schedule, time embedding and rotary table
+    (generator.cpp:39-80, transformer.cpp:20-45) equal the oracle's bit for
+    bit: both are float32 restatements run on the same host."""
+    import ctypes
+
+    lib = _lib.load()
+    for n in (1, 4, 10, 16, 25, 50):
+        t = np.empty(n, np.float32)
+        dt = np.empty(n, np.float32)
+        ev = np.empty(n, np.int32)
+        assert lib.vx_euler_schedule(n, 1.0, t.ctypes.data, dt.ctypes.data, ev.ctypes.data, n) == n
+        ot, odt, oev = oracle.euler_schedule(n)
+        assert np.array_equal(t, ot) and np.array_equal(dt, odt) and np.array_equal(ev.astype(bool), oev)
+    for t_value in (0.0, 0.63, 0.9564344, 1.0):
+        ours = np.empty(1024, np.float32)
+        assert lib.vx_sinusoid(t_value, 1024, ours.ctypes.data) == 0
+        assert np.array_equal(ours, oracle.sinusoid(t_value, 1024))
+    factors = (1.0 + np.random.default_rng(3).random(64) * 3.0).astype(np.float64)
+    ours = np.empty(64 * 128, np.float32)
+    ref = np.empty(64 * 128, np.float32)
+    assert lib.vx_rope_table(10000.0, 128, factors.ctypes.data, 1.0, 64, ours.ctypes.data) == 0
+    oracle.lib().vxo_rope_table(10000.0, 128, factors.ctypes.data, 1.0, 64, ref.ctypes.data)
+    assert np.array_equal(ours, ref)
+    del ctypes

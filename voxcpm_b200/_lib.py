@@ -27,6 +27,9 @@ WEIGHTS_Q8_TILES = 2
 OUT_F32 = 0
 OUT_BF16 = 1
 
+CACHE_F32 = 0
+CACHE_BF16 = 1
+
 
 class WmmaPlan(ctypes.Structure):
     """vx_wmma_plan (replaces WmmaPlan, kernels/wmma_products.hpp:74-81)."""
@@ -94,6 +97,34 @@ SIGNATURES: dict[str, tuple] = {
     ),
     "vx_random_q8_0": (c_int, [c_uint64, c_uint64, c_size_t, c_size_t, c_float, c_void_p]),
     "vx_random_bf16": (c_int, [c_uint64, c_uint64, c_size_t, c_float, c_float, c_void_p]),
+    "vx_embed": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_size_t, c_float, c_void_p]),
+    "vx_scatter_rows": (c_int, [c_void_p, c_void_p, c_void_p, c_size_t, c_size_t, c_void_p]),
+    "vx_gather_rows": (c_int, [c_void_p, c_void_p, c_void_p, c_size_t, c_size_t, c_void_p]),
+    "vx_rms_norm": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_size_t, c_float, c_void_p]),
+    "vx_qkv_rope": (
+        c_int,
+        [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int,
+         c_size_t, c_size_t, c_size_t, c_size_t, c_size_t, c_void_p],
+    ),
+    "vx_attention": (
+        c_int,
+        [c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_size_t, c_size_t, c_size_t, c_size_t,
+         c_void_p, c_int, c_size_t, c_size_t, c_size_t, c_size_t, c_size_t, c_void_p],
+    ),
+    "vx_swiglu": (c_int, [c_void_p, c_void_p, c_size_t, c_size_t, c_void_p]),
+    "vx_add_bias": (c_int, [c_void_p, c_void_p, c_size_t, c_size_t, c_void_p]),
+    "vx_to_bf16": (c_int, [c_void_p, c_void_p, c_size_t, c_int, c_void_p]),
+    "vx_concat_rows": (c_int, [c_void_p, c_void_p, c_size_t, c_void_p, c_void_p, c_size_t, c_void_p,
+                               c_size_t, c_void_p]),
+    "vx_quantize": (c_int, [c_void_p, c_void_p, c_size_t, c_float, c_void_p]),
+    "vx_select_rows": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_size_t, c_void_p]),
+    "vx_prepend_special": (c_int, [c_void_p, c_void_p, c_void_p, c_size_t, c_size_t, c_size_t, c_void_p]),
+    "vx_assemble_dit": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_size_t,
+                                c_void_p]),
+    "vx_guided_euler": (c_int, [c_void_p, c_void_p, c_size_t, c_float, c_float, c_void_p]),
+    "vx_rope_table": (c_int, [ctypes.c_double, c_size_t, c_void_p, ctypes.c_double, c_size_t, c_void_p]),
+    "vx_euler_schedule": (c_size_t, [c_size_t, c_float, c_void_p, c_void_p, c_void_p, c_size_t]),
+    "vx_sinusoid": (c_int, [c_float, c_size_t, c_void_p]),
     "vx_gemm_create": (c_void_p, [c_void_p]),
     "vx_gemm_destroy": (None, [c_void_p]),
     "vx_gemm_linear": (

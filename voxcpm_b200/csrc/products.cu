@@ -64,18 +64,26 @@ namespace {
 // ------------------------------------------------------------ kernel shapes
 
 struct VariantShape {
-  int warps;   // consumer warps per CTA
-  int groups;  // 16-row weight groups per warp
-  int stage;   // 32-column blocks per pipeline stage
-  int depth;   // stages in flight per warp
+  int cta_groups;  // 16-row weight groups per CTA
+  int ways;        // warps sharing a group, each taking every ways-th stage
+  int groups;      // 16-row groups per warp
+  int stage;       // 32-column blocks per pipeline stage
+  int depth;       // stages in flight per warp
 };
 
+__host__ __device__ constexpr int WarpsOf(const VariantShape& v) {
+  return v.cta_groups / v.groups * v.ways;
+}
+
 constexpr VariantShape kVariants[] = {
-    {8, 1, 4, 4},  // 128 rows per CTA
-    {4, 1, 4, 4},  // 64 rows per CTA
-    {4, 2, 2, 4},  // 128 rows per CTA, two groups per warp
-    {2, 1, 4, 6},  // 32 rows per CTA
-    {8, 1, 2, 6},  // 128 rows per CTA, shorter stages
+    {8, 1, 1, 4, 4},   // 0: 128 rows, 8 warps
+    {4, 1, 1, 4, 4},   // 1: 64 rows, 4 warps
+    {8, 2, 1, 2, 4},   // 2: 128 rows, 16 warps (2 ways)
+    {2, 1, 1, 4, 6},   // 3: 32 rows, 2 warps
+    {4, 2, 1, 2, 4},   // 4: 64 rows, 8 warps (2 ways)
+    {8, 2, 2, 2, 4},   // 5: 128 rows, 8 warps of 2 groups (2 ways)
+    {16, 1, 1, 2, 4},  // 6: 256 rows, 16 warps
+    {4, 4, 1, 2, 3},   // 7: 64 rows, 16 warps (4 ways)
 };
 constexpr int kNumVariants = sizeof(kVariants) / sizeof(kVariants[0]);
 
@@ -116,7 +124,7 @@ struct ProductArgs {
   int blocks_per_split;
   int accumulate;
   int x_stride;     // bytes per activation row in shared memory
-  int rings_bytes;  // bytes of all warps' rings (>= the reduction buffer)
+  int rings_bytes;  // bytes of all warps' rings (>= the reduction buffers)
 };
 
 // ------------------------------------------------------------ math pieces
@@ -150,12 +158,107 @@ __device__ inline void DequantWord(std::uint32_t w, std::uint32_t& pair01,
   pair23 = Prmt(__float_as_uint(b.x), __float_as_uint(b.y), 0x7632u);
 }
 
+/// One 32-column block of one 16-row group: the block's partial sums for
+/// every activation tile, added into `acc` (Q8: scaled; bf16: directly).
+template <int kFormat, int kNTiles, int kRowStride>
+__device__ __forceinline__ void BlockProduct(const unsigned char* base, int kb,
+                                             int gid, int tig,
+                                             const uint4 (&b)[kNTiles],
+                                             float (&acc)[kNTiles][4]) {
+  constexpr bool kQ8 = kFormat == static_cast<int>(WeightFormat::kQ8Tiles);
+  constexpr bool kRows = kFormat == static_cast<int>(WeightFormat::kBf16);
+  if constexpr (kQ8) {
+    const unsigned char* tile = base + kb * kQ8TileBytes;
+    const uint2 lo = *reinterpret_cast<const uint2*>(tile + gid * 32 + 8 * tig);
+    const uint2 hi =
+        *reinterpret_cast<const uint2*>(tile + (gid + 8) * 32 + 8 * tig);
+    const std::uint32_t sc =
+        *reinterpret_cast<const std::uint32_t*>(tile + 512 + 4 * gid);
+    const float s_lo =
+        HalfBitsToFloat(static_cast<std::uint16_t>(sc & 0xFFFFu));
+    const float s_hi = HalfBitsToFloat(static_cast<std::uint16_t>(sc >> 16));
+    std::uint32_t a00, a02, a01, a03, a10, a12, a11, a13;
+    DequantWord(lo.x, a00, a02);
+    DequantWord(hi.x, a01, a03);
+    DequantWord(lo.y, a10, a12);
+    DequantWord(hi.y, a11, a13);
+    const float zero[4] = {0.f, 0.f, 0.f, 0.f};
+#pragma unroll
+    for (int j = 0; j < kNTiles; ++j) {
+      float part[4];
+      Mma16816(part, a00, a01, a02, a03, b[j].x, b[j].y, zero);
+      Mma16816(part, a10, a11, a12, a13, b[j].z, b[j].w, part);
+      const float2 lo2 =
+          Fma2(make_float2(s_lo, s_lo), make_float2(part[0], part[1]),
+               make_float2(acc[j][0], acc[j][1]));
+      const float2 hi2 =
+          Fma2(make_float2(s_hi, s_hi), make_float2(part[2], part[3]),
+               make_float2(acc[j][2], acc[j][3]));
+      acc[j][0] = lo2.x;
+      acc[j][1] = lo2.y;
+      acc[j][2] = hi2.x;
+      acc[j][3] = hi2.y;
+    }
+  } else {
+    const unsigned char* row_lo;
+    const unsigned char* row_hi;
+    if constexpr (kRows) {
+      row_lo = base + gid * kRowStride + kb * 64;
+      row_hi = base + (gid + 8) * kRowStride + kb * 64;
+    } else {
+      const unsigned char* tile = base + kb * kBf16TileBytes;
+      row_lo = tile + gid * 64;
+      row_hi = tile + (gid + 8) * 64;
+    }
+    const uint4 lo = *reinterpret_cast<const uint4*>(row_lo + 16 * tig);
+    const uint4 hi = *reinterpret_cast<const uint4*>(row_hi + 16 * tig);
+#pragma unroll
+    for (int j = 0; j < kNTiles; ++j) {
+      Mma16816(acc[j], lo.x, hi.x, lo.y, hi.y, b[j].x, b[j].y, acc[j]);
+      Mma16816(acc[j], lo.z, hi.z, lo.w, hi.w, b[j].z, b[j].w, acc[j]);
+    }
+  }
+}
+
+/// All blocks of one landed stage. A full stage is unrolled without guards
+/// so the compiler can interleave the blocks' loads, conversions and MMAs.
+template <int kFormat, int kGroups, int kNTiles, int kStage>
+__device__ __forceinline__ void StageProduct(
+    const unsigned char* stage_base, int group_bytes, const unsigned char* xs,
+    int x_stride, int column0, int nb, int my_groups, int gid, int tig,
+    float (&acc)[kGroups][kNTiles][4]) {
+  constexpr int kRowStride = RowStrideBytes(kStage);
+  auto block = [&](int kb) {
+    uint4 b[kNTiles];
+    const int column = column0 + kb * 32 + 8 * tig;
+#pragma unroll
+    for (int j = 0; j < kNTiles; ++j)
+      b[j] = *reinterpret_cast<const uint4*>(xs + (8 * j + gid) * x_stride +
+                                             column * 2);
+#pragma unroll
+    for (int g = 0; g < kGroups; ++g)
+      if (g < my_groups)
+        BlockProduct<kFormat, kNTiles, kRowStride>(stage_base + g * group_bytes,
+                                                   kb, gid, tig, b, acc[g]);
+  };
+  if (nb == kStage) {
+#pragma unroll
+    for (int kb = 0; kb < kStage; ++kb)
+      block(kb);
+  } else {
+#pragma unroll 1
+    for (int kb = 0; kb < nb; ++kb)
+      block(kb);
+  }
+}
+
 // ------------------------------------------------------------ the kernel
 
-template <int kFormat, int kWarps, int kGroups, int kNTiles, int kStage,
-          int kDepth>
-__global__ void __launch_bounds__(kWarps * 32)
+template <int kFormat, int kCtaGroups, int kWays, int kGroups, int kNTiles,
+          int kStage, int kDepth>
+__global__ void __launch_bounds__(kCtaGroups / kGroups * kWays * 32)
     ProductKernel(const ProductArgs p) {
+  constexpr int kWarps = kCtaGroups / kGroups * kWays;
   constexpr int kGroupBytes = GroupStageBytes(kFormat, kStage);
   constexpr int kRingBytes = kDepth * kGroups * kGroupBytes;
   constexpr bool kQ8 = kFormat == static_cast<int>(WeightFormat::kQ8Tiles);
@@ -168,6 +271,8 @@ __global__ void __launch_bounds__(kWarps * 32)
   const int warp = threadIdx.x >> 5;
   const int gid = lane >> 2;
   const int tig = lane & 3;
+  const int way = warp % kWays;
+  const int group_warp = warp / kWays;
   const int split = static_cast<int>(blockIdx.x) % p.splits;
   const int panel = static_cast<int>(blockIdx.x) / p.splits;
   const int first = split * p.blocks_per_split;
@@ -175,7 +280,7 @@ __global__ void __launch_bounds__(kWarps * 32)
   const int nblocks = max(last - first, 0);
   const int x_rows = kNTiles * 8;
   const int groups_total = (p.n + 15) / 16;
-  const int group0 = (panel * kWarps + warp) * kGroups;
+  const int group0 = panel * kCtaGroups + group_warp * kGroups;
   const int my_groups = max(0, min(kGroups, groups_total - group0));
 
   unsigned char* xs = smem;
@@ -202,11 +307,14 @@ __global__ void __launch_bounds__(kWarps * 32)
 
   const std::uint64_t evict_first = PolicyEvictFirst();
   const int nstages = (nblocks + kStage - 1) / kStage;
+  // This warp takes stages way, way + kWays, ... of the split.
+  const int my_stages = way < nstages ? (nstages - way + kWays - 1) / kWays : 0;
 
-  // Issues stage `st` of this warp's weights into its ring slot.
-  auto issue = [&](int st) {
-    const int slot = st % kDepth;
-    const int b0 = first + st * kStage;
+  // Issues local stage `i` (stage way + i * kWays of the split) into its
+  // ring slot.
+  auto issue = [&](int i) {
+    const int slot = i % kDepth;
+    const int b0 = first + (way + i * kWays) * kStage;
     const int nb = min(kStage, last - b0);
     std::uint64_t* bar = &full[slot];
     unsigned char* dst = ring + slot * kGroups * kGroupBytes;
@@ -242,22 +350,22 @@ __global__ void __launch_bounds__(kWarps * 32)
     }
   };
 
-  const bool active = my_groups > 0 && nblocks > 0;
+  const bool active = my_groups > 0 && my_stages > 0;
   int issued = 0;
   if (active) {
-    for (; issued < min(kDepth, nstages); ++issued)
+    for (; issued < min(kDepth, my_stages); ++issued)
       issue(issued);
   }
   // Weights do not depend on earlier kernels; activations (and y) may.
   GridLaunchDependents();
   GridDependencyWait();
-  if (threadIdx.x == 0 && nblocks > 0) {
-    const std::uint64_t evict_last = PolicyEvictLast();
-    MbarArriveExpectTx(xbar, p.m * nblocks * 64);
-    for (int row = 0; row < p.m; ++row)
-      BulkLoad(xs + row * p.x_stride,
-               p.x + static_cast<std::size_t>(row) * p.k + first * 32,
-               nblocks * 64, xbar, evict_last);
+  if (warp == 0 && lane < p.m && nblocks > 0) {
+    if (lane == 0)
+      MbarArriveExpectTx(xbar, p.m * nblocks * 64);
+    __syncwarp(0xFFFFFFFFu >> (32 - p.m));
+    BulkLoad(xs + lane * p.x_stride,
+             p.x + static_cast<std::size_t>(lane) * p.k + first * 32,
+             nblocks * 64, xbar, PolicyEvictLast());
   }
 
   float acc[kGroups][kNTiles][4];
@@ -274,92 +382,22 @@ __global__ void __launch_bounds__(kWarps * 32)
   if (active) {
     if (!MbarWaitBounded(xbar, 0, &g_vx_device_error, kErrActivationWait))
       failed = true;
-    for (int st = 0; st < nstages && !failed; ++st) {
-      const int slot = st % kDepth;
-      if (!MbarWaitBounded(&full[slot], (st / kDepth) & 1,
-                           &g_vx_device_error, kErrWeightWait)) {
+    for (int i = 0; i < my_stages && !failed; ++i) {
+      const int slot = i % kDepth;
+      if (!MbarWaitBounded(&full[slot], (i / kDepth) & 1, &g_vx_device_error,
+                           kErrWeightWait)) {
         failed = true;
         break;
       }
       ++waited;
+      const int st = way + i * kWays;
       const int nb = min(kStage, last - (first + st * kStage));
-      const unsigned char* stage_base = ring + slot * kGroups * kGroupBytes;
-#pragma unroll 1
-      for (int kb = 0; kb < nb; ++kb) {
-        // B: 8 consecutive reduction columns of activation row 8j + gid.
-        uint4 b[kNTiles];
-        const int column = (st * kStage + kb) * 32 + 8 * tig;
-#pragma unroll
-        for (int j = 0; j < kNTiles; ++j)
-          b[j] = *reinterpret_cast<const uint4*>(
-              xs + (8 * j + gid) * p.x_stride + column * 2);
-#pragma unroll
-        for (int g = 0; g < kGroups; ++g) {
-          if (g >= my_groups)
-            break;
-          const unsigned char* base = stage_base + g * kGroupBytes;
-          if constexpr (kQ8) {
-            const unsigned char* tile = base + kb * kQ8TileBytes;
-            const uint2 lo =
-                *reinterpret_cast<const uint2*>(tile + gid * 32 + 8 * tig);
-            const uint2 hi = *reinterpret_cast<const uint2*>(
-                tile + (gid + 8) * 32 + 8 * tig);
-            const std::uint32_t sc =
-                *reinterpret_cast<const std::uint32_t*>(tile + 512 + 4 * gid);
-            const float s_lo = HalfBitsToFloat(
-                static_cast<std::uint16_t>(sc & 0xFFFFu));
-            const float s_hi =
-                HalfBitsToFloat(static_cast<std::uint16_t>(sc >> 16));
-            std::uint32_t a00, a02, a01, a03, a10, a12, a11, a13;
-            DequantWord(lo.x, a00, a02);
-            DequantWord(hi.x, a01, a03);
-            DequantWord(lo.y, a10, a12);
-            DequantWord(hi.y, a11, a13);
-            const float zero[4] = {0.f, 0.f, 0.f, 0.f};
-#pragma unroll
-            for (int j = 0; j < kNTiles; ++j) {
-              float part[4];
-              Mma16816(part, a00, a01, a02, a03, b[j].x, b[j].y, zero);
-              Mma16816(part, a10, a11, a12, a13, b[j].z, b[j].w, part);
-              const float2 lo2 = Fma2(make_float2(s_lo, s_lo),
-                                      make_float2(part[0], part[1]),
-                                      make_float2(acc[g][j][0], acc[g][j][1]));
-              const float2 hi2 = Fma2(make_float2(s_hi, s_hi),
-                                      make_float2(part[2], part[3]),
-                                      make_float2(acc[g][j][2], acc[g][j][3]));
-              acc[g][j][0] = lo2.x;
-              acc[g][j][1] = lo2.y;
-              acc[g][j][2] = hi2.x;
-              acc[g][j][3] = hi2.y;
-            }
-          } else {
-            const unsigned char* row_lo;
-            const unsigned char* row_hi;
-            if constexpr (kRows) {
-              row_lo = base + gid * kRowStride + kb * 64;
-              row_hi = base + (gid + 8) * kRowStride + kb * 64;
-            } else {
-              const unsigned char* tile = base + kb * kBf16TileBytes;
-              row_lo = tile + gid * 64;
-              row_hi = tile + (gid + 8) * 64;
-            }
-            const uint4 lo = *reinterpret_cast<const uint4*>(row_lo + 16 * tig);
-            const uint4 hi = *reinterpret_cast<const uint4*>(row_hi + 16 * tig);
-#pragma unroll
-            for (int j = 0; j < kNTiles; ++j) {
-              Mma16816(acc[g][j], lo.x, hi.x, lo.y, hi.y, b[j].x, b[j].y,
-                       acc[g][j]);
-              Mma16816(acc[g][j], lo.z, hi.z, lo.w, hi.w, b[j].z, b[j].w,
-                       acc[g][j]);
-            }
-          }
-        }
-      }
+      StageProduct<kFormat, kGroups, kNTiles, kStage>(
+          ring + slot * kGroups * kGroupBytes, kGroupBytes, xs, p.x_stride,
+          st * kStage * 32, nb, my_groups, gid, tig, acc);
+      // The slot's values are in registers (consumed above); refill it.
       __syncwarp();
-      if (issued < nstages) {
-        // The slot's generic-proxy reads are done; order them before the
-        // async-proxy writes of the next copy.
-        FenceProxyAsync();
+      if (issued < my_stages) {
         issue(issued);
         ++issued;
       }
@@ -367,35 +405,71 @@ __global__ void __launch_bounds__(kWarps * 32)
     if (failed) {
       // Give copies still in flight a bounded chance to land before the
       // shared memory is released.
-      for (int st = waited; st < issued; ++st)
-        (void)MbarWaitBounded(&full[st % kDepth], (st / kDepth) & 1,
+      for (int i = waited; i < issued; ++i)
+        (void)MbarWaitBounded(&full[i % kDepth], (i / kDepth) & 1,
                               &g_vx_device_error, kErrDrainWait,
                               100000000ull);
     }
   }
+  (void)kRowStride;
 
-  const int lanes_groups = kWarps * kGroups * kNTiles;
-  if (p.splits > 1) {
-    float4* red = reinterpret_cast<float4*>(rings);
+  // Ways of a group add up in way order through shared memory.
+  float4* red = reinterpret_cast<float4*>(rings);
+  constexpr int kSlots = kCtaGroups * kNTiles * 32;  // float4 per way
+  if (kWays > 1 || p.splits > 1)
     __syncthreads();  // every warp is done with its ring
-    if (split != 0) {
+  if constexpr (kWays > 1) {
+    if (way != 0) {
 #pragma unroll
       for (int g = 0; g < kGroups; ++g)
 #pragma unroll
         for (int j = 0; j < kNTiles; ++j)
-          red[((warp * kGroups + g) * kNTiles + j) * 32 + lane] =
+          red[(way - 1) * kSlots +
+              ((group_warp * kGroups + g) * kNTiles + j) * 32 + lane] =
+              make_float4(acc[g][j][0], acc[g][j][1], acc[g][j][2],
+                          acc[g][j][3]);
+    }
+    __syncthreads();
+    if (way == 0) {
+      for (int w = 1; w < kWays; ++w) {
+#pragma unroll
+        for (int g = 0; g < kGroups; ++g)
+#pragma unroll
+          for (int j = 0; j < kNTiles; ++j) {
+            const float4 v =
+                red[(w - 1) * kSlots +
+                    ((group_warp * kGroups + g) * kNTiles + j) * 32 + lane];
+            acc[g][j][0] += v.x;
+            acc[g][j][1] += v.y;
+            acc[g][j][2] += v.z;
+            acc[g][j][3] += v.w;
+          }
+      }
+    }
+  }
+  // Splits of the cluster add up in rank order through distributed shared
+  // memory (a region after the ways' buffers).
+  if (p.splits > 1) {
+    float4* part = red + (kWays - 1) * kSlots;
+    if (split != 0 && way == 0) {
+#pragma unroll
+      for (int g = 0; g < kGroups; ++g)
+#pragma unroll
+        for (int j = 0; j < kNTiles; ++j)
+          part[((group_warp * kGroups + g) * kNTiles + j) * 32 + lane] =
               make_float4(acc[g][j][0], acc[g][j][1], acc[g][j][2],
                           acc[g][j][3]);
     }
     ClusterSync();
-    if (split == 0) {
+    if (split == 0 && way == 0) {
       for (int r = 1; r < p.splits; ++r) {
 #pragma unroll
         for (int g = 0; g < kGroups; ++g)
 #pragma unroll
           for (int j = 0; j < kNTiles; ++j) {
             const float4 v = LoadSharedCluster4(MapShared(
-                &red[((warp * kGroups + g) * kNTiles + j) * 32 + lane], r));
+                &part[((group_warp * kGroups + g) * kNTiles + j) * 32 + lane],
+                r));
             acc[g][j][0] += v.x;
             acc[g][j][1] += v.y;
             acc[g][j][2] += v.z;
@@ -405,8 +479,7 @@ __global__ void __launch_bounds__(kWarps * 32)
     }
     ClusterSync();  // the others keep their shared memory until CTA 0 read it
   }
-  (void)lanes_groups;
-  if (split != 0)
+  if (split != 0 || way != 0)
     return;
 #pragma unroll
   for (int g = 0; g < kGroups; ++g) {
@@ -441,9 +514,10 @@ using KernelFn = void (*)(const ProductArgs);
 
 template <int kFormat, int kNTiles, int kVariant>
 constexpr KernelFn KernelFor() {
-  return ProductKernel<kFormat, kVariants[kVariant].warps,
-                       kVariants[kVariant].groups, kNTiles,
-                       kVariants[kVariant].stage, kVariants[kVariant].depth>;
+  return ProductKernel<kFormat, kVariants[kVariant].cta_groups,
+                       kVariants[kVariant].ways, kVariants[kVariant].groups,
+                       kNTiles, kVariants[kVariant].stage,
+                       kVariants[kVariant].depth>;
 }
 
 template <int kFormat, int kNTiles, int... kV>
@@ -452,7 +526,7 @@ struct VariantRow {
 };
 
 template <int kFormat, int kNTiles>
-using Row = VariantRow<kFormat, kNTiles, 0, 1, 2, 3, 4>;
+using Row = VariantRow<kFormat, kNTiles, 0, 1, 2, 3, 4, 5, 6, 7>;
 
 KernelFn Lookup(int format, int ntiles, int variant) {
   static const KernelFn* table[3][4] = {
@@ -487,12 +561,12 @@ Footprint FootprintOf(int format, int variant, int ntiles,
   const VariantShape& v = kVariants[variant];
   Footprint f;
   f.x_stride = XStrideBytes(blocks_per_split * 32);
-  const int rings =
-      v.warps * v.depth * v.groups * GroupStageBytes(format, v.stage);
-  const int reduction = v.warps * v.groups * ntiles * 32 * 16;
+  const int warps = WarpsOf(v);
+  const int rings = warps * v.depth * v.groups * GroupStageBytes(format, v.stage);
+  const int reduction = v.ways * v.cta_groups * ntiles * 32 * 16;
   f.rings_bytes = static_cast<int>(Align128(std::max(rings, reduction)));
   f.smem = Align128(static_cast<std::size_t>(ntiles) * 8 * f.x_stride) +
-           f.rings_bytes + (v.warps * v.depth + 1) * 8;
+           f.rings_bytes + (warps * v.depth + 1) * 8;
   return f;
 }
 
@@ -506,8 +580,8 @@ int NumProductVariants() { return kNumVariants; }
 void ProductVariantShape(int variant, int* warps, int* groups, int* stage,
                          int* depth) {
   const VariantShape& v = kVariants[variant];
-  *warps = v.warps;
-  *groups = v.groups;
+  *warps = WarpsOf(v);
+  *groups = v.cta_groups;
   *stage = v.stage;
   *depth = v.depth;
 }
@@ -529,7 +603,7 @@ ProductPlan PlanProduct(WeightFormat format, std::size_t rows, std::size_t in,
   double best_cost = 1e30;
   for (int variant = 0; variant < kNumVariants; ++variant) {
     const VariantShape& v = kVariants[variant];
-    const int rows_per_cta = 16 * v.groups * v.warps;
+    const int rows_per_cta = 16 * v.cta_groups;
     const int panels = (groups_total * 16 + rows_per_cta - 1) / rows_per_cta;
     for (int splits = std::max(1, min_splits); splits <= 8; ++splits) {
       if (splits > k_blocks)
@@ -551,8 +625,8 @@ ProductPlan PlanProduct(WeightFormat format, std::size_t rows, std::size_t in,
       } else {
         const int waves = (ctas + sms - 1) / sms;
         const double per_cta = static_cast<double>(rows_per_cta) / 16.0 * bps;
-        cost = waves * (per_cta + 2.0) + 1.5 * splits +
-               (v.warps < 4 ? 2.0 : 0.0);
+        cost = waves * (per_cta / v.ways + 2.0) + 1.5 * splits +
+               (WarpsOf(v) < 4 ? 2.0 : 0.0);
       }
       if (cost < best_cost) {
         best_cost = cost;
@@ -597,7 +671,7 @@ int LaunchProduct(WeightFormat format, const std::uint16_t* x, const void* w,
   if (fp.smem > 200 * 1024)
     return kUnsupported;
   const VariantShape& v = kVariants[plan.variant];
-  const int rows_per_cta = 16 * v.groups * v.warps;
+  const int rows_per_cta = 16 * v.cta_groups;
   const int panels =
       static_cast<int>((out + rows_per_cta - 1) / rows_per_cta);
   KernelFn kernel = Lookup(f, ntiles, plan.variant);
@@ -637,7 +711,7 @@ int LaunchProduct(WeightFormat format, const std::uint16_t* x, const void* w,
 
   cudaLaunchConfig_t config = {};
   config.gridDim = dim3(static_cast<unsigned>(panels * plan.splits));
-  config.blockDim = dim3(static_cast<unsigned>(v.warps * 32));
+  config.blockDim = dim3(static_cast<unsigned>(WarpsOf(v) * 32));
   config.dynamicSmemBytes = fp.smem;
   config.stream = stream;
   cudaLaunchAttribute attributes[2];

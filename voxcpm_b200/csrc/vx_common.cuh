@@ -93,11 +93,11 @@ __device__ inline bool MbarTryWait(std::uint64_t* bar, unsigned parity) {
   asm volatile(
       "{\n"
       ".reg .pred p;\n"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
       "selp.u32 %0, 1, 0, p;\n"
       "}\n"
       : "=r"(done)
-      : "r"(SmemAddr(bar)), "r"(parity), "r"(1000000u)
+      : "r"(SmemAddr(bar)), "r"(parity)
       : "memory");
   return done != 0;
 }
