@@ -277,6 +277,102 @@ VX_API size_t vx_euler_schedule(size_t timesteps, float sway, float* t,
 /* Host: SinusoidalPosEmb(width)(t), scale 1000 (generator.cpp:39-53). */
 VX_API vx_status vx_sinusoid(float t, size_t width, float* out);
 
+/* ------------------------------------------------------------ generator */
+
+/* One MiniCPM4 stack (config.hpp:15-31). */
+typedef struct vx_stack_config {
+  int hidden;
+  int intermediate;
+  int layers;
+  int heads;
+  int kv_heads;
+  int head_dim; /* 128: the attention kernels need it (config.cpp:302-306) */
+  float rms_eps;
+  int rope;
+} vx_stack_config;
+
+/* The generator's configuration (config.hpp:78-92). */
+typedef struct vx_model_config {
+  vx_stack_config lm, residual_lm, encoder, dit;
+  double rope_theta;
+  double rope_scaling;
+  double rope_factors[64]; /* head_dim / 2 LongRoPE factors */
+  int patch_size;
+  int feat_dim;
+  int fsq_latent_dim;
+  float fsq_scale;
+  int max_length; /* positions of each LM cache */
+  int vocab;      /* embedding rows (0: no embedding table, prefill of audio
+                     rows only) */
+} vx_model_config;
+
+/* Matrix formats of a seeded checkpoint: like a GGUF Q8_0 one (every matrix
+ * Q8 tiles) or like the HF bf16 one (the DiT in bf16 tiles, the rest bf16
+ * rows) (weights.cpp:138-144, :281-282). */
+#define VX_CHECKPOINT_Q8 0
+#define VX_CHECKPOINT_BF16 1
+
+/* The released checkpoint's shapes (tests/config_test.cpp:36-67); LongRoPE
+ * factors 1 and vocab 0 (set them for real use). */
+VX_API void vx_model_config_released(vx_model_config* config);
+
+/* VoxCPM2's generator on the current device with seeded weights. Replaces
+ * Generator::Create (generator.hpp:60-62, generator.cpp:82-174), whose file
+ * readers are out of scope. Returns null on failure (vx_last_error). */
+typedef struct vx_generator vx_generator;
+VX_API vx_generator* vx_generator_create(const vx_model_config* config,
+                                         uint64_t seed, int checkpoint,
+                                         int cache_type);
+VX_API void vx_generator_destroy(vx_generator* generator);
+/* Host arrays: tokens, masks [rows], feats [rows][patch][feat]. Replaces
+ * Generator::Prefill (generator.hpp:73-74, generator.cpp:326-422). */
+VX_API vx_status vx_generator_prefill(vx_generator* generator,
+                                      const int32_t* tokens,
+                                      const int32_t* text_mask,
+                                      const int32_t* audio_mask,
+                                      const float* feats, size_t rows);
+/* Host noise [patch][feat]; writes the stop logits [2] of the state before
+ * the patch and (when not null) its latent [patch][feat], then advances
+ * both LMs. One CUDA graph per patch when graphs are on (default).
+ * Synchronizes. Replaces Generator::Step (generator.hpp:76-86,
+ * generator.cpp:424-513). */
+VX_API vx_status vx_generator_step(vx_generator* generator, const float* noise,
+                                   size_t timesteps, float cfg, float* latent,
+                                   float* stop_logits);
+/* Host arrays: mu [2 * dit hidden], cond and x [patch][feat]; writes the
+ * CFG pair of velocities [2][patch][feat]. Replaces Generator::Velocity
+ * (generator.hpp:88-91, generator.cpp:515-538). */
+VX_API vx_status vx_generator_velocity(vx_generator* generator,
+                                       const float* mu, const float* cond,
+                                       const float* x, float t,
+                                       float* velocity);
+/* The DiT part of a step with the conditioning given (host mu, prefix cond,
+ * noise): dit_cond, then the Euler/CFG steps (generator.cpp:448-463);
+ * writes the latent when `latent` is not null (synchronizing). */
+VX_API vx_status vx_generator_dit_patch(vx_generator* generator,
+                                        const float* mu, const float* cond,
+                                        const float* noise, size_t timesteps,
+                                        float cfg, float* latent);
+/* Replays the last DiT patch (its captured graph) on the generator's stream
+ * without synchronizing (benchmarks). */
+VX_API vx_status vx_generator_replay_dit_patch(vx_generator* generator);
+/* Host copies of internal state (tests, benchmarks): names "lm_hidden",
+ * "residual_hidden", "prefix_cond", "x", "mu", "stop", "embed", "cond_rows",
+ * "velocity", "delta_time"; set_state takes "lm_hidden", "residual_hidden",
+ * "prefix_cond", "mu" and "position" (one value). Stands in for
+ * Generator::set_trace (generator.hpp:93-94). */
+VX_API vx_status vx_generator_state(vx_generator* generator, const char* name,
+                                    float* out, size_t count);
+VX_API vx_status vx_generator_set_state(vx_generator* generator,
+                                        const char* name, const float* in,
+                                        size_t count);
+/* CUDA graphs for Step and the DiT patch (default on). */
+VX_API vx_status vx_generator_set_graphs(vx_generator* generator, int enabled);
+/* Rows in the caches (Generator::position, generator.hpp:69-70). */
+VX_API size_t vx_generator_position(const vx_generator* generator);
+VX_API size_t vx_generator_weight_bytes(const vx_generator* generator);
+VX_API cudaStream_t vx_generator_stream(const vx_generator* generator);
+
 /* ------------------------------------------------------------ synthetic weights */
 
 /* Host: GGML Q8_0 blocks [rows][in/32] of seeded random weights, a pure

@@ -197,3 +197,126 @@ def sinusoid(t: float, width: int) -> np.ndarray:
     out = np.empty(width, np.float32)
     lib().vxo_sinusoid(t, width, _p(out))
     return out
+
+
+# ---------------------------------------------------------------- stack kernels
+
+def _f32(a):
+    return np.ascontiguousarray(a, dtype=np.float32)
+
+
+def _i32(a):
+    return np.ascontiguousarray(a, dtype=np.int32)
+
+
+def _u16(a):
+    return np.ascontiguousarray(a, dtype=np.uint16)
+
+
+def rms_norm(x: np.ndarray, weight: np.ndarray, eps: float, want_f32: bool = False):
+    """kernels/generator_kernels.hip:91-108 -> (bf16 bits, fp32 or None)."""
+    x = _f32(x)
+    rows, width = x.shape
+    out = np.empty((rows, width), np.uint16)
+    out32 = np.empty((rows, width), np.float32) if want_f32 else None
+    lib().vxo_rms_norm(_p(x), _p(_u16(weight)), _p(out), _p(out32), rows, width, eps)
+    return out, out32
+
+
+def rope_table(theta: float, dim: int, factors: np.ndarray, scaling: float, positions: int) -> np.ndarray:
+    table = np.empty((positions, dim), np.float32)
+    lib().vxo_rope_table(theta, dim, _p(np.ascontiguousarray(factors, np.float64)), scaling, positions,
+                         _p(table))
+    return table
+
+
+def qkv_rope(qkv, cos_sin, positions, cache_rows, k_cache, v_cache, heads, kv_heads, head_dim):
+    """kernels/generator_kernels.hip:110-158; k_cache/v_cache [kv][capacity][d]
+    float32 arrays updated in place. Returns q [rows][heads][d]."""
+    qkv = _f32(qkv)
+    rows = qkv.shape[0]
+    q = np.empty((rows, heads, head_dim), np.float32)
+    capacity = k_cache.shape[1]
+    lib().vxo_qkv_rope(_p(qkv), _p(None if cos_sin is None else _f32(cos_sin)), _p(_i32(positions)),
+                       _p(_i32(cache_rows)), _p(q), _p(k_cache), _p(v_cache), rows, heads, kv_heads,
+                       head_dim, capacity)
+    return q
+
+
+def attention(q, k_cache, v_cache, rows_per_sequence, keys_per_sequence, past, causal, heads, kv_heads,
+              head_dim):
+    """kernels/generator_kernels.hip:160-241 -> bf16 bits [rows][heads*d]."""
+    q = _f32(q)
+    rows = q.shape[0]
+    out = np.empty((rows, heads * head_dim), np.uint16)
+    lib().vxo_attention(_p(q), _p(_f32(k_cache)), _p(_f32(v_cache)), _p(out), rows, rows_per_sequence,
+                        keys_per_sequence, past, int(causal), heads, kv_heads, head_dim, k_cache.shape[1])
+    return out
+
+
+def swiglu(gate_up: np.ndarray) -> np.ndarray:
+    gate_up = _f32(gate_up)
+    rows, width2 = gate_up.shape
+    out = np.empty((rows, width2 // 2), np.uint16)
+    lib().vxo_swiglu(_p(gate_up), _p(out), rows, width2 // 2)
+    return out
+
+
+def add_bias(data: np.ndarray, bias: np.ndarray) -> np.ndarray:
+    data = _f32(data).copy()
+    rows, width = data.shape
+    lib().vxo_add_bias(_p(data), _p(_u16(bias)), rows, width)
+    return data
+
+
+def to_bf16(x: np.ndarray, silu: bool = False) -> np.ndarray:
+    x = _f32(x)
+    out = np.empty(x.shape, np.uint16)
+    lib().vxo_to_bf16(_p(x), _p(out), x.size, int(silu))
+    return out
+
+
+def concat_rows(a, b, a_scale=None, b_scale=None) -> np.ndarray:
+    a, b = _f32(a), _f32(b)
+    rows = a.shape[0]
+    out = np.empty((rows, a.shape[1] + b.shape[1]), np.uint16)
+    lib().vxo_concat_rows(_p(a), _p(None if a_scale is None else _f32(a_scale)), a.shape[1], _p(b),
+                          _p(None if b_scale is None else _f32(b_scale)), b.shape[1], _p(out), rows)
+    return out
+
+
+def quantize(x: np.ndarray, scale: float) -> np.ndarray:
+    x = _f32(x)
+    out = np.empty(x.shape, np.uint16)
+    lib().vxo_quantize(_p(x), _p(out), x.size, scale)
+    return out
+
+
+def prepend_special(rows_in: np.ndarray, special: np.ndarray, patches: int, patch_size: int) -> np.ndarray:
+    rows_in = _f32(rows_in)
+    width = rows_in.shape[-1]
+    out = np.empty((patches * (patch_size + 1), width), np.float32)
+    lib().vxo_prepend_special(_p(rows_in), _p(_u16(special)), _p(out), patches, patch_size, width)
+    return out
+
+
+def assemble_dit(mu, time, cond, x, patch_size: int) -> np.ndarray:
+    width = time.shape[-1]
+    out = np.empty((2 * (3 + 2 * patch_size), width), np.float32)
+    lib().vxo_assemble_dit(_p(_f32(mu)), _p(_f32(time)), _p(_f32(cond)), _p(_f32(x)), _p(out), patch_size,
+                           width)
+    return out
+
+
+def gather_rows(x: np.ndarray, indices) -> np.ndarray:
+    x = _f32(x)
+    idx = _i32(indices)
+    out = np.empty((idx.size, x.shape[1]), np.float32)
+    lib().vxo_gather_rows(_p(x), _p(idx), _p(out), idx.size, x.shape[1])
+    return out
+
+
+def guided_euler(velocity: np.ndarray, x: np.ndarray, cfg: float, dt: float) -> np.ndarray:
+    x = _f32(x).copy()
+    lib().vxo_guided_euler(_p(_f32(velocity)), _p(x), x.size, cfg, dt)
+    return x

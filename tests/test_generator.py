@@ -1,0 +1,146 @@
+"""The generator against the oracle's restatement, on a B200.
+
+Mirrors tests/generator_test.cpp's checks (one DiT velocity pair, a prefill
+followed by patches: latents, stop logits, LM states) on seeded weights:
+the OpenBMB golden tensors need the real checkpoint, which is absent, so the
+oracle (oracle/model.py, the reference's arithmetic in plain C) is the
+checker. The metric is relative L2, as in the reference's test. Both sides
+round to bf16 at the same points; they differ in float32 summation order
+(products, norms, softmax) and in expf / rsqrtf ulps, so a bf16 rounding
+flips now and then and the differences grow through the layers: the limits
+below are set from that noise, far below what a wrong operation produces.
+"""
+
+import numpy as np
+import pytest
+
+from oracle.model import OracleGenerator
+from voxcpm_b200 import _lib
+from voxcpm_b200.generator import Generator, released_config, small_config
+
+from _util import rel_l2
+
+pytestmark = pytest.mark.gpu
+
+VELOCITY_LIMIT = 1e-2
+LATENT_LIMIT = 2e-2
+STATE_LIMIT = 2e-2
+
+
+def dit_config():
+    """The released DiT and encoder (12 layers); 1-layer LMs."""
+    c = released_config()
+    c.lm.layers = 1
+    c.residual_lm.layers = 1
+    c.max_length = 64
+    return c
+
+
+def inputs(config, seed):
+    rng = np.random.default_rng(seed)
+    p, f = config.patch_size, config.feat_dim
+    mu = rng.normal(0, 1, 2 * config.dit.hidden).astype(np.float32)
+    cond = rng.normal(0, 1, (p, f)).astype(np.float32)
+    x = rng.normal(0, 1, (p, f)).astype(np.float32)
+    return mu, cond, x
+
+
+@pytest.mark.parametrize("checkpoint", [_lib.CHECKPOINT_Q8, _lib.CHECKPOINT_BF16])
+def test_velocity_small(cuda, checkpoint):
+    c = small_config()
+    gen = Generator(c, seed=3, checkpoint=checkpoint)
+    ref = OracleGenerator(c, seed=3, q8=checkpoint == _lib.CHECKPOINT_Q8)
+    assert np.array_equal(gen.State("delta_time", c.dit.hidden), ref.delta_time) or \
+        rel_l2(gen.State("delta_time", c.dit.hidden), ref.delta_time) < 1e-3
+    mu, cond, x = inputs(c, 1)
+    v = gen.Velocity(mu, cond, x, 0.63)
+    v_ref = ref.velocity(mu, cond, x, 0.63)
+    err = rel_l2(v, v_ref)
+    print(f"velocity rel L2 {err:.3e}")
+    assert err < VELOCITY_LIMIT
+    gen.close()
+
+
+def test_dit_patch_full_dit(cuda):
+    """BASELINE config 2 (12-layer DiT, 10 Euler steps of which 9 evaluate,
+    CFG 2.0): the latent of one patch, graphed and eager."""
+    c = dit_config()
+    gen = Generator(c, seed=7)
+    ref = OracleGenerator(c, seed=7)
+    mu, cond, noise = inputs(c, 2)
+    v = gen.Velocity(mu, cond, noise, 0.63)
+    v_ref = ref.velocity(mu, cond, noise, 0.63)
+    verr = rel_l2(v, v_ref)
+    latent = gen.DitPatch(mu, cond, noise, 10, 2.0)
+    gen.SetGraphs(False)
+    eager = gen.DitPatch(mu, cond, noise, 10, 2.0)
+    gen.SetGraphs(True)
+    again = gen.DitPatch(mu, cond, noise, 10, 2.0)
+    assert np.array_equal(latent, eager), "graph replay differs from eager launches"
+    assert np.array_equal(latent, again), "replays are not deterministic"
+    latent_ref = ref.dit_patch(mu, cond, noise, 10, 2.0)
+    lerr = rel_l2(latent, latent_ref)
+    print(f"full DiT: velocity rel L2 {verr:.3e}, patch latent rel L2 {lerr:.3e}")
+    assert verr < VELOCITY_LIMIT
+    assert lerr < LATENT_LIMIT
+    gen.close()
+
+
+def prompt(config, seed, rows=9, audio=(8,)):
+    rng = np.random.default_rng(seed)
+    tokens = rng.integers(0, config.vocab, rows).astype(np.int32)
+    audio_mask = np.zeros(rows, np.int32)
+    audio_mask[list(audio)] = 1
+    text_mask = 1 - audio_mask
+    feats = np.zeros((rows, config.patch_size, config.feat_dim), np.float32)
+    feats[list(audio)] = rng.normal(0, 1, (len(audio), config.patch_size, config.feat_dim))
+    return tokens, text_mask, audio_mask, feats
+
+
+@pytest.mark.parametrize("cache_type", [_lib.CACHE_F32, _lib.CACHE_BF16])
+def test_prefill_and_steps_small(cuda, cache_type):
+    """generator_test.cpp:108-146: prefill, then patches with seeded noise;
+    the graphed steps equal eager steps bit for bit."""
+    c = small_config()
+    hidden = c.lm.hidden
+    gen = Generator(c, seed=11, cache_type=cache_type)
+    eager = Generator(c, seed=11, cache_type=cache_type)
+    eager.SetGraphs(False)
+    ref = OracleGenerator(c, seed=11, bf16_cache=cache_type == _lib.CACHE_BF16)
+    p = prompt(c, 5)
+    gen.Prefill(*p)
+    eager.Prefill(*p)
+    ref.prefill(*p)
+    assert gen.position() == ref.position == 9
+    e_lm = rel_l2(gen.State("lm_hidden", hidden), ref.lm_hidden)
+    e_res = rel_l2(gen.State("residual_hidden", hidden), ref.residual_hidden)
+    print(f"prefill: lm {e_lm:.3e} residual {e_res:.3e}")
+    assert e_lm < STATE_LIMIT and e_res < STATE_LIMIT
+    rng = np.random.default_rng(9)
+    for k in range(3):
+        noise = rng.normal(0, 1, (c.patch_size, c.feat_dim)).astype(np.float32)
+        latent, stop = gen.Step(noise, 10, 2.0)
+        latent_e, stop_e = eager.Step(noise, 10, 2.0)
+        latent_r, stop_r = ref.step(noise, 10, 2.0)
+        assert np.array_equal(latent, latent_e) and np.array_equal(stop, stop_e)
+        errs = (rel_l2(latent, latent_r), rel_l2(stop, stop_r),
+                rel_l2(gen.State("lm_hidden", hidden), ref.lm_hidden),
+                rel_l2(gen.State("residual_hidden", hidden), ref.residual_hidden))
+        print(f"step {k}: latent {errs[0]:.3e} stop {errs[1]:.3e} lm {errs[2]:.3e} residual {errs[3]:.3e}")
+        assert errs[0] < LATENT_LIMIT and errs[1] < STATE_LIMIT
+        assert errs[2] < STATE_LIMIT and errs[3] < STATE_LIMIT
+        assert gen.position() == ref.position == 10 + k
+    gen.close()
+    eager.close()
+
+
+def test_step_errors(cuda):
+    """A step without a prefilled sequence is rejected (generator.cpp:426-427)."""
+    c = small_config()
+    gen = Generator(c, seed=1)
+    with pytest.raises(_lib.VxError):
+        gen.Step(np.zeros((c.patch_size, c.feat_dim), np.float32))
+    with pytest.raises(_lib.VxError):
+        gen.Prefill(np.array([c.vocab + 5], np.int32), np.array([1], np.int32), np.array([0], np.int32),
+                    np.zeros((1, c.patch_size, c.feat_dim), np.float32))
+    gen.close()

@@ -54,6 +54,25 @@ class SplitScratch(ctypes.Structure):
     ]
 
 
+class StackConfig(ctypes.Structure):
+    """vx_stack_config (config.hpp:15-31)."""
+
+    _fields_ = [("hidden", c_int), ("intermediate", c_int), ("layers", c_int), ("heads", c_int),
+                ("kv_heads", c_int), ("head_dim", c_int), ("rms_eps", c_float), ("rope", c_int)]
+
+
+class ModelConfig(ctypes.Structure):
+    """vx_model_config (config.hpp:78-92)."""
+
+    _fields_ = [("lm", StackConfig), ("residual_lm", StackConfig), ("encoder", StackConfig),
+                ("dit", StackConfig), ("rope_theta", ctypes.c_double), ("rope_scaling", ctypes.c_double),
+                ("rope_factors", ctypes.c_double * 64), ("patch_size", c_int), ("feat_dim", c_int),
+                ("fsq_latent_dim", c_int), ("fsq_scale", c_float), ("max_length", c_int), ("vocab", c_int)]
+
+
+CHECKPOINT_Q8 = 0
+CHECKPOINT_BF16 = 1
+
 # name -> (restype, argtypes)
 SIGNATURES: dict[str, tuple] = {
     "vx_last_error": (c_char_p, []),
@@ -125,6 +144,20 @@ SIGNATURES: dict[str, tuple] = {
     "vx_rope_table": (c_int, [ctypes.c_double, c_size_t, c_void_p, ctypes.c_double, c_size_t, c_void_p]),
     "vx_euler_schedule": (c_size_t, [c_size_t, c_float, c_void_p, c_void_p, c_void_p, c_size_t]),
     "vx_sinusoid": (c_int, [c_float, c_size_t, c_void_p]),
+    "vx_model_config_released": (None, [POINTER(ModelConfig)]),
+    "vx_generator_create": (c_void_p, [POINTER(ModelConfig), c_uint64, c_int, c_int]),
+    "vx_generator_destroy": (None, [c_void_p]),
+    "vx_generator_prefill": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_size_t]),
+    "vx_generator_step": (c_int, [c_void_p, c_void_p, c_size_t, c_float, c_void_p, c_void_p]),
+    "vx_generator_velocity": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_float, c_void_p]),
+    "vx_generator_dit_patch": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_float, c_void_p]),
+    "vx_generator_replay_dit_patch": (c_int, [c_void_p]),
+    "vx_generator_state": (c_int, [c_void_p, c_char_p, c_void_p, c_size_t]),
+    "vx_generator_set_state": (c_int, [c_void_p, c_char_p, c_void_p, c_size_t]),
+    "vx_generator_set_graphs": (c_int, [c_void_p, c_int]),
+    "vx_generator_position": (c_size_t, [c_void_p]),
+    "vx_generator_weight_bytes": (c_size_t, [c_void_p]),
+    "vx_generator_stream": (c_void_p, [c_void_p]),
     "vx_gemm_create": (c_void_p, [c_void_p]),
     "vx_gemm_destroy": (None, [c_void_p]),
     "vx_gemm_linear": (

@@ -175,3 +175,80 @@ def RandomBf16(seed: int, tensor: int, count: int, mean: float = 0.0, std: float
     out = np.empty(count, dtype=np.uint16)
     check(load().vx_random_bf16(seed, tensor, count, mean, std, out.ctypes.data))
     return out
+
+
+# ---------------------------------------------------------------- stack kernels
+# Named after kernels/generator_kernels.hpp; tensors are device tensors
+# (bf16 as int16/bfloat16 bit patterns), None for null pointers.
+
+def Embed(table, ids, text_mask, output, rows, width, scale, stream=None) -> None:
+    check(load().vx_embed(_ptr(table), _ptr(ids), _ptr(text_mask), _ptr(output), rows, width, scale,
+                          _stream(stream)))
+
+
+def ScatterRows(input, indices, output, rows, width, stream=None) -> None:
+    check(load().vx_scatter_rows(_ptr(input), _ptr(indices), _ptr(output), rows, width, _stream(stream)))
+
+
+def GatherRows(input, indices, output, rows, width, stream=None) -> None:
+    check(load().vx_gather_rows(_ptr(input), _ptr(indices), _ptr(output), rows, width, _stream(stream)))
+
+
+def RmsNorm(input, weight, output, output_f32, rows, width, epsilon, stream=None) -> None:
+    check(load().vx_rms_norm(_ptr(input), _ptr(weight), _ptr(output), _ptr(output_f32), rows, width,
+                             epsilon, _stream(stream)))
+
+
+def QkvRope(qkv, cos_sin, positions, cache_rows, q, k_cache, v_cache, rows, heads, kv_heads, head_dim,
+            capacity, cache_type=_lib.CACHE_F32, stream=None) -> None:
+    check(load().vx_qkv_rope(_ptr(qkv), _ptr(cos_sin), _ptr(positions), _ptr(cache_rows), _ptr(q),
+                             _ptr(k_cache), _ptr(v_cache), cache_type, rows, heads, kv_heads, head_dim,
+                             capacity, _stream(stream)))
+
+
+def Attention(q, k_cache, v_cache, output, rows, rows_per_sequence, keys_per_sequence, past, causal,
+              heads, kv_heads, head_dim, capacity, cache_type=_lib.CACHE_F32, past_device=None,
+              max_keys=0, stream=None) -> None:
+    check(load().vx_attention(_ptr(q), _ptr(k_cache), _ptr(v_cache), cache_type, _ptr(output), rows,
+                              rows_per_sequence, keys_per_sequence, past, _ptr(past_device), int(causal),
+                              heads, kv_heads, head_dim, capacity, max_keys, _stream(stream)))
+
+
+def SwiGlu(gate_up, output, rows, width, stream=None) -> None:
+    check(load().vx_swiglu(_ptr(gate_up), _ptr(output), rows, width, _stream(stream)))
+
+
+def AddBias(data, bias, rows, width, stream=None) -> None:
+    check(load().vx_add_bias(_ptr(data), _ptr(bias), rows, width, _stream(stream)))
+
+
+def ToBf16(input, output, count, silu=False, stream=None) -> None:
+    check(load().vx_to_bf16(_ptr(input), _ptr(output), count, int(silu), _stream(stream)))
+
+
+def ConcatRows(a, a_scale, a_width, b, b_scale, b_width, output, rows, stream=None) -> None:
+    check(load().vx_concat_rows(_ptr(a), _ptr(a_scale), a_width, _ptr(b), _ptr(b_scale), b_width,
+                                _ptr(output), rows, _stream(stream)))
+
+
+def Quantize(input, output, count, scale, stream=None) -> None:
+    check(load().vx_quantize(_ptr(input), _ptr(output), count, scale, _stream(stream)))
+
+
+def SelectRows(quantized, plain, mask, output, rows, width, stream=None) -> None:
+    check(load().vx_select_rows(_ptr(quantized), _ptr(plain), _ptr(mask), _ptr(output), rows, width,
+                                _stream(stream)))
+
+
+def PrependSpecial(rows_in, special, output, patches, patch_size, width, stream=None) -> None:
+    check(load().vx_prepend_special(_ptr(rows_in), _ptr(special), _ptr(output), patches, patch_size, width,
+                                    _stream(stream)))
+
+
+def AssembleDit(mu, time, cond, x, output, patch_size, width, stream=None) -> None:
+    check(load().vx_assemble_dit(_ptr(mu), _ptr(time), _ptr(cond), _ptr(x), _ptr(output), patch_size, width,
+                                 _stream(stream)))
+
+
+def GuidedEuler(velocity, x, count, cfg, dt, stream=None) -> None:
+    check(load().vx_guided_euler(_ptr(velocity), _ptr(x), count, cfg, dt, _stream(stream)))
