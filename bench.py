@@ -365,6 +365,7 @@ def run_ours(args, world, rank, local):
     e2e_value = sum_over_ranks(world, STEP_BYTES * e2e_steps) / (e_ms / 1e3) / 1e9
 
     clocks = sampler.summary()
+    generator = measure_generator(rank)
     if rank != 0:
         return
     peak, peak_kind = measured_peak()
@@ -395,8 +396,93 @@ def run_ours(args, world, rank, local):
                 "d2h_bytes_per_step": Y_BYTES, "steps": e2e_steps},
         "gpu_launches": args.steps,
         "clocks": clocks,
+        **generator,
     }
     print(json.dumps(line), flush=True)
+
+
+# ---------------------------------------------------------------- DiT patch and step
+
+DIT_LAYER_BYTES = (2560 * 1024 + 1024 * 2048 + 8192 * 1024 + 1024 * 4096) * 34 // 32  # 18,382,848
+DIT_EVAL_BYTES = 12 * DIT_LAYER_BYTES + 2 * 1024 * 64 * 34 // 32  # 220,733,440
+DIT_PATCH_BYTES = 9 * DIT_EVAL_BYTES  # 1,986,600,960: 10 Euler steps, 9 evaluations
+PATCH_AUDIO_S = 0.16  # 4 latent frames x 640 samples at 16 kHz
+
+
+def measure_generator(rank: int, context: int = 512, patch_replays: int = 50, steps: int = 32) -> dict:
+    """BASELINE configs 2 and 3 on the released shapes with seeded Q8_0
+    weights: the DiT patch (replays of its CUDA graph, inputs on the device)
+    and the full per-patch step at `context` positions with a bf16 KV cache
+    (host noise in, latent and stop logits out, one graph per step)."""
+    import numpy as np
+    import torch
+
+    from voxcpm_b200 import _lib
+    from voxcpm_b200.generator import Generator, released_config
+
+    c = released_config()
+    c.max_length = context + steps + 16
+    c.vocab = 1024
+    t0 = time.perf_counter()
+    gen = Generator(c, seed=100 + rank, checkpoint=_lib.CHECKPOINT_Q8, cache_type=_lib.CACHE_BF16)
+    create_s = time.perf_counter() - t0
+    stream = torch.cuda.ExternalStream(gen.stream())
+    rng = np.random.default_rng(rank)
+    mu = rng.normal(0, 1, 2 * c.dit.hidden).astype(np.float32)
+    cond = rng.normal(0, 1, (c.patch_size, c.feat_dim)).astype(np.float32)
+    noise = rng.normal(0, 1, (c.patch_size, c.feat_dim)).astype(np.float32)
+    gen.DitPatch(mu, cond, noise, 10, 2.0)  # captures the patch graph
+    for _ in range(3):
+        gen.ReplayDitPatch()
+    torch.cuda.synchronize()
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    a.record(stream)
+    for _ in range(patch_replays):
+        gen.ReplayDitPatch()
+    b.record(stream)
+    b.synchronize()
+    patch_us = a.elapsed_time(b) * 1e3 / patch_replays
+
+    # Full step at `context`: a prompt of `context` rows (one audio row last),
+    # then patches; each step's device time is bracketed by events on the
+    # generator's stream, its wall time includes the host copies.
+    tokens = rng.integers(0, c.vocab, context).astype(np.int32)
+    audio = np.zeros(context, np.int32)
+    audio[-1] = 1
+    feats = np.zeros((context, c.patch_size, c.feat_dim), np.float32)
+    feats[-1] = rng.normal(0, 1, (c.patch_size, c.feat_dim))
+    t0 = time.perf_counter()
+    gen.Prefill(tokens, 1 - audio, audio, feats)
+    prefill_s = time.perf_counter() - t0
+    device_ms, wall_ms = [], []
+    for k in range(steps):
+        n = rng.normal(0, 1, (c.patch_size, c.feat_dim)).astype(np.float32)
+        a.record(stream)
+        t0 = time.perf_counter()
+        gen.Step(n, 10, 2.0)
+        wall_ms.append((time.perf_counter() - t0) * 1e3)
+        b.record(stream)
+        b.synchronize()
+        device_ms.append(a.elapsed_time(b))
+    warm = 2  # the first steps capture the step graph
+    step_ms = float(np.median(device_ms[warm:]))
+    step_wall_ms = float(np.median(wall_ms[warm:]))
+    weight_bytes = gen.weight_bytes()
+    gen.close()
+    floor_us = DIT_PATCH_BYTES / (measured_peak()[0] * 1e9) * 1e6
+    return {
+        "dit_patch": {"us": patch_us, "bytes": DIT_PATCH_BYTES, "hbm_floor_us": floor_us,
+                      "frac_of_floor": floor_us / patch_us, "replays": patch_replays,
+                      "config": "12-layer DiT 1024 (16 q / 2 kv heads x 128), 22 rows, 10 Euler steps "
+                                "(9 evaluations), CFG 2.0, Q8_0 weights, one CUDA graph"},
+        "step": {"ms_per_patch": step_ms, "wall_ms_per_patch": step_wall_ms,
+                 "audio_s_per_s": PATCH_AUDIO_S / (step_wall_ms / 1e3), "rtf": step_wall_ms / 1e3 / PATCH_AUDIO_S,
+                 "context": context, "steps": steps - warm, "kv_cache": "bf16",
+                 "weight_bytes": weight_bytes, "prefill_s": prefill_s, "create_s": create_s,
+                 "config": "LM 28x2048 + residual LM 8x2048 + encoder 12x1024 + DiT 12x1024, Q8_0, "
+                           "one CUDA graph per patch"},
+    }
 
 
 def main():

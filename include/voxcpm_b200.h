@@ -358,7 +358,7 @@ VX_API vx_status vx_generator_dit_patch(vx_generator* generator,
 VX_API vx_status vx_generator_replay_dit_patch(vx_generator* generator);
 /* Host copies of internal state (tests, benchmarks): names "lm_hidden",
  * "residual_hidden", "prefix_cond", "x", "mu", "stop", "embed", "cond_rows",
- * "velocity", "delta_time"; set_state takes "lm_hidden", "residual_hidden",
+ * "velocity", "delta_time", "lm_output" (the LM's last row before FSQ); set_state takes "lm_hidden", "residual_hidden",
  * "prefix_cond", "mu" and "position" (one value). Stands in for
  * Generator::set_trace (generator.hpp:93-94). */
 VX_API vx_status vx_generator_state(vx_generator* generator, const char* name,

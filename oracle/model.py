@@ -290,6 +290,7 @@ class OracleGenerator:
         layout = dict(positions=np.arange(rows), cache_rows=np.arange(rows), rows_per_sequence=rows,
                       keys_per_sequence=0, past=0, causal=True)
         lm_out = self.forward_stack(self.w.base_lm, True, layout, self.base_cache, combined)
+        self.lm_output = lm_out[-1].copy()
         quantized = self.fsq(lm_out, rows)
         selected = np.where(audio_mask[:, None] != 0, quantized, lm_out).astype(np.float32)
         self.lm_hidden = selected[-1].copy()
@@ -318,6 +319,7 @@ class OracleGenerator:
         layout = dict(positions=[pos], cache_rows=[pos], rows_per_sequence=1, keys_per_sequence=0, past=pos,
                       causal=True)
         lm_out = self.forward_stack(self.w.base_lm, True, layout, self.base_cache, embed[None].copy())
+        self.lm_output = lm_out[0].copy()
         self.lm_hidden = self.fsq(lm_out, 1)[0]
         fused = self.project(self.w.fusion, concat_rows(self.lm_hidden[None], embed[None]), 1)
         self.residual_hidden = self.forward_stack(self.w.residual_lm, False, layout, self.residual_cache,

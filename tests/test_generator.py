@@ -25,6 +25,12 @@ pytestmark = pytest.mark.gpu
 VELOCITY_LIMIT = 1e-2
 LATENT_LIMIT = 2e-2
 STATE_LIMIT = 2e-2
+# FSQ rounds tanh(x) * 9 to integers: an input that differs in its last bits
+# can land on the neighbouring level (a jump of 1/9 in one of 512 latent
+# values), so the quantized state is checked more loosely than its input.
+FSQ_STATE_LIMIT = 6e-2
+# The stop logits are O(1e-2) with random weights; absolute bound.
+STOP_ATOL = 5e-3
 
 
 def dit_config():
@@ -112,10 +118,11 @@ def test_prefill_and_steps_small(cuda, cache_type):
     eager.Prefill(*p)
     ref.prefill(*p)
     assert gen.position() == ref.position == 9
+    e_out = rel_l2(gen.State("lm_output", hidden), ref.lm_output)
     e_lm = rel_l2(gen.State("lm_hidden", hidden), ref.lm_hidden)
     e_res = rel_l2(gen.State("residual_hidden", hidden), ref.residual_hidden)
-    print(f"prefill: lm {e_lm:.3e} residual {e_res:.3e}")
-    assert e_lm < STATE_LIMIT and e_res < STATE_LIMIT
+    print(f"prefill: lm output {e_out:.3e} lm (FSQ) {e_lm:.3e} residual {e_res:.3e}")
+    assert e_out < STATE_LIMIT and e_lm < FSQ_STATE_LIMIT and e_res < STATE_LIMIT
     rng = np.random.default_rng(9)
     for k in range(3):
         noise = rng.normal(0, 1, (c.patch_size, c.feat_dim)).astype(np.float32)
@@ -123,12 +130,14 @@ def test_prefill_and_steps_small(cuda, cache_type):
         latent_e, stop_e = eager.Step(noise, 10, 2.0)
         latent_r, stop_r = ref.step(noise, 10, 2.0)
         assert np.array_equal(latent, latent_e) and np.array_equal(stop, stop_e)
-        errs = (rel_l2(latent, latent_r), rel_l2(stop, stop_r),
+        errs = (rel_l2(latent, latent_r), float(np.max(np.abs(stop - stop_r))),
+                rel_l2(gen.State("lm_output", hidden), ref.lm_output),
                 rel_l2(gen.State("lm_hidden", hidden), ref.lm_hidden),
                 rel_l2(gen.State("residual_hidden", hidden), ref.residual_hidden))
-        print(f"step {k}: latent {errs[0]:.3e} stop {errs[1]:.3e} lm {errs[2]:.3e} residual {errs[3]:.3e}")
-        assert errs[0] < LATENT_LIMIT and errs[1] < STATE_LIMIT
-        assert errs[2] < STATE_LIMIT and errs[3] < STATE_LIMIT
+        print(f"step {k}: latent {errs[0]:.3e} stop |d| {errs[1]:.3e} (of {np.abs(stop_r).max():.3e}) "
+              f"lm output {errs[2]:.3e} lm (FSQ) {errs[3]:.3e} residual {errs[4]:.3e}")
+        assert errs[0] < LATENT_LIMIT and errs[1] < STOP_ATOL
+        assert errs[2] < STATE_LIMIT and errs[3] < FSQ_STATE_LIMIT and errs[4] < STATE_LIMIT
         assert gen.position() == ref.position == 10 + k
     gen.close()
     eager.close()

@@ -1110,6 +1110,7 @@ void Generator::Prefill(const std::int32_t* tokens,
     Check(Project(w_.fsq_out, bf16, a, rows, stream_), "fsq_out");
     Check(SelectRows(a, cbuf, amask, d, rows, hidden, stream_), "SelectRows");
     Check(CopyFloats(d + (r - 1) * hidden, lm_hidden_, hidden, stream_), "copy");
+    Check(CopyFloats(cbuf + (r - 1) * hidden, step_b_, hidden, stream_), "copy");
     Check(ConcatRows(d, nullptr, hidden, b, nullptr, hidden, bf16, rows, stream_),
           "ConcatRows");
     Check(Project(w_.fusion, bf16, a, rows, stream_), "fusion");
@@ -1157,6 +1158,7 @@ void Generator::State(const std::string& name, float* out, std::size_t count) {
       {"mu", {mu_, static_cast<std::size_t>(2 * c.dit.hidden)}},
       {"stop", {stop_, 2}},
       {"embed", {embed_, static_cast<std::size_t>(c.lm.hidden)}},
+      {"lm_output", {step_b_, static_cast<std::size_t>(c.lm.hidden)}},
       {"cond_rows", {cond_rows_, static_cast<std::size_t>(c.patch_size * c.dit.hidden)}},
       {"velocity", {velocity_, static_cast<std::size_t>(2 * c.patch_size * c.feat_dim)}},
       {"delta_time", {delta_time_, static_cast<std::size_t>(c.dit.hidden)}},
