@@ -1,0 +1,358 @@
+// voxcpm_b200.hpp — header-only C++ mirror of the reference's interfaces
+// over the C ABI (voxcpm_b200.h): the names, argument meanings and error
+// behaviour of gemm.hpp, matrix.hpp, kernels/wmma_products.hpp,
+// kernels/skinny_gemm.hpp, kernels/generator_kernels.hpp, transformer.hpp
+// (RopeTable) and generator.hpp (Prompt, EulerStep, EulerSchedule,
+// Generator), so that code written against the reference keeps compiling.
+//
+// Error behaviour: launchers that return bool in the reference return false
+// when the shape does not suit the kernels (VX_UNSUPPORTED, nothing
+// launched); every other failure throws GpuError (device.hpp:16-30). Link
+// with -lvoxcpm_b200 (the shared library builds in voxcpm_b200/).
+#ifndef VOXCPM_B200_HPP_
+#define VOXCPM_B200_HPP_
+
+#include <cstddef>
+#include <cstdint>
+#include <memory>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "voxcpm_b200.h"
+
+namespace voxcpm_b200 {
+
+/// device.hpp:16-19
+class GpuError : public std::runtime_error {
+ public:
+  using std::runtime_error::runtime_error;
+};
+
+inline void Check(vx_status status, const char* what) {
+  if (status != VX_OK)
+    throw GpuError(std::string(what) + ": " + vx_last_error());
+}
+
+/// false for VX_UNSUPPORTED, throws on other failures.
+inline bool Launched(vx_status status, const char* what) {
+  if (status == VX_UNSUPPORTED)
+    return false;
+  Check(status, what);
+  return true;
+}
+
+using Bf16 = std::uint16_t;
+
+/// matrix.hpp:9-19
+enum class WeightFormat : std::uint8_t { kBf16 = 0, kBf16Tiles = 1, kQ8Tiles = 2 };
+struct Matrix {
+  WeightFormat format = WeightFormat::kBf16;
+  const void* data = nullptr;
+};
+
+namespace kernels {
+
+inline constexpr std::size_t kTileRows = 16;
+inline constexpr std::size_t kTileColumns = 32;
+inline constexpr std::size_t kQ8TileBytes = 16 * 32 + 16 * 2;
+inline constexpr std::size_t kBf16TileBytes = 16 * 32 * 2;
+inline constexpr std::size_t kSkinnyRows = 32;
+
+inline std::size_t Q8TilesBytes(std::size_t rows, std::size_t in) {
+  return vx_q8_tiles_bytes(rows, in);
+}
+inline std::size_t Bf16TilesBytes(std::size_t rows, std::size_t in) {
+  return vx_bf16_tiles_bytes(rows, in);
+}
+inline void Q8_0ToTiles(const std::uint8_t* blocks, std::size_t rows,
+                        std::size_t in, std::uint8_t* output,
+                        cudaStream_t stream) {
+  Check(vx_q8_0_to_tiles(blocks, rows, in, output, stream), "Q8_0ToTiles");
+}
+inline void Bf16ToTiles(const Bf16* weights, std::size_t rows, std::size_t in,
+                        Bf16* output, cudaStream_t stream) {
+  Check(vx_bf16_to_tiles(weights, rows, in, output, stream), "Bf16ToTiles");
+}
+inline void Q8TilesToBf16(const std::uint8_t* tiles, std::size_t rows,
+                          std::size_t in, Bf16* output, cudaStream_t stream) {
+  Check(vx_q8_tiles_to_bf16(tiles, rows, in, output, stream), "Q8TilesToBf16");
+}
+inline void Bf16TilesToRows(const Bf16* tiles, std::size_t rows,
+                            std::size_t in, Bf16* output,
+                            cudaStream_t stream) {
+  Check(vx_bf16_tiles_to_rows(tiles, rows, in, output, stream),
+        "Bf16TilesToRows");
+}
+
+/// kernels/wmma_products.hpp:62-81 (no scratch is needed: splits reduce on
+/// chip, so partial_floats and counters stay 0).
+struct SplitScratch {
+  float* partials = nullptr;
+  std::size_t partial_floats = 0;
+  unsigned* counters = nullptr;
+  std::size_t counter_count = 0;
+};
+using WmmaPlan = vx_wmma_plan;
+
+inline WmmaPlan PlanWmma(std::size_t rows, std::size_t in, std::size_t out,
+                         std::size_t target_waves = 0) {
+  return vx_plan_wmma(rows, in, out, target_waves);
+}
+inline bool WmmaQ8(const Bf16* x, const std::uint8_t* w, float* y,
+                   std::size_t rows, std::size_t in, std::size_t out,
+                   bool accumulate, const WmmaPlan& plan,
+                   const SplitScratch& scratch, cudaStream_t stream) {
+  const vx_split_scratch s{scratch.partials, scratch.partial_floats,
+                           scratch.counters, scratch.counter_count};
+  return Launched(vx_wmma_q8(x, w, y, rows, in, out, accumulate ? 1 : 0, &plan,
+                             &s, stream),
+                  "WmmaQ8");
+}
+inline bool WmmaBf16(const Bf16* x, const Bf16* w, float* y, std::size_t rows,
+                     std::size_t in, std::size_t out, bool accumulate,
+                     const WmmaPlan& plan, const SplitScratch& scratch,
+                     cudaStream_t stream) {
+  const vx_split_scratch s{scratch.partials, scratch.partial_floats,
+                           scratch.counters, scratch.counter_count};
+  return Launched(vx_wmma_bf16(x, w, y, rows, in, out, accumulate ? 1 : 0,
+                               &plan, &s, stream),
+                  "WmmaBf16");
+}
+/// kernels/skinny_gemm.hpp:18-34
+inline bool SkinnyGemm(const Bf16* x, const Bf16* w, float* y,
+                       std::size_t rows, std::size_t in, std::size_t out,
+                       bool accumulate, cudaStream_t stream) {
+  return Launched(
+      vx_skinny_gemm(x, w, y, rows, in, out, accumulate ? 1 : 0, stream),
+      "SkinnyGemm");
+}
+inline bool SkinnyGemmWith(int vec, const Bf16* x, const Bf16* w, float* y,
+                           std::size_t rows, std::size_t in, std::size_t out,
+                           bool accumulate, cudaStream_t stream) {
+  return Launched(vx_skinny_gemm_with(vec, x, w, y, rows, in, out,
+                                      accumulate ? 1 : 0, stream),
+                  "SkinnyGemmWith");
+}
+inline void ReadProbe(const Bf16* data, std::size_t pieces, unsigned blocks,
+                      unsigned* sink, cudaStream_t stream) {
+  Check(vx_read_probe(data, pieces, blocks, sink, stream), "ReadProbe");
+}
+
+/// kernels/generator_kernels.hpp:18-107 (fp32 KV caches, as the
+/// reference's; the C ABI also takes bf16 caches).
+inline void Embed(const Bf16* table, const std::int32_t* ids,
+                  const std::int32_t* text_mask, float* output,
+                  std::size_t rows, std::size_t width, float scale,
+                  cudaStream_t stream) {
+  Check(vx_embed(table, ids, text_mask, output, rows, width, scale, stream),
+        "Embed");
+}
+inline void ScatterRows(const float* input, const std::int32_t* indices,
+                        float* output, std::size_t rows, std::size_t width,
+                        cudaStream_t stream) {
+  Check(vx_scatter_rows(input, indices, output, rows, width, stream),
+        "ScatterRows");
+}
+inline void GatherRows(const float* input, const std::int32_t* indices,
+                       float* output, std::size_t rows, std::size_t width,
+                       cudaStream_t stream) {
+  Check(vx_gather_rows(input, indices, output, rows, width, stream),
+        "GatherRows");
+}
+inline void RmsNorm(const float* input, const Bf16* weight, Bf16* output,
+                    float* output_f32, std::size_t rows, std::size_t width,
+                    float epsilon, cudaStream_t stream) {
+  Check(vx_rms_norm(input, weight, output, output_f32, rows, width, epsilon,
+                    stream),
+        "RmsNorm");
+}
+inline void QkvRope(const float* qkv, const float* cos_sin,
+                    const std::int32_t* positions,
+                    const std::int32_t* cache_rows, float* q, float* k_cache,
+                    float* v_cache, std::size_t rows, std::size_t heads,
+                    std::size_t kv_heads, std::size_t head_dim,
+                    std::size_t capacity, cudaStream_t stream) {
+  Check(vx_qkv_rope(qkv, cos_sin, positions, cache_rows, q, k_cache, v_cache,
+                    VX_CACHE_F32, rows, heads, kv_heads, head_dim, capacity,
+                    stream),
+        "QkvRope");
+}
+inline void Attention(const float* q, const float* k_cache,
+                      const float* v_cache, Bf16* output, std::size_t rows,
+                      std::size_t rows_per_sequence,
+                      std::size_t keys_per_sequence, std::size_t past,
+                      bool causal, std::size_t heads, std::size_t kv_heads,
+                      std::size_t head_dim, std::size_t capacity,
+                      cudaStream_t stream) {
+  Check(vx_attention(q, k_cache, v_cache, VX_CACHE_F32, output, rows,
+                     rows_per_sequence, keys_per_sequence, past, nullptr,
+                     causal ? 1 : 0, heads, kv_heads, head_dim, capacity, 0,
+                     stream),
+        "Attention");
+}
+inline void SwiGlu(const float* gate_up, Bf16* output, std::size_t rows,
+                   std::size_t width, cudaStream_t stream) {
+  Check(vx_swiglu(gate_up, output, rows, width, stream), "SwiGlu");
+}
+inline void AddBias(float* data, const Bf16* bias, std::size_t rows,
+                    std::size_t width, cudaStream_t stream) {
+  Check(vx_add_bias(data, bias, rows, width, stream), "AddBias");
+}
+inline void ToBf16(const float* input, Bf16* output, std::size_t count,
+                   bool silu, cudaStream_t stream) {
+  Check(vx_to_bf16(input, output, count, silu ? 1 : 0, stream), "ToBf16");
+}
+inline void ConcatRows(const float* a, const float* a_scale,
+                       std::size_t a_width, const float* b,
+                       const float* b_scale, std::size_t b_width, Bf16* output,
+                       std::size_t rows, cudaStream_t stream) {
+  Check(vx_concat_rows(a, a_scale, a_width, b, b_scale, b_width, output, rows,
+                       stream),
+        "ConcatRows");
+}
+inline void Quantize(const float* input, Bf16* output, std::size_t count,
+                     float scale, cudaStream_t stream) {
+  Check(vx_quantize(input, output, count, scale, stream), "Quantize");
+}
+inline void SelectRows(const float* quantized, const float* plain,
+                       const std::int32_t* mask, float* output,
+                       std::size_t rows, std::size_t width,
+                       cudaStream_t stream) {
+  Check(vx_select_rows(quantized, plain, mask, output, rows, width, stream),
+        "SelectRows");
+}
+inline void PrependSpecial(const float* rows_in, const Bf16* special,
+                           float* output, std::size_t patches,
+                           std::size_t patch_size, std::size_t width,
+                           cudaStream_t stream) {
+  Check(vx_prepend_special(rows_in, special, output, patches, patch_size,
+                           width, stream),
+        "PrependSpecial");
+}
+inline void AssembleDit(const float* mu, const float* time, const float* cond,
+                        const float* x, float* output, std::size_t patch_size,
+                        std::size_t width, cudaStream_t stream) {
+  Check(vx_assemble_dit(mu, time, cond, x, output, patch_size, width, stream),
+        "AssembleDit");
+}
+inline void GuidedEuler(const float* velocity, float* x, std::size_t count,
+                        float cfg, float dt, cudaStream_t stream) {
+  Check(vx_guided_euler(velocity, x, count, cfg, dt, stream), "GuidedEuler");
+}
+
+}  // namespace kernels
+
+/// gemm.hpp:49-72. The reference's constructor also takes a hipBLAS handle
+/// for its library fallback; these products need none.
+class Bf16Gemm {
+ public:
+  explicit Bf16Gemm(cudaStream_t stream) : gemm_(vx_gemm_create(stream)) {
+    if (gemm_ == nullptr)
+      throw GpuError("vx_gemm_create failed");
+  }
+  ~Bf16Gemm() { vx_gemm_destroy(gemm_); }
+  Bf16Gemm(const Bf16Gemm&) = delete;
+  Bf16Gemm& operator=(const Bf16Gemm&) = delete;
+
+  void Linear(const void* x, const Matrix& w, float* y, std::size_t rows,
+              std::size_t in, std::size_t out, bool accumulate) {
+    Check(vx_gemm_linear(gemm_, static_cast<const std::uint16_t*>(x),
+                         static_cast<int>(w.format), w.data, y, rows, in, out,
+                         accumulate ? 1 : 0),
+          "Bf16Gemm::Linear");
+  }
+
+ private:
+  vx_gemm* gemm_;
+};
+
+/// transformer.hpp:63-66 (factors per frequency; the reference derives them
+/// from its RopeConfig).
+inline std::vector<float> RopeTable(double theta, std::size_t dim,
+                                    const std::vector<double>& factors,
+                                    double scaling, std::size_t positions) {
+  std::vector<float> table(positions * dim);
+  Check(vx_rope_table(theta, dim, factors.data(), scaling, positions,
+                      table.data()),
+        "RopeTable");
+  return table;
+}
+
+/// generator.hpp:24-44
+struct Prompt {
+  std::vector<std::int32_t> tokens;
+  std::vector<std::int32_t> text_mask;
+  std::vector<std::int32_t> audio_mask;
+  std::vector<float> feats;  // [rows][patch_size][feat_dim]
+};
+
+struct EulerStep {
+  float t = 0.0f;
+  float dt = 0.0f;
+  bool evaluate = true;
+};
+
+inline std::vector<EulerStep> EulerSchedule(std::size_t timesteps,
+                                            float sway = 1.0f) {
+  std::vector<float> t(timesteps), dt(timesteps);
+  std::vector<std::int32_t> evaluate(timesteps);
+  const std::size_t n = vx_euler_schedule(timesteps, sway, t.data(), dt.data(),
+                                          evaluate.data(), timesteps);
+  std::vector<EulerStep> steps;
+  for (std::size_t i = 0; i < n && i < timesteps; ++i)
+    steps.push_back({t[i], dt[i], evaluate[i] != 0});
+  return steps;
+}
+
+/// generator.hpp:58-179 with seeded weights (the reference's Create reads
+/// checkpoint files, which are out of scope here).
+class Generator {
+ public:
+  static std::unique_ptr<Generator> Create(const vx_model_config& config,
+                                           std::uint64_t seed, int checkpoint,
+                                           int cache_type,
+                                           std::string* error = nullptr) {
+    vx_generator* g = vx_generator_create(&config, seed, checkpoint, cache_type);
+    if (g == nullptr) {
+      if (error != nullptr)
+        *error = vx_last_error();
+      return nullptr;
+    }
+    return std::unique_ptr<Generator>(new Generator(g, config));
+  }
+  ~Generator() { vx_generator_destroy(g_); }
+  Generator(const Generator&) = delete;
+  Generator& operator=(const Generator&) = delete;
+
+  std::size_t capacity() const { return static_cast<std::size_t>(config_.max_length); }
+  std::size_t position() const { return vx_generator_position(g_); }
+
+  void Prefill(const Prompt& prompt) {
+    Check(vx_generator_prefill(g_, prompt.tokens.data(),
+                               prompt.text_mask.data(),
+                               prompt.audio_mask.data(), prompt.feats.data(),
+                               prompt.tokens.size()),
+          "Generator::Prefill");
+  }
+  void Step(const float* noise, std::size_t timesteps, float cfg,
+            float* latent, float* stop_logits) {
+    Check(vx_generator_step(g_, noise, timesteps, cfg, latent, stop_logits),
+          "Generator::Step");
+  }
+  void Velocity(const float* mu, const float* cond, const float* x, float t,
+                float* velocity) {
+    Check(vx_generator_velocity(g_, mu, cond, x, t, velocity),
+          "Generator::Velocity");
+  }
+
+ private:
+  Generator(vx_generator* g, const vx_model_config& config)
+      : g_(g), config_(config) {}
+  vx_generator* g_;
+  vx_model_config config_;
+};
+
+}  // namespace voxcpm_b200
+
+#endif  // VOXCPM_B200_HPP_

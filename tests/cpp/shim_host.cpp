@@ -1,0 +1,25 @@
+// Host-only use of the C++ mirror header (no GPU calls): compiles against
+// include/voxcpm_b200.hpp, links libvoxcpm_b200.so and prints the Euler
+// schedule, a product plan and tile sizes for the Python test to check.
+#include <cstdio>
+
+#include "voxcpm_b200.hpp"
+
+int main() {
+  namespace vb = voxcpm_b200;
+  for (const vb::EulerStep& s : vb::EulerSchedule(10))
+    std::printf("step %.9g %.9g %d\n", s.t, s.dt, s.evaluate ? 1 : 0);
+  const vb::kernels::WmmaPlan plan = vb::kernels::PlanWmma(22, 2048, 6144);
+  std::printf("plan %zu %zu %zu %zu\n", plan.splits, plan.blocks_per_split,
+              plan.partial_floats, plan.counters);
+  std::printf("tiles %zu %zu\n", vb::kernels::Q8TilesBytes(6144, 2048),
+              vb::kernels::Bf16TilesBytes(72, 1024));
+  const std::vector<float> table = vb::RopeTable(10000.0, 128, std::vector<double>(64, 1.0), 1.0, 4);
+  std::printf("rope %.9g %.9g\n", table[128 + 1], table[3 * 128 + 64 + 5]);
+  try {
+    vb::Check(VX_INVALID, "forced");
+  } catch (const vb::GpuError& e) {
+    std::printf("error ok\n");
+  }
+  return 0;
+}
