@@ -158,6 +158,21 @@ VX_API vx_status vx_product(int format, const uint16_t* x, const void* w, void* 
                      int accumulate, const vx_wmma_plan* plan,
                      cudaStream_t stream);
 
+/* Flags of vx_product_ex. */
+#define VX_PRODUCT_ACCUMULATE 1u
+/* The launch reads nothing that earlier kernels on the stream write (x, w
+ * and, when accumulating, y are ready before it is enqueued): it may overlap
+ * them instead of waiting for their completion. */
+#define VX_PRODUCT_INDEPENDENT 2u
+
+/* vx_product with flags (VX_PRODUCT_ACCUMULATE, VX_PRODUCT_INDEPENDENT).
+ * Extends WmmaQ8/WmmaBf16/SkinnyGemm (kernels/wmma_products.hpp:87-99,
+ * kernels/skinny_gemm.hpp:18-24). */
+VX_API vx_status vx_product_ex(int format, const uint16_t* x, const void* w,
+                               void* y, int out_dtype, size_t rows, size_t in,
+                               size_t out, unsigned flags,
+                               const vx_wmma_plan* plan, cudaStream_t stream);
+
 /* Programmatic dependent launch for every kernel of the library (default on).
  * No reference counterpart (HIP has none). */
 VX_API void vx_set_programmatic_launch(int enabled);

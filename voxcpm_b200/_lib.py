@@ -27,6 +27,9 @@ WEIGHTS_Q8_TILES = 2
 OUT_F32 = 0
 OUT_BF16 = 1
 
+PRODUCT_ACCUMULATE = 1
+PRODUCT_INDEPENDENT = 2
+
 CACHE_F32 = 0
 CACHE_BF16 = 1
 
@@ -108,6 +111,11 @@ SIGNATURES: dict[str, tuple] = {
         c_int,
         [c_int, c_void_p, c_void_p, c_void_p, c_int, c_size_t, c_size_t, c_size_t,
          c_int, POINTER(WmmaPlan), c_void_p],
+    ),
+    "vx_product_ex": (
+        c_int,
+        [c_int, c_void_p, c_void_p, c_void_p, c_int, c_size_t, c_size_t, c_size_t,
+         c_uint, POINTER(WmmaPlan), c_void_p],
     ),
     "vx_set_programmatic_launch": (None, [c_int]),
     "vx_product_variants": (c_int, []),

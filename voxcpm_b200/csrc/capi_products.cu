@@ -61,7 +61,8 @@ vx::ProductPlan ToPlan(const vx_wmma_plan* plan) {
 vx_status Product(int format, const uint16_t* x, const void* w, void* y,
                   int out_dtype, size_t rows, size_t in, size_t out,
                   int accumulate, const vx_wmma_plan* plan,
-                  cudaStream_t stream, const char* what) {
+                  cudaStream_t stream, const char* what,
+                  bool independent = false) {
   if (out_dtype != VX_OUT_F32 && out_dtype != VX_OUT_BF16)
     return vx::Fail(vx::kInvalid, std::string(what) + ": unknown out_dtype");
   const vx::ProductPlan p = ToPlan(plan);
@@ -70,7 +71,7 @@ vx_status Product(int format, const uint16_t* x, const void* w, void* y,
       out_dtype == VX_OUT_F32 ? static_cast<float*>(y) : nullptr,
       out_dtype == VX_OUT_BF16 ? static_cast<uint16_t*>(y) : nullptr, rows,
       in, out, accumulate != 0, plan != nullptr && plan->splits > 0 ? &p : nullptr,
-      stream);
+      stream, independent);
   return vx::Checked(status, what);
 }
 
@@ -188,6 +189,17 @@ vx_status vx_product(int format, const uint16_t* x, const void* w, void* y,
                      cudaStream_t stream) {
   return Product(format, x, w, y, out_dtype, rows, in, out, accumulate, plan,
                  stream, "vx_product");
+}
+
+vx_status vx_product_ex(int format, const uint16_t* x, const void* w, void* y,
+                        int out_dtype, size_t rows, size_t in, size_t out,
+                        unsigned flags, const vx_wmma_plan* plan,
+                        cudaStream_t stream) {
+  if ((flags & ~(VX_PRODUCT_ACCUMULATE | VX_PRODUCT_INDEPENDENT)) != 0)
+    return vx::Fail(vx::kInvalid, "vx_product_ex: unknown flags");
+  return Product(format, x, w, y, out_dtype, rows, in, out,
+                 (flags & VX_PRODUCT_ACCUMULATE) != 0 ? 1 : 0, plan, stream,
+                 "vx_product_ex", (flags & VX_PRODUCT_INDEPENDENT) != 0);
 }
 
 void vx_set_programmatic_launch(int enabled) {

@@ -57,10 +57,14 @@ ProductPlan PlanProduct(WeightFormat format, std::size_t rows, std::size_t in,
 
 /// Launches one product of at most kMaxProductRows rows. Returns kOk,
 /// kUnsupported (nothing launched) or kInvalid / kCudaError.
+/// `independent`: the launch reads nothing that the kernels before it on
+/// the stream write, so it skips the programmatic-launch wait and may overlap
+/// them (streams of independent products).
 int LaunchProduct(WeightFormat format, const std::uint16_t* x, const void* w,
                   float* y, std::uint16_t* y_bf16, std::size_t rows,
                   std::size_t in, std::size_t out, bool accumulate,
-                  const ProductPlan* plan, cudaStream_t stream);
+                  const ProductPlan* plan, cudaStream_t stream,
+                  bool independent = false);
 
 /// Whether kernels are launched with programmatic dependent launch.
 void SetProgrammaticLaunch(bool enabled);

@@ -88,16 +88,20 @@ __device__ inline void MbarArriveExpectTx(std::uint64_t* bar, unsigned bytes) {
       : "memory");
 }
 
-__device__ inline bool MbarTryWait(std::uint64_t* bar, unsigned parity) {
+/// Tests phase `parity` of `bar`; a thread whose phase is not complete is
+/// suspended by the hardware until it completes or `suspend_ns` pass, so a
+/// waiting warp takes no issue slots from the warps that compute.
+__device__ inline bool MbarTryWait(std::uint64_t* bar, unsigned parity,
+                                   std::uint32_t suspend_ns = 10000000u) {
   std::uint32_t done;
   asm volatile(
       "{\n"
       ".reg .pred p;\n"
-      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2;\n"
+      "mbarrier.try_wait.parity.shared::cta.b64 p, [%1], %2, %3;\n"
       "selp.u32 %0, 1, 0, p;\n"
       "}\n"
       : "=r"(done)
-      : "r"(SmemAddr(bar)), "r"(parity)
+      : "r"(SmemAddr(bar)), "r"(parity), "r"(suspend_ns)
       : "memory");
   return done != 0;
 }
