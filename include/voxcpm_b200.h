@@ -383,6 +383,15 @@ VX_API vx_status vx_generator_set_state(vx_generator* generator,
                                         size_t count);
 /* CUDA graphs for Step and the DiT patch (default on). */
 VX_API vx_status vx_generator_set_graphs(vx_generator* generator, int enabled);
+/* The DiT patch as one persistent cooperative kernel (default on when the
+ * DiT has VoxCPM2's shape: hidden 1024, FFN 4096, 16/2 heads of 128, patch
+ * 4 x 64) or as the per-kernel sequence (generator.cpp:297-324, :457-463).
+ * Enabling it for another DiT shape returns VX_UNSUPPORTED. No reference
+ * counterpart: the reference always runs the per-kernel sequence. */
+VX_API vx_status vx_generator_set_persistent(vx_generator* generator,
+                                             int enabled);
+/* 1 when the DiT patch runs as the persistent kernel. */
+VX_API int vx_generator_persistent(const vx_generator* generator);
 /* Rows in the caches (Generator::position, generator.hpp:69-70). */
 VX_API size_t vx_generator_position(const vx_generator* generator);
 VX_API size_t vx_generator_weight_bytes(const vx_generator* generator);

@@ -163,6 +163,8 @@ SIGNATURES: dict[str, tuple] = {
     "vx_generator_state": (c_int, [c_void_p, c_char_p, c_void_p, c_size_t]),
     "vx_generator_set_state": (c_int, [c_void_p, c_char_p, c_void_p, c_size_t]),
     "vx_generator_set_graphs": (c_int, [c_void_p, c_int]),
+    "vx_generator_set_persistent": (c_int, [c_void_p, c_int]),
+    "vx_generator_persistent": (c_int, [c_void_p]),
     "vx_generator_position": (c_size_t, [c_void_p]),
     "vx_generator_weight_bytes": (c_size_t, [c_void_p]),
     "vx_generator_stream": (c_void_p, [c_void_p]),

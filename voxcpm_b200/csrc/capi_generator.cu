@@ -192,6 +192,25 @@ vx_status vx_generator_set_graphs(vx_generator* generator, int enabled) {
                [&](vx::Generator& g) { g.set_graphs(enabled != 0); });
 }
 
+vx_status vx_generator_set_persistent(vx_generator* generator, int enabled) {
+  bool served = true;
+  const vx_status status =
+      Guard(generator, "vx_generator_set_persistent",
+            [&](vx::Generator& g) { served = g.set_persistent(enabled != 0); });
+  if (status == vx::kOk && !served)
+    return vx::Fail(vx::kUnsupported,
+                    "vx_generator_set_persistent: the DiT does not have the "
+                    "shape the persistent kernel serves");
+  return status;
+}
+
+int vx_generator_persistent(const vx_generator* generator) {
+  return generator != nullptr && generator->impl &&
+                 generator->impl->persistent()
+             ? 1
+             : 0;
+}
+
 size_t vx_generator_position(const vx_generator* generator) {
   return generator != nullptr && generator->impl
              ? static_cast<size_t>(generator->impl->position())

@@ -575,6 +575,7 @@ std::unique_ptr<Generator> Generator::Create(const ModelConfig& config,
                "delta_time_2");
       g->CheckCuda(cudaStreamSynchronize(g->stream_), "create");
     }
+    g->SetupPersistent();
   } catch (const std::exception& failure) {
     if (error != nullptr)
       *error = failure.what();
@@ -607,6 +608,11 @@ Generator::~Generator() {
   free(encoder_a_);
   free(encoder_b_);
   free(encoder_c_);
+  free(dit_layers_);
+  free(dit_work_);
+  free(dit_io_tiles_);
+  free(dit_times_);
+  free(dit_dts_);
   if (pinned_noise_ != nullptr)
     cudaFreeHost(pinned_noise_);
   if (pinned_latent_ != nullptr)
@@ -678,9 +684,128 @@ void Generator::PrepareTimes(int timesteps) {
                       evaluate.data(), timesteps);
     schedule_eval_.assign(evaluate.begin(), evaluate.end());
   }
+  std::vector<const float*> times;
+  std::vector<float> dts;
   for (int i = 0; i < timesteps; ++i)
-    if (schedule_eval_[i])
-      (void)TimeVector(schedule_t_[i]);
+    if (schedule_eval_[i]) {
+      times.push_back(TimeVector(schedule_t_[i]));
+      dts.push_back(schedule_dt_[i]);
+    }
+  if (!persistent_ok_ || dit_schedule_timesteps_ == timesteps)
+    return;
+  // The persistent kernel's per-evaluation schedule, on the device.
+  const int count = static_cast<int>(times.size());
+  CheckCuda(cudaStreamSynchronize(stream_), "sync");
+  if (count > dit_schedule_capacity_) {
+    DestroyGraphs();  // graphs hold the old schedule pointers
+    for (void* p : {static_cast<void*>(dit_times_), static_cast<void*>(dit_dts_)})
+      if (p != nullptr)
+        cudaFree(p);
+    dit_times_ = nullptr;
+    dit_dts_ = nullptr;
+    dit_schedule_capacity_ = 0;
+    const std::size_t capacity = std::max(count, 16);
+    CheckCuda(cudaMalloc(reinterpret_cast<void**>(&dit_times_),
+                         capacity * sizeof(float*)), "cudaMalloc schedule");
+    CheckCuda(cudaMalloc(reinterpret_cast<void**>(&dit_dts_),
+                         capacity * sizeof(float)), "cudaMalloc schedule");
+    dit_schedule_capacity_ = static_cast<int>(capacity);
+  }
+  if (count > 0) {
+    CheckCuda(cudaMemcpy(dit_times_, times.data(), count * sizeof(float*),
+                         cudaMemcpyHostToDevice), "upload schedule");
+    CheckCuda(cudaMemcpy(dit_dts_, dts.data(), count * sizeof(float),
+                         cudaMemcpyHostToDevice), "upload schedule");
+  }
+  dit_evaluations_ = count;
+  dit_schedule_timesteps_ = timesteps;
+}
+
+void Generator::SetupPersistent() {
+  // The persistent patch serves VoxCPM2's DiT shape with tiled layer
+  // weights (both checkpoint kinds store the DiT stack as tiles).
+  const ModelConfig& c = config_;
+  const StackConfig& d = c.dit;
+  using Shape = DitShape;
+  if (d.hidden != Shape::kHidden || d.intermediate != Shape::kIntermediate ||
+      d.heads != Shape::kHeads || d.kv_heads != Shape::kKvHeads ||
+      d.head_dim != Shape::kHeadDim || c.patch_size != Shape::kPatch ||
+      c.feat_dim != Shape::kFeat || d.layers < 1)
+    return;
+  const WeightFormat format = w_.dit.layers[0].qkv.format;
+  if (format != WeightFormat::kQ8Tiles && format != WeightFormat::kBf16Tiles)
+    return;
+  std::vector<DitLayer> layers(d.layers);
+  for (int i = 0; i < d.layers; ++i) {
+    const LayerWeights& w = w_.dit.layers[i];
+    layers[i].qkv = static_cast<const unsigned char*>(w.qkv.weight);
+    layers[i].o = static_cast<const unsigned char*>(w.o.weight);
+    layers[i].gate_up = static_cast<const unsigned char*>(w.gate_up.weight);
+    layers[i].down = static_cast<const unsigned char*>(w.down.weight);
+    layers[i].input_norm = w.input_norm;
+    layers[i].post_norm = w.post_norm;
+  }
+  CheckCuda(cudaMalloc(reinterpret_cast<void**>(&dit_layers_),
+                       layers.size() * sizeof(DitLayer)), "cudaMalloc layers");
+  CheckCuda(cudaMemcpy(dit_layers_, layers.data(),
+                       layers.size() * sizeof(DitLayer), cudaMemcpyHostToDevice),
+            "upload layers");
+  CheckCuda(cudaMalloc(&dit_work_, DitWorkBytes()), "cudaMalloc DiT work");
+  DitPatchParams& p = dit_params_;
+  DitWorkLayout(dit_work_, p);
+  p.format = format;
+  p.layers = d.layers;
+  p.bf16_kv = dit_cache_.type() == CacheType::kBf16 ? 1 : 0;
+  p.eps = d.rms_eps;
+  p.attention_scale = 1.0f / std::sqrt(static_cast<float>(d.head_dim));
+  p.layer = dit_layers_;
+  p.final_norm = w_.dit.norm;
+  p.rope = d.rope ? rope_ : nullptr;
+  p.mu = mu_;
+  p.cond_rows = cond_rows_;
+  p.x = x_;
+  p.dit_in_bias = w_.dit_in.bias;
+  p.dit_out_bias = w_.dit_out.bias;
+  if (w_.dit_in.format == format && w_.dit_out.format == format) {
+    p.dit_in = static_cast<const unsigned char*>(w_.dit_in.weight);
+    p.dit_out = static_cast<const unsigned char*>(w_.dit_out.weight);
+  } else if (format == WeightFormat::kBf16Tiles &&
+             w_.dit_in.format == WeightFormat::kBf16 &&
+             w_.dit_out.format == WeightFormat::kBf16) {
+    // The bf16 checkpoint keeps the DiT's in/out projections as rows; the
+    // persistent kernel streams them as tiles.
+    const std::size_t in_bytes = Bf16TilesBytes(w_.dit_in.out, w_.dit_in.in);
+    const std::size_t out_bytes = Bf16TilesBytes(w_.dit_out.out, w_.dit_out.in);
+    CheckCuda(cudaMalloc(reinterpret_cast<void**>(&dit_io_tiles_),
+                         in_bytes + out_bytes), "cudaMalloc tiles");
+    Check(Bf16ToTiles(static_cast<const std::uint16_t*>(w_.dit_in.weight),
+                      w_.dit_in.out, w_.dit_in.in,
+                      reinterpret_cast<std::uint16_t*>(dit_io_tiles_), stream_),
+          "dit_in tiles");
+    Check(Bf16ToTiles(static_cast<const std::uint16_t*>(w_.dit_out.weight),
+                      w_.dit_out.out, w_.dit_out.in,
+                      reinterpret_cast<std::uint16_t*>(dit_io_tiles_ + in_bytes),
+                      stream_),
+          "dit_out tiles");
+    CheckCuda(cudaStreamSynchronize(stream_), "tiles");
+    p.dit_in = dit_io_tiles_;
+    p.dit_out = dit_io_tiles_ + in_bytes;
+  } else {
+    return;
+  }
+  persistent_ok_ = true;
+  persistent_ = true;
+}
+
+bool Generator::set_persistent(bool enabled) {
+  if (enabled && !persistent_ok_)
+    return false;
+  if (enabled != persistent_) {
+    CheckCuda(cudaStreamSynchronize(stream_), "sync");
+    DestroyGraphs();
+    persistent_ = enabled;
+  }
+  return true;
 }
 
 const float* Generator::TimeVector(float t) {
@@ -844,6 +969,20 @@ void Generator::DitCond() {
 
 void Generator::EulerLoop(int timesteps, float cfg) {
   const int values = config_.patch_size * config_.feat_dim;
+  if (persistent_) {
+    // PrepareTimes(timesteps) uploaded this schedule beforehand.
+    if (dit_schedule_timesteps_ != timesteps)
+      throw std::logic_error("DiT schedule not prepared");
+    if (dit_evaluations_ == 0)
+      return;
+    DitPatchParams p = dit_params_;
+    p.cfg = cfg;
+    p.evaluations = dit_evaluations_;
+    p.time_vectors = dit_times_;
+    p.dts = dit_dts_;
+    Check(LaunchDitPatch(p, stream_), "persistent DiT patch");
+    return;
+  }
   for (int i = 0; i < timesteps; ++i) {
     if (!schedule_eval_[i])
       continue;  // zero velocity (CFG-Zero*)

@@ -15,6 +15,7 @@
 #include <string>
 #include <vector>
 
+#include "persistent_dit.cuh"
 #include "products.cuh"
 #include "stack_kernels.cuh"
 
@@ -192,6 +193,11 @@ class Generator {
   void SetState(const std::string& name, const float* in, std::size_t count);
   void set_graphs(bool enabled) { graphs_ = enabled; }
   bool graphs() const { return graphs_; }
+  /// Whether the DiT patch runs as the persistent kernel (default when the
+  /// DiT has VoxCPM2's shape). Returns false when asked to enable it for a
+  /// DiT of another shape.
+  bool set_persistent(bool enabled);
+  bool persistent() const { return persistent_; }
   /// Device buffers of the DiT patch's inputs and output (benchmarks).
   float* device_mu() const { return mu_; }
   float* device_prefix() const { return prefix_cond_; }
@@ -212,6 +218,7 @@ class Generator {
   void PrepareTimes(int timesteps);
   void EnsureRows(int rows);
   void DestroyGraphs();
+  void SetupPersistent();
 
   ModelConfig config_;
   cudaStream_t stream_ = nullptr;
@@ -276,6 +283,19 @@ class Generator {
   float patch_graph_cfg_ = 0.0f;
   std::vector<float> schedule_t_, schedule_dt_;
   std::vector<int> schedule_eval_;
+
+  // The persistent DiT patch.
+  bool persistent_ok_ = false;
+  bool persistent_ = false;
+  DitPatchParams dit_params_;
+  DitLayer* dit_layers_ = nullptr;
+  void* dit_work_ = nullptr;
+  unsigned char* dit_io_tiles_ = nullptr;  // bf16 rows of dit_in/out as tiles
+  const float** dit_times_ = nullptr;      // device: time vector per evaluation
+  float* dit_dts_ = nullptr;               // device: dt per evaluation
+  int dit_schedule_capacity_ = 0;
+  int dit_schedule_timesteps_ = -1;
+  int dit_evaluations_ = 0;
 };
 
 /// The reference's released shapes (tests/config_test.cpp:36-67): LM 28 x

@@ -1,0 +1,1183 @@
+// The persistent DiT patch kernel (see persistent_dit.cuh).
+//
+// Arithmetic follows the per-kernel path it replaces, operation by
+// operation (kernels/generator_kernels.hip:91-360 for the norms, RoPE,
+// attention, SwiGLU, biases and the CFG-Zero* update; transformer.cpp:55-100
+// for the layer order): bf16 roundings sit at the same points, products
+// accumulate in fp32 per 32-column block with the Q8 scale applied per
+// block. Only float summation orders differ (products split over warps and
+// CTAs, two-pass softmax), so results agree with the per-kernel path to
+// float32 rounding noise, and are bit-for-bit repeatable run to run.
+#include "persistent_dit.cuh"
+
+#include <cmath>
+#include <mutex>
+
+#include "product_math.cuh"
+#include "vx_common.cuh"
+#include "vx_status.h"
+
+namespace vx {
+namespace {
+
+using Shape = DitShape;
+
+constexpr int kChunk = 1024;                        // reduction columns per unit
+constexpr int kUnitTiles = kChunk / kTileColumns;   // 32 tiles per unit
+constexpr int kQkvWidth =
+    (Shape::kHeads + 2 * Shape::kKvHeads) * Shape::kHeadDim;  // 2560
+constexpr int kAttWidth = Shape::kHeads * Shape::kHeadDim;    // 2048
+constexpr int kRows = Shape::kRows;                           // 22
+constexpr int kSeq = Shape::kSequence;                        // 11
+constexpr int kHidden = Shape::kHidden;
+constexpr int kInter = Shape::kIntermediate;
+constexpr int kConsumerWarps = 16;
+constexpr int kConsumers = kConsumerWarps * 32;
+constexpr int kThreads = kConsumers + 64;  // + producer and publisher warps
+constexpr int kXRows = 24;                 // three MMA column tiles of 8
+constexpr int kXStride = kChunk * 2 + 64;  // bytes per staged row (bank skew)
+constexpr int kRedFloats = 32 * 12;        // one warp's accumulators, 3 tiles
+constexpr int kOParts = kAttWidth / kChunk;   // 2
+constexpr int kDownParts = kInter / kChunk;   // 4
+constexpr int kDitInSlots = (kHidden / 16) * (Shape::kFeat / 32) / kUnitTiles;
+constexpr int kDitOutSlots = Shape::kFeat / 16;
+constexpr int kKvGroups = 2 * Shape::kKvHeads * Shape::kHeadDim / 16;  // 32
+constexpr int kHeadGroups = Shape::kHeadDim / 16;                       // 8
+constexpr int kHeadsPerKv = Shape::kHeads / Shape::kKvHeads;            // 8
+constexpr int kHeadsPerChunk = kChunk / Shape::kHeadDim;                // 8
+constexpr int kAttentionTasks = 2 * Shape::kHeads;  // (head, sequence)
+constexpr int kGuPerChunk = kChunk / 16;            // 64
+constexpr int kGroups = kHidden / 16;               // 64
+constexpr int kPubSlots = 8;
+constexpr std::uint64_t kWaitLimitNs = 2000000000ull;
+constexpr std::uint32_t kSuspendNs = 100000u;
+
+// Sync words (zeroed per launch), all monotone over the launch: the abort
+// flag; per query head the count of its q groups done, per KV head the
+// count of its k and v groups; per 1024-column chunk of the attention
+// output the count of (head, sequence) tasks done; the count of residual
+// groups folded; the count of assembled evaluations; per chunk of the
+// SwiGLU activation the count of gate/up units done; per residual group
+// the count of split parts stored (all but the folding one).
+constexpr int kSyncAbort = 0;
+constexpr int kSyncQ = 32;          // [16]
+constexpr int kSyncKv = 48;         // [2]
+constexpr int kSyncAtt = 64;        // [2]
+constexpr int kSyncHidden = 96;
+constexpr int kSyncAssembled = 97;
+constexpr int kSyncAct = 128;       // [4]
+constexpr int kSyncParts = 160;     // [64]
+constexpr unsigned kPartsPerLayer = (kOParts - 1) + (kDownParts - 1);
+
+static_assert(kHidden == kChunk, "QKV and gate/up reduce over one chunk");
+static_assert(kRows <= kXRows, "activation rows fit three column tiles");
+static_assert(kSyncParts + kGroups <= kDitSyncWords, "part counters");
+static_assert(kSyncQ + Shape::kHeads <= kSyncKv, "head counters");
+static_assert(Shape::kHeadDim == 128, "attention lanes hold 4 of 128");
+static_assert(kSeq <= kConsumerWarps, "one warp per query row");
+static_assert(2 * Shape::kPatch <= 8, "DiT outputs fit one column tile");
+static_assert(kDitInSlots * kUnitTiles == (kHidden / 16) * (Shape::kFeat / 32),
+              "dit_in tiles fill whole slots");
+static_assert(kRows == 22 && kHidden == 1024, "staging layouts");
+
+enum Phase : int { kQkv = 0, kO = 1, kGu = 2, kDown = 3 };
+
+__host__ __device__ constexpr int PhaseUnits(int phase) {
+  return phase == kQkv  ? kQkvWidth / 16
+         : phase == kO  ? kGroups * kOParts
+         : phase == kGu ? kInter / 16
+                        : kGroups * kDownParts;
+}
+__host__ __device__ constexpr int SlotsPerUnit(int phase) {
+  return phase == kGu ? 2 : 1;  // gate group and up group
+}
+/// QKV units take the key and value groups first.
+__host__ __device__ constexpr int QkvGroup(int u) {
+  return u < kKvGroups ? kAttWidth / 16 + u : u - kKvGroups;
+}
+
+template <int kFormat>
+struct RingShape {
+  static constexpr bool kQ8 =
+      kFormat == static_cast<int>(WeightFormat::kQ8Tiles);
+  static constexpr int kTile = kQ8 ? kQ8TileBytes : kBf16TileBytes;
+  static constexpr int kSlots = kQ8 ? 8 : 4;
+  static constexpr int kSlotBytes = kTile * kUnitTiles;
+  static constexpr int kXsOffset = kSlots * kSlotBytes;
+  static constexpr int kRedOffset = kXsOffset + kXRows * kXStride;
+  static constexpr int kVelOffset =
+      kRedOffset + kConsumerWarps * kRedFloats * 4;
+  static constexpr int kSumsOffset =
+      kVelOffset + 2 * Shape::kPatch * Shape::kFeat * 4;
+  static constexpr int kPubOffset = kSumsOffset + 256 * 4;
+  static constexpr int kBarOffset = kPubOffset + kPubSlots * 16;
+  static constexpr int kFlagOffset = kBarOffset + 2 * (kSlots + kPubSlots) * 8;
+  static constexpr int kSmemBytes = kFlagOffset + 16;
+  static_assert(kSlotBytes % 128 == 0 && kXsOffset % 128 == 0, "alignment");
+  static_assert(kSmemBytes <= 227 * 1024, "shared memory");
+  // Attention keys and values of one (head, sequence) use the reduction
+  // buffer.
+  static_assert(2 * kSeq * Shape::kHeadDim * 4 <= kConsumerWarps * kRedFloats * 4,
+                "attention staging");
+};
+
+/// One request to the publisher warp: add `value` to `counter`.
+struct PubEntry {
+  unsigned* counter;
+  unsigned value;
+  unsigned pad;
+};
+
+// ---------------------------------------------------------------- helpers
+
+__device__ inline void ConsumerSync() {
+  asm volatile("bar.sync 1, %0;" ::"n"(kConsumers) : "memory");
+}
+
+/// Consumer barrier that also ORs a predicate over the consumer threads.
+__device__ inline bool ConsumerSyncOr(bool value) {
+  unsigned result;
+  asm volatile(
+      "{\n.reg .pred p, q;\nsetp.ne.u32 q, %1, 0;\n"
+      "bar.red.or.pred p, 1, %2, q;\nselp.u32 %0, 1, 0, p;\n}"
+      : "=r"(result)
+      : "r"(static_cast<unsigned>(value)), "n"(kConsumers)
+      : "memory");
+  return result != 0;
+}
+
+__device__ inline void MbarArrive(std::uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(SmemAddr(bar))
+               : "memory");
+}
+
+__device__ inline unsigned LoadAcquire(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.acquire.gpu.global.u32 %0, [%1];"
+               : "=r"(v)
+               : "l"(p)
+               : "memory");
+  return v;
+}
+
+__device__ inline unsigned LoadRelaxed(const unsigned* p) {
+  unsigned v;
+  asm volatile("ld.relaxed.gpu.global.u32 %0, [%1];"
+               : "=r"(v)
+               : "l"(p)
+               : "memory");
+  return v;
+}
+
+__device__ inline void RedRelease(unsigned* p, unsigned v) {
+  asm volatile("red.release.gpu.global.add.u32 [%0], %1;" ::"l"(p), "r"(v)
+               : "memory");
+}
+
+__device__ inline float WarpAllSum(float v) {
+#pragma unroll
+  for (int o = 16; o > 0; o >>= 1)
+    v += __shfl_xor_sync(0xFFFFFFFFu, v, o);
+  return v;
+}
+
+/// Two floats -> packed bf16 pair (lo in the low half), round to nearest
+/// even (the hardware conversion; equal to the software rounding for every
+/// non-NaN input).
+__device__ inline unsigned PackBf16x2(float lo, float hi) {
+  unsigned d;
+  asm("cvt.rn.bf16x2.f32 %0, %1, %2;" : "=r"(d) : "f"(hi), "f"(lo));
+  return d;
+}
+
+__device__ inline uint2 PackBf16x4(float a, float b, float c, float d) {
+  return make_uint2(PackBf16x2(a, b), PackBf16x2(c, d));
+}
+
+__device__ inline Bf16 ToBf16(float v) {
+  return static_cast<Bf16>(PackBf16x2(v, 0.0f) & 0xFFFFu);
+}
+
+__device__ inline float RoundBf16(float v) {
+  return Bf16ToFloat(ToBf16(v));
+}
+
+/// Abort state shared by the CTA's warps and, through `sync`, all CTAs.
+struct Control {
+  unsigned* sync;
+  unsigned* error_word;
+  volatile int* aborted;  // shared
+};
+
+__device__ inline void Abort(const Control& c, unsigned error) {
+  if (error != 0)
+    atomicOr(c.error_word, error);
+  atomicExch(c.sync + kSyncAbort, 1u);
+  *c.aborted = 1;
+}
+
+/// Waits for phase `parity` of `bar`, giving up when any CTA aborted or
+/// after the time limit (which aborts the launch).
+__device__ bool WaitSlot(std::uint64_t* bar, unsigned parity,
+                         const Control& c, unsigned error) {
+  if (MbarTryWait(bar, parity, kSuspendNs))
+    return true;
+  const std::uint64_t start = GlobalTimerNs();
+  while (true) {
+    if (MbarTryWait(bar, parity, kSuspendNs))
+      return true;
+    if (*c.aborted != 0 || LoadRelaxed(c.sync + kSyncAbort) != 0) {
+      *c.aborted = 1;
+      return false;
+    }
+    if (GlobalTimerNs() - start > kWaitLimitNs) {
+      Abort(c, error);
+      return false;
+    }
+  }
+}
+
+/// Consumer-wide wait until `*counter >= target` (thread 0 polls with
+/// acquire loads). Returns false, uniformly, once the launch aborted.
+__device__ bool WaitCount(const Control& c, const unsigned* counter,
+                          unsigned target) {
+  bool aborted = false;
+  if (threadIdx.x == 0) {
+    if (*c.aborted == 0 && LoadAcquire(counter) < target) {
+      const std::uint64_t start = GlobalTimerNs();
+      unsigned spins = 0;
+      while (LoadAcquire(counter) < target) {
+        if (LoadRelaxed(c.sync + kSyncAbort) != 0) {
+          *c.aborted = 1;
+          break;
+        }
+        if ((++spins & 63u) == 0 && GlobalTimerNs() - start > kWaitLimitNs) {
+          Abort(c, kErrBarrierWait);
+          break;
+        }
+      }
+    }
+    aborted = *c.aborted != 0;
+  }
+  return !ConsumerSyncOr(aborted);
+}
+
+__device__ inline int FirstUnit(int cta, int ctas, int base) {
+  return (cta - base + ctas) % ctas;
+}
+
+/// Source of one slot: unit `u` of `phase` (`which`: gate 0 / up 1).
+template <int kTile>
+__device__ inline const unsigned char* SlotSource(const DitLayer& layer,
+                                                  int phase, int u,
+                                                  int which) {
+  std::size_t tile;
+  const unsigned char* base;
+  switch (phase) {
+    case kQkv:
+      base = layer.qkv;
+      tile = static_cast<std::size_t>(QkvGroup(u)) * kUnitTiles;
+      break;
+    case kO:
+      base = layer.o;
+      tile = static_cast<std::size_t>(u / kOParts) * (kAttWidth / 32) +
+             (u % kOParts) * kUnitTiles;
+      break;
+    case kGu:
+      base = layer.gate_up;
+      tile = static_cast<std::size_t>(u + which * (kInter / 16)) * kUnitTiles;
+      break;
+    default:
+      base = layer.down;
+      tile = static_cast<std::size_t>(u / kDownParts) * (kInter / 32) +
+             (u % kDownParts) * kUnitTiles;
+      break;
+  }
+  return base + tile * kTile;
+}
+
+/// (output feature within the 16-row group, activation row) of reduced
+/// accumulator `t` for `ntiles` column tiles.
+__device__ inline void Decode(int t, int ntiles, int& feature, int& row) {
+  const int per_lane = ntiles * 4;
+  const int lane = t / per_lane;
+  const int jq = t % per_lane;
+  const int q = jq & 3;
+  feature = (lane >> 2) + 8 * (q >> 1);
+  row = 8 * (jq >> 2) + 2 * (lane & 3) + (q & 1);
+}
+
+/// Sum over warps [first, first + count) of the reduction buffer, in order.
+__device__ inline float Reduce(const float* red, int t, int stride,
+                              int first = 0, int count = kConsumerWarps) {
+  float s = red[first * stride + t];
+  for (int w = 1; w < count; ++w)
+    s += red[(first + w) * stride + t];
+  return s;
+}
+
+/// `kTiles` consecutive tiles from `kb0` of a 32-tile slot against the
+/// staged rows; the accumulators go to red[warp].
+template <int kFormat, int kNTiles, int kTiles>
+__device__ __forceinline__ void SlotProduct(const unsigned char* slot,
+                                            int kb0, const unsigned char* xs,
+                                            int warp, int lane, float* red) {
+  const int gid = lane >> 2;
+  const int tig = lane & 3;
+  float acc[kNTiles][4];
+#pragma unroll
+  for (int j = 0; j < kNTiles; ++j)
+    acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.0f;
+#pragma unroll
+  for (int t = 0; t < kTiles; ++t) {
+    const int kb = kb0 + t;
+    uint4 b[kNTiles];
+#pragma unroll
+    for (int j = 0; j < kNTiles; ++j)
+      b[j] = *reinterpret_cast<const uint4*>(xs + (8 * j + gid) * kXStride +
+                                             (kb * 32 + 8 * tig) * 2);
+    BlockProduct<kFormat, kNTiles, 0>(slot, kb, gid, tig, b, acc);
+  }
+  float* out = red + warp * (32 * kNTiles * 4) + lane * (kNTiles * 4);
+#pragma unroll
+  for (int j = 0; j < kNTiles; ++j)
+    *reinterpret_cast<float4*>(out + 4 * j) =
+        make_float4(acc[j][0], acc[j][1], acc[j][2], acc[j][3]);
+}
+
+/// bf16(w * x * rsqrt(mean(x^2) + eps)) of one 1024-wide row into a staged
+/// row (kernels/generator_kernels.hip:91-108); one warp.
+__device__ inline void StageNormRow(const float* src, const Bf16* weight,
+                                    float eps, unsigned char* dst, int lane) {
+  float4 v[8];
+  uint2 wb[8];
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    v[k] = __ldcg(reinterpret_cast<const float4*>(src) + lane + 32 * k);
+    wb[k] = __ldg(reinterpret_cast<const uint2*>(weight) + lane + 32 * k);
+  }
+  float sum = 0.0f;
+#pragma unroll
+  for (int k = 0; k < 8; ++k)
+    sum += v[k].x * v[k].x + v[k].y * v[k].y + v[k].z * v[k].z +
+           v[k].w * v[k].w;
+  sum = WarpAllSum(sum);
+  const float inverse = rsqrtf(sum / static_cast<float>(kHidden) + eps);
+#pragma unroll
+  for (int k = 0; k < 8; ++k) {
+    const int i = 4 * (lane + 32 * k);
+    const float o0 = v[k].x * inverse * Bf16ToFloat(static_cast<Bf16>(wb[k].x & 0xFFFFu));
+    const float o1 = v[k].y * inverse * Bf16ToFloat(static_cast<Bf16>(wb[k].x >> 16));
+    const float o2 = v[k].z * inverse * Bf16ToFloat(static_cast<Bf16>(wb[k].y & 0xFFFFu));
+    const float o3 = v[k].w * inverse * Bf16ToFloat(static_cast<Bf16>(wb[k].y >> 16));
+    *reinterpret_cast<uint2*>(dst + i * 2) = PackBf16x4(o0, o1, o2, o3);
+  }
+}
+
+/// The norm of all 22 rows into the staged rows with every load in flight
+/// at once: thread t takes float4 column t % 256 of rows t / 256, +2, ...
+/// `wb`: this thread's four norm weights (loaded early by the caller).
+/// Row sums: warp partials in `sums` [22][8], summed in order by 22
+/// threads, whose inverse norms go to sums[176 + row].
+__device__ void StageNorm(const float* hidden, uint2 wb, float eps,
+                          unsigned char* xs, float* sums, int tid, int lane) {
+  constexpr int kPerThread = kRows / 2;
+  const int column = tid & 255;
+  const int parity = tid >> 8;
+  float4 v[kPerThread];
+#pragma unroll
+  for (int k = 0; k < kPerThread; ++k)
+    v[k] = __ldcg(reinterpret_cast<const float4*>(
+                      hidden + static_cast<std::size_t>(parity + 2 * k) * kHidden) +
+                  column);
+  const int slot = column >> 5;
+#pragma unroll
+  for (int k = 0; k < kPerThread; ++k) {
+    const float s = WarpAllSum(v[k].x * v[k].x + v[k].y * v[k].y +
+                               v[k].z * v[k].z + v[k].w * v[k].w);
+    if (lane == 0)
+      sums[(parity + 2 * k) * 8 + slot] = s;
+  }
+  ConsumerSync();
+  if (tid < kRows) {
+    float total = sums[tid * 8];
+#pragma unroll
+    for (int w = 1; w < 8; ++w)
+      total += sums[tid * 8 + w];
+    sums[kRows * 8 + tid] = rsqrtf(total / static_cast<float>(kHidden) + eps);
+  }
+  ConsumerSync();
+  const float w0 = Bf16ToFloat(static_cast<Bf16>(wb.x & 0xFFFFu));
+  const float w1 = Bf16ToFloat(static_cast<Bf16>(wb.x >> 16));
+  const float w2 = Bf16ToFloat(static_cast<Bf16>(wb.y & 0xFFFFu));
+  const float w3 = Bf16ToFloat(static_cast<Bf16>(wb.y >> 16));
+#pragma unroll
+  for (int k = 0; k < kPerThread; ++k) {
+    const int row = parity + 2 * k;
+    const float inverse = sums[kRows * 8 + row];
+    *reinterpret_cast<uint2*>(xs + row * kXStride + column * 8) =
+        PackBf16x4(v[k].x * inverse * w0, v[k].y * inverse * w1,
+                   v[k].z * inverse * w2, v[k].w * inverse * w3);
+  }
+}
+
+/// One 1024-column chunk of bf16 rows [22][ld] into the staged rows, every
+/// load in flight at once.
+__device__ inline void StageBf16(const Bf16* src, int ld, int column0,
+                                 unsigned char* xs, int tid) {
+  constexpr int kPieces = kChunk / 8;  // 16-byte pieces per row
+  constexpr int kTotal = kRows * kPieces;
+  constexpr int kPerThread = (kTotal + kConsumers - 1) / kConsumers;
+  uint4 v[kPerThread];
+#pragma unroll
+  for (int k = 0; k < kPerThread; ++k) {
+    const int i = tid + k * kConsumers;
+    if (i < kTotal)
+      v[k] = __ldcg(reinterpret_cast<const uint4*>(
+          src + static_cast<std::size_t>(i / kPieces) * ld + column0 +
+          (i % kPieces) * 8));
+  }
+#pragma unroll
+  for (int k = 0; k < kPerThread; ++k) {
+    const int i = tid + k * kConsumers;
+    if (i < kTotal)
+      *reinterpret_cast<uint4*>(xs + (i / kPieces) * kXStride +
+                                (i % kPieces) * 16) = v[k];
+  }
+}
+
+/// hidden[:, group] += sum of the group's parts in part order (the
+/// folding CTA, once the other parts are published).
+__device__ void FoldGroup(const DitPatchParams& p, int group, int parts,
+                          const float* part, int tid) {
+  if (tid < kRows * 16) {
+    const std::size_t at =
+        static_cast<std::size_t>(tid >> 4) * kHidden + group * 16 + (tid & 15);
+    float v[kDownParts];
+#pragma unroll
+    for (int k = 0; k < kDownParts; ++k)
+      if (k < parts)
+        v[k] = __ldcg(part + static_cast<std::size_t>(k) * kRows * kHidden + at);
+    const float h = __ldcg(p.hidden + at);
+    float sum = v[0];
+#pragma unroll
+    for (int k = 1; k < kDownParts; ++k)
+      if (k < parts)
+        sum += v[k];
+    p.hidden[at] = h + sum;
+  }
+}
+
+/// Attention of one (query head, CFG sequence): RoPE on q and k at
+/// positions 0..10, keys/values rounded as the cache stores them, scale
+/// 1/sqrt(128), non-causal over the sequence's 11 rows, bf16 output
+/// (kernels/generator_kernels.hip:110-241). Keys and values are staged in
+/// `kv` ([2][11][128] fp32); warp w < 11 takes query row w.
+__device__ void AttentionTask(const DitPatchParams& p, int head, int sequence,
+                              float* kv, int tid, int warp, int lane) {
+  constexpr int kD = Shape::kHeadDim;
+  constexpr int kHalf = kD / 2;
+  const int kv_head = head / kHeadsPerKv;
+  const float* rows = p.qkv + static_cast<std::size_t>(sequence) * kSeq * kQkvWidth;
+  float* ks = kv;
+  float* vs = kv + kSeq * kD;
+  // Everything this thread reads, in flight at once: its warp's query row
+  // with its rotary factors, its share of key pairs (with factors) and of
+  // values.
+  const bool has_query = warp < kSeq;
+  float4 q = make_float4(0.f, 0.f, 0.f, 0.f);
+  float4 qc = q, qs = q;
+  if (has_query) {
+    q = __ldcg(reinterpret_cast<const float4*>(rows + warp * kQkvWidth + head * kD) + lane);
+    if (p.rope != nullptr) {
+      const int d = 4 * (lane & 15);
+      qc = *reinterpret_cast<const float4*>(p.rope + warp * kD + d);
+      qs = *reinterpret_cast<const float4*>(p.rope + warp * kD + kHalf + d);
+    }
+  }
+  constexpr int kPairs = kSeq * kHalf;   // 704
+  constexpr int kValues = kSeq * kD;     // 1408
+  constexpr int kPerThread = (kPairs + kValues + kConsumers - 1) / kConsumers;
+  float a[kPerThread], b[kPerThread], cs[kPerThread], sn[kPerThread];
+#pragma unroll
+  for (int k = 0; k < kPerThread; ++k) {
+    const int i = tid + k * kConsumers;
+    cs[k] = 1.0f;
+    sn[k] = 0.0f;
+    if (i < kPairs) {
+      const int row = i / kHalf;
+      const int d = i % kHalf;
+      const float* src = rows + row * kQkvWidth + kAttWidth + kv_head * kD + d;
+      a[k] = __ldcg(src);
+      b[k] = __ldcg(src + kHalf);
+      if (p.rope != nullptr) {
+        cs[k] = p.rope[row * kD + d];
+        sn[k] = p.rope[row * kD + kHalf + d];
+      }
+    } else if (i < kPairs + kValues) {
+      const int j = i - kPairs;
+      a[k] = __ldcg(rows + (j / kD) * kQkvWidth + kAttWidth +
+                    (Shape::kKvHeads + kv_head) * kD + j % kD);
+    }
+  }
+#pragma unroll
+  for (int k = 0; k < kPerThread; ++k) {
+    const int i = tid + k * kConsumers;
+    if (i < kPairs) {
+      const int row = i / kHalf;
+      const int d = i % kHalf;
+      float first = a[k];
+      float second = b[k];
+      if (p.rope != nullptr) {
+        first = a[k] * cs[k] - b[k] * sn[k];
+        second = b[k] * cs[k] + a[k] * sn[k];
+      }
+      if (p.bf16_kv) {
+        first = RoundBf16(first);
+        second = RoundBf16(second);
+      }
+      ks[row * kD + d] = first;
+      ks[row * kD + kHalf + d] = second;
+    } else if (i < kPairs + kValues) {
+      vs[i - kPairs] = p.bf16_kv ? RoundBf16(a[k]) : a[k];
+    }
+  }
+  // The query: lane l holds dims 4l..4l+3; its RoPE partner dims are in
+  // lane l ^ 16 (first = a c - b s below 64, second = b c + a s above).
+  if (has_query && p.rope != nullptr) {
+    const float4 partner = make_float4(__shfl_xor_sync(0xFFFFFFFFu, q.x, 16),
+                                       __shfl_xor_sync(0xFFFFFFFFu, q.y, 16),
+                                       __shfl_xor_sync(0xFFFFFFFFu, q.z, 16),
+                                       __shfl_xor_sync(0xFFFFFFFFu, q.w, 16));
+    if (lane < 16)
+      q = make_float4(q.x * qc.x - partner.x * qs.x, q.y * qc.y - partner.y * qs.y,
+                      q.z * qc.z - partner.z * qs.z, q.w * qc.w - partner.w * qs.w);
+    else
+      q = make_float4(q.x * qc.x + partner.x * qs.x, q.y * qc.y + partner.y * qs.y,
+                      q.z * qc.z + partner.z * qs.z, q.w * qc.w + partner.w * qs.w);
+  }
+  ConsumerSync();
+  if (has_query) {
+    q.x *= p.attention_scale;
+    q.y *= p.attention_scale;
+    q.z *= p.attention_scale;
+    q.w *= p.attention_scale;
+    float score[kSeq];
+    float maximum = -INFINITY;
+#pragma unroll
+    for (int key = 0; key < kSeq; ++key) {
+      const float4 k = reinterpret_cast<const float4*>(ks + key * kD)[lane];
+      score[key] = WarpAllSum(q.x * k.x + q.y * k.y + q.z * k.z + q.w * k.w);
+      maximum = fmaxf(maximum, score[key]);
+    }
+    float total = 0.0f;
+    float4 out = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int key = 0; key < kSeq; ++key) {
+      const float weight = expf(score[key] - maximum);
+      const float4 v = reinterpret_cast<const float4*>(vs + key * kD)[lane];
+      total += weight;
+      out.x += weight * v.x;
+      out.y += weight * v.y;
+      out.z += weight * v.z;
+      out.w += weight * v.w;
+    }
+    const float inverse = 1.0f / total;
+    *reinterpret_cast<uint2*>(
+        p.att + static_cast<std::size_t>(sequence * kSeq + warp) * kAttWidth +
+        head * kD + lane * 4) =
+        PackBf16x4(out.x * inverse, out.y * inverse, out.z * inverse,
+                   out.w * inverse);
+  }
+  ConsumerSync();
+}
+
+// ---------------------------------------------------------------- producer
+
+template <int kFormat>
+__device__ void Produce(const DitPatchParams& p, unsigned char* ring,
+                        std::uint64_t* full, std::uint64_t* empty,
+                        const Control& c) {
+  using R = RingShape<kFormat>;
+  const std::uint64_t policy = PolicyEvictFirst();
+  const int cta = static_cast<int>(blockIdx.x);
+  const int ctas = static_cast<int>(gridDim.x);
+  unsigned issued = 0;
+  bool stop = false;
+  auto issue = [&](const unsigned char* source) {
+    if (stop)
+      return;
+    const unsigned slot = issued % R::kSlots;
+    if (issued >= static_cast<unsigned>(R::kSlots) &&
+        !WaitSlot(&empty[slot], ((issued / R::kSlots) - 1) & 1u, c,
+                  kErrWeightWait)) {
+      stop = true;
+      return;
+    }
+    MbarArriveExpectTx(&full[slot], R::kSlotBytes);
+    BulkLoad(ring + slot * R::kSlotBytes, source, R::kSlotBytes, &full[slot],
+             policy);
+    ++issued;
+  };
+  auto dit_in = [&]() {
+    for (int s = 0; s < kDitInSlots; ++s)
+      issue(p.dit_in + static_cast<std::size_t>(s) * R::kSlotBytes);
+  };
+  if (cta == 0)
+    dit_in();
+  int base = 0;
+  for (int e = 0; e < p.evaluations && !stop; ++e) {
+    for (int l = 0; l < p.layers && !stop; ++l) {
+      const DitLayer layer = p.layer[l];
+      for (int phase = kQkv; phase <= kDown; ++phase) {
+        const int units = PhaseUnits(phase);
+        for (int u = FirstUnit(cta, ctas, base); u < units; u += ctas)
+          for (int which = 0; which < SlotsPerUnit(phase); ++which)
+            issue(SlotSource<R::kTile>(layer, phase, u, which));
+        base = (base + units) % ctas;
+      }
+    }
+    if (cta == 0) {
+      for (int g = 0; g < kDitOutSlots; ++g)
+        issue(p.dit_out + static_cast<std::size_t>(g) * R::kSlotBytes);
+      if (e + 1 < p.evaluations)
+        dit_in();
+    }
+  }
+  // Every copy this warp started lands before the CTA may exit.
+  const unsigned first =
+      issued > static_cast<unsigned>(R::kSlots) ? issued - R::kSlots : 0u;
+  for (unsigned k = first; k < issued; ++k)
+    (void)MbarWaitBounded(&full[k % R::kSlots], (k / R::kSlots) & 1u,
+                          c.error_word, kErrDrainWait);
+}
+
+// ---------------------------------------------------------------- publisher
+
+/// Lane 0 of the publisher warp: for each request of the consumers, in
+/// order, makes the CTA's writes visible device-wide (the consumers synced
+/// before queueing, so a fence here covers them) and adds to the counter
+/// with release semantics. The consumers never wait for a fence.
+__device__ void Publish(PubEntry* entries, std::uint64_t* pub_full,
+                        std::uint64_t* pub_empty, const Control& c) {
+  for (unsigned k = 0;; ++k) {
+    const unsigned slot = k % kPubSlots;
+    if (!WaitSlot(&pub_full[slot], (k / kPubSlots) & 1u, c, kErrPublishWait))
+      return;
+    const volatile PubEntry* e = entries + slot;
+    unsigned* counter = e->counter;
+    const unsigned value = e->value;
+    if (counter == nullptr)
+      return;
+    __threadfence();
+    RedRelease(counter, value);
+    MbarArrive(&pub_empty[slot]);
+  }
+}
+
+// ---------------------------------------------------------------- consumers
+
+template <int kFormat>
+__device__ void Consume(const DitPatchParams& p, unsigned char* smem,
+                        const Control& c) {
+  using R = RingShape<kFormat>;
+  unsigned char* ring = smem;
+  unsigned char* xs = smem + R::kXsOffset;
+  float* red = reinterpret_cast<float*>(smem + R::kRedOffset);
+  float* vel = reinterpret_cast<float*>(smem + R::kVelOffset);
+  float* sums = reinterpret_cast<float*>(smem + R::kSumsOffset);
+  PubEntry* entries = reinterpret_cast<PubEntry*>(smem + R::kPubOffset);
+  std::uint64_t* full = reinterpret_cast<std::uint64_t*>(smem + R::kBarOffset);
+  std::uint64_t* empty = full + R::kSlots;
+  std::uint64_t* pub_full = empty + R::kSlots;
+  std::uint64_t* pub_empty = pub_full + kPubSlots;
+  const int tid = static_cast<int>(threadIdx.x);
+  const int warp = tid >> 5;
+  const int lane = tid & 31;
+  const int gid = lane >> 2;
+  const int tig = lane & 3;
+  const int cta = static_cast<int>(blockIdx.x);
+  const int ctas = static_cast<int>(gridDim.x);
+  unsigned* sync = p.sync;
+  unsigned consumed = 0;
+  unsigned published = 0;
+
+  // Slot `consumed + ahead` of the ring, once it landed.
+  auto acquire = [&](unsigned ahead = 0) -> const unsigned char* {
+    const unsigned item = consumed + ahead;
+    const unsigned slot = item % R::kSlots;
+    if (*c.aborted == 0)
+      (void)WaitSlot(&full[slot], (item / R::kSlots) & 1u, c, kErrWeightWait);
+    return ring + slot * R::kSlotBytes;
+  };
+  // This warp is done with the next `count` slots.
+  auto release = [&](unsigned count = 1) {
+    __syncwarp();
+    if (lane == 0)
+      for (unsigned k = 0; k < count; ++k)
+        MbarArrive(&empty[(consumed + k) % R::kSlots]);
+    consumed += count;
+  };
+  // After a consumer barrier that follows the writes: queue a release-add
+  // of `value` to `counter` for the publisher warp (null ends its loop).
+  auto publish = [&](unsigned* counter, unsigned value) {
+    if (tid == 0) {
+      const unsigned slot = published % kPubSlots;
+      if (published >= static_cast<unsigned>(kPubSlots))
+        (void)WaitSlot(&pub_empty[slot], ((published / kPubSlots) - 1) & 1u, c,
+                       kErrPublishWait);
+      volatile PubEntry* entry = entries + slot;
+      entry->counter = counter;
+      entry->value = value;
+      MbarArrive(&pub_full[slot]);
+    }
+    ++published;
+  };
+  // One product unit's reduced values: `store(feature, row, value)` for
+  // rows < 22, then a consumer barrier.
+  auto reduce_store = [&](auto&& store) {
+    ConsumerSync();
+    if (tid < kRedFloats) {
+      int feature, row;
+      Decode(tid, 3, feature, row);
+      if (row < kRows)
+        store(feature, row, Reduce(red, tid, kRedFloats));
+    }
+    ConsumerSync();
+  };
+
+  // dit_in(bf16(x)) + bias into the x rows of both sequences, then the
+  // other rows [mu_a, mu_b, time, cond x4] (uncond: zero mu); publishes the
+  // assembled evaluation (kernels/generator_kernels.hip:320-340;
+  // generator.cpp:297-310).
+  auto boundary_in = [&](int e) {
+    for (int i = tid; i < 8 * Shape::kFeat; i += kConsumers) {
+      const int r = i / Shape::kFeat;
+      const int col = i % Shape::kFeat;
+      const float v = r < Shape::kPatch ? __ldcg(p.x + r * Shape::kFeat + col) : 0.0f;
+      *reinterpret_cast<Bf16*>(xs + r * kXStride + col * 2) = ToBf16(v);
+    }
+    ConsumerSync();
+    for (int s = 0; s < kDitInSlots; ++s) {
+      const unsigned char* slot = acquire();
+      float acc[1][4] = {{0.f, 0.f, 0.f, 0.f}};
+      // Warp w: row group 16 s + w, its two tiles (the whole 64 columns).
+#pragma unroll
+      for (int kb = 0; kb < Shape::kFeat / 32; ++kb) {
+        uint4 b[1];
+        b[0] = *reinterpret_cast<const uint4*>(xs + gid * kXStride +
+                                               (kb * 32 + 8 * tig) * 2);
+        BlockProduct<kFormat, 1, 0>(slot + warp * (Shape::kFeat / 32) * R::kTile,
+                                    kb, gid, tig, b, acc);
+      }
+      release();
+      const int group = s * kConsumerWarps + warp;
+#pragma unroll
+      for (int q = 0; q < 4; ++q) {
+        const int row = 2 * tig + (q & 1);
+        const int feature = group * 16 + gid + 8 * (q >> 1);
+        if (row < Shape::kPatch) {
+          const float v = acc[0][q] + Bf16ToFloat(p.dit_in_bias[feature]);
+          const int x_row = 3 + Shape::kPatch + row;
+          p.hidden[static_cast<std::size_t>(x_row) * kHidden + feature] = v;
+          p.hidden[static_cast<std::size_t>(kSeq + x_row) * kHidden + feature] = v;
+        }
+      }
+    }
+    const float* time = p.time_vectors[e];
+    constexpr int kFixed = 3 + Shape::kPatch;
+    for (int i = tid; i < 2 * kFixed * kHidden; i += kConsumers) {
+      const int sequence = i / (kFixed * kHidden);
+      const int row = (i / kHidden) % kFixed;
+      const int col = i % kHidden;
+      float v;
+      if (row < 2)
+        v = sequence == 0 ? p.mu[row * kHidden + col] : 0.0f;
+      else if (row == 2)
+        v = time[col];
+      else
+        v = p.cond_rows[(row - 3) * kHidden + col];
+      p.hidden[static_cast<std::size_t>(sequence * kSeq + row) * kHidden + col] = v;
+    }
+    ConsumerSync();
+    publish(sync + kSyncAssembled, 1u);
+  };
+
+  // Final norm of the 2P output rows, dit_out + bias, CFG-Zero* Euler
+  // update of x (kernels/generator_kernels.hip:342-360).
+  auto boundary_out = [&](int e) {
+    if (warp < 2 * Shape::kPatch) {
+      const int k = warp;
+      const int row = (k < Shape::kPatch ? 0 : kSeq - Shape::kPatch) + 3 +
+                      Shape::kPatch + k;
+      StageNormRow(p.hidden + static_cast<std::size_t>(row) * kHidden,
+                   p.final_norm, p.eps, xs + k * kXStride, lane);
+    }
+    ConsumerSync();
+    for (int g = 0; g < kDitOutSlots; ++g) {
+      SlotProduct<kFormat, 1, 2>(acquire(), 2 * warp, xs, warp, lane, red);
+      release();
+      ConsumerSync();
+      if (tid < 32 * 4) {
+        int feature, row;
+        Decode(tid, 1, feature, row);
+        feature += g * 16;
+        vel[row * Shape::kFeat + feature] =
+            Reduce(red, tid, 32 * 4) + Bf16ToFloat(p.dit_out_bias[feature]);
+      }
+      ConsumerSync();
+    }
+    constexpr int kCount = Shape::kPatch * Shape::kFeat;  // 256
+    float cv = 0.f, uv = 0.f;
+    if (tid < kCount) {
+      cv = vel[tid];
+      uv = vel[kCount + tid];
+      const float dot = WarpAllSum(cv * uv);
+      const float norm = WarpAllSum(uv * uv);
+      if (lane == 0) {
+        sums[warp] = dot;
+        sums[16 + warp] = norm;
+      }
+    }
+    ConsumerSync();
+    if (tid < kCount) {
+      float dot = sums[0];
+      float norm = sums[16];
+      for (int w = 1; w < kCount / 32; ++w) {
+        dot += sums[w];
+        norm += sums[16 + w];
+      }
+      const float s = dot / (norm + 1e-8f);
+      const float guided = uv * s + p.cfg * (cv - uv * s);
+      p.x[tid] -= p.dts[e] * guided;
+    }
+    ConsumerSync();
+  };
+
+  // Split products: the CTA holding a group's last part folds the group
+  // after all of its own units of the phase (so no CTA waits on another
+  // inside a phase), once the other parts are published.
+  int pending[4];
+  int pending_count = 0;
+  auto fold_pending = [&](int parts, const float* part, unsigned target) {
+    for (int k = 0; k < pending_count; ++k) {
+      if (!WaitCount(c, sync + kSyncParts + pending[k], target))
+        return false;
+      FoldGroup(p, pending[k], parts, part, tid);
+      ConsumerSync();
+      publish(sync + kSyncHidden, 1u);
+    }
+    pending_count = 0;
+    return true;
+  };
+
+  if (cta == 0)
+    boundary_in(0);
+  int base = 0;
+  const int column = tid & 255;
+  for (int e = 0; e < p.evaluations; ++e) {
+    for (int l = 0; l < p.layers; ++l) {
+      const DitLayer layer = p.layer[l];
+      const unsigned index = static_cast<unsigned>(e * p.layers + l);
+
+      // QKV: norm(hidden) x W_qkv -> qkv (fp32), then this CTA's attention
+      // task when it has one.
+      {
+        const int units = PhaseUnits(kQkv);
+        const int mine = FirstUnit(cta, ctas, base);
+        if (mine < units) {
+          const uint2 wb = __ldg(reinterpret_cast<const uint2*>(layer.input_norm) + column);
+          const bool ready =
+              l == 0 ? WaitCount(c, sync + kSyncAssembled, e + 1)
+                     : WaitCount(c, sync + kSyncHidden, 2 * kGroups * index);
+          if (!ready)
+            return;
+          StageNorm(p.hidden, wb, p.eps, xs, sums, tid, lane);
+          ConsumerSync();
+        }
+        for (int u = mine; u < units; u += ctas) {
+          const int group = QkvGroup(u);
+          SlotProduct<kFormat, 3, 2>(acquire(), 2 * warp, xs, warp, lane, red);
+          release();
+          reduce_store([&](int feature, int row, float v) {
+            p.qkv[static_cast<std::size_t>(row) * kQkvWidth + group * 16 + feature] = v;
+          });
+          const int q_groups = kAttWidth / 16;
+          publish(group < q_groups
+                      ? sync + kSyncQ + group / kHeadGroups
+                      : sync + kSyncKv + ((group - q_groups) % (kKvGroups / 2)) / kHeadGroups,
+                  1u);
+        }
+        // Attention: 32 (head, sequence) tasks on CTAs holding one unit.
+        const int task = mine - (units > ctas ? units - ctas : 0);
+        if (mine < units && task >= 0 && task < kAttentionTasks) {
+          const int head = task >> 1;
+          const int sequence = task & 1;
+          if (!WaitCount(c, sync + kSyncKv + head / kHeadsPerKv,
+                         2 * kHeadGroups * (index + 1)) ||
+              !WaitCount(c, sync + kSyncQ + head, kHeadGroups * (index + 1)))
+            return;
+          AttentionTask(p, head, sequence, red, tid, warp, lane);
+          publish(sync + kSyncAtt + head / kHeadsPerChunk, 1u);
+        }
+        base = (base + units) % ctas;
+      }
+
+      // O: att x W_o over two column chunks, folded into hidden.
+      {
+        const int units = PhaseUnits(kO);
+        int staged = -1;
+        for (int u = FirstUnit(cta, ctas, base); u < units; u += ctas) {
+          const int group = u / kOParts;
+          const int part = u % kOParts;
+          if (part != staged) {
+            if (!WaitCount(c, sync + kSyncAtt + part,
+                           2 * kHeadsPerChunk * (index + 1)))
+              return;
+            StageBf16(p.att, kAttWidth, part * kChunk, xs, tid);
+            ConsumerSync();
+            staged = part;
+          }
+          SlotProduct<kFormat, 3, 2>(acquire(), 2 * warp, xs, warp, lane, red);
+          release();
+          float* out = p.o_parts + static_cast<std::size_t>(part) * kRows * kHidden;
+          reduce_store([&](int feature, int row, float v) {
+            out[static_cast<std::size_t>(row) * kHidden + group * 16 + feature] = v;
+          });
+          if (part == kOParts - 1)
+            pending[pending_count++] = group;
+          else
+            publish(sync + kSyncParts + group, 1u);
+        }
+        if (!fold_pending(kOParts, p.o_parts,
+                          kPartsPerLayer * index + (kOParts - 1)))
+          return;
+        base = (base + units) % ctas;
+      }
+
+      // gate/up: norm(hidden) x W_gate, W_up -> bf16(silu(g) * u). Warps
+      // 0-7 take the gate slot, 8-15 the up slot, four tiles each.
+      {
+        const int units = PhaseUnits(kGu);
+        const int mine = FirstUnit(cta, ctas, base);
+        if (mine < units) {
+          const uint2 wb = __ldg(reinterpret_cast<const uint2*>(layer.post_norm) + column);
+          if (!WaitCount(c, sync + kSyncHidden, kGroups * (2 * index + 1)))
+            return;
+          StageNorm(p.hidden, wb, p.eps, xs, sums, tid, lane);
+          ConsumerSync();
+        }
+        for (int u = mine; u < units; u += ctas) {
+          const int half = warp >> 3;
+          SlotProduct<kFormat, 3, 4>(acquire(half), 4 * (warp & 7), xs, warp,
+                                     lane, red);
+          release(2);
+          ConsumerSync();
+          if (tid < kRedFloats) {
+            int feature, row;
+            Decode(tid, 3, feature, row);
+            if (row < kRows) {
+              const float g = Reduce(red, tid, kRedFloats, 0, 8);
+              const float up = Reduce(red, tid, kRedFloats, 8, 8);
+              p.act[static_cast<std::size_t>(row) * kInter + u * 16 + feature] =
+                  ToBf16(g / (1.0f + expf(-g)) * up);
+            }
+          }
+          ConsumerSync();
+          publish(sync + kSyncAct + u / kGuPerChunk, 1u);
+        }
+        base = (base + units) % ctas;
+      }
+
+      // down: act x W_down over four column chunks, folded into hidden.
+      {
+        const int units = PhaseUnits(kDown);
+        int staged = -1;
+        for (int u = FirstUnit(cta, ctas, base); u < units; u += ctas) {
+          const int group = u / kDownParts;
+          const int part = u % kDownParts;
+          if (part != staged) {
+            if (!WaitCount(c, sync + kSyncAct + part, kGuPerChunk * (index + 1)))
+              return;
+            StageBf16(p.act, kInter, part * kChunk, xs, tid);
+            ConsumerSync();
+            staged = part;
+          }
+          SlotProduct<kFormat, 3, 2>(acquire(), 2 * warp, xs, warp, lane, red);
+          release();
+          float* out =
+              p.down_parts + static_cast<std::size_t>(part) * kRows * kHidden;
+          reduce_store([&](int feature, int row, float v) {
+            out[static_cast<std::size_t>(row) * kHidden + group * 16 + feature] = v;
+          });
+          if (part == kDownParts - 1)
+            pending[pending_count++] = group;
+          else
+            publish(sync + kSyncParts + group, 1u);
+        }
+        if (!fold_pending(kDownParts, p.down_parts, kPartsPerLayer * (index + 1)))
+          return;
+        base = (base + units) % ctas;
+      }
+    }
+    if (cta == 0) {
+      if (!WaitCount(c, sync + kSyncHidden,
+                     2 * kGroups * static_cast<unsigned>((e + 1) * p.layers)))
+        return;
+      boundary_out(e);
+      if (e + 1 < p.evaluations)
+        boundary_in(e + 1);
+    }
+  }
+  publish(nullptr, 0u);
+}
+
+template <int kFormat>
+__global__ void __launch_bounds__(kThreads, 1)
+    DitPatchKernel(const DitPatchParams p, unsigned* error_word) {
+  using R = RingShape<kFormat>;
+  extern __shared__ __align__(128) unsigned char smem[];
+  std::uint64_t* full = reinterpret_cast<std::uint64_t*>(smem + R::kBarOffset);
+  std::uint64_t* empty = full + R::kSlots;
+  std::uint64_t* pub_full = empty + R::kSlots;
+  std::uint64_t* pub_empty = pub_full + kPubSlots;
+  volatile int* aborted = reinterpret_cast<volatile int*>(smem + R::kFlagOffset);
+  const Control c{p.sync, error_word, aborted};
+  if (threadIdx.x == 0) {
+    for (int s = 0; s < R::kSlots; ++s) {
+      MbarInit(&full[s], 1);
+      MbarInit(&empty[s], kConsumerWarps);
+    }
+    for (int s = 0; s < kPubSlots; ++s) {
+      MbarInit(&pub_full[s], 1);
+      MbarInit(&pub_empty[s], 1);
+    }
+    *aborted = 0;
+    FenceMbarInit();
+  }
+  // Staged rows start at zero; rows 22 and 23 stay zero for the whole patch.
+  uint4* xs = reinterpret_cast<uint4*>(smem + R::kXsOffset);
+  for (int i = threadIdx.x; i < kXRows * kXStride / 16; i += kThreads)
+    xs[i] = make_uint4(0u, 0u, 0u, 0u);
+  __syncthreads();
+  if (threadIdx.x >= kConsumers) {
+    if (threadIdx.x == kConsumers)
+      Produce<kFormat>(p, smem, full, empty, c);
+    else if (threadIdx.x == kConsumers + 32)
+      Publish(reinterpret_cast<PubEntry*>(smem + R::kPubOffset), pub_full,
+              pub_empty, c);
+    return;
+  }
+  Consume<kFormat>(p, smem, c);
+}
+
+constexpr std::size_t Align256(std::size_t n) { return (n + 255) & ~std::size_t{255}; }
+
+struct DeviceState {
+  int sms = 0;
+  bool configured[2] = {false, false};
+};
+
+}  // namespace
+
+std::size_t DitWorkBytes() {
+  return Align256(kRows * kHidden * 4) + Align256(kRows * kQkvWidth * 4) +
+         Align256(kRows * kAttWidth * 2) + Align256(kRows * kInter * 2) +
+         Align256(std::size_t{kOParts} * kRows * kHidden * 4) +
+         Align256(std::size_t{kDownParts} * kRows * kHidden * 4) +
+         Align256(kDitSyncWords * 4);
+}
+
+void DitWorkLayout(void* base, DitPatchParams& params) {
+  auto* at = static_cast<unsigned char*>(base);
+  auto take = [&](std::size_t bytes) {
+    unsigned char* p = at;
+    at += Align256(bytes);
+    return p;
+  };
+  params.hidden = reinterpret_cast<float*>(take(kRows * kHidden * 4));
+  params.qkv = reinterpret_cast<float*>(take(kRows * kQkvWidth * 4));
+  params.att = reinterpret_cast<std::uint16_t*>(take(kRows * kAttWidth * 2));
+  params.act = reinterpret_cast<std::uint16_t*>(take(kRows * kInter * 2));
+  params.o_parts = reinterpret_cast<float*>(take(std::size_t{kOParts} * kRows * kHidden * 4));
+  params.down_parts =
+      reinterpret_cast<float*>(take(std::size_t{kDownParts} * kRows * kHidden * 4));
+  params.sync = reinterpret_cast<unsigned*>(take(kDitSyncWords * 4));
+}
+
+int LaunchDitPatch(const DitPatchParams& p, cudaStream_t stream) {
+  const bool q8 = p.format == WeightFormat::kQ8Tiles;
+  if (!q8 && p.format != WeightFormat::kBf16Tiles)
+    return Fail(kInvalid, "persistent DiT: weights must be Q8 or bf16 tiles");
+  if (p.layers < 1 || p.evaluations < 1 || p.layer == nullptr ||
+      p.final_norm == nullptr || p.dit_in == nullptr ||
+      p.dit_in_bias == nullptr || p.dit_out == nullptr ||
+      p.dit_out_bias == nullptr || p.mu == nullptr || p.cond_rows == nullptr ||
+      p.time_vectors == nullptr || p.dts == nullptr || p.x == nullptr ||
+      p.hidden == nullptr || p.qkv == nullptr || p.att == nullptr ||
+      p.act == nullptr || p.o_parts == nullptr || p.down_parts == nullptr ||
+      p.sync == nullptr)
+    return Fail(kInvalid, "persistent DiT: missing argument");
+  int device = 0;
+  if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= 64)
+    return Fail(kCudaError, "persistent DiT: no current device");
+  static std::mutex mutex;
+  static DeviceState states[64];
+  void (*kernel)(const DitPatchParams, unsigned*) =
+      q8 ? DitPatchKernel<static_cast<int>(WeightFormat::kQ8Tiles)>
+         : DitPatchKernel<static_cast<int>(WeightFormat::kBf16Tiles)>;
+  const int smem =
+      q8 ? RingShape<static_cast<int>(WeightFormat::kQ8Tiles)>::kSmemBytes
+         : RingShape<static_cast<int>(WeightFormat::kBf16Tiles)>::kSmemBytes;
+  int sms = 0;
+  {
+    std::lock_guard<std::mutex> lock(mutex);
+    DeviceState& state = states[device];
+    if (state.sms == 0) {
+      int cooperative = 0;
+      if (cudaDeviceGetAttribute(&cooperative, cudaDevAttrCooperativeLaunch,
+                                 device) != cudaSuccess ||
+          cooperative == 0)
+        return Fail(kUnsupported, "persistent DiT: no cooperative launch");
+      if (cudaDeviceGetAttribute(&state.sms, cudaDevAttrMultiProcessorCount,
+                                 device) != cudaSuccess)
+        return Fail(kCudaError, "persistent DiT: SM count");
+    }
+    if (!state.configured[q8 ? 0 : 1]) {
+      if (cudaFuncSetAttribute(kernel,
+                               cudaFuncAttributeMaxDynamicSharedMemorySize,
+                               smem) != cudaSuccess)
+        return Fail(kCudaError, "persistent DiT: shared memory attribute");
+      int blocks = 0;
+      if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, kernel,
+                                                        kThreads, smem) !=
+              cudaSuccess ||
+          blocks < 1)
+        return Fail(kUnsupported, "persistent DiT: one CTA per SM does not fit");
+      state.configured[q8 ? 0 : 1] = true;
+    }
+    sms = state.sms;
+  }
+  if (sms < 64)
+    return Fail(kUnsupported, "persistent DiT: needs at least 64 SMs");
+  unsigned* error_word = DeviceErrorWord();
+  if (error_word == nullptr)
+    return Fail(kCudaError, "persistent DiT: device error word");
+  if (cudaMemsetAsync(p.sync, 0, kDitSyncWords * sizeof(unsigned), stream) !=
+      cudaSuccess)
+    return Fail(kCudaError, "persistent DiT: memset");
+  cudaLaunchConfig_t config = {};
+  config.gridDim = dim3(static_cast<unsigned>(sms));
+  config.blockDim = dim3(kThreads);
+  config.dynamicSmemBytes = static_cast<std::size_t>(smem);
+  config.stream = stream;
+  cudaLaunchAttribute attribute[1];
+  attribute[0].id = cudaLaunchAttributeCooperative;
+  attribute[0].val.cooperative = 1;
+  config.attrs = attribute;
+  config.numAttrs = 1;
+  return FromCuda(cudaLaunchKernelEx(&config, kernel, p, error_word),
+                  "persistent DiT launch");
+}
+
+}  // namespace vx

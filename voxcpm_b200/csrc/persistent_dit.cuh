@@ -1,0 +1,99 @@
+// The persistent DiT patch: the whole Euler/CFG loop of one patch (every
+// DiT evaluation of the local DiT, its in/out projections and the CFG-Zero*
+// Euler updates) as ONE cooperative kernel with one CTA per SM. It replaces
+// the per-kernel sequence of Generator::EvaluateDit / GuidedEuler
+// (generator.cpp:297-324, :457-463) and ForwardStack (transformer.cpp:55-100)
+// for VoxCPM2's DiT shape.
+//
+// Work split: every product is cut into units of one 16-row weight group
+// times 1024 reduction columns (32 tiles, one contiguous run of the tile
+// layout). A producer warp per CTA streams its units for the whole patch
+// into a ring of unit-sized shared-memory slots with 1-D TMA bulk copies,
+// running ahead across layers; sixteen consumer warps take two tiles each
+// and reduce in a fixed order. There is no grid barrier: each phase (QKV,
+// O, gate/up, down, the patch boundary) waits only on monotone ready
+// counters of the data it reads, published with release semantics by the
+// CTAs that wrote it. Attention for a head runs on the CTA that completes
+// the head's last q/k/v group; split reductions of O and down are folded
+// into the residual stream by the CTA that completes a group's last part
+// (an atomic ticket), summing the parts in a fixed order, so results are
+// deterministic.
+#pragma once
+
+#include <cuda_runtime.h>
+
+#include <cstddef>
+#include <cstdint>
+
+#include "products.cuh"
+
+namespace vx {
+
+/// The DiT shape the persistent kernel is built for (VoxCPM2's local DiT).
+struct DitShape {
+  static constexpr int kHidden = 1024;
+  static constexpr int kIntermediate = 4096;
+  static constexpr int kHeads = 16;
+  static constexpr int kKvHeads = 2;
+  static constexpr int kHeadDim = 128;
+  static constexpr int kPatch = 4;
+  static constexpr int kFeat = 64;
+  static constexpr int kSequence = 3 + 2 * kPatch;  // mu, mu, time, cond, x
+  static constexpr int kRows = 2 * kSequence;       // CFG pair
+};
+
+/// One DiT layer's device weights (Q8 tiles or bf16 tiles) and norms.
+struct DitLayer {
+  const unsigned char* qkv = nullptr;      // [q 2048 | k 256 | v 256][1024]
+  const unsigned char* o = nullptr;        // [1024][2048]
+  const unsigned char* gate_up = nullptr;  // [gate 4096 | up 4096][1024]
+  const unsigned char* down = nullptr;     // [1024][4096]
+  const std::uint16_t* input_norm = nullptr;
+  const std::uint16_t* post_norm = nullptr;
+};
+
+/// Words of the per-launch synchronization block (zeroed by the launcher).
+constexpr int kDitSyncWords = 256;
+
+/// Everything the persistent patch reads and writes.
+struct DitPatchParams {
+  WeightFormat format = WeightFormat::kQ8Tiles;  // kQ8Tiles or kBf16Tiles
+  int layers = 0;
+  int evaluations = 0;      // Euler steps that evaluate the DiT
+  int bf16_kv = 0;          // round keys and values to bf16 (bf16 KV cache)
+  float eps = 1e-5f;
+  float cfg = 2.0f;
+  float attention_scale = 0.0f;
+  const DitLayer* layer = nullptr;  // device array [layers]
+  const std::uint16_t* final_norm = nullptr;
+  const unsigned char* dit_in = nullptr;  // tiles [1024][64]
+  const std::uint16_t* dit_in_bias = nullptr;
+  const unsigned char* dit_out = nullptr;  // tiles [64][1024]
+  const std::uint16_t* dit_out_bias = nullptr;
+  const float* rope = nullptr;       // [position][cos 64 | sin 64] or null
+  const float* mu = nullptr;         // [2][1024]
+  const float* cond_rows = nullptr;  // [4][1024]
+  const float* const* time_vectors = nullptr;  // device [evaluations] -> [1024]
+  const float* dts = nullptr;                  // device [evaluations]
+  float* x = nullptr;                // [4][64]: noise in, latent out
+  // Work buffers (device).
+  float* hidden = nullptr;      // [22][1024] residual stream
+  float* qkv = nullptr;         // [22][2560]
+  std::uint16_t* att = nullptr; // [22][2048]
+  std::uint16_t* act = nullptr; // [22][4096]
+  float* o_parts = nullptr;     // [2][22][1024]
+  float* down_parts = nullptr;  // [4][22][1024]
+  unsigned* sync = nullptr;     // [kDitSyncWords]
+};
+
+/// Device bytes of the work buffers above (hidden .. down_parts), laid out
+/// in that order with 256-byte alignment by DitWorkLayout.
+std::size_t DitWorkBytes();
+/// Points the work-buffer fields of `params` into `base` (DitWorkBytes()).
+void DitWorkLayout(void* base, DitPatchParams& params);
+
+/// Enqueues the persistent patch on `stream`: a memset of the sync words,
+/// then the cooperative kernel (one CTA per SM). Returns a Status.
+int LaunchDitPatch(const DitPatchParams& params, cudaStream_t stream);
+
+}  // namespace vx

@@ -25,6 +25,8 @@ enum DeviceError : unsigned {
   kErrWeightWait = 1u << 0,
   kErrActivationWait = 1u << 1,
   kErrDrainWait = 1u << 2,
+  kErrBarrierWait = 1u << 3,
+  kErrPublishWait = 1u << 4,
 };
 
 /// The device word the library's kernels or their error bits into; defined

@@ -106,6 +106,14 @@ class Generator:
     def SetGraphs(self, enabled: bool) -> None:
         check(self._lib.vx_generator_set_graphs(self._handle, int(enabled)))
 
+    def SetPersistent(self, enabled: bool) -> None:
+        """The DiT patch as one persistent kernel (VoxCPM2's DiT shape) or as
+        the per-kernel sequence."""
+        check(self._lib.vx_generator_set_persistent(self._handle, int(enabled)))
+
+    def persistent(self) -> bool:
+        return bool(self._lib.vx_generator_persistent(self._handle))
+
     def position(self) -> int:
         return self._lib.vx_generator_position(self._handle)
 
