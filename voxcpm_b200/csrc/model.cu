@@ -733,7 +733,7 @@ void Generator::SetupPersistent() {
       c.feat_dim != Shape::kFeat || d.layers < 1)
     return;
   const WeightFormat format = w_.dit.layers[0].qkv.format;
-  if (format != WeightFormat::kQ8Tiles && format != WeightFormat::kBf16Tiles)
+  if (!DitPatchSupported(format))
     return;
   std::vector<DitLayer> layers(d.layers);
   for (int i = 0; i < d.layers; ++i) {

@@ -34,7 +34,7 @@ constexpr int kInter = Shape::kIntermediate;
 constexpr int kConsumerWarps = 16;
 constexpr int kConsumers = kConsumerWarps * 32;
 constexpr int kThreads = kConsumers + 64;  // + producer and publisher warps
-constexpr int kXRows = 24;                 // three MMA column tiles of 8
+constexpr int kXRows = 8;                  // staged rows of the patch boundary
 constexpr int kXStride = kChunk * 2 + 64;  // bytes per staged row (bank skew)
 constexpr int kRedFloats = 32 * 12;        // one warp's accumulators, 3 tiles
 constexpr int kOParts = kAttWidth / kChunk;   // 2
@@ -57,8 +57,8 @@ constexpr std::uint32_t kSuspendNs = 100000u;
 // count of its k and v groups; per 1024-column chunk of the attention
 // output the count of (head, sequence) tasks done; the count of residual
 // groups folded; the count of assembled evaluations; per chunk of the
-// SwiGLU activation the count of gate/up units done; per residual group
-// the count of split parts stored (all but the folding one).
+// SwiGLU activation the count of gate/up units done. One thread per CTA
+// polls a counter, so the polling load on L2 stays small.
 constexpr int kSyncAbort = 0;
 constexpr int kSyncQ = 32;          // [16]
 constexpr int kSyncKv = 48;         // [2]
@@ -66,19 +66,23 @@ constexpr int kSyncAtt = 64;        // [2]
 constexpr int kSyncHidden = 96;
 constexpr int kSyncAssembled = 97;
 constexpr int kSyncAct = 128;       // [4]
-constexpr int kSyncParts = 160;     // [64]
-constexpr unsigned kPartsPerLayer = (kOParts - 1) + (kDownParts - 1);
+
+// O and down groups belong to a CTA pair (a cluster of two): rank r takes
+// O part r and down parts r and r + 2; rank 1 sends its reduced parts to
+// rank 0 through distributed shared memory, and rank 0 folds.
+constexpr int kPairParts = kDownParts / 2;
 
 static_assert(kHidden == kChunk, "QKV and gate/up reduce over one chunk");
-static_assert(kRows <= kXRows, "activation rows fit three column tiles");
-static_assert(kSyncParts + kGroups <= kDitSyncWords, "part counters");
+static_assert(2 * Shape::kPatch <= kXRows, "the boundary stages the output rows");
+static_assert(kSyncAct + kDownParts <= kDitSyncWords, "act counters");
+static_assert(kOParts == 2 && kDownParts == 4, "pair split");
 static_assert(kSyncQ + Shape::kHeads <= kSyncKv, "head counters");
 static_assert(Shape::kHeadDim == 128, "attention lanes hold 4 of 128");
-static_assert(kSeq <= kConsumerWarps, "one warp per query row");
+static_assert(kConsumerWarps * 64 == kChunk, "a warp owns 64 columns");
 static_assert(2 * Shape::kPatch <= 8, "DiT outputs fit one column tile");
 static_assert(kDitInSlots * kUnitTiles == (kHidden / 16) * (Shape::kFeat / 32),
               "dit_in tiles fill whole slots");
-static_assert(kRows == 22 && kHidden == 1024, "staging layouts");
+static_assert(kRows == 22 && kHidden == 1024, "fragment layouts");
 
 enum Phase : int { kQkv = 0, kO = 1, kGu = 2, kDown = 3 };
 
@@ -105,18 +109,23 @@ struct RingShape {
   static constexpr int kSlotBytes = kTile * kUnitTiles;
   static constexpr int kXsOffset = kSlots * kSlotBytes;
   static constexpr int kRedOffset = kXsOffset + kXRows * kXStride;
+  // red[2][16 warps][384]: gate/up units reduce both slots at once.
   static constexpr int kVelOffset =
-      kRedOffset + kConsumerWarps * kRedFloats * 4;
+      kRedOffset + 2 * kConsumerWarps * kRedFloats * 4;
   static constexpr int kSumsOffset =
       kVelOffset + 2 * Shape::kPatch * Shape::kFeat * 4;
-  static constexpr int kPubOffset = kSumsOffset + 256 * 4;
-  static constexpr int kBarOffset = kPubOffset + kPubSlots * 16;
-  static constexpr int kFlagOffset = kBarOffset + 2 * (kSlots + kPubSlots) * 8;
+  // sums: [22][16] per-warp row partials, [22] inverse norms, scratch.
+  static constexpr int kPubOffset = kSumsOffset + 512 * 4;
+  static constexpr int kRecvOffset = kPubOffset + kPubSlots * 16;
+  static constexpr int kBarOffset = kRecvOffset + kPairParts * kRedFloats * 4;
+  // full[kSlots], empty[kSlots], pub_full[8], pub_empty[8], recv, done
+  static constexpr int kFlagOffset =
+      kBarOffset + (2 * (kSlots + kPubSlots) + 2) * 8;
   static constexpr int kSmemBytes = kFlagOffset + 16;
   static_assert(kSlotBytes % 128 == 0 && kXsOffset % 128 == 0, "alignment");
   static_assert(kSmemBytes <= 227 * 1024, "shared memory");
-  // Attention keys and values of one (head, sequence) use the reduction
-  // buffer.
+  // Attention keys and values of one (head, sequence) use the first
+  // reduction buffer.
   static_assert(2 * kSeq * Shape::kHeadDim * 4 <= kConsumerWarps * kRedFloats * 4,
                 "attention staging");
 };
@@ -149,6 +158,31 @@ __device__ inline bool ConsumerSyncOr(bool value) {
 __device__ inline void MbarArrive(std::uint64_t* bar) {
   asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(SmemAddr(bar))
                : "memory");
+}
+
+/// Arrives on the mbarrier at shared::cluster address `addr` (a peer's),
+/// releasing this thread's prior writes at cluster scope.
+__device__ inline void MbarArriveCluster(std::uint32_t addr) {
+  asm volatile("mbarrier.arrive.release.cluster.shared::cluster.b64 _, [%0];" ::"r"(addr)
+               : "memory");
+}
+
+/// try_wait with acquire at cluster scope (arrivals from the peer CTA).
+__device__ inline bool MbarTryWaitCluster(std::uint64_t* bar, unsigned parity,
+                                          std::uint32_t suspend_ns) {
+  std::uint32_t done;
+  asm volatile(
+      "{\n.reg .pred p;\n"
+      "mbarrier.try_wait.parity.acquire.cluster.shared::cta.b64 p, [%1], %2, %3;\n"
+      "selp.u32 %0, 1, 0, p;\n}\n"
+      : "=r"(done)
+      : "r"(SmemAddr(bar)), "r"(parity), "r"(suspend_ns)
+      : "memory");
+  return done != 0;
+}
+
+__device__ inline void StoreSharedCluster(std::uint32_t addr, float v) {
+  asm volatile("st.shared::cluster.f32 [%0], %1;" ::"r"(addr), "f"(v) : "memory");
 }
 
 __device__ inline unsigned LoadAcquire(const unsigned* p) {
@@ -235,6 +269,29 @@ __device__ bool WaitSlot(std::uint64_t* bar, unsigned parity,
       return false;
     }
   }
+}
+
+/// Consumer-wide wait for phase `parity` of the local mbarrier `bar` that
+/// the peer CTA arrives on. Returns false, uniformly, once aborted.
+__device__ bool WaitPeer(std::uint64_t* bar, unsigned parity, const Control& c) {
+  bool aborted = false;
+  if (threadIdx.x == 0) {
+    if (*c.aborted == 0 && !MbarTryWaitCluster(bar, parity, kSuspendNs)) {
+      const std::uint64_t start = GlobalTimerNs();
+      while (!MbarTryWaitCluster(bar, parity, kSuspendNs)) {
+        if (*c.aborted != 0 || LoadRelaxed(c.sync + kSyncAbort) != 0) {
+          *c.aborted = 1;
+          break;
+        }
+        if (GlobalTimerNs() - start > kWaitLimitNs) {
+          Abort(c, kErrPeerWait);
+          break;
+        }
+      }
+    }
+    aborted = *c.aborted != 0;
+  }
+  return !ConsumerSyncOr(aborted);
 }
 
 /// Consumer-wide wait until `*counter >= target` (thread 0 polls with
@@ -374,98 +431,121 @@ __device__ inline void StageNormRow(const float* src, const Bf16* weight,
   }
 }
 
-/// The norm of all 22 rows into the staged rows with every load in flight
-/// at once: thread t takes float4 column t % 256 of rows t / 256, +2, ...
-/// `wb`: this thread's four norm weights (loaded early by the caller).
-/// Row sums: warp partials in `sums` [22][8], summed in order by 22
-/// threads, whose inverse norms go to sums[176 + row].
-__device__ void StageNorm(const float* hidden, uint2 wb, float eps,
-                          unsigned char* xs, float* sums, int tid, int lane) {
-  constexpr int kPerThread = kRows / 2;
-  const int column = tid & 255;
-  const int parity = tid >> 8;
-  float4 v[kPerThread];
+/// B fragments of this warp's two tiles (reduction columns column0 + 64w ..
+/// + 63) for three column tiles of 8 rows: lane (gid, tig) holds, for tile
+/// t and column tile j, the 8 columns 32t + 8tig .. of row 8j + gid.
+using Fragments = uint4[2][3];
+
+/// Fragments from bf16 rows [22][ld] (rows 22, 23 zero).
+__device__ inline void BfFragments(const Bf16* src, int ld, int column0,
+                                   int warp, int lane, Fragments& b) {
+  const int gid = lane >> 2;
+  const int tig = lane & 3;
 #pragma unroll
-  for (int k = 0; k < kPerThread; ++k)
-    v[k] = __ldcg(reinterpret_cast<const float4*>(
-                      hidden + static_cast<std::size_t>(parity + 2 * k) * kHidden) +
-                  column);
-  const int slot = column >> 5;
+  for (int j = 0; j < 3; ++j) {
+    const int row = 8 * j + gid;
 #pragma unroll
-  for (int k = 0; k < kPerThread; ++k) {
-    const float s = WarpAllSum(v[k].x * v[k].x + v[k].y * v[k].y +
-                               v[k].z * v[k].z + v[k].w * v[k].w);
-    if (lane == 0)
-      sums[(parity + 2 * k) * 8 + slot] = s;
+    for (int t = 0; t < 2; ++t)
+      b[t][j] = row < kRows
+                    ? __ldcg(reinterpret_cast<const uint4*>(
+                          src + static_cast<std::size_t>(row) * ld + column0 +
+                          64 * warp + 32 * t + 8 * tig))
+                    : make_uint4(0u, 0u, 0u, 0u);
+  }
+}
+
+/// Fragments of bf16(w * x * rsqrt(mean(x^2) + eps)) of the fp32 rows
+/// `hidden` [22][1024] (kernels/generator_kernels.hip:91-108): each warp
+/// loads its 64 columns, row sums go through `sums` ([22][16] warp partials
+/// summed in warp order, then [22] inverse norms), one CTA barrier each.
+/// `weight`: this lane's 16 norm weights (two runs of 8 columns).
+__device__ void NormFragments(const float* hidden, const uint4 (&weight)[2],
+                              float eps, float* sums, int tid, int warp,
+                              int lane, Fragments& b) {
+  const int gid = lane >> 2;
+  const int tig = lane & 3;
+  float4 v[3][2][2];
+#pragma unroll
+  for (int j = 0; j < 3; ++j) {
+    const int row = 8 * j + gid;
+#pragma unroll
+    for (int t = 0; t < 2; ++t) {
+      const float* src = hidden + static_cast<std::size_t>(row) * kHidden +
+                         64 * warp + 32 * t + 8 * tig;
+      v[j][t][0] = row < kRows ? __ldcg(reinterpret_cast<const float4*>(src))
+                               : make_float4(0.f, 0.f, 0.f, 0.f);
+      v[j][t][1] = row < kRows ? __ldcg(reinterpret_cast<const float4*>(src) + 1)
+                               : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 3; ++j) {
+    float s = 0.0f;
+#pragma unroll
+    for (int t = 0; t < 2; ++t)
+#pragma unroll
+      for (int h = 0; h < 2; ++h)
+        s += v[j][t][h].x * v[j][t][h].x + v[j][t][h].y * v[j][t][h].y +
+             v[j][t][h].z * v[j][t][h].z + v[j][t][h].w * v[j][t][h].w;
+    s += __shfl_xor_sync(0xFFFFFFFFu, s, 1);
+    s += __shfl_xor_sync(0xFFFFFFFFu, s, 2);
+    const int row = 8 * j + gid;
+    if (tig == 0 && row < kRows)
+      sums[row * kConsumerWarps + warp] = s;
   }
   ConsumerSync();
+  float* inverse = sums + kRows * kConsumerWarps;
   if (tid < kRows) {
-    float total = sums[tid * 8];
+    float total = sums[tid * kConsumerWarps];
 #pragma unroll
-    for (int w = 1; w < 8; ++w)
-      total += sums[tid * 8 + w];
-    sums[kRows * 8 + tid] = rsqrtf(total / static_cast<float>(kHidden) + eps);
+    for (int w = 1; w < kConsumerWarps; ++w)
+      total += sums[tid * kConsumerWarps + w];
+    inverse[tid] = rsqrtf(total / static_cast<float>(kHidden) + eps);
   }
   ConsumerSync();
-  const float w0 = Bf16ToFloat(static_cast<Bf16>(wb.x & 0xFFFFu));
-  const float w1 = Bf16ToFloat(static_cast<Bf16>(wb.x >> 16));
-  const float w2 = Bf16ToFloat(static_cast<Bf16>(wb.y & 0xFFFFu));
-  const float w3 = Bf16ToFloat(static_cast<Bf16>(wb.y >> 16));
 #pragma unroll
-  for (int k = 0; k < kPerThread; ++k) {
-    const int row = parity + 2 * k;
-    const float inverse = sums[kRows * 8 + row];
-    *reinterpret_cast<uint2*>(xs + row * kXStride + column * 8) =
-        PackBf16x4(v[k].x * inverse * w0, v[k].y * inverse * w1,
-                   v[k].z * inverse * w2, v[k].w * inverse * w3);
+  for (int j = 0; j < 3; ++j) {
+    const int row = 8 * j + gid;
+    const float r = row < kRows ? inverse[row] : 0.0f;
+#pragma unroll
+    for (int t = 0; t < 2; ++t) {
+      const uint4 w = weight[t];
+      const float4 lo = v[j][t][0];
+      const float4 hi = v[j][t][1];
+      b[t][j].x = PackBf16x2(lo.x * r * Bf16ToFloat(static_cast<Bf16>(w.x & 0xFFFFu)),
+                             lo.y * r * Bf16ToFloat(static_cast<Bf16>(w.x >> 16)));
+      b[t][j].y = PackBf16x2(lo.z * r * Bf16ToFloat(static_cast<Bf16>(w.y & 0xFFFFu)),
+                             lo.w * r * Bf16ToFloat(static_cast<Bf16>(w.y >> 16)));
+      b[t][j].z = PackBf16x2(hi.x * r * Bf16ToFloat(static_cast<Bf16>(w.z & 0xFFFFu)),
+                             hi.y * r * Bf16ToFloat(static_cast<Bf16>(w.z >> 16)));
+      b[t][j].w = PackBf16x2(hi.z * r * Bf16ToFloat(static_cast<Bf16>(w.w & 0xFFFFu)),
+                             hi.w * r * Bf16ToFloat(static_cast<Bf16>(w.w >> 16)));
+    }
   }
 }
 
-/// One 1024-column chunk of bf16 rows [22][ld] into the staged rows, every
-/// load in flight at once.
-__device__ inline void StageBf16(const Bf16* src, int ld, int column0,
-                                 unsigned char* xs, int tid) {
-  constexpr int kPieces = kChunk / 8;  // 16-byte pieces per row
-  constexpr int kTotal = kRows * kPieces;
-  constexpr int kPerThread = (kTotal + kConsumers - 1) / kConsumers;
-  uint4 v[kPerThread];
+/// This warp's two tiles (2w, 2w + 1) of a 32-tile slot against its
+/// fragments; the accumulators go to red[warp].
+template <int kFormat>
+__device__ __forceinline__ void FragProduct(const unsigned char* slot,
+                                            const Fragments& b, int warp,
+                                            int lane, float* red) {
+  const int gid = lane >> 2;
+  const int tig = lane & 3;
+  float acc[3][4];
 #pragma unroll
-  for (int k = 0; k < kPerThread; ++k) {
-    const int i = tid + k * kConsumers;
-    if (i < kTotal)
-      v[k] = __ldcg(reinterpret_cast<const uint4*>(
-          src + static_cast<std::size_t>(i / kPieces) * ld + column0 +
-          (i % kPieces) * 8));
+  for (int j = 0; j < 3; ++j)
+    acc[j][0] = acc[j][1] = acc[j][2] = acc[j][3] = 0.0f;
+#pragma unroll
+  for (int t = 0; t < 2; ++t) {
+    const uint4 bt[3] = {b[t][0], b[t][1], b[t][2]};
+    BlockProduct<kFormat, 3, 0>(slot, 2 * warp + t, gid, tig, bt, acc);
   }
+  float* out = red + warp * kRedFloats + lane * 12;
 #pragma unroll
-  for (int k = 0; k < kPerThread; ++k) {
-    const int i = tid + k * kConsumers;
-    if (i < kTotal)
-      *reinterpret_cast<uint4*>(xs + (i / kPieces) * kXStride +
-                                (i % kPieces) * 16) = v[k];
-  }
-}
-
-/// hidden[:, group] += sum of the group's parts in part order (the
-/// folding CTA, once the other parts are published).
-__device__ void FoldGroup(const DitPatchParams& p, int group, int parts,
-                          const float* part, int tid) {
-  if (tid < kRows * 16) {
-    const std::size_t at =
-        static_cast<std::size_t>(tid >> 4) * kHidden + group * 16 + (tid & 15);
-    float v[kDownParts];
-#pragma unroll
-    for (int k = 0; k < kDownParts; ++k)
-      if (k < parts)
-        v[k] = __ldcg(part + static_cast<std::size_t>(k) * kRows * kHidden + at);
-    const float h = __ldcg(p.hidden + at);
-    float sum = v[0];
-#pragma unroll
-    for (int k = 1; k < kDownParts; ++k)
-      if (k < parts)
-        sum += v[k];
-    p.hidden[at] = h + sum;
-  }
+  for (int j = 0; j < 3; ++j)
+    *reinterpret_cast<float4*>(out + 4 * j) =
+        make_float4(acc[j][0], acc[j][1], acc[j][2], acc[j][3]);
 }
 
 /// Attention of one (query head, CFG sequence): RoPE on q and k at
@@ -625,11 +705,28 @@ __device__ void Produce(const DitPatchParams& p, unsigned char* ring,
   };
   if (cta == 0)
     dit_in();
+  const int pair = cta >> 1;
+  const int rank = cta & 1;
+  const int pairs = ctas >> 1;
   int base = 0;
+  int pair_base = 0;
   for (int e = 0; e < p.evaluations && !stop; ++e) {
     for (int l = 0; l < p.layers && !stop; ++l) {
       const DitLayer layer = p.layer[l];
       for (int phase = kQkv; phase <= kDown; ++phase) {
+        if (phase == kO || phase == kDown) {
+          for (int g = FirstUnit(pair, pairs, pair_base); g < kGroups; g += pairs) {
+            if (phase == kO) {
+              issue(SlotSource<R::kTile>(layer, kO, g * kOParts + rank, 0));
+            } else {
+              for (int k = 0; k < kPairParts; ++k)
+                issue(SlotSource<R::kTile>(layer, kDown,
+                                           g * kDownParts + rank + 2 * k, 0));
+            }
+          }
+          pair_base = (pair_base + kGroups) % pairs;
+          continue;
+        }
         const int units = PhaseUnits(phase);
         for (int u = FirstUnit(cta, ctas, base); u < units; u += ctas)
           for (int which = 0; which < SlotsPerUnit(phase); ++which)
@@ -655,9 +752,9 @@ __device__ void Produce(const DitPatchParams& p, unsigned char* ring,
 // ---------------------------------------------------------------- publisher
 
 /// Lane 0 of the publisher warp: for each request of the consumers, in
-/// order, makes the CTA's writes visible device-wide (the consumers synced
-/// before queueing, so a fence here covers them) and adds to the counter
-/// with release semantics. The consumers never wait for a fence.
+/// order, adds to the counter with release semantics (device scope), which
+/// makes the CTA's writes before the request visible to whoever acquires the
+/// counter. The consumers never wait for the release.
 __device__ void Publish(PubEntry* entries, std::uint64_t* pub_full,
                         std::uint64_t* pub_empty, const Control& c) {
   for (unsigned k = 0;; ++k) {
@@ -669,7 +766,9 @@ __device__ void Publish(PubEntry* entries, std::uint64_t* pub_full,
     const unsigned value = e->value;
     if (counter == nullptr)
       return;
-    __threadfence();
+    // The consumers' writes precede their barrier and the queue entry's
+    // release-arrive; this release-add is ordered after them, so whoever
+    // acquires the counter sees them.
     RedRelease(counter, value);
     MbarArrive(&pub_empty[slot]);
   }
@@ -691,6 +790,8 @@ __device__ void Consume(const DitPatchParams& p, unsigned char* smem,
   std::uint64_t* empty = full + R::kSlots;
   std::uint64_t* pub_full = empty + R::kSlots;
   std::uint64_t* pub_empty = pub_full + kPubSlots;
+  std::uint64_t* recv_bar = pub_empty + kPubSlots;
+  float* recv = reinterpret_cast<float*>(smem + R::kRecvOffset);
   const int tid = static_cast<int>(threadIdx.x);
   const int warp = tid >> 5;
   const int lane = tid & 31;
@@ -698,9 +799,16 @@ __device__ void Consume(const DitPatchParams& p, unsigned char* smem,
   const int tig = lane & 3;
   const int cta = static_cast<int>(blockIdx.x);
   const int ctas = static_cast<int>(gridDim.x);
+  const int pair = cta >> 1;
+  const int rank = cta & 1;
+  const int pairs = ctas >> 1;
   unsigned* sync = p.sync;
   unsigned consumed = 0;
   unsigned published = 0;
+  unsigned folds = 0;  // pair folds this CTA took part in
+  // The peer's receive buffer and barrier (rank 1 sends to rank 0).
+  const std::uint32_t peer_recv = MapShared(recv, rank ^ 1);
+  const std::uint32_t peer_recv_bar = MapShared(recv_bar, rank ^ 1);
 
   // Slot `consumed + ahead` of the ring, once it landed.
   auto acquire = [&](unsigned ahead = 0) -> const unsigned char* {
@@ -854,27 +962,66 @@ __device__ void Consume(const DitPatchParams& p, unsigned char* smem,
     ConsumerSync();
   };
 
-  // Split products: the CTA holding a group's last part folds the group
-  // after all of its own units of the phase (so no CTA waits on another
-  // inside a phase), once the other parts are published.
-  int pending[4];
-  int pending_count = 0;
-  auto fold_pending = [&](int parts, const float* part, unsigned target) {
-    for (int k = 0; k < pending_count; ++k) {
-      if (!WaitCount(c, sync + kSyncParts + pending[k], target))
-        return false;
-      FoldGroup(p, pending[k], parts, part, tid);
-      ConsumerSync();
-      publish(sync + kSyncHidden, 1u);
+  // A pair's split product: rank 1 stores its reduced part `k` into rank
+  // 0's receive buffer; rank 0 keeps its own in `keep`.
+  auto reduce_part = [&](int k, float& keep) {
+    ConsumerSync();
+    if (tid < kRedFloats) {
+      const float v = Reduce(red, tid, kRedFloats);
+      if (rank == 1)
+        StoreSharedCluster(peer_recv + static_cast<std::uint32_t>(
+                                           (k * kRedFloats + tid) * 4), v);
+      else
+        keep = v;
     }
-    pending_count = 0;
+    ConsumerSync();
+  };
+  // Rank 1: signal rank 0. Rank 0: wait, then hidden[:, group] += the
+  // parts in part order (kept ones at even parts, received ones at odd),
+  // and publish one folded group.
+  auto fold_pair = [&](int group, int parts, const float* keep) {
+    if (rank == 1) {
+      if (tid == 0)
+        MbarArriveCluster(peer_recv_bar);
+      ++folds;
+      return true;
+    }
+    if (!WaitPeer(recv_bar, folds & 1u, c))
+      return false;
+    ++folds;
+    if (tid < kRedFloats) {
+      int feature, row;
+      Decode(tid, 3, feature, row);
+      if (row < kRows) {
+        float sum = keep[0] + recv[tid];  // parts 0 and 1
+        if (parts == kDownParts) {
+          sum += keep[1];                  // part 2
+          sum += recv[kRedFloats + tid];   // part 3
+        }
+        const std::size_t at =
+            static_cast<std::size_t>(row) * kHidden + group * 16 + feature;
+        p.hidden[at] = __ldcg(p.hidden + at) + sum;
+      }
+    }
+    ConsumerSync();
+    publish(sync + kSyncHidden, 1u);
     return true;
   };
 
   if (cta == 0)
     boundary_in(0);
   int base = 0;
-  const int column = tid & 255;
+  int pair_base = 0;
+  float* red2 = red + kConsumerWarps * kRedFloats;  // second reduction buffer
+  // Norm weights of this lane's 16 columns (two runs of 8).
+  auto norm_weights = [&](const Bf16* weight, uint4 (&w)[2]) {
+#pragma unroll
+    for (int t = 0; t < 2; ++t)
+      w[t] = __ldg(reinterpret_cast<const uint4*>(weight + 64 * warp + 32 * t +
+                                                  8 * tig));
+  };
+  auto check = [&]() { return !ConsumerSyncOr(*c.aborted != 0); };
+  Fragments frag;
   for (int e = 0; e < p.evaluations; ++e) {
     for (int l = 0; l < p.layers; ++l) {
       const DitLayer layer = p.layer[l];
@@ -886,18 +1033,18 @@ __device__ void Consume(const DitPatchParams& p, unsigned char* smem,
         const int units = PhaseUnits(kQkv);
         const int mine = FirstUnit(cta, ctas, base);
         if (mine < units) {
-          const uint2 wb = __ldg(reinterpret_cast<const uint2*>(layer.input_norm) + column);
+          uint4 w[2];
+          norm_weights(layer.input_norm, w);
           const bool ready =
               l == 0 ? WaitCount(c, sync + kSyncAssembled, e + 1)
                      : WaitCount(c, sync + kSyncHidden, 2 * kGroups * index);
           if (!ready)
             return;
-          StageNorm(p.hidden, wb, p.eps, xs, sums, tid, lane);
-          ConsumerSync();
+          NormFragments(p.hidden, w, p.eps, sums, tid, warp, lane, frag);
         }
         for (int u = mine; u < units; u += ctas) {
           const int group = QkvGroup(u);
-          SlotProduct<kFormat, 3, 2>(acquire(), 2 * warp, xs, warp, lane, red);
+          FragProduct<kFormat>(acquire(), frag, warp, lane, red);
           release();
           reduce_store([&](int feature, int row, float v) {
             p.qkv[static_cast<std::size_t>(row) * kQkvWidth + group * 16 + feature] = v;
@@ -908,6 +1055,8 @@ __device__ void Consume(const DitPatchParams& p, unsigned char* smem,
                       : sync + kSyncKv + ((group - q_groups) % (kKvGroups / 2)) / kHeadGroups,
                   1u);
         }
+        if (!check())
+          return;
         // Attention: 32 (head, sequence) tasks on CTAs holding one unit.
         const int task = mine - (units > ctas ? units - ctas : 0);
         if (mine < units && task >= 0 && task < kAttentionTasks) {
@@ -923,62 +1072,48 @@ __device__ void Consume(const DitPatchParams& p, unsigned char* smem,
         base = (base + units) % ctas;
       }
 
-      // O: att x W_o over two column chunks, folded into hidden.
+      // O: att x W_o, the two column chunks on the two CTAs of a pair,
+      // folded into hidden by rank 0. Warp w's columns belong to head
+      // 8 rank + w / 2.
       {
-        const int units = PhaseUnits(kO);
-        int staged = -1;
-        for (int u = FirstUnit(cta, ctas, base); u < units; u += ctas) {
-          const int group = u / kOParts;
-          const int part = u % kOParts;
-          if (part != staged) {
-            if (!WaitCount(c, sync + kSyncAtt + part,
-                           2 * kHeadsPerChunk * (index + 1)))
-              return;
-            StageBf16(p.att, kAttWidth, part * kChunk, xs, tid);
-            ConsumerSync();
-            staged = part;
-          }
-          SlotProduct<kFormat, 3, 2>(acquire(), 2 * warp, xs, warp, lane, red);
+        for (int g = FirstUnit(pair, pairs, pair_base); g < kGroups; g += pairs) {
+          if (!WaitCount(c, sync + kSyncAtt + rank,
+                         2 * kHeadsPerChunk * (index + 1)))
+            return;
+          BfFragments(p.att, kAttWidth, rank * kChunk, warp, lane, frag);
+          FragProduct<kFormat>(acquire(), frag, warp, lane, red);
           release();
-          float* out = p.o_parts + static_cast<std::size_t>(part) * kRows * kHidden;
-          reduce_store([&](int feature, int row, float v) {
-            out[static_cast<std::size_t>(row) * kHidden + group * 16 + feature] = v;
-          });
-          if (part == kOParts - 1)
-            pending[pending_count++] = group;
-          else
-            publish(sync + kSyncParts + group, 1u);
+          float keep[kPairParts] = {0.f, 0.f};
+          reduce_part(0, keep[0]);
+          if (!check() || !fold_pair(g, kOParts, keep))
+            return;
         }
-        if (!fold_pending(kOParts, p.o_parts,
-                          kPartsPerLayer * index + (kOParts - 1)))
-          return;
-        base = (base + units) % ctas;
+        pair_base = (pair_base + kGroups) % pairs;
       }
 
-      // gate/up: norm(hidden) x W_gate, W_up -> bf16(silu(g) * u). Warps
-      // 0-7 take the gate slot, 8-15 the up slot, four tiles each.
+      // gate/up: norm(hidden) x W_gate, W_up -> bf16(silu(g) * u); all
+      // warps take both slots.
       {
         const int units = PhaseUnits(kGu);
         const int mine = FirstUnit(cta, ctas, base);
         if (mine < units) {
-          const uint2 wb = __ldg(reinterpret_cast<const uint2*>(layer.post_norm) + column);
+          uint4 w[2];
+          norm_weights(layer.post_norm, w);
           if (!WaitCount(c, sync + kSyncHidden, kGroups * (2 * index + 1)))
             return;
-          StageNorm(p.hidden, wb, p.eps, xs, sums, tid, lane);
-          ConsumerSync();
+          NormFragments(p.hidden, w, p.eps, sums, tid, warp, lane, frag);
         }
         for (int u = mine; u < units; u += ctas) {
-          const int half = warp >> 3;
-          SlotProduct<kFormat, 3, 4>(acquire(half), 4 * (warp & 7), xs, warp,
-                                     lane, red);
+          FragProduct<kFormat>(acquire(0), frag, warp, lane, red);
+          FragProduct<kFormat>(acquire(1), frag, warp, lane, red2);
           release(2);
           ConsumerSync();
           if (tid < kRedFloats) {
             int feature, row;
             Decode(tid, 3, feature, row);
             if (row < kRows) {
-              const float g = Reduce(red, tid, kRedFloats, 0, 8);
-              const float up = Reduce(red, tid, kRedFloats, 8, 8);
+              const float g = Reduce(red, tid, kRedFloats);
+              const float up = Reduce(red2, tid, kRedFloats);
               p.act[static_cast<std::size_t>(row) * kInter + u * 16 + feature] =
                   ToBf16(g / (1.0f + expf(-g)) * up);
             }
@@ -986,41 +1121,34 @@ __device__ void Consume(const DitPatchParams& p, unsigned char* smem,
           ConsumerSync();
           publish(sync + kSyncAct + u / kGuPerChunk, 1u);
         }
-        base = (base + units) % ctas;
-      }
-
-      // down: act x W_down over four column chunks, folded into hidden.
-      {
-        const int units = PhaseUnits(kDown);
-        int staged = -1;
-        for (int u = FirstUnit(cta, ctas, base); u < units; u += ctas) {
-          const int group = u / kDownParts;
-          const int part = u % kDownParts;
-          if (part != staged) {
-            if (!WaitCount(c, sync + kSyncAct + part, kGuPerChunk * (index + 1)))
-              return;
-            StageBf16(p.act, kInter, part * kChunk, xs, tid);
-            ConsumerSync();
-            staged = part;
-          }
-          SlotProduct<kFormat, 3, 2>(acquire(), 2 * warp, xs, warp, lane, red);
-          release();
-          float* out =
-              p.down_parts + static_cast<std::size_t>(part) * kRows * kHidden;
-          reduce_store([&](int feature, int row, float v) {
-            out[static_cast<std::size_t>(row) * kHidden + group * 16 + feature] = v;
-          });
-          if (part == kDownParts - 1)
-            pending[pending_count++] = group;
-          else
-            publish(sync + kSyncParts + group, 1u);
-        }
-        if (!fold_pending(kDownParts, p.down_parts, kPartsPerLayer * (index + 1)))
+        if (!check())
           return;
         base = (base + units) % ctas;
       }
+
+      // down: act x W_down over four column chunks, parts r and r + 2 on
+      // rank r of a pair, folded into hidden by rank 0. Warp w's columns of
+      // chunk c come from gate/up units 64 c + 4 w .. + 3.
+      {
+        for (int g = FirstUnit(pair, pairs, pair_base); g < kGroups; g += pairs) {
+          float keep[kPairParts] = {0.f, 0.f};
+          for (int k = 0; k < kPairParts; ++k) {
+            const int part = rank + 2 * k;
+            if (!WaitCount(c, sync + kSyncAct + part, kGuPerChunk * (index + 1)))
+              return;
+            BfFragments(p.act, kInter, part * kChunk, warp, lane, frag);
+            FragProduct<kFormat>(acquire(), frag, warp, lane, red);
+            release();
+            reduce_part(k, keep[k]);
+          }
+          if (!check() || !fold_pair(g, kDownParts, keep))
+            return;
+        }
+        pair_base = (pair_base + kGroups) % pairs;
+      }
     }
     if (cta == 0) {
+      // Every residual group folded by the last layer's down.
       if (!WaitCount(c, sync + kSyncHidden,
                      2 * kGroups * static_cast<unsigned>((e + 1) * p.layers)))
         return;
@@ -1052,6 +1180,8 @@ __global__ void __launch_bounds__(kThreads, 1)
       MbarInit(&pub_full[s], 1);
       MbarInit(&pub_empty[s], 1);
     }
+    MbarInit(pub_empty + kPubSlots, 1);      // recv: one arrival per fold
+    MbarInit(pub_empty + kPubSlots + 1, 1);  // done: the peer's teardown
     *aborted = 0;
     FenceMbarInit();
   }
@@ -1059,7 +1189,8 @@ __global__ void __launch_bounds__(kThreads, 1)
   uint4* xs = reinterpret_cast<uint4*>(smem + R::kXsOffset);
   for (int i = threadIdx.x; i < kXRows * kXStride / 16; i += kThreads)
     xs[i] = make_uint4(0u, 0u, 0u, 0u);
-  __syncthreads();
+  // Both CTAs of the pair see each other's initialized barriers.
+  ClusterSync();
   if (threadIdx.x >= kConsumers) {
     if (threadIdx.x == kConsumers)
       Produce<kFormat>(p, smem, full, empty, c);
@@ -1069,13 +1200,27 @@ __global__ void __launch_bounds__(kThreads, 1)
     return;
   }
   Consume<kFormat>(p, smem, c);
+  // Teardown: neither CTA of the pair exits while its peer may still write
+  // into its shared memory. Each signals the other, then waits (bounded)
+  // for the peer's signal.
+  if (threadIdx.x == 0) {
+    std::uint64_t* done = pub_empty + kPubSlots + 1;
+    MbarArriveCluster(MapShared(done, (blockIdx.x & 1) ^ 1));
+    const std::uint64_t start = GlobalTimerNs();
+    while (!MbarTryWaitCluster(done, 0, kSuspendNs))
+      if (GlobalTimerNs() - start > kWaitLimitNs) {
+        atomicOr(error_word, kErrPeerWait);
+        break;
+      }
+  }
 }
 
 constexpr std::size_t Align256(std::size_t n) { return (n + 255) & ~std::size_t{255}; }
 
 struct DeviceState {
-  int sms = 0;
+  bool probed = false;
   bool configured[2] = {false, false};
+  int ctas[2] = {0, 0};  // CTAs of the launch (two per co-resident cluster)
 };
 
 }  // namespace
@@ -1083,8 +1228,6 @@ struct DeviceState {
 std::size_t DitWorkBytes() {
   return Align256(kRows * kHidden * 4) + Align256(kRows * kQkvWidth * 4) +
          Align256(kRows * kAttWidth * 2) + Align256(kRows * kInter * 2) +
-         Align256(std::size_t{kOParts} * kRows * kHidden * 4) +
-         Align256(std::size_t{kDownParts} * kRows * kHidden * 4) +
          Align256(kDitSyncWords * 4);
 }
 
@@ -1099,10 +1242,81 @@ void DitWorkLayout(void* base, DitPatchParams& params) {
   params.qkv = reinterpret_cast<float*>(take(kRows * kQkvWidth * 4));
   params.att = reinterpret_cast<std::uint16_t*>(take(kRows * kAttWidth * 2));
   params.act = reinterpret_cast<std::uint16_t*>(take(kRows * kInter * 2));
-  params.o_parts = reinterpret_cast<float*>(take(std::size_t{kOParts} * kRows * kHidden * 4));
-  params.down_parts =
-      reinterpret_cast<float*>(take(std::size_t{kDownParts} * kRows * kHidden * 4));
   params.sync = reinterpret_cast<unsigned*>(take(kDitSyncWords * 4));
+}
+
+namespace {
+
+void (*DitKernel(bool q8))(const DitPatchParams, unsigned*) {
+  return q8 ? DitPatchKernel<static_cast<int>(WeightFormat::kQ8Tiles)>
+            : DitPatchKernel<static_cast<int>(WeightFormat::kBf16Tiles)>;
+}
+
+int DitSmem(bool q8) {
+  return q8 ? RingShape<static_cast<int>(WeightFormat::kQ8Tiles)>::kSmemBytes
+            : RingShape<static_cast<int>(WeightFormat::kBf16Tiles)>::kSmemBytes;
+}
+
+cudaLaunchConfig_t DitConfig(bool q8, unsigned ctas, cudaStream_t stream,
+                             cudaLaunchAttribute (&attribute)[2]) {
+  cudaLaunchConfig_t config = {};
+  config.gridDim = dim3(ctas);
+  config.blockDim = dim3(kThreads);
+  config.dynamicSmemBytes = static_cast<std::size_t>(DitSmem(q8));
+  config.stream = stream;
+  attribute[0].id = cudaLaunchAttributeClusterDimension;
+  attribute[0].val.clusterDim.x = 2;
+  attribute[0].val.clusterDim.y = 1;
+  attribute[0].val.clusterDim.z = 1;
+  attribute[1].id = cudaLaunchAttributeCooperative;
+  attribute[1].val.cooperative = 1;
+  config.attrs = attribute;
+  config.numAttrs = 2;
+  return config;
+}
+
+/// CTAs of a launch on the current device (0 when it cannot run: no
+/// cooperative launch, or fewer co-resident CTA pairs than residual groups).
+int DitCtas(bool q8) {
+  int device = 0;
+  if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= 64)
+    return 0;
+  static std::mutex mutex;
+  static DeviceState states[64];
+  std::lock_guard<std::mutex> lock(mutex);
+  DeviceState& state = states[device];
+  const int which = q8 ? 0 : 1;
+  if (!state.configured[which]) {
+    state.configured[which] = true;
+    int cooperative = 0;
+    if (cudaDeviceGetAttribute(&cooperative, cudaDevAttrCooperativeLaunch,
+                               device) != cudaSuccess ||
+        cooperative == 0)
+      return 0;
+    if (cudaFuncSetAttribute(DitKernel(q8),
+                             cudaFuncAttributeMaxDynamicSharedMemorySize,
+                             DitSmem(q8)) != cudaSuccess)
+      return 0;
+    cudaLaunchAttribute attribute[2];
+    cudaLaunchConfig_t config = DitConfig(q8, 2, nullptr, attribute);
+    config.numAttrs = 1;  // the occupancy query takes the cluster shape only
+    int clusters = 0;
+    if (cudaOccupancyMaxActiveClusters(&clusters, DitKernel(q8), &config) !=
+        cudaSuccess)
+      return 0;
+    state.ctas[which] = clusters >= kGroups ? 2 * clusters : 0;
+  }
+  return state.ctas[which];
+}
+
+}  // namespace
+
+bool DitPatchSupported(WeightFormat format) {
+  if (format != WeightFormat::kQ8Tiles && format != WeightFormat::kBf16Tiles)
+    return false;
+  const bool ok = DitCtas(format == WeightFormat::kQ8Tiles) > 0;
+  (void)cudaGetLastError();  // a failed query leaves no sticky error behind
+  return ok;
 }
 
 int LaunchDitPatch(const DitPatchParams& p, cudaStream_t stream) {
@@ -1115,68 +1329,23 @@ int LaunchDitPatch(const DitPatchParams& p, cudaStream_t stream) {
       p.dit_out_bias == nullptr || p.mu == nullptr || p.cond_rows == nullptr ||
       p.time_vectors == nullptr || p.dts == nullptr || p.x == nullptr ||
       p.hidden == nullptr || p.qkv == nullptr || p.att == nullptr ||
-      p.act == nullptr || p.o_parts == nullptr || p.down_parts == nullptr ||
-      p.sync == nullptr)
+      p.act == nullptr || p.sync == nullptr)
     return Fail(kInvalid, "persistent DiT: missing argument");
-  int device = 0;
-  if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= 64)
-    return Fail(kCudaError, "persistent DiT: no current device");
-  static std::mutex mutex;
-  static DeviceState states[64];
-  void (*kernel)(const DitPatchParams, unsigned*) =
-      q8 ? DitPatchKernel<static_cast<int>(WeightFormat::kQ8Tiles)>
-         : DitPatchKernel<static_cast<int>(WeightFormat::kBf16Tiles)>;
-  const int smem =
-      q8 ? RingShape<static_cast<int>(WeightFormat::kQ8Tiles)>::kSmemBytes
-         : RingShape<static_cast<int>(WeightFormat::kBf16Tiles)>::kSmemBytes;
-  int sms = 0;
-  {
-    std::lock_guard<std::mutex> lock(mutex);
-    DeviceState& state = states[device];
-    if (state.sms == 0) {
-      int cooperative = 0;
-      if (cudaDeviceGetAttribute(&cooperative, cudaDevAttrCooperativeLaunch,
-                                 device) != cudaSuccess ||
-          cooperative == 0)
-        return Fail(kUnsupported, "persistent DiT: no cooperative launch");
-      if (cudaDeviceGetAttribute(&state.sms, cudaDevAttrMultiProcessorCount,
-                                 device) != cudaSuccess)
-        return Fail(kCudaError, "persistent DiT: SM count");
-    }
-    if (!state.configured[q8 ? 0 : 1]) {
-      if (cudaFuncSetAttribute(kernel,
-                               cudaFuncAttributeMaxDynamicSharedMemorySize,
-                               smem) != cudaSuccess)
-        return Fail(kCudaError, "persistent DiT: shared memory attribute");
-      int blocks = 0;
-      if (cudaOccupancyMaxActiveBlocksPerMultiprocessor(&blocks, kernel,
-                                                        kThreads, smem) !=
-              cudaSuccess ||
-          blocks < 1)
-        return Fail(kUnsupported, "persistent DiT: one CTA per SM does not fit");
-      state.configured[q8 ? 0 : 1] = true;
-    }
-    sms = state.sms;
-  }
-  if (sms < 64)
-    return Fail(kUnsupported, "persistent DiT: needs at least 64 SMs");
+  const int ctas = DitCtas(q8);
+  if (ctas == 0)
+    return Fail(kUnsupported,
+                "persistent DiT: the device cannot hold one CTA pair per "
+                "residual group co-resident");
   unsigned* error_word = DeviceErrorWord();
   if (error_word == nullptr)
     return Fail(kCudaError, "persistent DiT: device error word");
   if (cudaMemsetAsync(p.sync, 0, kDitSyncWords * sizeof(unsigned), stream) !=
       cudaSuccess)
     return Fail(kCudaError, "persistent DiT: memset");
-  cudaLaunchConfig_t config = {};
-  config.gridDim = dim3(static_cast<unsigned>(sms));
-  config.blockDim = dim3(kThreads);
-  config.dynamicSmemBytes = static_cast<std::size_t>(smem);
-  config.stream = stream;
-  cudaLaunchAttribute attribute[1];
-  attribute[0].id = cudaLaunchAttributeCooperative;
-  attribute[0].val.cooperative = 1;
-  config.attrs = attribute;
-  config.numAttrs = 1;
-  return FromCuda(cudaLaunchKernelEx(&config, kernel, p, error_word),
+  cudaLaunchAttribute attribute[2];
+  const cudaLaunchConfig_t config =
+      DitConfig(q8, static_cast<unsigned>(ctas), stream, attribute);
+  return FromCuda(cudaLaunchKernelEx(&config, DitKernel(q8), p, error_word),
                   "persistent DiT launch");
 }
 

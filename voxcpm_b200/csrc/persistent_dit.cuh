@@ -12,12 +12,13 @@
 // running ahead across layers; sixteen consumer warps take two tiles each
 // and reduce in a fixed order. There is no grid barrier: each phase (QKV,
 // O, gate/up, down, the patch boundary) waits only on monotone ready
-// counters of the data it reads, published with release semantics by the
-// CTAs that wrote it. Attention for a head runs on the CTA that completes
-// the head's last q/k/v group; split reductions of O and down are folded
-// into the residual stream by the CTA that completes a group's last part
-// (an atomic ticket), summing the parts in a fixed order, so results are
-// deterministic.
+// counters of the data it reads, published with release semantics (by a
+// publisher warp, so compute warps never stall on a fence). Attention runs
+// as 32 (head, sequence) tasks on CTAs that hold a single QKV unit. The
+// split reductions of O (two 1024-column parts) and down (four) live on a
+// CTA pair (a cluster of two): rank 1 sends its reduced parts through
+// distributed shared memory and rank 0 adds them into the residual stream
+// in a fixed part order, so results are deterministic.
 #pragma once
 
 #include <cuda_runtime.h>
@@ -81,19 +82,23 @@ struct DitPatchParams {
   float* qkv = nullptr;         // [22][2560]
   std::uint16_t* att = nullptr; // [22][2048]
   std::uint16_t* act = nullptr; // [22][4096]
-  float* o_parts = nullptr;     // [2][22][1024]
-  float* down_parts = nullptr;  // [4][22][1024]
   unsigned* sync = nullptr;     // [kDitSyncWords]
 };
 
-/// Device bytes of the work buffers above (hidden .. down_parts), laid out
+/// Device bytes of the work buffers above (hidden .. sync), laid out
 /// in that order with 256-byte alignment by DitWorkLayout.
 std::size_t DitWorkBytes();
 /// Points the work-buffer fields of `params` into `base` (DitWorkBytes()).
 void DitWorkLayout(void* base, DitPatchParams& params);
 
+/// Whether the current device can run the persistent patch for `format`
+/// (cooperative launch of co-resident CTA pairs, at least one pair per
+/// 16-column residual group).
+bool DitPatchSupported(WeightFormat format);
+
 /// Enqueues the persistent patch on `stream`: a memset of the sync words,
-/// then the cooperative kernel (one CTA per SM). Returns a Status.
+/// then the cooperative kernel (CTA pairs as clusters of two, one CTA per
+/// SM). Returns a Status.
 int LaunchDitPatch(const DitPatchParams& params, cudaStream_t stream);
 
 }  // namespace vx

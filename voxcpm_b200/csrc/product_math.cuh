@@ -15,7 +15,9 @@ __device__ inline void Mma16816(float (&d)[4], std::uint32_t a0,
                                 std::uint32_t a1, std::uint32_t a2,
                                 std::uint32_t a3, std::uint32_t b0,
                                 std::uint32_t b1, const float (&c)[4]) {
-  asm volatile(
+  // Not volatile: the MMA has no side effects, so the compiler may
+  // interleave the independent MMAs of neighbouring tiles.
+  asm(
       "mma.sync.aligned.m16n8k16.row.col.f32.bf16.bf16.f32 {%0,%1,%2,%3}, "
       "{%4,%5,%6,%7}, {%8,%9}, {%10,%11,%12,%13};"
       : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])

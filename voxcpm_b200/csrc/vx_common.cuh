@@ -27,6 +27,7 @@ enum DeviceError : unsigned {
   kErrDrainWait = 1u << 2,
   kErrBarrierWait = 1u << 3,
   kErrPublishWait = 1u << 4,
+  kErrPeerWait = 1u << 5,
 };
 
 /// The device word the library's kernels or their error bits into; defined
