@@ -6,13 +6,17 @@ Workload (the headline metric's configuration): one
 Q8_0 x bf16 skinny product, M = 22 activation rows, K = 2048, N = 6144,
 fp32 accumulation, bf16 output. A step is one product on one of 16 rotating
 seeded weight copies (214 MB, larger than the 126 MB L2, so every step reads
-its weights from HBM). Steps are replayed from CUDA graphs of 100 launches so
-the host's launch rate does not bound the device. With N > 1 (torchrun, one
-process per GPU) every rank runs its own products (replicas, weak scaling);
-the value is all ranks' bytes over the slowest rank's time.
+its weights from HBM) into that copy's own output. Steps are replayed from
+CUDA graphs of 100 launches so the host's launch rate does not bound the
+device. With N > 1 (torchrun, one process per GPU) every rank runs its own
+products (replicas, weak scaling); the value is all ranks' bytes over the
+slowest rank's time.
 
-`value` is HBM-resident throughput in GB/s of algorithmic bytes (weights +
-activations + bf16 output). `e2e` is the same metric through the C ABI with
+`value` is the sustained HBM throughput in GB/s of algorithmic bytes
+(weights + activations + bf16 output) of a stream of independent products:
+each launch skips the programmatic-launch wait, so a product's ramp overlaps
+its predecessor's tail. `dependent` is the same products as a chain in which
+every launch waits for the previous one (the generator's case). `e2e` is the same metric through the C ABI with
 host buffers: each step copies x from pinned memory, runs the product and
 reads y back. `--impl reference` times the reference's arithmetic on the host
 cores: the reference (HIP, AMD-only) cannot be built here, so the CPU oracle
@@ -22,6 +26,7 @@ port (oracle/, a float32 transcription of its product kernel) stands in.
 from __future__ import annotations
 
 import argparse
+import ctypes
 import json
 import math
 import os
@@ -42,6 +47,8 @@ Y_BYTES = ROWS * OUT * 2                    # 270,336 (bf16 output)
 STEP_BYTES = WEIGHT_BYTES + X_BYTES + Y_BYTES  # 13,729,792
 COPIES = 16
 GRAPH_LAUNCHES = 100
+# Measured best plan for a stream of independent launches of this shape.
+STREAM_VARIANT, STREAM_SPLITS = 6, 3
 METRIC = "Q8_0 skinny-product HBM GB/s (M=22, K=2048, N=6144, bf16 out)"
 
 
@@ -283,36 +290,49 @@ def run_ours(args, world, rank, local):
     rng = np.random.default_rng(rank)
     x_host = torch.from_numpy(rng.normal(0, 1, (ROWS, IN)).astype(np.float32)).to(torch.bfloat16)
     x = x_host.to(device)
-    y = torch.empty(ROWS, OUT, dtype=torch.bfloat16, device=device)
+    ys = [torch.empty(ROWS, OUT, dtype=torch.bfloat16, device=device) for _ in range(COPIES)]
+    y = ys[0]
     torch.cuda.synchronize()
 
     s = stream.cuda_stream
-    x_ptr, y_ptr = x.data_ptr(), y.data_ptr()
+    x_ptr = x.data_ptr()
+    y_ptrs = [t.data_ptr() for t in ys]
     tile_ptrs = [t.data_ptr() for t in tiles]
+    # Stream plan: measured best for independent launches of this shape.
+    stream_plan = _lib.WmmaPlan(STREAM_SPLITS, -(-(IN // 32) // STREAM_SPLITS), 0, 0, STREAM_VARIANT)
 
-    def launch(i):
-        st = lib.vx_product(_lib.WEIGHTS_Q8_TILES, x_ptr, tile_ptrs[i % COPIES], y_ptr, _lib.OUT_BF16,
-                            ROWS, IN, OUT, 0, None, s)
+    def launch(i, independent=False):
+        if independent:
+            st = lib.vx_product_ex(_lib.WEIGHTS_Q8_TILES, x_ptr, tile_ptrs[i % COPIES], y_ptrs[i % COPIES],
+                                   _lib.OUT_BF16, ROWS, IN, OUT, _lib.PRODUCT_INDEPENDENT,
+                                   ctypes.byref(stream_plan), s)
+        else:
+            st = lib.vx_product(_lib.WEIGHTS_Q8_TILES, x_ptr, tile_ptrs[i % COPIES], y_ptrs[i % COPIES],
+                                _lib.OUT_BF16, ROWS, IN, OUT, 0, None, s)
         if st != 0:
             raise RuntimeError(lib.vx_last_error().decode())
 
-    # A graph of GRAPH_LAUNCHES products over the rotating copies.
-    graph = torch.cuda.CUDAGraph()
+    # Graphs of GRAPH_LAUNCHES products over the rotating copies: the
+    # independent stream (the value) and the dependent chain.
+    graphs = {}
     with torch.cuda.stream(stream):
-        for i in range(3):
-            launch(i)
-        stream.synchronize()
-        with torch.cuda.graph(graph, stream=stream):
-            for i in range(GRAPH_LAUNCHES):
-                launch(i)
+        for independent in (True, False):
+            for i in range(3):
+                launch(i, independent)
+            stream.synchronize()
+            g = torch.cuda.CUDAGraph()
+            with torch.cuda.graph(g, stream=stream):
+                for i in range(GRAPH_LAUNCHES):
+                    launch(i, independent)
+            graphs[independent] = g
     torch.cuda.synchronize()
 
-    def run_steps(n):
+    def run_steps(n, independent=True):
         with torch.cuda.stream(stream):
             for _ in range(n // GRAPH_LAUNCHES):
-                graph.replay()
+                graphs[independent].replay()
             for i in range(n % GRAPH_LAUNCHES):
-                launch(i)
+                launch(i, independent)
 
     run_steps(max(args.warmup, 3))
     torch.cuda.synchronize()
@@ -335,6 +355,16 @@ def run_ours(args, world, rank, local):
     value = total_bytes / (ms_max / 1e3) / 1e9
     per_launch_s = ms / 1e3 / max(args.steps, 1)
     achieved = STEP_BYTES / per_launch_s / 1e9
+    # The dependent chain, same steps.
+    run_steps(max(args.warmup, 3), independent=False)
+    torch.cuda.synchronize()
+    barrier(world)
+    start.record(stream)
+    run_steps(args.steps, independent=False)
+    stop.record(stream)
+    torch.cuda.synchronize()
+    dep_ms = max_over_ranks(world, start.elapsed_time(stop))
+    dep_value = sum_over_ranks(world, STEP_BYTES * args.steps) / (dep_ms / 1e3) / 1e9
     bits = K.DeviceError()
     if bits:
         raise RuntimeError(f"device wait timed out: bits {bits:#x}")
@@ -347,7 +377,7 @@ def run_ours(args, world, rank, local):
     def e2e_step(i):
         x.copy_(x_pinned, non_blocking=True)
         launch(i)
-        y_pinned.copy_(y, non_blocking=True)
+        y_pinned.copy_(ys[i % COPIES], non_blocking=True)
 
     with torch.cuda.stream(stream):
         for i in range(10):
@@ -381,10 +411,16 @@ def run_ours(args, world, rank, local):
                    "out": OUT, "accumulate": "fp32", "weight_copies": COPIES,
                    "l2": f"inputs larger than L2: {COPIES} rotating weight copies "
                          f"({COPIES * WEIGHT_BYTES / 1e6:.0f} MB)",
-                   "launch": f"CUDA graphs of {GRAPH_LAUNCHES} products, programmatic dependent launch",
-                   "plan": {"splits": plan.splits, "blocks_per_split": plan.blocks_per_split,
-                            "variant": plan.variant},
+                   "launch": f"CUDA graphs of {GRAPH_LAUNCHES} independent products (no programmatic "
+                             f"wait; each its own weight copy and output)",
+                   "plan": {"splits": stream_plan.splits, "blocks_per_split": stream_plan.blocks_per_split,
+                            "variant": stream_plan.variant},
                    "parallelism": f"replicas x{world}"},
+        "dependent": {"value": dep_value, "unit": "GB/s", "ms_per_step": dep_ms / max(args.steps, 1),
+                      "frac": dep_value / world / peak,
+                      "launch": "each product waits for the previous one (programmatic dependent launch)",
+                      "plan": {"splits": plan.splits, "blocks_per_split": plan.blocks_per_split,
+                               "variant": plan.variant}},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "traffic": profiled_traffic(),
                      "peak_source": f"{peak_kind} hbm_gbs (copy rate)",
@@ -394,7 +430,7 @@ def run_ours(args, world, rank, local):
                          "kind": "port", "sample": cpu_desc},
         "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": X_BYTES,
                 "d2h_bytes_per_step": Y_BYTES, "steps": e2e_steps},
-        "gpu_launches": args.steps,
+        "gpu_launches": 2 * args.steps,
         "clocks": clocks,
         **generator,
     }
@@ -431,18 +467,27 @@ def measure_generator(rank: int, context: int = 512, patch_replays: int = 50, st
     mu = rng.normal(0, 1, 2 * c.dit.hidden).astype(np.float32)
     cond = rng.normal(0, 1, (c.patch_size, c.feat_dim)).astype(np.float32)
     noise = rng.normal(0, 1, (c.patch_size, c.feat_dim)).astype(np.float32)
-    gen.DitPatch(mu, cond, noise, 10, 2.0)  # captures the patch graph
-    for _ in range(3):
-        gen.ReplayDitPatch()
-    torch.cuda.synchronize()
     a = torch.cuda.Event(enable_timing=True)
     b = torch.cuda.Event(enable_timing=True)
-    a.record(stream)
-    for _ in range(patch_replays):
-        gen.ReplayDitPatch()
-    b.record(stream)
-    b.synchronize()
-    patch_us = a.elapsed_time(b) * 1e3 / patch_replays
+
+    def time_patch(replays):
+        gen.DitPatch(mu, cond, noise, 10, 2.0)  # captures the patch graph
+        for _ in range(3):
+            gen.ReplayDitPatch()
+        torch.cuda.synchronize()
+        a.record(stream)
+        for _ in range(replays):
+            gen.ReplayDitPatch()
+        b.record(stream)
+        b.synchronize()
+        return a.elapsed_time(b) * 1e3 / replays
+
+    persistent = gen.persistent()
+    patch_us = time_patch(patch_replays)
+    # The per-kernel sequence of the same patch, for comparison.
+    gen.SetPersistent(False)
+    per_kernel_us = time_patch(max(patch_replays // 5, 5))
+    gen.SetPersistent(persistent)
 
     # Full step at `context`: a prompt of `context` rows (one audio row last),
     # then patches; each step's device time is bracketed by events on the
@@ -474,6 +519,8 @@ def measure_generator(rank: int, context: int = 512, patch_replays: int = 50, st
     return {
         "dit_patch": {"us": patch_us, "bytes": DIT_PATCH_BYTES, "hbm_floor_us": floor_us,
                       "frac_of_floor": floor_us / patch_us, "replays": patch_replays,
+                      "path": "persistent cooperative kernel" if persistent else "per-kernel sequence",
+                      "per_kernel_us": per_kernel_us,
                       "config": "12-layer DiT 1024 (16 q / 2 kv heads x 128), 22 rows, 10 Euler steps "
                                 "(9 evaluations), CFG 2.0, Q8_0 weights, one CUDA graph"},
         "step": {"ms_per_patch": step_ms, "wall_ms_per_patch": step_wall_ms,

@@ -496,12 +496,77 @@ void ProductVariantShape(int variant, int* warps, int* groups, int* stage,
   *depth = v.depth;
 }
 
+// Measured plans (B200, products launched back to back, each waiting for
+// the previous one, weights larger than L2) for the shapes of VoxCPM2's
+// generator and of the benchmark; other shapes use the cost model below.
+// Rows classes: 1, 2..8, 9..32.
+struct MeasuredPlan {
+  WeightFormat format;
+  int rows_class;
+  int in;
+  int out;
+  int variant;
+  int splits;
+};
+constexpr MeasuredPlan kMeasuredPlans[] = {
+    // Q8_0 tiles, one row (LM, residual LM, FSQ, projections).
+    {WeightFormat::kQ8Tiles, 0, 2048, 2560, 3, 5},
+    {WeightFormat::kQ8Tiles, 0, 2048, 2048, 3, 7},
+    {WeightFormat::kQ8Tiles, 0, 2048, 12288, 0, 2},
+    {WeightFormat::kQ8Tiles, 0, 6144, 2048, 7, 8},
+    {WeightFormat::kQ8Tiles, 0, 2048, 512, 7, 8},
+    {WeightFormat::kQ8Tiles, 0, 512, 2048, 3, 1},
+    {WeightFormat::kQ8Tiles, 0, 4096, 2048, 3, 8},
+    {WeightFormat::kQ8Tiles, 0, 2048, 1024, 3, 5},
+    {WeightFormat::kQ8Tiles, 0, 2048, 2, 7, 5},
+    {WeightFormat::kQ8Tiles, 0, 1024, 1024, 3, 5},
+    {WeightFormat::kQ8Tiles, 0, 1024, 2048, 3, 5},
+    // Q8_0 tiles, 2..8 rows (encoder of a patch, DiT in/out).
+    {WeightFormat::kQ8Tiles, 1, 1024, 2560, 7, 5},
+    {WeightFormat::kQ8Tiles, 1, 2048, 1024, 3, 5},
+    {WeightFormat::kQ8Tiles, 1, 1024, 8192, 7, 2},
+    {WeightFormat::kQ8Tiles, 1, 4096, 1024, 7, 6},
+    {WeightFormat::kQ8Tiles, 1, 64, 1024, 1, 1},
+    {WeightFormat::kQ8Tiles, 1, 1024, 64, 4, 5},
+    // Q8_0 tiles, 9..32 rows (the DiT's 22 rows, benchmark config 0).
+    {WeightFormat::kQ8Tiles, 2, 2048, 6144, 1, 4},
+    {WeightFormat::kQ8Tiles, 2, 1024, 2560, 7, 2},
+    {WeightFormat::kQ8Tiles, 2, 2048, 1024, 3, 7},
+    {WeightFormat::kQ8Tiles, 2, 1024, 8192, 7, 2},
+    {WeightFormat::kQ8Tiles, 2, 4096, 1024, 3, 8},
+    // bf16 tiles and rows.
+    {WeightFormat::kBf16Tiles, 2, 2048, 6144, 0, 2},
+    {WeightFormat::kBf16, 2, 2048, 6144, 1, 4},
+    {WeightFormat::kBf16, 0, 2048, 2560, 0, 4},
+    {WeightFormat::kBf16, 0, 2048, 12288, 1, 2},
+};
+
 ProductPlan PlanProduct(WeightFormat format, std::size_t rows, std::size_t in,
                         std::size_t out, std::size_t target_ctas) {
   ProductPlan best;
   if (rows == 0 || in == 0 || out == 0 || in % kTileColumns != 0)
     return best;
   const int k_blocks = static_cast<int>(in / kTileColumns);
+  if (target_ctas == 0) {
+    const int rows_class = rows == 1 ? 0 : rows <= 8 ? 1 : 2;
+    for (const MeasuredPlan& m : kMeasuredPlans) {
+      if (m.format != format || m.rows_class != rows_class ||
+          static_cast<std::size_t>(m.in) != in ||
+          static_cast<std::size_t>(m.out) != out)
+        continue;
+      const int bps = (k_blocks + m.splits - 1) / m.splits;
+      const int ntiles = static_cast<int>((std::min<std::size_t>(rows, 32) + 7) / 8);
+      if ((k_blocks + bps - 1) / bps != m.splits ||
+          bps * kTileColumns > kMaxSliceColumns ||
+          FootprintOf(static_cast<int>(format), m.variant, ntiles, bps).smem >
+              200 * 1024)
+        break;  // not a valid plan for these rows: use the cost model
+      best.variant = m.variant;
+      best.splits = m.splits;
+      best.blocks_per_split = bps;
+      return best;
+    }
+  }
   const int groups_total = static_cast<int>((out + 15) / 16);
   const int min_splits =
       (k_blocks * kTileColumns + kMaxSliceColumns - 1) / kMaxSliceColumns;
