@@ -368,6 +368,26 @@ VX_API vx_status vx_generator_dit_patch(vx_generator* generator,
                                         const float* mu, const float* cond,
                                         const float* noise, size_t timesteps,
                                         float cfg, float* latent);
+/* The DiT patch of vx_generator_dit_patch for callers that must not allocate
+ * device memory while generating: a host that sized all of its GPU memory at
+ * start-up, or a real-time audio loop that cannot wait on the driver's
+ * allocator. No reference counterpart. All arrays are DEVICE pointers: mu
+ * [2][dit hidden], cond and noise [patch][feat] in, latent [patch][feat] out.
+ * The persistent kernel's work buffers live in a fixed 1 MiB device array of
+ * the library instead of the generator's own allocation; the call allocates
+ * nothing. Needs the persistent kernel (a generator whose DiT has another
+ * shape gets VX_INVALID) and a schedule prepared by an earlier
+ * vx_generator_dit_patch or vx_generator_step with the same `timesteps`
+ * (else VX_INVALID). The first call on a device looks the array's address up
+ * (make that first call before any stream capture). Calls that overlap on
+ * the GPU, from any generator, share the array and race. Synchronizes the
+ * generator's stream. */
+VX_API vx_status vx_generator_dit_patch_static(vx_generator* generator,
+                                               const float* mu,
+                                               const float* cond,
+                                               const float* noise,
+                                               size_t timesteps, float cfg,
+                                               float* latent);
 /* Replays the last DiT patch (its captured graph) on the generator's stream
  * without synchronizing (benchmarks). */
 VX_API vx_status vx_generator_replay_dit_patch(vx_generator* generator);

@@ -159,6 +159,7 @@ SIGNATURES: dict[str, tuple] = {
     "vx_generator_step": (c_int, [c_void_p, c_void_p, c_size_t, c_float, c_void_p, c_void_p]),
     "vx_generator_velocity": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_float, c_void_p]),
     "vx_generator_dit_patch": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_float, c_void_p]),
+    "vx_generator_dit_patch_static": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_float, c_void_p]),
     "vx_generator_replay_dit_patch": (c_int, [c_void_p]),
     "vx_generator_state": (c_int, [c_void_p, c_char_p, c_void_p, c_size_t]),
     "vx_generator_set_state": (c_int, [c_void_p, c_char_p, c_void_p, c_size_t]),

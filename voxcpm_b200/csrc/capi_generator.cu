@@ -164,6 +164,20 @@ vx_status vx_generator_dit_patch(vx_generator* generator, const float* mu,
   });
 }
 
+vx_status vx_generator_dit_patch_static(vx_generator* generator,
+                                        const float* mu, const float* cond,
+                                        const float* noise, size_t timesteps,
+                                        float cfg, float* latent) {
+  return Guard(generator, "vx_generator_dit_patch_static",
+               [&](vx::Generator& g) {
+                 if (mu == nullptr || cond == nullptr || noise == nullptr ||
+                     latent == nullptr || timesteps == 0)
+                   throw std::invalid_argument("null array or no timesteps");
+                 g.DitPatchStatic(mu, cond, noise, static_cast<int>(timesteps),
+                                  cfg, latent);
+               });
+}
+
 vx_status vx_generator_replay_dit_patch(vx_generator* generator) {
   return Guard(generator, "vx_generator_replay_dit_patch",
                [&](vx::Generator& g) { g.ReplayDitPatch(); });

@@ -1162,6 +1162,39 @@ void Generator::DitPatch(const float* mu, const float* cond,
   }
 }
 
+void Generator::DitPatchStatic(const float* mu, const float* cond,
+                               const float* noise, int timesteps, float cfg,
+                               float* latent) {
+  if (!persistent_ok_)
+    throw std::logic_error(
+        "the allocation-free DiT patch needs the persistent kernel (VoxCPM2's "
+        "DiT shape)");
+  if (dit_schedule_timesteps_ != timesteps)
+    throw std::logic_error(
+        "no prepared schedule for these timesteps: run DitPatch or Step once "
+        "with them first");
+  const ModelConfig& c = config_;
+  const int values = c.patch_size * c.feat_dim;
+  CheckCuda(cudaMemcpyAsync(mu_, mu, 2 * c.dit.hidden * sizeof(float),
+                            cudaMemcpyDeviceToDevice, stream_), "mu");
+  CheckCuda(cudaMemcpyAsync(prefix_cond_, cond, values * sizeof(float),
+                            cudaMemcpyDeviceToDevice, stream_), "cond");
+  CheckCuda(cudaMemcpyAsync(x_, noise, values * sizeof(float),
+                            cudaMemcpyDeviceToDevice, stream_), "noise");
+  DitCond();
+  if (dit_evaluations_ > 0) {
+    DitPatchParams p = dit_params_;
+    p.cfg = cfg;
+    p.evaluations = dit_evaluations_;
+    p.time_vectors = dit_times_;
+    p.dts = dit_dts_;
+    Check(LaunchDitPatchStatic(p, stream_), "allocation-free DiT patch");
+  }
+  CheckCuda(cudaMemcpyAsync(latent, x_, values * sizeof(float),
+                            cudaMemcpyDeviceToDevice, stream_), "latent");
+  CheckCuda(cudaStreamSynchronize(stream_), "patch");
+}
+
 void Generator::ReplayDitPatch() {
   if (patch_graph_ == nullptr)
     throw std::logic_error("no captured DiT patch (call DitPatch first)");

@@ -187,6 +187,12 @@ class Generator {
                 int timesteps, float cfg, float* latent);
   /// Replays the last captured DiT patch (inputs already on the device).
   void ReplayDitPatch();
+  /// DitPatch from device arrays with the persistent kernel's work buffers
+  /// in the library's static scratch; allocates nothing. Needs the
+  /// persistent kernel and a schedule prepared by an earlier DitPatch or
+  /// Step with the same `timesteps`. Synchronizes the generator's stream.
+  void DitPatchStatic(const float* mu, const float* cond, const float* noise,
+                      int timesteps, float cfg, float* latent);
   /// Downloads an internal state vector (tests).
   void State(const std::string& name, float* out, std::size_t count);
   /// Uploads an internal state vector (tests and benchmarks).

@@ -12,6 +12,7 @@
 
 #include <cmath>
 #include <mutex>
+#include <string>
 
 #include "product_math.cuh"
 #include "vx_common.cuh"
@@ -1317,6 +1318,53 @@ bool DitPatchSupported(WeightFormat format) {
   const bool ok = DitCtas(format == WeightFormat::kQ8Tiles) > 0;
   (void)cudaGetLastError();  // a failed query leaves no sticky error behind
   return ok;
+}
+
+// ---------------------------------------------------------------- static scratch
+
+namespace {
+
+/// The work buffers of the allocation-free patch live in this fixed device
+/// array instead of memory the caller allocated. One array per process and
+/// device: launches that overlap on the GPU share it and race.
+constexpr std::size_t kDitStaticScratchBytes = std::size_t{1} << 20;
+static __device__ __align__(256) unsigned char g_dit_static_scratch[kDitStaticScratchBytes];
+
+}  // namespace
+
+int LaunchDitPatchStatic(const DitPatchParams& base, cudaStream_t stream) {
+  if (DitWorkBytes() > kDitStaticScratchBytes)
+    return Fail(kInvalid,
+                "allocation-free DiT patch: the work buffers need " +
+                    std::to_string(DitWorkBytes()) + " bytes, more than the " +
+                    std::to_string(kDitStaticScratchBytes) +
+                    "-byte static scratch");
+  int device = 0;
+  if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= 64)
+    return Fail(kCudaError, "allocation-free DiT patch: no current device");
+  // The array's device address, looked up once per device (with that device
+  // current) on the first call there.
+  static std::mutex mutex;
+  static void* addresses[64] = {};
+  void* scratch = nullptr;
+  {
+    std::lock_guard<std::mutex> lock(mutex);
+    if (addresses[device] == nullptr) {
+      void* address = nullptr;
+      const cudaError_t error =
+          cudaGetSymbolAddress(&address, g_dit_static_scratch);
+      if (error != cudaSuccess || address == nullptr)
+        return Fail(kCudaError,
+                    std::string("allocation-free DiT patch: static scratch "
+                                "address: ") +
+                        cudaGetErrorString(error));
+      addresses[device] = address;
+    }
+    scratch = addresses[device];
+  }
+  DitPatchParams p = base;
+  DitWorkLayout(scratch, p);  // the sync words are zeroed by LaunchDitPatch
+  return LaunchDitPatch(p, stream);
 }
 
 int LaunchDitPatch(const DitPatchParams& p, cudaStream_t stream) {

@@ -101,4 +101,11 @@ bool DitPatchSupported(WeightFormat format);
 /// SM). Returns a Status.
 int LaunchDitPatch(const DitPatchParams& params, cudaStream_t stream);
 
+/// LaunchDitPatch with the work buffers (and sync words) placed in a fixed
+/// 1 MiB device array of this library instead of `params`' buffers: nothing
+/// is allocated. The first call on a device looks the array's address up
+/// (make it before any stream capture). Launches overlapping on the GPU
+/// share the array and race.
+int LaunchDitPatchStatic(const DitPatchParams& params, cudaStream_t stream);
+
 }  // namespace vx
