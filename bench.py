@@ -58,6 +58,8 @@ def parse():
     p.add_argument("--steps", type=int, default=400_000)
     p.add_argument("--warmup", type=int, default=20_000)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
+    p.add_argument("--case", choices=["product", "dit"], default=None,
+                   help="run a few launches of one kernel for a profiler and exit (no JSON line)")
     return p.parse_args()
 
 
@@ -532,8 +534,63 @@ def measure_generator(rank: int, context: int = 512, patch_replays: int = 50, st
     }
 
 
+def profile_case(case: str) -> None:
+    """A few launches of one kernel on a small case, for ncu captures:
+    `product`: 8 config-0 products with the stream plan (independent), then 8
+    with the planner's plan (dependent); `dit`: two eager DiT patches (the
+    persistent kernel) on the released DiT with one-layer LMs."""
+    import numpy as np
+    import torch
+
+    from voxcpm_b200 import _lib
+    from voxcpm_b200 import kernels as K
+
+    lib = _lib.load()
+    torch.cuda.set_device(0)
+    if case == "product":
+        tiles, ys = [], []
+        for c in range(COPIES):
+            blocks = torch.from_numpy(K.RandomQ8_0(1000, c, OUT, IN)).cuda()
+            t = torch.empty(K.Q8TilesBytes(OUT, IN), dtype=torch.uint8, device="cuda")
+            K.Q8_0ToTiles(blocks, OUT, IN, t)
+            tiles.append(t)
+            ys.append(torch.empty(ROWS, OUT, dtype=torch.bfloat16, device="cuda"))
+        x = torch.randn(ROWS, IN, device="cuda").to(torch.bfloat16)
+        plan = _lib.WmmaPlan(STREAM_SPLITS, -(-(IN // 32) // STREAM_SPLITS), 0, 0, STREAM_VARIANT)
+        for i in range(8):
+            _lib.check(lib.vx_product_ex(_lib.WEIGHTS_Q8_TILES, x.data_ptr(), tiles[i].data_ptr(),
+                                         ys[i].data_ptr(), _lib.OUT_BF16, ROWS, IN, OUT,
+                                         _lib.PRODUCT_INDEPENDENT, ctypes.byref(plan), None))
+        for i in range(8):
+            _lib.check(lib.vx_product(_lib.WEIGHTS_Q8_TILES, x.data_ptr(), tiles[8 + i].data_ptr(),
+                                      ys[8 + i].data_ptr(), _lib.OUT_BF16, ROWS, IN, OUT, 0, None, None))
+        torch.cuda.synchronize()
+    else:
+        from voxcpm_b200.generator import Generator, released_config
+
+        c = released_config()
+        c.lm.layers = 1
+        c.residual_lm.layers = 1
+        c.max_length = 64
+        gen = Generator(c, seed=7)
+        gen.SetGraphs(False)
+        rng = np.random.default_rng(0)
+        mu = rng.normal(0, 1, 2 * c.dit.hidden).astype(np.float32)
+        cond = rng.normal(0, 1, (c.patch_size, c.feat_dim)).astype(np.float32)
+        noise = rng.normal(0, 1, (c.patch_size, c.feat_dim)).astype(np.float32)
+        for _ in range(2):
+            gen.DitPatch(mu, cond, noise, 10, 2.0)
+        gen.close()
+    if K.DeviceError():
+        raise RuntimeError("a bounded device wait expired")
+    print(f"case {case}: ok", flush=True)
+
+
 def main():
     args = parse()
+    if args.case is not None:
+        profile_case(args.case)
+        return
     world, rank, local = init_dist(args.gpus)
     try:
         if args.impl == "reference":
