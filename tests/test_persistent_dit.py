@@ -146,3 +146,43 @@ def test_persistent_unsupported_shape(cuda):
         gen.SetPersistent(True)
     gen.SetPersistent(False)
     gen.close()
+
+
+@pytest.mark.parametrize("cache_type", [_lib.CACHE_BF16, _lib.CACHE_F32])
+def test_persistent_stacks_match_per_kernel_steps(cuda, cache_type):
+    """Steps with the persistent DiT and one-row LM stacks against the same
+    steps on the per-kernel path (the small configuration: released widths,
+    two layers per stack), and against the oracle."""
+    from voxcpm_b200.generator import small_config
+
+    c = small_config()
+    hidden = c.lm.hidden
+    fast = Generator(c, seed=21, cache_type=cache_type)
+    slow = Generator(c, seed=21, cache_type=cache_type)
+    slow.SetPersistent(False)
+    ref = OracleGenerator(c, seed=21, bf16_cache=cache_type == _lib.CACHE_BF16)
+    p = prompt(c, 6, rows=12, audio=(5, 11))
+    for g in (fast, slow):
+        g.Prefill(*p)
+    ref.prefill(*p)
+    rng = np.random.default_rng(3)
+    for k in range(3):
+        noise = rng.normal(0, 1, (c.patch_size, c.feat_dim)).astype(np.float32)
+        latent_f, stop_f = fast.Step(noise, 10, 2.0)
+        latent_s, stop_s = slow.Step(noise, 10, 2.0)
+        latent_r, stop_r = ref.step(noise, 10, 2.0)
+        e_paths = rel_l2(latent_f, latent_s)
+        e_lm = rel_l2(fast.State("lm_output", hidden), slow.State("lm_output", hidden))
+        e_res = rel_l2(fast.State("residual_hidden", hidden), slow.State("residual_hidden", hidden))
+        e_ref = rel_l2(latent_f, latent_r)
+        e_lm_ref = rel_l2(fast.State("lm_output", hidden), ref.lm_output)
+        print(f"step {k}: persistent vs per-kernel latent {e_paths:.3e} lm output {e_lm:.3e} "
+              f"residual {e_res:.3e}; vs oracle latent {e_ref:.3e} lm output {e_lm_ref:.3e}")
+        # States pass through FSQ, whose level flips (1/9 steps) feed the
+        # residual LM: they get the state limit, the latent the tighter one.
+        assert e_paths < PATHS_LIMIT and e_lm < STATE_LIMIT and e_res < STATE_LIMIT
+        assert e_ref < LATENT_LIMIT and e_lm_ref < STATE_LIMIT
+        assert float(np.max(np.abs(stop_f - stop_r))) < STOP_ATOL
+    assert DeviceError() == 0
+    fast.close()
+    slow.close()

@@ -576,6 +576,7 @@ std::unique_ptr<Generator> Generator::Create(const ModelConfig& config,
       g->CheckCuda(cudaStreamSynchronize(g->stream_), "create");
     }
     g->SetupPersistent();
+    g->SetupPersistentLm();
   } catch (const std::exception& failure) {
     if (error != nullptr)
       *error = failure.what();
@@ -613,6 +614,8 @@ Generator::~Generator() {
   free(dit_io_tiles_);
   free(dit_times_);
   free(dit_dts_);
+  free(lm_layers_);
+  free(lm_work_);
   if (pinned_noise_ != nullptr)
     cudaFreeHost(pinned_noise_);
   if (pinned_latent_ != nullptr)
@@ -795,6 +798,82 @@ void Generator::SetupPersistent() {
   }
   persistent_ok_ = true;
   persistent_ = true;
+}
+
+void Generator::SetupPersistentLm() {
+  // The persistent one-row stacks serve VoxCPM2's LM shape with Q8 tiles.
+  const ModelConfig& c = config_;
+  for (const StackConfig* stack : {&c.lm, &c.residual_lm})
+    if (stack->hidden != LmShape::kHidden ||
+        stack->intermediate != LmShape::kIntermediate ||
+        stack->heads != LmShape::kHeads || stack->kv_heads != LmShape::kKvHeads ||
+        stack->head_dim != LmShape::kHeadDim || stack->layers < 1)
+      return;
+  for (const StackWeights* stack : {&w_.base_lm, &w_.residual_lm})
+    for (const LayerWeights& layer : stack->layers)
+      for (const Projection* m : {&layer.qkv, &layer.o, &layer.gate_up, &layer.down})
+        if (m->format != WeightFormat::kQ8Tiles)
+          return;
+  if (!LmStackSupported())
+    return;
+  const StackWeights* stacks[2] = {&w_.base_lm, &w_.residual_lm};
+  KvCache* caches[2] = {&base_cache_, &residual_cache_};
+  std::vector<LmLayer> layers;
+  for (int k = 0; k < 2; ++k)
+    for (int i = 0; i < stacks[k]->config.layers; ++i) {
+      const LayerWeights& w = stacks[k]->layers[i];
+      LmLayer l;
+      l.qkv = static_cast<const unsigned char*>(w.qkv.weight);
+      l.o = static_cast<const unsigned char*>(w.o.weight);
+      l.gate_up = static_cast<const unsigned char*>(w.gate_up.weight);
+      l.down = static_cast<const unsigned char*>(w.down.weight);
+      l.input_norm = w.input_norm;
+      l.post_norm = w.post_norm;
+      l.keys = caches[k]->keys(i);
+      l.values = caches[k]->values(i);
+      layers.push_back(l);
+    }
+  CheckCuda(cudaMalloc(reinterpret_cast<void**>(&lm_layers_),
+                       layers.size() * sizeof(LmLayer)), "cudaMalloc layers");
+  CheckCuda(cudaMemcpy(lm_layers_, layers.data(), layers.size() * sizeof(LmLayer),
+                       cudaMemcpyHostToDevice), "upload layers");
+  CheckCuda(cudaMalloc(&lm_work_, LmWorkBytes()), "cudaMalloc stack work");
+  int offset = 0;
+  for (int k = 0; k < 2; ++k) {
+    LmStackParams& p = lm_params_[k];
+    LmWorkLayout(lm_work_, p);
+    const StackConfig& sc = stacks[k]->config;
+    p.layers = sc.layers;
+    p.bf16_kv = caches[k]->type() == CacheType::kBf16 ? 1 : 0;
+    p.capacity = caches[k]->capacity();
+    p.eps = sc.rms_eps;
+    p.attention_scale = 1.0f / std::sqrt(static_cast<float>(sc.head_dim));
+    p.layer = lm_layers_ + offset;
+    p.final_norm = stacks[k]->norm;
+    p.rope = sc.rope ? rope_ : nullptr;
+    p.position = position_counter_;
+    offset += sc.layers;
+  }
+  lm_persistent_ok_ = true;
+}
+
+void Generator::StepStack(int which, const AttentionLayout& layout,
+                          float* hidden, float* output) {
+  if (persistent_ && lm_persistent_ok_) {
+    LmStackParams p = lm_params_[which];
+    p.hidden = hidden;
+    p.output = output;
+    Check(LaunchLmStack(p, stream_), which == 0 ? "persistent lm" : "persistent residual lm");
+    return;
+  }
+  if (which == 0)
+    Check(ForwardStack(w_.base_lm, rope_, layout, base_cache_, hidden, output,
+                       1, scratch_, stream_),
+          "base lm");
+  else
+    Check(ForwardStack(w_.residual_lm, nullptr, layout, residual_cache_, hidden,
+                       output, 1, scratch_, stream_),
+          "residual lm");
 }
 
 bool Generator::set_persistent(bool enabled) {
@@ -1028,17 +1107,13 @@ void Generator::StepBody(int timesteps, float cfg) {
   layout.max_keys = capacity();
   layout.causal = true;
   Check(CopyFloats(embed_, step_a_, hidden, stream_), "copy");
-  Check(ForwardStack(w_.base_lm, rope_, layout, base_cache_, step_a_, step_b_,
-                     1, scratch_, stream_),
-        "base lm");
+  StepStack(0, layout, step_a_, step_b_);
   Fsq(step_b_, lm_hidden_, 1);
   Check(ConcatRows(lm_hidden_, nullptr, hidden, embed_, nullptr, hidden,
                    step_bf16_, 1, stream_),
         "ConcatRows");
   Check(Project(w_.fusion, step_bf16_, step_a_, 1, stream_), "fusion");
-  Check(ForwardStack(w_.residual_lm, nullptr, layout, residual_cache_, step_a_,
-                     residual_hidden_, 1, scratch_, stream_),
-        "residual lm");
+  StepStack(1, layout, step_a_, residual_hidden_);
   Check(AdvancePosition(position_counter_, step_positions_, stream_),
         "advance");
 }

@@ -16,6 +16,7 @@
 #include <vector>
 
 #include "persistent_dit.cuh"
+#include "persistent_lm.cuh"
 #include "products.cuh"
 #include "stack_kernels.cuh"
 
@@ -225,6 +226,11 @@ class Generator {
   void EnsureRows(int rows);
   void DestroyGraphs();
   void SetupPersistent();
+  void SetupPersistentLm();
+  /// One of the two one-row stacks of a step (0: LM, 1: residual LM):
+  /// the persistent kernel when enabled, else ForwardStack.
+  void StepStack(int which, const AttentionLayout& layout, float* hidden,
+                 float* output);
 
   ModelConfig config_;
   cudaStream_t stream_ = nullptr;
@@ -302,6 +308,12 @@ class Generator {
   int dit_schedule_capacity_ = 0;
   int dit_schedule_timesteps_ = -1;
   int dit_evaluations_ = 0;
+
+  // The persistent one-row stacks (LM, residual LM).
+  bool lm_persistent_ok_ = false;
+  LmLayer* lm_layers_ = nullptr;  // [LM layers | residual layers]
+  void* lm_work_ = nullptr;
+  LmStackParams lm_params_[2];
 };
 
 /// The reference's released shapes (tests/config_test.cpp:36-67): LM 28 x
