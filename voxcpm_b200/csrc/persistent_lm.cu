@@ -73,6 +73,8 @@ static_assert(kRedOffset % 128 == 0, "alignment");
 // Attention: per-warp partials (o[128], max, sum) in the reduction buffers.
 static_assert(kConsumerWarps * kPartFloats <= 2 * kConsumerWarps * kRed1,
               "attention partials");
+static_assert(kHeads * 32 == kConsumers, "a thread per 4 dims of the attention row");
+static_assert(kAttWidth * 2 <= kConsumerWarps * kRed1 * 4, "attention row in red2");
 
 enum Phase : int { kQkv = 0, kO = 1, kGu = 2, kDown = 3 };
 
@@ -206,26 +208,36 @@ __device__ void NormRow(const float* x, const uint4 (&weight)[2][2], float eps,
     }
 }
 
+/// A cache row's 4 dims of this lane as stored (fp32: float4, bf16: uint2).
 template <typename CacheT>
-__device__ inline float4 LoadCacheRow(const void* base, std::size_t row, int lane);
+struct CacheRaw;
 template <>
-__device__ inline float4 LoadCacheRow<float>(const void* base, std::size_t row,
-                                             int lane) {
-  return __ldcg(reinterpret_cast<const float4*>(static_cast<const float*>(base) +
-                                                row * kD) +
-                lane);
-}
+struct CacheRaw<float> {
+  using Type = float4;
+  __device__ static Type Load(const void* base, std::size_t row, int lane) {
+    return __ldcg(reinterpret_cast<const float4*>(static_cast<const float*>(base) +
+                                                  row * kD) +
+                  lane);
+  }
+  __device__ static float4 Widen(Type v) { return v; }
+  __device__ static Type Narrow(float4 v) { return v; }
+};
 template <>
-__device__ inline float4 LoadCacheRow<Bf16>(const void* base, std::size_t row,
-                                            int lane) {
-  const uint2 v = __ldcg(reinterpret_cast<const uint2*>(
-                             static_cast<const Bf16*>(base) + row * kD) +
-                         lane);
-  return make_float4(Bf16ToFloat(static_cast<Bf16>(v.x & 0xFFFFu)),
-                     Bf16ToFloat(static_cast<Bf16>(v.x >> 16)),
-                     Bf16ToFloat(static_cast<Bf16>(v.y & 0xFFFFu)),
-                     Bf16ToFloat(static_cast<Bf16>(v.y >> 16)));
-}
+struct CacheRaw<Bf16> {
+  using Type = uint2;
+  __device__ static Type Load(const void* base, std::size_t row, int lane) {
+    return __ldcg(reinterpret_cast<const uint2*>(static_cast<const Bf16*>(base) +
+                                                 row * kD) +
+                  lane);
+  }
+  __device__ static float4 Widen(Type v) {
+    return make_float4(Bf16ToFloat(static_cast<Bf16>(v.x & 0xFFFFu)),
+                       Bf16ToFloat(static_cast<Bf16>(v.x >> 16)),
+                       Bf16ToFloat(static_cast<Bf16>(v.y & 0xFFFFu)),
+                       Bf16ToFloat(static_cast<Bf16>(v.y >> 16)));
+  }
+  __device__ static Type Narrow(float4 v) { return PackBf16x4(v.x, v.y, v.z, v.w); }
+};
 
 /// RoPE of a 128-wide vector held 4 dims per lane: the pair of dim d < 64
 /// is d + 64, held by lane ^ 16 (first = a c - b s, second = b c + a s).
@@ -292,25 +304,44 @@ __device__ void AttentionTask(const LmStackParams& p, const LmLayer& layer,
   float maximum = -INFINITY;
   float sum = 0.0f;
   float4 out = make_float4(0.f, 0.f, 0.f, 0.f);
-  for (int key = k0 + warp; key < k1; key += kConsumerWarps) {
-    float4 k, v;
-    if (key == position) {
-      k = new_k;
-      v = new_v;
-    } else {
-      k = LoadCacheRow<CacheT>(layer.keys, base + key, lane);
-      v = LoadCacheRow<CacheT>(layer.values, base + key, lane);
+  // This warp's keys k0 + warp, + 16, ... in batches whose rows are all in
+  // flight before the first is used.
+  using Raw = CacheRaw<CacheT>;
+  constexpr int kBatch = sizeof(CacheT) == 2 ? 8 : 4;
+  // The new row as stored (already rounded to the cache's type).
+  const typename Raw::Type new_kr = Raw::Narrow(new_k);
+  const typename Raw::Type new_vr = Raw::Narrow(new_v);
+  for (int first = k0 + warp; first < k1; first += kBatch * kConsumerWarps) {
+    typename Raw::Type kr[kBatch], vr[kBatch];
+#pragma unroll
+    for (int i = 0; i < kBatch; ++i) {
+      const int key = first + i * kConsumerWarps;
+      if (key < k1 && key != position) {
+        kr[i] = Raw::Load(layer.keys, base + key, lane);
+        vr[i] = Raw::Load(layer.values, base + key, lane);
+      } else {
+        kr[i] = new_kr;
+        vr[i] = new_vr;
+      }
     }
-    const float score = WarpAllSum(q.x * k.x + q.y * k.y + q.z * k.z + q.w * k.w);
-    const float next = fmaxf(maximum, score);
-    const float decay = expf(maximum - next);
-    const float weight = expf(score - next);
-    sum = sum * decay + weight;
-    out.x = out.x * decay + weight * v.x;
-    out.y = out.y * decay + weight * v.y;
-    out.z = out.z * decay + weight * v.z;
-    out.w = out.w * decay + weight * v.w;
-    maximum = next;
+#pragma unroll
+    for (int i = 0; i < kBatch; ++i) {
+      if (first + i * kConsumerWarps >= k1)
+        break;
+      const float4 ki = Raw::Widen(kr[i]);
+      const float4 vi = Raw::Widen(vr[i]);
+      const float score =
+          WarpAllSum(q.x * ki.x + q.y * ki.y + q.z * ki.z + q.w * ki.w);
+      const float next = fmaxf(maximum, score);
+      const float decay = expf(maximum - next);
+      const float weight = expf(score - next);
+      sum = sum * decay + weight;
+      out.x = out.x * decay + weight * vi.x;
+      out.y = out.y * decay + weight * vi.y;
+      out.z = out.z * decay + weight * vi.z;
+      out.w = out.w * decay + weight * vi.w;
+      maximum = next;
+    }
   }
   float* mine = scratch + warp * kPartFloats;
   reinterpret_cast<float4*>(mine)[lane] = out;
@@ -357,55 +388,49 @@ __device__ void AttentionTask(const LmStackParams& p, const LmLayer& layer,
   ConsumerSync();
 }
 
-/// This warp's attention-output fragments for one 1024-column chunk: its
-/// 64 columns are half of head 8 chunk + warp / 2; lanes 0..3 merge the
-/// head's split partials for their 16 columns and round to bf16.
-__device__ inline void AttentionFragments(const float* parts, int chunk,
-                                          int warp, int lane, RowFragments& b) {
-  b[0] = b[1] = make_uint4(0u, 0u, 0u, 0u);
-  if (lane >= 4)
-    return;
-  const int head = chunk * (kChunk / kD) + warp / 2;
-  const int dim0 = (warp & 1) * 64;
+/// The attention output row (bf16 [2048]) into `row`: thread t merges the
+/// split partials of head t / 32 for dims 4 (t % 32) .. + 3, every load in
+/// flight at once (split order fixed, so the merge is deterministic).
+__device__ void MergeAttention(const float* parts, Bf16* row, int tid) {
+  const int head = tid >> 5;
+  const int d = 4 * (tid & 31);
   const float* hp = parts + static_cast<std::size_t>(head) * kSplits * kPartFloats;
   float mx[kSplits], sm[kSplits];
-  float m = -INFINITY;
+  float4 o[kSplits];
 #pragma unroll
   for (int s = 0; s < kSplits; ++s) {
     mx[s] = __ldcg(hp + s * kPartFloats + kD);
     sm[s] = __ldcg(hp + s * kPartFloats + kD + 1);
-    m = fmaxf(m, mx[s]);
+    o[s] = __ldcg(reinterpret_cast<const float4*>(hp + s * kPartFloats + d));
   }
+  float m = -INFINITY;
+#pragma unroll
+  for (int s = 0; s < kSplits; ++s)
+    m = fmaxf(m, mx[s]);
   float total = 0.0f;
-  float f[kSplits];
+  float4 r = make_float4(0.f, 0.f, 0.f, 0.f);
 #pragma unroll
   for (int s = 0; s < kSplits; ++s) {
-    f[s] = mx[s] == -INFINITY ? 0.0f : expf(mx[s] - m);
-    total += sm[s] * f[s];
+    const float f = mx[s] == -INFINITY ? 0.0f : expf(mx[s] - m);
+    total += sm[s] * f;
+    r.x += o[s].x * f;
+    r.y += o[s].y * f;
+    r.z += o[s].z * f;
+    r.w += o[s].w * f;
   }
   const float inverse = 1.0f / total;
+  *reinterpret_cast<uint2*>(row + head * kD + d) =
+      PackBf16x4(r.x * inverse, r.y * inverse, r.z * inverse, r.w * inverse);
+}
+
+/// Fragments of a bf16 row held in shared memory (lanes 0..3).
+__device__ inline void SharedRowFragments(const Bf16* row, int chunk, int warp,
+                                          int lane, RowFragments& b) {
 #pragma unroll
-  for (int t = 0; t < 2; ++t) {
-    float o[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
-    const int d = dim0 + 32 * t + 8 * lane;
-#pragma unroll
-    for (int s = 0; s < kSplits; ++s) {
-      const float4 a = __ldcg(reinterpret_cast<const float4*>(hp + s * kPartFloats + d));
-      const float4 c = __ldcg(reinterpret_cast<const float4*>(hp + s * kPartFloats + d) + 1);
-      o[0] += a.x * f[s];
-      o[1] += a.y * f[s];
-      o[2] += a.z * f[s];
-      o[3] += a.w * f[s];
-      o[4] += c.x * f[s];
-      o[5] += c.y * f[s];
-      o[6] += c.z * f[s];
-      o[7] += c.w * f[s];
-    }
-    b[t] = make_uint4(PackBf16x2(o[0] * inverse, o[1] * inverse),
-                      PackBf16x2(o[2] * inverse, o[3] * inverse),
-                      PackBf16x2(o[4] * inverse, o[5] * inverse),
-                      PackBf16x2(o[6] * inverse, o[7] * inverse));
-  }
+  for (int t = 0; t < 2; ++t)
+    b[t] = lane < 4 ? *reinterpret_cast<const uint4*>(row + chunk * kChunk + 64 * warp +
+                                                      32 * t + 8 * lane)
+                    : make_uint4(0u, 0u, 0u, 0u);
 }
 
 /// Fragments of bf16 row `src` for chunk `chunk` (lanes 0..3).
@@ -580,10 +605,13 @@ __device__ void Consume(const LmStackParams& p, unsigned char* smem,
       for (int u = mine; u < kOUnits; u += ctas) {
         if (!WaitCount(c, sync + kSyncAtt, kTasks * (index + 1)))
           return;
+        Bf16* att_row = reinterpret_cast<Bf16*>(red2);
+        MergeAttention(p.att_parts, att_row, tid);
+        ConsumerSync();
         float acc[1][4] = {{0.f, 0.f, 0.f, 0.f}};
         for (int ch = 0; ch < kAttWidth / kChunk; ++ch) {
           RowFragments b;
-          AttentionFragments(p.att_parts, ch, warp, lane, b);
+          SharedRowFragments(att_row, ch, warp, lane, b);
           RowProduct(acquire(), b, warp, lane, acc);
           release();
         }
