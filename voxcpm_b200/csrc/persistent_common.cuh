@@ -256,5 +256,13 @@ __device__ void Publish(PubEntry* entries, std::uint64_t* pub_full,
   }
 }
 
+/// Brings `bytes` of global memory into L2 ahead of use (one 128-byte line
+/// per consumer thread, no register or wait).
+__device__ inline void PrefetchL2(const void* p, int bytes, int tid) {
+  const char* base = static_cast<const char*>(p);
+  for (int at = tid * 128; at < bytes; at += kConsumers * 128)
+    asm volatile("prefetch.global.L2 [%0];" ::"l"(base + at));
+}
+
 }  // namespace
 }  // namespace vx

@@ -747,22 +747,28 @@ __device__ void Consume(const DitPatchParams& p, unsigned char* smem,
       ++folds;
       return true;
     }
-    if (!WaitPeer(recv_bar, folds & 1u, c))
-      return false;
-    ++folds;
+    // This thread's residual value, loaded while the peer finishes.
+    std::size_t at = 0;
+    float h = 0.0f;
+    bool mine = false;
     if (tid < kRedFloats) {
       int feature, row;
       Decode(tid, 3, feature, row);
-      if (row < kRows) {
-        float sum = keep[0] + recv[tid];  // parts 0 and 1
-        if (parts == kDownParts) {
-          sum += keep[1];                  // part 2
-          sum += recv[kRedFloats + tid];   // part 3
-        }
-        const std::size_t at =
-            static_cast<std::size_t>(row) * kHidden + group * 16 + feature;
-        p.hidden[at] = __ldcg(p.hidden + at) + sum;
+      mine = row < kRows;
+      at = static_cast<std::size_t>(row) * kHidden + group * 16 + feature;
+      if (mine)
+        h = __ldcg(p.hidden + at);
+    }
+    if (!WaitPeer(recv_bar, folds & 1u, c))
+      return false;
+    ++folds;
+    if (mine) {
+      float sum = keep[0] + recv[tid];  // parts 0 and 1
+      if (parts == kDownParts) {
+        sum += keep[1];                 // part 2
+        sum += recv[kRedFloats + tid];  // part 3
       }
+      p.hidden[at] = h + sum;
     }
     ConsumerSync();
     publish(sync + kSyncHidden, 1u);
@@ -787,6 +793,15 @@ __device__ void Consume(const DitPatchParams& p, unsigned char* smem,
     for (int l = 0; l < p.layers; ++l) {
       const DitLayer layer = p.layer[l];
       const unsigned index = static_cast<unsigned>(e * p.layers + l);
+      // This layer's post norm and the next layer's input norm (or the
+      // final norm) into L2 now, so the norm stages wait on L2, not HBM.
+      PrefetchL2(layer.post_norm, kHidden * 2, tid);
+      if (l + 1 < p.layers) {
+        PrefetchL2(p.layer[l + 1].input_norm, kHidden * 2, tid);
+      } else {
+        PrefetchL2(p.final_norm, kHidden * 2, tid);
+        PrefetchL2(p.layer[0].input_norm, kHidden * 2, tid);
+      }
 
       // QKV: norm(hidden) x W_qkv -> qkv (fp32), then this CTA's attention
       // task when it has one.
@@ -893,15 +908,18 @@ __device__ void Consume(const DitPatchParams& p, unsigned char* smem,
       {
         for (int g = FirstUnit(pair, pairs, pair_base); g < kGroups; g += pairs) {
           float keep[kPairParts] = {0.f, 0.f};
-          for (int k = 0; k < kPairParts; ++k) {
-            const int part = rank + 2 * k;
-            if (!WaitCount(c, sync + kSyncAct + part, kGuPerChunk * (index + 1)))
-              return;
-            BfFragments(p.act, kInter, part * kChunk, warp, lane, frag);
-            FragProduct<kFormat>(acquire(), frag, warp, lane, red);
-            release();
-            reduce_part(k, keep[k]);
-          }
+          if (!WaitCount(c, sync + kSyncAct + rank, kGuPerChunk * (index + 1)) ||
+              !WaitCount(c, sync + kSyncAct + rank + 2, kGuPerChunk * (index + 1)))
+            return;
+          Fragments frag2;
+          BfFragments(p.act, kInter, rank * kChunk, warp, lane, frag);
+          BfFragments(p.act, kInter, (rank + 2) * kChunk, warp, lane, frag2);
+          FragProduct<kFormat>(acquire(), frag, warp, lane, red);
+          release();
+          reduce_part(0, keep[0]);
+          FragProduct<kFormat>(acquire(), frag2, warp, lane, red);
+          release();
+          reduce_part(1, keep[1]);
           if (!check() || !fold_pair(g, kDownParts, keep))
             return;
         }

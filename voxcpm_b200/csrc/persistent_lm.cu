@@ -557,6 +557,11 @@ __device__ void Consume(const LmStackParams& p, unsigned char* smem,
   for (int l = 0; l < p.layers; ++l) {
     const LmLayer layer = p.layer[l];
     const unsigned index = static_cast<unsigned>(l);
+    // This layer's post norm and the next layer's input norm (or the final
+    // norm) into L2 now, so the norm stages wait on L2, not HBM.
+    PrefetchL2(layer.post_norm, kHidden * 2, tid);
+    PrefetchL2(l + 1 < p.layers ? p.layer[l + 1].input_norm : p.final_norm,
+               kHidden * 2, tid);
 
     // QKV: norm(row) x W_qkv -> qkv (fp32).
     {
