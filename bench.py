@@ -499,22 +499,29 @@ def measure_generator(rank: int, context: int = 512, patch_replays: int = 50, st
     audio[-1] = 1
     feats = np.zeros((context, c.patch_size, c.feat_dim), np.float32)
     feats[-1] = rng.normal(0, 1, (c.patch_size, c.feat_dim))
-    t0 = time.perf_counter()
-    gen.Prefill(tokens, 1 - audio, audio, feats)
-    prefill_s = time.perf_counter() - t0
-    device_ms, wall_ms = [], []
-    for k in range(steps):
-        n = rng.normal(0, 1, (c.patch_size, c.feat_dim)).astype(np.float32)
-        a.record(stream)
-        t0 = time.perf_counter()
-        gen.Step(n, 10, 2.0)
-        wall_ms.append((time.perf_counter() - t0) * 1e3)
-        b.record(stream)
-        b.synchronize()
-        device_ms.append(a.elapsed_time(b))
+    noises = [rng.normal(0, 1, (c.patch_size, c.feat_dim)).astype(np.float32) for _ in range(steps)]
     warm = 2  # the first steps capture the step graph
-    step_ms = float(np.median(device_ms[warm:]))
-    step_wall_ms = float(np.median(wall_ms[warm:]))
+
+    def time_steps():
+        t0 = time.perf_counter()
+        gen.Prefill(tokens, 1 - audio, audio, feats)
+        prefill = time.perf_counter() - t0
+        device_ms, wall_ms = [], []
+        for n in noises:
+            a.record(stream)
+            t0 = time.perf_counter()
+            gen.Step(n, 10, 2.0)
+            wall_ms.append((time.perf_counter() - t0) * 1e3)
+            b.record(stream)
+            b.synchronize()
+            device_ms.append(a.elapsed_time(b))
+        return float(np.median(device_ms[warm:])), float(np.median(wall_ms[warm:])), prefill
+
+    step_ms, step_wall_ms, prefill_s = time_steps()
+    # The same steps from the same prompt on the per-kernel path.
+    gen.SetPersistent(False)
+    per_kernel_step_ms, _, _ = time_steps()
+    gen.SetPersistent(persistent)
     weight_bytes = gen.weight_bytes()
     gen.close()
     floor_us = DIT_PATCH_BYTES / (measured_peak()[0] * 1e9) * 1e6
@@ -526,9 +533,12 @@ def measure_generator(rank: int, context: int = 512, patch_replays: int = 50, st
                       "config": "12-layer DiT 1024 (16 q / 2 kv heads x 128), 22 rows, 10 Euler steps "
                                 "(9 evaluations), CFG 2.0, Q8_0 weights, one CUDA graph"},
         "step": {"ms_per_patch": step_ms, "wall_ms_per_patch": step_wall_ms,
+                 "per_kernel_ms_per_patch": per_kernel_step_ms,
                  "audio_s_per_s": PATCH_AUDIO_S / (step_wall_ms / 1e3), "rtf": step_wall_ms / 1e3 / PATCH_AUDIO_S,
                  "context": context, "steps": steps - warm, "kv_cache": "bf16",
                  "weight_bytes": weight_bytes, "prefill_s": prefill_s, "create_s": create_s,
+                 "path": "persistent DiT patch and one-row LM stacks" if persistent
+                         else "per-kernel sequence",
                  "config": "LM 28x2048 + residual LM 8x2048 + encoder 12x1024 + DiT 12x1024, Q8_0, "
                            "one CUDA graph per patch"},
     }
