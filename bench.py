@@ -47,8 +47,9 @@ Y_BYTES = ROWS * OUT * 2                    # 270,336 (bf16 output)
 STEP_BYTES = WEIGHT_BYTES + X_BYTES + Y_BYTES  # 13,729,792
 COPIES = 16
 GRAPH_LAUNCHES = 100
+E2E_STREAMS = 4  # streams the end-to-end steps rotate over (COPIES % E2E_STREAMS == 0)
 # Measured best plan for a stream of independent launches of this shape.
-STREAM_VARIANT, STREAM_SPLITS = 6, 3
+STREAM_VARIANT, STREAM_SPLITS = 9, 2
 METRIC = "Q8_0 skinny-product HBM GB/s (M=22, K=2048, N=6144, bf16 out)"
 
 
@@ -303,14 +304,14 @@ def run_ours(args, world, rank, local):
     # Stream plan: measured best for independent launches of this shape.
     stream_plan = _lib.WmmaPlan(STREAM_SPLITS, -(-(IN // 32) // STREAM_SPLITS), 0, 0, STREAM_VARIANT)
 
-    def launch(i, independent=False):
+    def launch(i, independent=False, x_at=x_ptr, on=s):
         if independent:
-            st = lib.vx_product_ex(_lib.WEIGHTS_Q8_TILES, x_ptr, tile_ptrs[i % COPIES], y_ptrs[i % COPIES],
+            st = lib.vx_product_ex(_lib.WEIGHTS_Q8_TILES, x_at, tile_ptrs[i % COPIES], y_ptrs[i % COPIES],
                                    _lib.OUT_BF16, ROWS, IN, OUT, _lib.PRODUCT_INDEPENDENT,
-                                   ctypes.byref(stream_plan), s)
+                                   ctypes.byref(stream_plan), on)
         else:
-            st = lib.vx_product(_lib.WEIGHTS_Q8_TILES, x_ptr, tile_ptrs[i % COPIES], y_ptrs[i % COPIES],
-                                _lib.OUT_BF16, ROWS, IN, OUT, 0, None, s)
+            st = lib.vx_product(_lib.WEIGHTS_Q8_TILES, x_at, tile_ptrs[i % COPIES], y_ptrs[i % COPIES],
+                                _lib.OUT_BF16, ROWS, IN, OUT, 0, None, on)
         if st != 0:
             raise RuntimeError(lib.vx_last_error().decode())
 
@@ -371,30 +372,50 @@ def run_ours(args, world, rank, local):
     if bits:
         raise RuntimeError(f"device wait timed out: bits {bits:#x}")
 
-    # e2e through the C ABI with host buffers: H2D x, product, D2H y per step.
+    # e2e through the C ABI with host buffers: every step copies x in from
+    # pinned memory, runs the product (vx_product, the default plan) and
+    # copies y out. Steps rotate over E2E_STREAMS streams, each with its own
+    # x and pinned y, so one step's copies overlap another step's product;
+    # a step and the next one on its stream share a weight copy's output.
+    lanes = [stream] + [torch.cuda.Stream(device) for _ in range(E2E_STREAMS - 1)]
+    x_lanes = [x] + [torch.empty_like(x) for _ in range(E2E_STREAMS - 1)]
     x_pinned = x_host.pin_memory()
-    y_pinned = torch.empty(ROWS, OUT, dtype=torch.bfloat16).pin_memory()
-    e2e_steps = min(max(args.steps // 100, 50), 5000)
+    y_pinned = [torch.empty(ROWS, OUT, dtype=torch.bfloat16).pin_memory() for _ in range(E2E_STREAMS)]
+    e2e_steps = min(max(args.steps // 100, 200), 5000)
 
     def e2e_step(i):
-        x.copy_(x_pinned, non_blocking=True)
-        launch(i)
-        y_pinned.copy_(ys[i % COPIES], non_blocking=True)
+        k = i % E2E_STREAMS
+        with torch.cuda.stream(lanes[k]):
+            x_lanes[k].copy_(x_pinned, non_blocking=True)
+            launch(i, x_at=x_lanes[k].data_ptr(), on=lanes[k].cuda_stream)
+            y_pinned[k].copy_(ys[i % COPIES], non_blocking=True)
 
-    with torch.cuda.stream(stream):
-        for i in range(10):
-            e2e_step(i)
-        stream.synchronize()
-        barrier(world)
-        e_start = torch.cuda.Event(enable_timing=True)
-        e_stop = torch.cuda.Event(enable_timing=True)
-        e_start.record(stream)
-        for i in range(e2e_steps):
-            e2e_step(i)
-        e_stop.record(stream)
-        stream.synchronize()
+    def join(into):
+        for lane in lanes:
+            if lane is not into:
+                ev = torch.cuda.Event()
+                ev.record(lane)
+                into.wait_event(ev)
+
+    for i in range(4 * E2E_STREAMS):
+        e2e_step(i)
+    torch.cuda.synchronize()
+    barrier(world)
+    e_start = torch.cuda.Event(enable_timing=True)
+    e_stop = torch.cuda.Event(enable_timing=True)
+    e_start.record(stream)
+    for lane in lanes[1:]:
+        lane.wait_event(e_start)
+    for i in range(e2e_steps):
+        e2e_step(i)
+    join(stream)
+    e_stop.record(stream)
+    torch.cuda.synchronize()
     e_ms = max_over_ranks(world, e_start.elapsed_time(e_stop))
     e2e_value = sum_over_ranks(world, STEP_BYTES * e2e_steps) / (e_ms / 1e3) / 1e9
+    y_check = ys[(e2e_steps - 1) % COPIES].cpu()
+    if not torch.equal(y_pinned[(e2e_steps - 1) % E2E_STREAMS], y_check):
+        raise RuntimeError("end-to-end output copy differs from the device output")
 
     clocks = sampler.summary()
     generator = measure_generator(rank)
@@ -431,7 +452,8 @@ def run_ours(args, world, rank, local):
         "cpu_baseline": {"value": cpu_value, "unit": "GB/s", "cores": os.cpu_count() or 1,
                          "kind": "port", "sample": cpu_desc},
         "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": X_BYTES,
-                "d2h_bytes_per_step": Y_BYTES, "steps": e2e_steps},
+                "d2h_bytes_per_step": Y_BYTES, "steps": e2e_steps, "streams": E2E_STREAMS,
+                "api": "vx_product (default plan), pinned host x in and y out every step"},
         "gpu_launches": 2 * args.steps,
         "clocks": clocks,
         **generator,

@@ -176,6 +176,13 @@ VX_API vx_status vx_product_ex(int format, const uint16_t* x, const void* w,
 /* Programmatic dependent launch for every kernel of the library (default on).
  * No reference counterpart (HIP has none). */
 VX_API void vx_set_programmatic_launch(int enabled);
+/* Whether the planner gives Q8_0 products of 9..32 rows to the tensor-core
+ * (tcgen05) kernel, plan variant VX_TENSOR_CORE_VARIANT, or (default) to the
+ * mma.sync kernels. A plan with that variant runs it either way. No reference counterpart (the reference has one
+ * WMMA kernel, kernels/wmma_products.hip:139-296). */
+#define VX_TENSOR_CORE_VARIANT 16
+VX_API void vx_set_tensor_core_products(int enabled);
+VX_API int vx_tensor_core_products(void);
 /* Number of product kernel shapes and the shape of one (benchmarks). */
 VX_API int vx_product_variants(void);
 VX_API void vx_product_variant_shape(int variant, int* warps, int* groups,

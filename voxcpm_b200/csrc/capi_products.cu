@@ -206,6 +206,12 @@ void vx_set_programmatic_launch(int enabled) {
   vx::SetProgrammaticLaunch(enabled != 0);
 }
 
+void vx_set_tensor_core_products(int enabled) {
+  vx::SetTensorCoreProducts(enabled != 0);
+}
+
+int vx_tensor_core_products(void) { return vx::TensorCoreProducts() ? 1 : 0; }
+
 int vx_product_variants(void) { return vx::NumProductVariants(); }
 
 void vx_product_variant_shape(int variant, int* warps, int* groups,

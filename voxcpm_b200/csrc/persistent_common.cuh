@@ -47,11 +47,6 @@ __device__ inline bool ConsumerSyncOr(bool value) {
   return result != 0;
 }
 
-__device__ inline void MbarArrive(std::uint64_t* bar) {
-  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(SmemAddr(bar))
-               : "memory");
-}
-
 /// Arrives on the mbarrier at shared::cluster address `addr` (a peer's),
 /// releasing this thread's prior writes at cluster scope.
 __device__ inline void MbarArriveCluster(std::uint32_t addr) {

@@ -85,6 +85,14 @@ constexpr VariantShape kVariants[] = {
     {8, 2, 2, 2, 4},   // 5: 128 rows, 8 warps of 2 groups (2 ways)
     {16, 1, 1, 2, 4},  // 6: 256 rows, 16 warps
     {4, 4, 1, 2, 3},   // 7: 64 rows, 16 warps (4 ways)
+    // Eight-block stages: one 4.3 KB (Q8) copy per group and stage. A TMA
+    // request costs the SM about 30-40 ns to issue whatever its size, so
+    // two-block stages (1.1 KB copies) cap a CTA near 30 GB/s.
+    {8, 1, 1, 8, 2},   // 8: 128 rows, 8 warps
+    {16, 1, 1, 8, 2},  // 9: 256 rows, 16 warps
+    {16, 1, 2, 8, 2},  // 10: 256 rows, 8 warps of 2 groups
+    {8, 1, 2, 8, 2},   // 11: 128 rows, 4 warps of 2 groups
+    {8, 2, 1, 8, 2},   // 12: 128 rows, 16 warps (2 ways)
 };
 constexpr int kNumVariants = sizeof(kVariants) / sizeof(kVariants[0]);
 
@@ -436,7 +444,8 @@ struct VariantRow {
 };
 
 template <int kFormat, int kNTiles>
-using Row = VariantRow<kFormat, kNTiles, 0, 1, 2, 3, 4, 5, 6, 7>;
+using Row = VariantRow<kFormat, kNTiles, 0, 1, 2, 3, 4, 5, 6, 7, 8, 9, 10, 11,
+                       12>;
 
 KernelFn Lookup(int format, int ntiles, int variant) {
   static const KernelFn* table[3][4] = {
@@ -448,6 +457,7 @@ KernelFn Lookup(int format, int ntiles, int variant) {
 }
 
 std::atomic<bool> g_programmatic{true};
+std::atomic<bool> g_tensor_core{false};
 
 int SmCount() {
   static int count = [] {
@@ -484,6 +494,8 @@ Footprint FootprintOf(int format, int variant, int ntiles,
 
 void SetProgrammaticLaunch(bool enabled) { g_programmatic = enabled; }
 bool ProgrammaticLaunch() { return g_programmatic; }
+void SetTensorCoreProducts(bool enabled) { g_tensor_core = enabled; }
+bool TensorCoreProducts() { return g_tensor_core; }
 
 int NumProductVariants() { return kNumVariants; }
 
@@ -546,6 +558,15 @@ ProductPlan PlanProduct(WeightFormat format, std::size_t rows, std::size_t in,
   ProductPlan best;
   if (rows == 0 || in == 0 || out == 0 || in % kTileColumns != 0)
     return best;
+  // Q8_0 tiles with 9..32 rows: the tensor-core kernel (the mma.sync tile
+  // math needs three or four MMAs per 16 x 16 step there).
+  if (format == WeightFormat::kQ8Tiles && target_ctas == 0 &&
+      g_tensor_core && rows >= kTensorCoreMinRows &&
+      rows <= kMaxProductRows) {
+    const ProductPlan tc = PlanTensorCoreProduct(rows, in, out, SmCount());
+    if (tc.variant >= 0)
+      return tc;
+  }
   const int k_blocks = static_cast<int>(in / kTileColumns);
   if (target_ctas == 0) {
     const int rows_class = rows == 1 ? 0 : rows <= 8 ? 1 : 2;
@@ -634,6 +655,15 @@ int LaunchProduct(WeightFormat format, const std::uint16_t* x, const void* w,
   ProductPlan plan = plan_in != nullptr && plan_in->variant >= 0
                          ? *plan_in
                          : PlanProduct(format, rows, in, out, 0);
+  if (plan.variant == kTensorCoreVariant) {
+    if (format == WeightFormat::kQ8Tiles)
+      return LaunchTensorCoreProduct(x, w, y, y_bf16, rows, in, out,
+                                     accumulate, plan, stream, independent,
+                                     g_programmatic);
+    // A tensor-core plan given for bf16 weights (the reference's PlanWmma
+    // serves both formats): the planner's mma.sync plan for this format.
+    plan = PlanProduct(format, rows, in, out, 0);
+  }
   if (plan.variant < 0 || plan.variant >= kNumVariants || plan.splits < 1 ||
       plan.splits > 8 || plan.blocks_per_split < 1 ||
       plan.blocks_per_split * 32 > kMaxSliceColumns ||

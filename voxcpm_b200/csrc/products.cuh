@@ -50,6 +50,25 @@ struct ProductPlan {
   int blocks_per_split = 0;
 };
 
+/// Plan variant of the tensor-core (tcgen05) kernel for Q8_0 tiles
+/// (products_tc.cu): 128 weight rows per CTA, at most
+/// kTensorCoreMaxBlocks 32-column blocks of the reduction per split.
+constexpr int kTensorCoreVariant = 16;
+constexpr int kTensorCoreMaxBlocks = 24;
+/// Fewest activation rows the planner gives to the tensor-core kernel.
+constexpr int kTensorCoreMinRows = 9;
+
+/// The tensor-core plan for Q8_0 tiles: about one CTA per SM (`sms`).
+ProductPlan PlanTensorCoreProduct(std::size_t rows, std::size_t in,
+                                  std::size_t out, int sms);
+/// Launches the tensor-core kernel with `plan` (variant
+/// kTensorCoreVariant). Returns kOk, kUnsupported or kCudaError.
+int LaunchTensorCoreProduct(const std::uint16_t* x, const void* w, float* y,
+                            std::uint16_t* y_bf16, std::size_t rows,
+                            std::size_t in, std::size_t out, bool accumulate,
+                            const ProductPlan& plan, cudaStream_t stream,
+                            bool independent, bool programmatic);
+
 /// The plan for a product (target_ctas 0: the planner's choice; otherwise
 /// about that many CTAs).
 ProductPlan PlanProduct(WeightFormat format, std::size_t rows, std::size_t in,
@@ -69,6 +88,10 @@ int LaunchProduct(WeightFormat format, const std::uint16_t* x, const void* w,
 /// Whether kernels are launched with programmatic dependent launch.
 void SetProgrammaticLaunch(bool enabled);
 bool ProgrammaticLaunch();
+/// Whether the planner gives Q8_0 products of 9..32 rows to the
+/// tensor-core kernel or (default) to the mma.sync kernels.
+void SetTensorCoreProducts(bool enabled);
+bool TensorCoreProducts();
 
 int NumProductVariants();
 /// Warps, row groups per warp, blocks per stage, stages of a variant.

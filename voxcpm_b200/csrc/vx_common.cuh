@@ -91,6 +91,12 @@ __device__ inline void MbarArriveExpectTx(std::uint64_t* bar, unsigned bytes) {
       : "memory");
 }
 
+/// Arrives once on `bar` (no transaction bytes).
+__device__ inline void MbarArrive(std::uint64_t* bar) {
+  asm volatile("mbarrier.arrive.shared::cta.b64 _, [%0];" ::"r"(SmemAddr(bar))
+               : "memory");
+}
+
 /// Tests phase `parity` of `bar`; a thread whose phase is not complete is
 /// suspended by the hardware until it completes or `suspend_ns` pass, so a
 /// waiting warp takes no issue slots from the warps that compute.

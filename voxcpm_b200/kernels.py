@@ -145,8 +145,36 @@ def DeviceError() -> int:
     return bits.value
 
 
+def ProductEx(fmt: int, x, w, y, rows, columns, out, flags: int = 0, plan=None, stream=None) -> bool:
+    """vx_product_ex: `flags` of PRODUCT_ACCUMULATE and PRODUCT_INDEPENDENT."""
+    if y.dtype == torch.float32:
+        out_dtype = _lib.OUT_F32
+    elif y.dtype == torch.bfloat16:
+        out_dtype = _lib.OUT_BF16
+    else:
+        raise ValueError("y must be float32 or bfloat16")
+    return check(
+        load().vx_product_ex(fmt, _ptr(x), _ptr(w), _ptr(y), out_dtype, rows, columns, out,
+                             int(flags), _plan_arg(plan), _stream(stream)),
+        unsupported_ok=True,
+    )
+
+
 def SetProgrammaticLaunch(enabled: bool) -> None:
     load().vx_set_programmatic_launch(int(enabled))
+
+
+TENSOR_CORE_VARIANT = 16  # VX_TENSOR_CORE_VARIANT
+
+
+def SetTensorCoreProducts(enabled: bool) -> None:
+    """Q8_0 products of 9..32 rows planned onto the tcgen05 kernel, or
+    (default) onto the mma.sync kernels."""
+    load().vx_set_tensor_core_products(int(enabled))
+
+
+def TensorCoreProducts() -> bool:
+    return bool(load().vx_tensor_core_products())
 
 
 def ProductVariants() -> list[tuple[int, int, int, int]]:
