@@ -93,6 +93,8 @@ constexpr VariantShape kVariants[] = {
     {16, 1, 2, 8, 2},  // 10: 256 rows, 8 warps of 2 groups
     {8, 1, 2, 8, 2},   // 11: 128 rows, 4 warps of 2 groups
     {8, 2, 1, 8, 2},   // 12: 128 rows, 16 warps (2 ways)
+    {16, 1, 1, 8, 1},  // 13: 256 rows, 16 warps, one stage in flight
+    {16, 1, 1, 4, 2},  // 14: 256 rows, 16 warps, four-block stages
 };
 constexpr int kNumVariants = sizeof(kVariants) / sizeof(kVariants[0]);
 
@@ -445,7 +447,7 @@ struct VariantRow {
 
 template <int kFormat, int kNTiles>
 using Row = VariantRow<kFormat, kNTiles, 0, 1, 2, 3, 4, 5, 6, 7, 8, 9, 10, 11,
-                       12>;
+                       12, 13, 14>;
 
 KernelFn Lookup(int format, int ntiles, int variant) {
   static const KernelFn* table[3][4] = {

@@ -12,27 +12,29 @@
 // Here one thread issues 128 x N x 16 tcgen05 MMAs, so the SM's issue slots
 // go to the exact dequantisation only.
 //
-// One CTA owns 128 weight rows (8 tile groups) over a slice of at most 24
-// blocks of the reduction; the CTAs of a thread-block cluster take
+// One CTA per SM owns 128 weight rows (8 tile groups) over a slice of at
+// most 24 blocks of the reduction; the CTAs of a thread-block cluster take
 // consecutive slices of the same rows and add up in cluster-rank order
 // through distributed shared memory (the reference's ordered split sum,
-// kernels/wmma_products.hip:249-295). Per CTA:
-// - a producer warp streams the rows' tiles, two blocks per stage, into a
-//   ring of 1-D TMA bulk copies (L2 evict-first);
-// - eight worker warps, two per TMEM lane quarter, take alternate blocks:
-//   each thread owns one weight row, turns its 32 biased int8 values into
-//   bf16 exactly, and stores them into a TMEM A slot (tcgen05.st);
-// - an MMA warp issues D[slot] = A[slot] x x_block (two K=16 steps, fresh
-//   accumulator) and commits to the slot's mbarrier;
-// - the worker reads the block sums back (tcgen05.ld) and adds them into its
-//   registers with the row's fp16 scale;
-// - the producer also brings the CTA's slice of x in with 2-D TMA, one box
-//   of 8 columns x 32 rows per copy, which lands as the MMA's B operand in
-//   the no-swizzle K-major layout (8-row x 16-byte core matrices); rows past
-//   the activation rows are zero-filled by the copy.
-// Weights do not depend on earlier kernels, so the first ring of them
-// streams (and is converted) before the programmatic-launch wait; x is
-// read after it.
+// kernels/wmma_products.hip:249-295). Per CTA, a three-stage pipeline over
+// ten TMEM slots (A: 16 columns, block sums: 32 columns each):
+// - a producer warp brings the whole weight slice in with one 1-D TMA bulk
+//   copy per tile group and 8-block part, from eight lanes at once (L2
+//   evict-first), and x, after the programmatic-launch wait, with one 3-D
+//   tensor-map copy per part that lands as the MMA's B operand in the
+//   no-swizzle K-major layout (8-row x 16-byte core matrices; rows past the
+//   activation rows are zero-filled by the copy);
+// - three conversion teams of four warps (one warp per TMEM lane quarter)
+//   take every third block: each thread owns one weight row, turns its 32
+//   biased int8 values into bf16 exactly and stores them into the block's
+//   TMEM A slot (tcgen05.st); the team meets at a named barrier and one lane
+//   issues D[slot] = A[slot] x x_block (two K=16 steps, fresh accumulator),
+//   committing to the slot's mbarrier;
+// - two read teams take alternate blocks: they read the block sums back
+//   (tcgen05.ld), free the slot and add the sums into their rows'
+//   accumulators with the rows' fp16 scales.
+// A TMA request or a tcgen05.mma costs its issuing thread 30-40 ns whatever
+// its size: hence few, large copies and one MMA issuer per team.
 #include "products.cuh"
 #include "product_math.cuh"
 #include "tcgen05.cuh"
@@ -49,29 +51,33 @@ namespace {
 
 constexpr int kTcGroups = 8;                  // 16-row tile groups per CTA
 constexpr int kTcRows = 16 * kTcGroups;       // = the MMA's M (TMEM lanes)
-constexpr int kTcStage = 2;                   // blocks per ring stage
-constexpr int kTcRing = 5;                    // ring stages
-constexpr int kTcSlots = 5;                   // TMEM A / accumulator slots
-constexpr int kTcWorkerWarps = 8;
+constexpr int kTcPartBlocks = 8;              // blocks per weight / x copy
+constexpr int kTcParts = kTensorCoreMaxBlocks / kTcPartBlocks;
+constexpr int kTcSlots = 10;                  // TMEM A / accumulator slots
+constexpr int kTcConvertTeams = 3;            // teams of four warps: int8 -> TMEM
+constexpr int kTcReadTeams = 2;               // teams of four warps: sums back
+constexpr int kTcConvertWarps = 4 * kTcConvertTeams;
+constexpr int kTcWorkerWarps = kTcConvertWarps + 4 * kTcReadTeams;
 constexpr int kTcProducerWarp = kTcWorkerWarps;
-constexpr int kTcMmaWarp = kTcWorkerWarps + 1;
-constexpr int kTcThreads = 32 * (kTcWorkerWarps + 2);
+constexpr int kTcThreads = 32 * (kTcWorkerWarps + 1);
 constexpr int kTcXRows = 32;                  // B rows staged (M <= 32)
 constexpr int kTcXChunkBytes = kTcXRows * 16; // 8 K-values of all 32 rows
-constexpr int kTcXBytes = kTcXRows * kTensorCoreMaxBlocks * 32 * 2;
-constexpr int kTcStageBytes = kTcGroups * kTcStage * kQ8TileBytes;
-constexpr int kTcRingBytes = kTcRing * kTcStageBytes;
-constexpr int kTcBarriers = 2 * kTcRing + 3 * kTcSlots + 1;
-constexpr int kTcSmemBytes = kTcXBytes + kTcRingBytes + kTcBarriers * 8 + 16;
-constexpr std::uint32_t kTcColumns = 256;     // two CTAs fit on one SM
+constexpr int kTcXPartBytes = kTcPartBlocks * 4 * kTcXChunkBytes;
+constexpr int kTcXBytes = kTcParts * kTcXPartBytes;
+constexpr int kTcWeightBytes = kTcGroups * kTensorCoreMaxBlocks * kQ8TileBytes;
+constexpr int kTcBarriers = 2 * kTcParts + 2 * kTcSlots;
+constexpr int kTcSmemBytes = kTcXBytes + kTcWeightBytes + kTcBarriers * 8 + 16;
+constexpr std::uint32_t kTcColumns = 512;     // one CTA per SM
 constexpr int kTcDColumn = 0;                 // slot t: columns 32t..32t+31
 constexpr int kTcAColumn = 32 * kTcSlots;     // slot t: columns +16t..+15
 
+static_assert(kTensorCoreMaxBlocks % kTcPartBlocks == 0, "whole parts");
 static_assert(kTcAColumn + 16 * kTcSlots <= static_cast<int>(kTcColumns),
               "TMEM slots exceed the allocation");
-static_assert(2 * kTcRows * 32 * 4 <= kTcRingBytes,
-              "the reduction buffers reuse the ring");
-static_assert(kTcSmemBytes <= 113 * 1024, "two CTAs per SM");
+static_assert(kTcReadTeams * kTcRows * 32 * 4 <= kTcWeightBytes,
+              "the reduction buffers reuse the weight area");
+static_assert(kTcSmemBytes > 114 * 1024 && kTcSmemBytes <= 227 * 1024,
+              "exactly one CTA per SM, which owns all 512 TMEM columns");
 
 struct TcArgs {
   const Bf16* x;
@@ -86,6 +92,7 @@ struct TcArgs {
   int blocks_per_split;
   int accumulate;
   int wait;
+  int x_boxes;      // 1: one 3-D box per part; 32: 2-D boxes of 8 columns
   unsigned* error;  // the library's device error word
 };
 
@@ -97,12 +104,25 @@ __device__ inline bool WarpWait(std::uint64_t* bar, unsigned parity,
   return __all_sync(0xFFFFFFFFu, ok) != 0;
 }
 
+/// Named barrier of one conversion team (its 128 threads, id 1 + team)
+/// that ands `value` over them.
+__device__ inline bool TeamAll(int team, bool value) {
+  unsigned result;
+  asm volatile(
+      "{\n.reg .pred p, q;\nsetp.ne.u32 q, %1, 0;\n"
+      "bar.red.and.pred p, %2, 128, q;\nselp.u32 %0, 1, 0, p;\n}"
+      : "=r"(result)
+      : "r"(static_cast<unsigned>(value)), "r"(team + 1)
+      : "memory");
+  return result != 0;
+}
+
 __device__ inline float4 LoadFloat4(const float* p) {
   return *reinterpret_cast<const float4*>(p);
 }
 
 template <int kRead>
-__global__ void __launch_bounds__(kTcThreads, 2)
+__global__ void __launch_bounds__(kTcThreads, 1)
     TcProductKernel(const TcArgs p, const __grid_constant__ CUtensorMap x_map) {
   constexpr int kN = kRead <= 16 ? 16 : 32;  // the MMA's N (x rows, padded)
   constexpr std::uint32_t kInstruction = MmaBf16Descriptor(kTcRows, kN);
@@ -113,35 +133,32 @@ __global__ void __launch_bounds__(kTcThreads, 2)
   const int panel = static_cast<int>(blockIdx.x) / p.splits;
   const int first = split * p.blocks_per_split;
   const int nb = max(0, min(p.k_blocks - first, p.blocks_per_split));
+  const int parts = (nb + kTcPartBlocks - 1) / kTcPartBlocks;
   const int group0 = panel * kTcGroups;
   const int my_groups = min(kTcGroups, (p.n + 15) / 16 - group0);
 
-  unsigned char* xs = smem;
-  unsigned char* ring = smem + kTcXBytes;
-  std::uint64_t* wfull = reinterpret_cast<std::uint64_t*>(ring + kTcRingBytes);
-  std::uint64_t* wempty = wfull + kTcRing;
-  std::uint64_t* aready = wempty + kTcRing;
-  std::uint64_t* dfull = aready + kTcSlots;
+  unsigned char* xs = smem;                 // [part][32 chunks][32 rows][16 B]
+  unsigned char* wts = smem + kTcXBytes;    // [group][nb blocks] tiles
+  std::uint64_t* wfull = reinterpret_cast<std::uint64_t*>(wts + kTcWeightBytes);
+  std::uint64_t* xfull = wfull + kTcParts;
+  std::uint64_t* dfull = xfull + kTcParts;
   std::uint64_t* tfree = dfull + kTcSlots;
-  std::uint64_t* xready = tfree + kTcSlots;
-  std::uint32_t* tmem_word = reinterpret_cast<std::uint32_t*>(xready + 1);
+  std::uint32_t* tmem_word = reinterpret_cast<std::uint32_t*>(tfree + kTcSlots);
   volatile std::uint32_t* aborted = tmem_word + 1;
 
   if (threadIdx.x == 0) {
-    for (int i = 0; i < kTcRing; ++i) {
-      MbarInit(&wfull[i], 1);
-      MbarInit(&wempty[i], kTcWorkerWarps);
+    for (int q = 0; q < kTcParts; ++q) {
+      MbarInit(&wfull[q], 1);
+      MbarInit(&xfull[q], 1);
     }
     for (int t = 0; t < kTcSlots; ++t) {
-      MbarInit(&aready[t], 4);
       MbarInit(&dfull[t], 1);
       MbarInit(&tfree[t], 4);
     }
-    MbarInit(xready, 1);
     *aborted = 0;
     FenceMbarInit();
   }
-  if (warp == kTcMmaWarp) {
+  if (warp == kTcProducerWarp) {
     TmemAlloc(tmem_word, kTcColumns);
     TmemRelinquish();
   }
@@ -151,133 +168,103 @@ __global__ void __launch_bounds__(kTcThreads, 2)
   const std::uint32_t tmem = *tmem_word;
   GridLaunchDependents();
 
-  const bool worker = warp < kTcWorkerWarps;
   const int quarter = warp & 3;
-  const int half = (warp >> 2) & 1;
   const int row = 32 * quarter + lane;  // CTA-local weight row (workers)
+  const bool reader = warp >= kTcConvertWarps && warp < kTcWorkerWarps;
+  const int read_team = (warp - kTcConvertWarps) >> 2;
   float acc[kRead];
 #pragma unroll
   for (int c = 0; c < kRead; ++c)
     acc[c] = 0.0f;
 
   if (warp == kTcProducerWarp) {
+    // Weights: one copy per group and part, from eight lanes at once (a TMA
+    // request costs its issuing thread some 30-40 ns).
     if (lane == 0) {
+      for (int q = 0; q < parts; ++q)
+        MbarArriveExpectTx(&wfull[q],
+                           my_groups * min(kTcPartBlocks, nb - kTcPartBlocks * q) *
+                               kQ8TileBytes);
+    }
+    __syncwarp();
+    if (lane < my_groups) {
       const std::uint64_t policy = PolicyEvictFirst();
-      const int stages = (nb + kTcStage - 1) / kTcStage;
-      int issued = 0;
-      auto issue = [&](int i) {
-        const int slot = i % kTcRing;
-        const int b0 = first + i * kTcStage;
-        const int count = min(kTcStage, first + nb - b0);
-        MbarArriveExpectTx(&wfull[slot], my_groups * count * kQ8TileBytes);
-        for (int g = 0; g < my_groups; ++g)
-          BulkLoad(ring + slot * kTcStageBytes + g * kTcStage * kQ8TileBytes,
-                   p.w + (static_cast<std::size_t>(group0 + g) * p.k_blocks +
-                          b0) * kQ8TileBytes,
-                   count * kQ8TileBytes, &wfull[slot], policy);
-      };
-      // The first ring of weights before the wait for the preceding kernel.
-      for (; issued < min(stages, kTcRing); ++issued)
-        issue(issued);
-      if (p.wait)
-        GridDependencyWait();
-      // x: four boxes of 8 columns per block, 32 rows each (rows past
-      // p.m read as zeros).
-      MbarArriveExpectTx(xready, 4 * nb * kTcXChunkBytes);
-      for (int c = 0; c < 4 * nb; ++c)
-        TmaLoad2D(xs + c * kTcXChunkBytes, &x_map, first * 32 + 8 * c, 0,
-                  xready);
-      for (; issued < stages && *aborted == 0; ++issued) {
-        const int slot = issued % kTcRing;
-        if (!MbarWaitBounded(&wempty[slot], (issued / kTcRing - 1) & 1,
-                             p.error, kErrWeightWait)) {
-          *aborted = 1;
-          break;
-        }
-        issue(issued);
+      for (int q = 0; q < parts; ++q) {
+        const int b0 = kTcPartBlocks * q;
+        const int count = min(kTcPartBlocks, nb - b0);
+        BulkLoad(wts + (lane * nb + b0) * kQ8TileBytes,
+                 p.w + (static_cast<std::size_t>(group0 + lane) * p.k_blocks +
+                        first + b0) * kQ8TileBytes,
+                 count * kQ8TileBytes, &wfull[q], policy);
       }
-      // Copies still in flight land before the shared memory is released.
-      (void)MbarWaitBounded(xready, 0, p.error, kErrDrainWait, 100000000ull);
-      for (int i = max(0, issued - kTcRing); i < issued; ++i)
-        (void)MbarWaitBounded(&wfull[i % kTcRing], (i / kTcRing) & 1,
-                              p.error, kErrDrainWait, 100000000ull);
     }
-    __syncwarp();
-  } else if (warp == kTcMmaWarp) {
+    // x after the preceding kernel (which may write it) has finished.
+    if (p.wait)
+      GridDependencyWait();
     if (lane == 0) {
-      int issued = 0;
-      if (!MbarWaitBounded(xready, 0, p.error,
-                           kErrActivationWait))
-        *aborted = 1;
-      for (int b = 0; b < nb && *aborted == 0; ++b) {
-        const int t = b % kTcSlots;
-        if (!MbarWaitBounded(&aready[t], (b / kTcSlots) & 1,
-                             p.error, kErrWeightWait)) {
-          *aborted = 1;
-          break;
-        }
-        TcFenceAfter();
-        const std::uint32_t a = tmem + kTcAColumn + 16 * t;
-        const std::uint32_t d = tmem + kTcDColumn + 32 * t;
-#pragma unroll
-        for (int s = 0; s < 2; ++s)
-          MmaBf16TmemA(d, a + 8 * s,
-                       SmemDescriptorNoSwizzle(
-                           xs + (4 * b + 2 * s) * kTcXChunkBytes,
-                           kTcXChunkBytes, 128),
-                       kInstruction, static_cast<std::uint32_t>(s));
-        MmaCommit(&dfull[t]);
-        ++issued;
-      }
-      // Every MMA has completed before the columns are freed.
-      if (issued > 0)
-        (void)MbarWaitBounded(&dfull[(issued - 1) % kTcSlots],
-                              ((issued - 1) / kTcSlots) & 1,
-                              p.error, kErrDrainWait,
-                              100000000ull);
+      for (int q = 0; q < parts; ++q)
+        MbarArriveExpectTx(&xfull[q], kTcXPartBytes);
     }
     __syncwarp();
-  } else {
+    if (p.x_boxes == 1) {
+      if (lane < parts)
+        TmaLoad3D(xs + lane * kTcXPartBytes, &x_map, 0, 0,
+                  (first + kTcPartBlocks * lane) * 4, &xfull[lane]);
+    } else {
+      for (int q = 0; q < parts; ++q)
+        TmaLoad2D(xs + q * kTcXPartBytes + lane * kTcXChunkBytes, &x_map,
+                  (first + kTcPartBlocks * q) * 32 + 8 * lane, 0, &xfull[q]);
+    }
+    // Copies still in flight land before the shared memory is released.
+    if (lane == 0) {
+      for (int q = 0; q < parts; ++q) {
+        (void)MbarWaitBounded(&wfull[q], 0, p.error, kErrDrainWait,
+                              100000000ull);
+        (void)MbarWaitBounded(&xfull[q], 0, p.error, kErrDrainWait,
+                              100000000ull);
+      }
+    }
+    __syncwarp();
+  } else if (warp < kTcConvertWarps) {
+    // Conversion team `team` takes blocks team, team + 3, ...: each thread
+    // turns its row's 32 values into bf16 in the block's TMEM A slot, the
+    // team meets, and its issuer sends the block's two K=16 MMAs.
+    const int team = warp >> 2;
     const int g = row >> 4;
     const int r = row & 15;
     const bool live = g < my_groups;
-    const int scale_offset = 512 + (r < 8 ? 4 * r : 4 * (r - 8) + 2);
     // Rows 4..7 of each 8 read their two 16-byte halves in the other order,
     // so the eight lanes of a shared-memory phase hit distinct banks.
     const int swap = (r >> 2) & 1;
     const std::uint32_t lanes = static_cast<std::uint32_t>(32 * quarter) << 16;
-    int prev = -1;
-    float prev_scale = 0.0f;
-    for (int b = half; b < nb + 2; b += 2) {
+    const bool issuer = quarter == 0 && lane == 0;
+    int w_parts_ready = 0;  // parts of the weights known to have landed
+    int x_parts_ready = 0;  // issuer: parts of x known to have landed
+    for (int b = team; b < nb; b += kTcConvertTeams) {
       // Warp-uniform view of the abort flag (the .sync.aligned tcgen05
       // operations below need the whole warp).
       const bool quit = __shfl_sync(0xFFFFFFFFu, *aborted, 0) != 0u;
-      const bool has = b < nb && !quit;
-      float scale = 0.0f;
+      const int t = b % kTcSlots;
       bool stored = false;
-      if (has) {
-        const int i = b / kTcStage;
-        const int rs = i % kTcRing;
-        if (!WarpWait(&wfull[rs], (i / kTcRing) & 1, p.error, kErrWeightWait)) {
+      if (!quit) {
+        bool ok = true;
+        for (; w_parts_ready <= b / kTcPartBlocks && ok; ++w_parts_ready)
+          ok = WarpWait(&wfull[w_parts_ready], 0, p.error, kErrWeightWait);
+        if (ok && b >= kTcSlots)
+          ok = WarpWait(&tfree[t], (b / kTcSlots - 1) & 1, p.error,
+                        kErrWeightWait);
+        if (!ok) {
           *aborted = 1;
         } else {
-          const unsigned char* tile =
-              ring + rs * kTcStageBytes +
-              (g * kTcStage + (b % kTcStage)) * kQ8TileBytes;
+          const unsigned char* tile = wts + (g * nb + b) * kQ8TileBytes;
           uint4 c0 = *reinterpret_cast<const uint4*>(tile + 32 * r + 16 * swap);
           uint4 c1 =
               *reinterpret_cast<const uint4*>(tile + 32 * r + 16 * (swap ^ 1));
-          const std::uint16_t bits =
-              *reinterpret_cast<const std::uint16_t*>(tile + scale_offset);
-          __syncwarp();
-          if (lane == 0)
-            MbarArrive(&wempty[rs]);
           if (swap) {
-            const uint4 t = c0;
+            const uint4 tmp = c0;
             c0 = c1;
-            c1 = t;
+            c1 = tmp;
           }
-          scale = live ? HalfBitsToFloat(bits) : 0.0f;
           std::uint32_t a[16];
           DequantWord(c0.x, a[0], a[1]);
           DequantWord(c0.y, a[2], a[3]);
@@ -292,85 +279,123 @@ __global__ void __launch_bounds__(kTcThreads, 2)
             for (int j = 0; j < 16; ++j)
               a[j] = 0u;
           }
-          const int t = b % kTcSlots;
-          if (b >= kTcSlots &&
-              !WarpWait(&tfree[t], (b / kTcSlots - 1) & 1, p.error,
-                        kErrWeightWait)) {
-            *aborted = 1;
-          } else {
-            TmemStore16(tmem + lanes + kTcAColumn + 16 * t, a);
-            TcFenceBefore();
-            __syncwarp();
-            if (lane == 0)
-              MbarArrive(&aready[t]);
-            stored = true;
-          }
+          TmemStore16(tmem + lanes + kTcAColumn + 16 * t, a);
+          TcFenceBefore();
+          stored = true;
         }
       }
-      if (prev >= 0 && !quit) {
-        const int t = prev % kTcSlots;
-        if (!WarpWait(&dfull[t], (prev / kTcSlots) & 1, p.error,
-                      kErrWeightWait)) {
+      // Every iteration meets, so the barrier counts match.
+      const bool all_stored = TeamAll(team, stored);
+      if (all_stored && issuer) {
+        bool ok = true;
+        for (; x_parts_ready <= b / kTcPartBlocks && ok; ++x_parts_ready)
+          ok = MbarWaitBounded(&xfull[x_parts_ready], 0, p.error,
+                               kErrActivationWait);
+        if (!ok) {
           *aborted = 1;
         } else {
           TcFenceAfter();
-          std::uint32_t d[kRead];
-          TmemLoad<kRead>(tmem + lanes + kTcDColumn + 32 * t, d);
-          TcFenceBefore();
-          __syncwarp();
-          if (lane == 0)
-            MbarArrive(&tfree[t]);
 #pragma unroll
-          for (int c = 0; c < kRead; c += 2) {
-            const float2 v = Fma2(make_float2(prev_scale, prev_scale),
-                                  make_float2(__uint_as_float(d[c]),
-                                              __uint_as_float(d[c + 1])),
-                                  make_float2(acc[c], acc[c + 1]));
-            acc[c] = v.x;
-            acc[c + 1] = v.y;
-          }
+          for (int s = 0; s < 2; ++s)
+            MmaBf16TmemA(tmem + kTcDColumn + 32 * t,
+                         tmem + kTcAColumn + 16 * t + 8 * s,
+                         SmemDescriptorNoSwizzle(
+                             xs + (4 * b + 2 * s) * kTcXChunkBytes,
+                             kTcXChunkBytes, 128),
+                         kInstruction, static_cast<std::uint32_t>(s));
+          MmaCommit(&dfull[t]);
         }
       }
-      prev = stored ? b : -1;
-      prev_scale = scale;
+      __syncwarp();
+    }
+  } else {
+    // Read team `read_team` takes blocks read_team, read_team + 2, ...: it
+    // waits for the block's sums, frees the slot and adds them into the
+    // rows' accumulators with the rows' fp16 scales (still in shared
+    // memory with the weights).
+    const int g = row >> 4;
+    const int r = row & 15;
+    const bool live = g < my_groups;
+    const int scale_offset = 512 + (r < 8 ? 4 * r : 4 * (r - 8) + 2);
+    const std::uint32_t lanes = static_cast<std::uint32_t>(32 * quarter) << 16;
+    int w_parts_ready = 0;  // parts of the weights (and scales) seen landed
+    for (int b = read_team; b < nb; b += kTcReadTeams) {
+      const bool quit = __shfl_sync(0xFFFFFFFFu, *aborted, 0) != 0u;
+      if (quit)
+        break;
+      const int t = b % kTcSlots;
+      bool ok = true;
+      for (; w_parts_ready <= b / kTcPartBlocks && ok; ++w_parts_ready)
+        ok = WarpWait(&wfull[w_parts_ready], 0, p.error, kErrWeightWait);
+      if (!ok) {
+        *aborted = 1;
+        break;
+      }
+      if (!WarpWait(&dfull[t], (b / kTcSlots) & 1, p.error, kErrWeightWait)) {
+        *aborted = 1;
+        break;
+      }
+      TcFenceAfter();
+      std::uint32_t d[kRead];
+      TmemLoad<kRead>(tmem + lanes + kTcDColumn + 32 * t, d);
+      TcFenceBefore();
+      __syncwarp();
+      if (lane == 0)
+        MbarArrive(&tfree[t]);
+      const std::uint16_t bits = *reinterpret_cast<const std::uint16_t*>(
+          wts + (g * nb + b) * kQ8TileBytes + scale_offset);
+      const float scale = live ? HalfBitsToFloat(bits) : 0.0f;
+#pragma unroll
+      for (int c = 0; c < kRead; c += 2) {
+        const float2 v = Fma2(make_float2(scale, scale),
+                              make_float2(__uint_as_float(d[c]),
+                                          __uint_as_float(d[c + 1])),
+                              make_float2(acc[c], acc[c + 1]));
+        acc[c] = v.x;
+        acc[c + 1] = v.y;
+      }
     }
   }
 
   // Every wait above is bounded, so every thread gets here.
   __syncthreads();
   TcFenceAfter();
-  if (warp == kTcMmaWarp)
+  if (warp == kTcProducerWarp)
     TmemDealloc(tmem, kTcColumns);
 
-  // The two halves, then the cluster's splits, add up in a fixed order.
-  float* red = reinterpret_cast<float*>(ring);      // [128][kRead]
-  float* part = red + kTcRows * kRead;              // [128][kRead]
-  if (worker && half == 1) {
+  // The read teams, then the cluster's splits, add up in a fixed order.
+  float* red = reinterpret_cast<float*>(wts);  // [read team - 1][128][kRead]
+  float* part = red + (kTcReadTeams - 1) * kTcRows * kRead;  // [128][kRead]
+  if (reader && read_team != 0) {
 #pragma unroll
     for (int c = 0; c < kRead; c += 4)
-      *reinterpret_cast<float4*>(red + row * kRead + c) =
+      *reinterpret_cast<float4*>(red + ((read_team - 1) * kTcRows + row) *
+                                           kRead + c) =
           make_float4(acc[c], acc[c + 1], acc[c + 2], acc[c + 3]);
   }
   __syncthreads();
-  if (worker && half == 0) {
+  if (reader && read_team == 0) {
+    for (int other = 1; other < kTcReadTeams; ++other) {
 #pragma unroll
-    for (int c = 0; c < kRead; c += 4) {
-      const float4 v = LoadFloat4(red + row * kRead + c);
-      acc[c] += v.x;
-      acc[c + 1] += v.y;
-      acc[c + 2] += v.z;
-      acc[c + 3] += v.w;
+      for (int c = 0; c < kRead; c += 4) {
+        const float4 v =
+            LoadFloat4(red + ((other - 1) * kTcRows + row) * kRead + c);
+        acc[c] += v.x;
+        acc[c + 1] += v.y;
+        acc[c + 2] += v.z;
+        acc[c + 3] += v.w;
+      }
     }
   }
   if (p.splits > 1) {
-    if (worker && half == 0 && split != 0) {
+    if (reader && read_team == 0 && split != 0) {
 #pragma unroll
       for (int c = 0; c < kRead; c += 4)
         *reinterpret_cast<float4*>(part + row * kRead + c) =
             make_float4(acc[c], acc[c + 1], acc[c + 2], acc[c + 3]);
     }
     ClusterSync();
-    if (worker && half == 0 && split == 0) {
+    if (reader && read_team == 0 && split == 0) {
       for (int rank = 1; rank < p.splits; ++rank) {
 #pragma unroll
         for (int c = 0; c < kRead; c += 4) {
@@ -385,7 +410,7 @@ __global__ void __launch_bounds__(kTcThreads, 2)
     }
     ClusterSync();  // the others keep their shared memory until it was read
   }
-  if (!worker || half != 0 || split != 0 || *aborted != 0)
+  if (!reader || read_team != 0 || split != 0 || *aborted != 0)
     return;
   const int n = group0 * 16 + row;
   if (n >= p.n)
@@ -432,20 +457,41 @@ EncodeTiledFn TensorMapEncoder() {
   return fn;
 }
 
-/// The tensor map of x [rows][in] bf16 with a box of 8 columns x 32 rows.
+/// The tensor map of x [rows][in] bf16 for the B operand. Preferred: x
+/// viewed as 3-D {8 columns, rows, in / 8 chunks} (strides in*2 and 16
+/// bytes) with a box of {8, 32, 32}, which lands one part (32 chunks of all
+/// 32 rows, 16 KB) as K-major core matrices in one request (`*boxes` = 1).
+/// If the driver does not take that view: 2-D with a box of 8 columns x 32
+/// rows, 32 requests per part (`*boxes` = 32).
 bool EncodeActivations(const std::uint16_t* x, std::size_t rows,
-                       std::size_t in, CUtensorMap* map) {
+                       std::size_t in, CUtensorMap* map, int* boxes) {
   const EncodeTiledFn encode = TensorMapEncoder();
   if (encode == nullptr)
     return false;
+  void* base = const_cast<std::uint16_t*>(x);
+  {
+    const cuuint64_t dims[3] = {8, static_cast<cuuint64_t>(rows),
+                                static_cast<cuuint64_t>(in / 8)};
+    const cuuint64_t strides[2] = {static_cast<cuuint64_t>(in) * 2, 16};
+    const cuuint32_t box[3] = {8, static_cast<cuuint32_t>(kTcXRows),
+                               4 * kTcPartBlocks};
+    const cuuint32_t element_strides[3] = {1, 1, 1};
+    if (encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, base, dims, strides,
+               box, element_strides, CU_TENSOR_MAP_INTERLEAVE_NONE,
+               CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
+               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS) {
+      *boxes = 1;
+      return true;
+    }
+  }
   const cuuint64_t dims[2] = {static_cast<cuuint64_t>(in),
                               static_cast<cuuint64_t>(rows)};
   const cuuint64_t strides[1] = {static_cast<cuuint64_t>(in) * 2};
   const cuuint32_t box[2] = {8, static_cast<cuuint32_t>(kTcXRows)};
   const cuuint32_t element_strides[2] = {1, 1};
-  return encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2,
-                const_cast<std::uint16_t*>(x), dims, strides, box,
-                element_strides, CU_TENSOR_MAP_INTERLEAVE_NONE,
+  *boxes = 32;
+  return encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, dims, strides,
+                box, element_strides, CU_TENSOR_MAP_INTERLEAVE_NONE,
                 CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
                 CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
@@ -553,7 +599,7 @@ int LaunchTensorCoreProduct(const std::uint16_t* x, const void* w, float* y,
   config.attrs = attributes;
   config.numAttrs = count;
   CUtensorMap x_map;
-  if (!EncodeActivations(x, rows, in, &x_map))
+  if (!EncodeActivations(x, rows, in, &x_map, &args.x_boxes))
     return kInvalid;
   if (cudaLaunchKernelEx(&config, kernel, args, x_map) != cudaSuccess)
     return kCudaError;

@@ -165,6 +165,17 @@ __device__ inline void TmaLoad2D(void* dst, const CUtensorMap* map, int c0,
       : "memory");
 }
 
+/// Tiled 3-D TMA load (no multicast), as TmaLoad2D.
+__device__ inline void TmaLoad3D(void* dst, const CUtensorMap* map, int c0,
+                                 int c1, int c2, std::uint64_t* bar) {
+  asm volatile(
+      "cp.async.bulk.tensor.3d.shared::cluster.global.tile.mbarrier::complete_"
+      "tx::bytes [%0], [%1, {%2, %3, %4}], [%5];" ::"r"(SmemAddr(dst)),
+      "l"(reinterpret_cast<std::uint64_t>(map)), "r"(c0), "r"(c1), "r"(c2),
+      "r"(SmemAddr(bar))
+      : "memory");
+}
+
 /// Arrives once on `bar` when every tcgen05.mma this thread issued before
 /// has completed.
 __device__ inline void MmaCommit(std::uint64_t* bar) {
