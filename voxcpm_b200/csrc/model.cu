@@ -596,6 +596,7 @@ Generator::~Generator() {
       cudaFree(p);
     p = nullptr;
   };
+  free(prefill_block_);
   free(scratch_.normed);
   free(scratch_.qkv);
   free(scratch_.q);
@@ -1292,11 +1293,32 @@ void Generator::Prefill(const std::int32_t* tokens,
       throw std::invalid_argument("token outside the vocabulary");
   CheckCuda(cudaStreamSynchronize(stream_), "sync");
   EnsureRows(std::max(rows, scratch_rows_));
-  std::vector<void*> temporaries;
+  // Work buffers from one grow-only block: an upper bound for this prompt
+  // (every row an audio row), then bump allocation.
+  auto rounded = [](std::size_t bytes) { return (std::max<std::size_t>(bytes, 4) + 255) / 256 * 256; };
+  {
+    const std::size_t r = rows;
+    const std::size_t bound = 5 * rounded(r * 4) + 5 * rounded(r * hidden * 4) +
+                              rounded(r * 2 * hidden * 2) +
+                              rounded(r * c.fsq_latent_dim * 4) +
+                              rounded(r * patch_values * 4);
+    if (bound > prefill_bytes_) {
+      if (prefill_block_ != nullptr)
+        cudaFree(prefill_block_);
+      prefill_block_ = nullptr;
+      prefill_bytes_ = 0;
+      CheckCuda(cudaMalloc(reinterpret_cast<void**>(&prefill_block_), bound),
+                "cudaMalloc prefill");
+      prefill_bytes_ = bound;
+    }
+  }
+  std::size_t used = 0;
   auto temp = [&](std::size_t bytes) {
-    void* p = nullptr;
-    CheckCuda(cudaMalloc(&p, std::max<std::size_t>(bytes, 4)), "cudaMalloc prefill");
-    temporaries.push_back(p);
+    const std::size_t size = rounded(bytes);
+    if (used + size > prefill_bytes_)
+      throw std::logic_error("prefill work buffers exceed their bound");
+    void* p = prefill_block_ + used;
+    used += size;
     return p;
   };
   try {
@@ -1377,12 +1399,8 @@ void Generator::Prefill(const std::int32_t* tokens,
     CheckCuda(cudaStreamSynchronize(stream_), "prefill");
   } catch (...) {
     cudaStreamSynchronize(stream_);
-    for (void* p : temporaries)
-      cudaFree(p);
     throw;
   }
-  for (void* p : temporaries)
-    cudaFree(p);
   position_ = rows;
 }
 

@@ -241,6 +241,10 @@ class Generator {
   KvCache base_cache_, residual_cache_, encoder_cache_, dit_cache_;
   StackScratch scratch_;
   int scratch_rows_ = 0;
+  // Prefill work buffers, grown to the largest prompt seen (reused, so a
+  // prefill allocates nothing once the block is large enough).
+  unsigned char* prefill_block_ = nullptr;
+  std::size_t prefill_bytes_ = 0;
   int position_ = 0;
   bool graphs_ = true;
 
