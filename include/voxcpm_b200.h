@@ -162,7 +162,8 @@ VX_API vx_status vx_product(int format, const uint16_t* x, const void* w, void* 
 #define VX_PRODUCT_ACCUMULATE 1u
 /* The launch reads nothing that earlier kernels on the stream write (x, w
  * and, when accumulating, y are ready before it is enqueued): it may overlap
- * them instead of waiting for their completion. */
+ * them instead of waiting for their completion. With a null plan it takes
+ * the library's measured plan for such streams where it has one. */
 #define VX_PRODUCT_INDEPENDENT 2u
 
 /* vx_product with flags (VX_PRODUCT_ACCUMULATE, VX_PRODUCT_INDEPENDENT).
@@ -180,7 +181,7 @@ VX_API void vx_set_programmatic_launch(int enabled);
  * (tcgen05) kernel, plan variant VX_TENSOR_CORE_VARIANT, or (default) to the
  * mma.sync kernels. A plan with that variant runs it either way. No reference counterpart (the reference has one
  * WMMA kernel, kernels/wmma_products.hip:139-296). */
-#define VX_TENSOR_CORE_VARIANT 16
+#define VX_TENSOR_CORE_VARIANT 100
 VX_API void vx_set_tensor_core_products(int enabled);
 VX_API int vx_tensor_core_products(void);
 /* Number of product kernel shapes and the shape of one (benchmarks). */

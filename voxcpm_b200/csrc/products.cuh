@@ -28,8 +28,10 @@ constexpr int kQ8TileBytes = 16 * 32 + 16 * 2;
 constexpr int kBf16TileBytes = 16 * 32 * 2;
 /// Most activation rows one launch takes (4 MMA column tiles of 8).
 constexpr int kMaxProductRows = 32;
-/// Longest reduction slice one CTA holds in shared memory.
-constexpr int kMaxSliceColumns = 1024;
+/// Longest reduction slice one CTA holds in shared memory (explicit plans).
+constexpr int kMaxSliceColumns = 2048;
+/// Longest slice the planner's cost model gives one CTA.
+constexpr int kPlannedSliceColumns = 1024;
 
 inline std::size_t Q8TilesBytes(std::size_t rows, std::size_t in) {
   return (rows + kTileRows - 1) / kTileRows * (in / kTileColumns) *
@@ -53,7 +55,7 @@ struct ProductPlan {
 /// Plan variant of the tensor-core (tcgen05) kernel for Q8_0 tiles
 /// (products_tc.cu): 128 weight rows per CTA, at most
 /// kTensorCoreMaxBlocks 32-column blocks of the reduction per split.
-constexpr int kTensorCoreVariant = 16;
+constexpr int kTensorCoreVariant = 100;  // above every mma.sync variant
 constexpr int kTensorCoreMaxBlocks = 24;
 /// Fewest activation rows the planner gives to the tensor-core kernel.
 constexpr int kTensorCoreMinRows = 9;
@@ -78,7 +80,8 @@ ProductPlan PlanProduct(WeightFormat format, std::size_t rows, std::size_t in,
 /// kUnsupported (nothing launched) or kInvalid / kCudaError.
 /// `independent`: the launch reads nothing that the kernels before it on
 /// the stream write, so it skips the programmatic-launch wait and may overlap
-/// them (streams of independent products).
+/// them (streams of independent products); with no plan it takes the
+/// measured stream plan for its shape where there is one.
 int LaunchProduct(WeightFormat format, const std::uint16_t* x, const void* w,
                   float* y, std::uint16_t* y_bf16, std::size_t rows,
                   std::size_t in, std::size_t out, bool accumulate,

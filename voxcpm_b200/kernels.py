@@ -164,7 +164,7 @@ def SetProgrammaticLaunch(enabled: bool) -> None:
     load().vx_set_programmatic_launch(int(enabled))
 
 
-TENSOR_CORE_VARIANT = 16  # VX_TENSOR_CORE_VARIANT
+TENSOR_CORE_VARIANT = 100  # VX_TENSOR_CORE_VARIANT
 
 
 def SetTensorCoreProducts(enabled: bool) -> None:
