@@ -91,23 +91,16 @@ constexpr VariantShape kVariants[] = {
     {16, 1, 1, 2, 4},  // 6: 256 rows, 16 warps
     {4, 4, 1, 2, 3},   // 7: 64 rows, 16 warps (4 ways)
     // Eight-block stages: one 4.3 KB (Q8) copy per group and stage. A TMA
-    // request costs the SM about 30-40 ns to issue whatever its size, so
-    // two-block stages (1.1 KB copies) cap a CTA near 30 GB/s.
+    // request costs its issuing thread about 30-40 ns whatever its size, so
+    // two-block stages (1.1 KB copies) cap a warp's stream.
     {8, 1, 1, 8, 2},   // 8: 128 rows, 8 warps
     {16, 1, 1, 8, 2},  // 9: 256 rows, 16 warps
     {16, 1, 2, 8, 2},  // 10: 256 rows, 8 warps of 2 groups
     {8, 1, 2, 8, 2},   // 11: 128 rows, 4 warps of 2 groups
     {8, 2, 1, 8, 2},   // 12: 128 rows, 16 warps (2 ways)
-    {16, 1, 1, 8, 1},  // 13: 256 rows, 16 warps, one stage in flight
-    {16, 1, 1, 4, 2},  // 14: 256 rows, 16 warps, four-block stages
-    // Whole-reduction CTAs without clusters (streams of independent launches).
-    {24, 1, 1, 8, 1},  // 15: 384 rows, 24 warps
-    {16, 1, 2, 8, 1},  // 16: 256 rows, 8 warps of 2 groups
-    {32, 1, 2, 4, 1},  // 17: 512 rows, 16 warps of 2 groups, four-block stages
-    {8, 2, 1, 8, 1},   // 18: 128 rows, 16 warps (2 ways)
-    {32, 1, 1, 4, 1},  // 19: 512 rows, 32 warps, four-block stages
-    {24, 1, 1, 4, 2},  // 20: 384 rows, 24 warps, two four-block stages
-    {24, 1, 1, 2, 4},  // 21: 384 rows, 24 warps, four two-block stages
+    // A whole-reduction CTA without a cluster (streams of independent
+    // launches: 16 CTAs per config-0 launch, several launches side by side).
+    {24, 1, 1, 8, 1},  // 13: 384 rows, 24 warps, one 8-block stage per warp
 };
 constexpr int kNumVariants = sizeof(kVariants) / sizeof(kVariants[0]);
 static_assert(kNumVariants <= kTensorCoreVariant, "variant ids overlap");
@@ -461,7 +454,7 @@ struct VariantRow {
 
 template <int kFormat, int kNTiles>
 using Row = VariantRow<kFormat, kNTiles, 0, 1, 2, 3, 4, 5, 6, 7, 8, 9, 10, 11,
-                       12, 13, 14, 15, 16, 17, 18, 19, 20, 21>;
+                       12, 13>;
 
 KernelFn Lookup(int format, int ntiles, int variant) {
   static const KernelFn* table[3][4] = {
@@ -574,7 +567,7 @@ constexpr MeasuredPlan kMeasuredPlans[] = {
 // CTAs without clusters win (config 0: 3.2 us per product against 4.4 us
 // for the best clustered plan).
 constexpr MeasuredPlan kStreamPlans[] = {
-    {WeightFormat::kQ8Tiles, 2, 2048, 6144, 15, 1},
+    {WeightFormat::kQ8Tiles, 2, 2048, 6144, 13, 1},
 };
 
 ProductPlan StreamPlan(WeightFormat format, std::size_t rows, std::size_t in,
