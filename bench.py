@@ -438,6 +438,7 @@ def run_ours(args, world, rank, local):
     if rank != 0:
         return
     peak, peak_kind = measured_peak()
+    sweep = measure_sweep(peak)
     cpu_value, cpu_desc = cpu_sample(os.cpu_count() or 1, 10.0)
     plan = K.PlanWmma(ROWS, IN, OUT, 0)
     line = {
@@ -472,6 +473,10 @@ def run_ours(args, world, rank, local):
                 "api": "vx_product (default plan), pinned host x in and y out every step",
                 "launch": f"one CUDA graph of {E2E_GRAPH_STEPS} steps per stream (copies and "
                           f"product of every step inside), replayed {e2e_reps} times"},
+        "sweep": {"rows": sweep, "metric": "GB/s of algorithmic bytes (weights + x + fp32 y) per "
+                  "Bf16Gemm::Linear call; err = max |y - exact| / sum |x w| (limit 1e-5)",
+                  "launch": "dependent chain over rotating weight copies (more than L2), CUDA graph",
+                  "config": "BASELINE config 1"},
         "gpu_launches": 2 * args.steps,
         "clocks": clocks,
         **generator,
@@ -493,6 +498,80 @@ STEP_BYTES_CONFIG3 = 4_034_512_896 + 18_874_368
 BOX_REQUESTS = 64        # independent requests over the box
 BOX_PATCHES = 63         # patches per request (about 10 s of audio)
 BOX_PER_RANK = 8         # requests each rank runs (a bounded sample of its share)
+
+
+SWEEP_ROWS = (1, 2, 8, 22, 64, 128)
+SWEEP_SHAPES = ((1024, 3072), (1024, 1024), (2048, 6144), (6144, 2048), (2048, 2560))
+SWEEP_L2_BYTES = 160 << 20  # rotating weight copies per shape: more than the 126 MB L2
+
+
+def measure_sweep(peak_gbs: float) -> list:
+    """every M x (K, N) with Q8_0 tiles and bf16 rows
+    (q uniform in [-127, 127] with fp16 scales |N(0, 0.02)|/127; bf16
+    weights ~N(0, 0.02); x ~ N(0, 1) bf16), through Bf16Gemm::Linear (the
+    reference's dispatch: 32-row products, larger row counts in 32-row
+    chunks), fp32 output. Time: a dependent chain of launches over rotating
+    weight copies, replayed from a CUDA graph. Error: max |y - exact| /
+    sum |x w| per output against a float64 product of the same operands."""
+    import numpy as np
+    import torch
+
+    from voxcpm_b200 import _lib
+    from voxcpm_b200 import kernels as K
+    from voxcpm_b200.gemm import Bf16Gemm, Matrix
+
+    stream = torch.cuda.Stream()
+    gemm = Bf16Gemm(stream)
+    out_rows = []
+    for (k, n) in SWEEP_SHAPES:
+        blocks = K.RandomQ8_0(77, n, n, k)
+        raw = blocks.reshape(-1, 34)
+        scales = torch.from_numpy(raw[:, :2].copy().view(np.float16).astype(np.float64)).cuda()
+        q = torch.from_numpy(raw[:, 2:].copy().view(np.int8).astype(np.float64)).cuda()
+        w_q8_exact = (q * scales).reshape(n, k)
+        tiles = torch.empty(K.Q8TilesBytes(n, k), dtype=torch.uint8, device="cuda")
+        K.Q8_0ToTiles(torch.from_numpy(blocks).cuda(), n, k, tiles)
+        w_bf16 = (torch.randn(n, k, device="cuda") * 0.02).to(torch.bfloat16)
+        for fmt, w_one, exact_w, w_bytes in (
+                (_lib.WEIGHTS_Q8_TILES, tiles, w_q8_exact, n * k * 34 // 32),
+                (_lib.WEIGHTS_BF16, w_bf16.view(torch.int16), w_bf16.double(), n * k * 2)):
+            copies = max(2, min(160, -(-SWEEP_L2_BYTES // w_bytes)))
+            ws = [w_one.clone() for _ in range(copies)]
+            for m in SWEEP_ROWS:
+                x = torch.randn(m, k, device="cuda").to(torch.bfloat16)
+                ys = [torch.empty(m, n, dtype=torch.float32, device="cuda") for _ in range(2)]
+                torch.cuda.synchronize()
+                with torch.cuda.stream(stream):
+                    gemm.Linear(x.view(torch.int16), Matrix(fmt, ws[0]), ys[0], m, k, n, False)
+                    stream.synchronize()
+                    exact = x.double() @ exact_w.t()
+                    mag = x.double().abs() @ exact_w.abs().t()
+                    err = float(((ys[0].double() - exact).abs() / mag.clamp_min(1e-300)).max())
+                    launches = max(copies, 20)
+                    g = torch.cuda.CUDAGraph()
+                    with torch.cuda.graph(g, stream=stream):
+                        for i in range(launches):
+                            gemm.Linear(x.view(torch.int16), Matrix(fmt, ws[i % copies]), ys[i % 2],
+                                        m, k, n, False)
+                    g.replay()
+                    a = torch.cuda.Event(enable_timing=True)
+                    b = torch.cuda.Event(enable_timing=True)
+                    a.record(stream)
+                    for _ in range(3):
+                        g.replay()
+                    b.record(stream)
+                    b.synchronize()
+                us = a.elapsed_time(b) * 1e3 / (3 * launches)
+                step_bytes = w_bytes + m * k * 2 + m * n * 4
+                gbs = step_bytes / us / 1e3
+                out_rows.append({"m": m, "k": k, "n": n,
+                                 "weights": "q8_0" if fmt == _lib.WEIGHTS_Q8_TILES else "bf16",
+                                 "us": round(us, 3), "gbs": round(gbs, 1),
+                                 "frac": round(gbs / peak_gbs, 4), "err": err})
+                del g
+            del ws
+    gemm.close()
+    return out_rows
 
 
 def measure_generator(rank: int, world=None, context: int = 512, patch_replays: int = 50,

@@ -235,3 +235,25 @@ def test_unsupported_shapes(cuda):
     assert not K.WmmaQ8(x, w, y, 1, 48, 16, False)       # in not a multiple of 32
     assert not K.WmmaQ8(x, w, y, 0, 32, 16, False)       # no rows
     assert not K.SkinnyGemm(x, x, y, 1, 16384, 2, False)  # in > 8192
+
+
+def test_independent_launch_stream_plan(cuda):
+    """Independent launches with no plan take the library's measured stream
+    plan (config 0: one 384-row CTA per panel over the whole reduction) and
+    give the same sums as the planner's dependent plan."""
+    rng = np.random.default_rng(41)
+    rows, columns, out = 22, 2048, 6144
+    blocks, q8_tiles, _, _ = prepare(out, columns, rng)
+    x = make_activations(rows, columns, rng)
+    x_dev = to_dev(x)
+    exact = oracle.product_exact(x, oracle.Q8_0, blocks, rows, columns, out)
+    y_stream = torch.empty(rows, out, dtype=torch.float32, device="cuda")
+    y_chain = torch.empty_like(y_stream)
+    assert K.ProductEx(_lib.WEIGHTS_Q8_TILES, x_dev, q8_tiles, y_stream, rows, columns, out,
+                       _lib.PRODUCT_INDEPENDENT)
+    assert K.ProductEx(_lib.WEIGHTS_Q8_TILES, x_dev, q8_tiles, y_chain, rows, columns, out, 0)
+    torch.cuda.synchronize()
+    for name, y in (("stream plan", y_stream), ("planner", y_chain)):
+        err = oracle.relative_error(y.cpu().numpy(), *exact)
+        assert err <= LIMIT, f"{name}: {err:.3e}"
+    assert K.DeviceError() == 0

@@ -103,6 +103,11 @@ constexpr VariantShape kVariants[] = {
     {24, 1, 1, 8, 1},  // 13: 384 rows, 24 warps, one 8-block stage per warp
 };
 constexpr int kNumVariants = sizeof(kVariants) / sizeof(kVariants[0]);
+// The cost model chooses among the first eight shapes only: their plans fit
+// every weight format (a Q8_0 plan may be given to bf16 weights, as the
+// reference's PlanWmma plans serve both); the larger ones are for measured
+// and explicit plans.
+constexpr int kPlannerVariants = 8;
 static_assert(kNumVariants <= kTensorCoreVariant, "variant ids overlap");
 
 __host__ __device__ constexpr int RowStrideBytes(int stage) {
@@ -636,7 +641,7 @@ ProductPlan PlanProduct(WeightFormat format, std::size_t rows, std::size_t in,
   // weight blocks a CTA streams (one wave of CTAs), plus a small charge per
   // split for the activation slice and the cluster reduction.
   double best_cost = 1e30;
-  for (int variant = 0; variant < kNumVariants; ++variant) {
+  for (int variant = 0; variant < kPlannerVariants; ++variant) {
     const VariantShape& v = kVariants[variant];
     const int rows_per_cta = 16 * v.cta_groups;
     const int panels = (groups_total * 16 + rows_per_cta - 1) / rows_per_cta;
