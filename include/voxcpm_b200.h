@@ -118,8 +118,9 @@ typedef struct vx_split_scratch {
 VX_API vx_wmma_plan vx_plan_wmma(size_t rows, size_t in, size_t out,
                           size_t target_waves);
 
-/* y[rows][out] (+)= x[rows][in] * W^T for bf16 x and Q8 tiles W, at most 32
- * rows, `in` a multiple of 32 (at most 8192). `plan` may be null (planner's
+/* y[rows][out] (+)= x[rows][in] * W^T for bf16 x and Q8 tiles W, at most
+ * 128 rows (the reference's kernel takes 32 per launch; 33..128 run in one
+ * launch here), `in` a multiple of 32 (at most 8192). `plan` may be null (planner's
  * choice), `scratch` may be null. Replaces WmmaQ8
  * (kernels/wmma_products.hpp:87-93). */
 VX_API vx_status vx_wmma_q8(const uint16_t* x, const uint8_t* w, float* y,
@@ -132,7 +133,8 @@ VX_API vx_status vx_wmma_bf16(const uint16_t* x, const uint16_t* w, float* y,
                        size_t rows, size_t in, size_t out, int accumulate,
                        const vx_wmma_plan* plan,
                        const vx_split_scratch* scratch, cudaStream_t stream);
-/* y (+)= x * W^T for bf16 rows W ([out][in]), at most 32 rows, `in` a
+/* y (+)= x * W^T for bf16 rows W ([out][in]), at most 32 rows (as the
+ * reference's SkinnyGemm), `in` a
  * multiple of 8 (the kernels need a multiple of 32; other sizes return
  * VX_UNSUPPORTED). Replaces SkinnyGemm (kernels/skinny_gemm.hpp:18-24). */
 VX_API vx_status vx_skinny_gemm(const uint16_t* x, const uint16_t* w, float* y,
@@ -150,7 +152,7 @@ VX_API vx_status vx_read_probe(const void* data, size_t pieces, unsigned blocks,
                         unsigned* sink, cudaStream_t stream);
 
 /* The general product: any weight format, fp32 or bf16 output
- * (`out_dtype`), at most 32 rows per launch. Extends WmmaQ8/WmmaBf16/
+ * (`out_dtype`), at most 128 rows per launch. Extends WmmaQ8/WmmaBf16/
  * SkinnyGemm (kernels/wmma_products.hpp:87-99, kernels/skinny_gemm.hpp:
  * 18-24) with the bf16-output epilogue. */
 VX_API vx_status vx_product(int format, const uint16_t* x, const void* w, void* y,

@@ -231,7 +231,8 @@ def test_unsupported_shapes(cuda):
     x = torch.zeros(64 * 48, dtype=torch.int16, device="cuda")
     w = torch.zeros(4096, dtype=torch.uint8, device="cuda")
     y = torch.zeros(64 * 64, dtype=torch.float32, device="cuda")
-    assert not K.WmmaQ8(x, w, y, 33, 32, 16, False)      # more than 32 rows
+    assert not K.WmmaQ8(x, w, y, 129, 32, 16, False)     # more than 128 rows
+    assert not K.SkinnyGemm(x, x, y, 33, 32, 16, False)   # SkinnyGemm: at most 32 rows
     assert not K.WmmaQ8(x, w, y, 1, 48, 16, False)       # in not a multiple of 32
     assert not K.WmmaQ8(x, w, y, 0, 32, 16, False)       # no rows
     assert not K.SkinnyGemm(x, x, y, 1, 16384, 2, False)  # in > 8192
@@ -256,4 +257,41 @@ def test_independent_launch_stream_plan(cuda):
     for name, y in (("stream plan", y_stream), ("planner", y_chain)):
         err = oracle.relative_error(y.cpu().numpy(), *exact)
         assert err <= LIMIT, f"{name}: {err:.3e}"
+    assert K.DeviceError() == 0
+
+
+@pytest.mark.parametrize("columns,out", [(1024, 2560), (2048, 1024), (6144, 512)])
+def test_wide_rows(cuda, columns, out):
+    """33..128 activation rows in one launch (8 or 16 B tiles per warp) on
+    every weight format, plain and accumulating, fp32 and bf16 output; for a
+    long reduction (6144) no one-launch plan fits and the launcher runs
+    32-row launches."""
+    rng = np.random.default_rng(53 + columns)
+    blocks, q8_tiles, dequant, bf16_tiles = prepare(out, columns, rng)
+    host_dequant = from_dev_u16(dequant)
+    for rows in (33, 48, 64, 65, 100, 128):
+        x = make_activations(rows, columns, rng)
+        x_dev = to_dev(x)
+        before = rng.normal(0.0, 1.0, size=(rows, out)).astype(np.float32)
+        y = torch.empty(rows, out, dtype=torch.float32, device="cuda")
+        for accumulate in (False, True):
+            for fmt, w, ref_fmt, ref_w in (
+                (_lib.WEIGHTS_Q8_TILES, q8_tiles, oracle.Q8_0, blocks),
+                (_lib.WEIGHTS_BF16_TILES, bf16_tiles, oracle.BF16_ROWS, host_dequant),
+                (_lib.WEIGHTS_BF16, dequant, oracle.BF16_ROWS, host_dequant),
+            ):
+                y.copy_(torch.from_numpy(before))
+                assert K.Product(fmt, x_dev, w, y, rows, columns, out, accumulate), (fmt, rows)
+                torch.cuda.synchronize()
+                exact = oracle.product_exact(x, ref_fmt, ref_w, rows, columns, out,
+                                             before if accumulate else None)
+                err = oracle.relative_error(y.cpu().numpy(), *exact)
+                assert err <= LIMIT, f"fmt {fmt} rows {rows} acc {accumulate}: {err:.3e}"
+        y16 = torch.empty(rows, out, dtype=torch.bfloat16, device="cuda")
+        assert K.Product(_lib.WEIGHTS_Q8_TILES, x_dev, q8_tiles, y16, rows, columns, out)
+        y32 = torch.empty(rows, out, dtype=torch.float32, device="cuda")
+        assert K.Product(_lib.WEIGHTS_Q8_TILES, x_dev, q8_tiles, y32, rows, columns, out)
+        torch.cuda.synchronize()
+        assert np.array_equal(y16.cpu().view(torch.int16).numpy().view(np.uint16),
+                              oracle.bf16_bits(y32.cpu().numpy()))
     assert K.DeviceError() == 0

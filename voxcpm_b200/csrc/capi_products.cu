@@ -155,6 +155,8 @@ vx_status vx_skinny_gemm(const uint16_t* x, const uint16_t* w, float* y,
                          cudaStream_t stream) {
   if (in > 8192)
     return vx::Fail(vx::kUnsupported, "vx_skinny_gemm: in > 8192");
+  if (rows > 32)
+    return vx::Fail(vx::kUnsupported, "vx_skinny_gemm: more than 32 rows");
   return Product(VX_WEIGHTS_BF16, x, w, y, VX_OUT_F32, rows, in, out,
                  accumulate, nullptr, stream, "vx_skinny_gemm");
 }
@@ -240,8 +242,8 @@ vx_status vx_gemm_linear(vx_gemm* gemm, const uint16_t* x, int format,
     return vx::Fail(vx::kInvalid, "vx_gemm_linear: null gemm");
   if (rows == 0)
     return vx::kOk;
-  // Chunks of up to 32 rows (gemm.cpp:270-303 chunks the matrix-core
-  // products the same way).
+  // Chunks of up to 128 rows, one launch each (gemm.cpp:270-303 chunks the
+  // reference's matrix-core products by 32 rows).
   for (size_t first = 0; first < rows; first += vx::kMaxProductRows) {
     const size_t count =
         rows - first < static_cast<size_t>(vx::kMaxProductRows)

@@ -291,13 +291,15 @@ __global__ void __launch_bounds__(kCtaGroups / kGroups * kWays * 32)
   GridLaunchDependents();
   if (p.wait)
     GridDependencyWait();
-  if (warp == 0 && lane < p.m && nblocks > 0) {
+  if (warp == 0 && nblocks > 0) {
+    // One bulk copy per activation row, rows strided over the warp's lanes.
     if (lane == 0)
       MbarArriveExpectTx(xbar, p.m * nblocks * 64);
-    __syncwarp(0xFFFFFFFFu >> (32 - p.m));
-    BulkLoad(xs + lane * p.x_stride,
-             p.x + static_cast<std::size_t>(lane) * p.k + first * 32,
-             nblocks * 64, xbar, PolicyEvictLast());
+    __syncwarp();
+    for (int row = lane; row < p.m; row += 32)
+      BulkLoad(xs + row * p.x_stride,
+               p.x + static_cast<std::size_t>(row) * p.k + first * 32,
+               nblocks * 64, xbar, PolicyEvictLast());
   }
 
   float acc[kGroups][kNTiles][4];
@@ -444,12 +446,22 @@ __global__ void __launch_bounds__(kCtaGroups / kGroups * kWays * 32)
 
 using KernelFn = void (*)(const ProductArgs);
 
+// Variants that take 33..128 activation rows (8 or 16 B tiles per warp):
+// the small CTAs, whose registers and activation slices stay in bounds.
+__host__ __device__ constexpr bool WideVariant(int variant) {
+  return variant == 0 || variant == 1 || variant == 3;
+}
+
 template <int kFormat, int kNTiles, int kVariant>
 constexpr KernelFn KernelFor() {
-  return ProductKernel<kFormat, kVariants[kVariant].cta_groups,
-                       kVariants[kVariant].ways, kVariants[kVariant].groups,
-                       kNTiles, kVariants[kVariant].stage,
-                       kVariants[kVariant].depth>;
+  if constexpr (kNTiles > 4 && !WideVariant(kVariant)) {
+    return nullptr;
+  } else {
+    return ProductKernel<kFormat, kVariants[kVariant].cta_groups,
+                         kVariants[kVariant].ways, kVariants[kVariant].groups,
+                         kNTiles, kVariants[kVariant].stage,
+                         kVariants[kVariant].depth>;
+  }
 }
 
 template <int kFormat, int kNTiles, int... kV>
@@ -461,13 +473,31 @@ template <int kFormat, int kNTiles>
 using Row = VariantRow<kFormat, kNTiles, 0, 1, 2, 3, 4, 5, 6, 7, 8, 9, 10, 11,
                        12, 13>;
 
+/// Row classes of the measured plan tables: 1, 2..8, 9..32, 33..128.
+int RowsClass(std::size_t rows) {
+  return rows == 1 ? 0 : rows <= 8 ? 1 : rows <= 32 ? 2 : 3;
+}
+
+/// Index of a B-tile count (1, 2, 3, 4, 8, 16) in the tables.
+int TileIndex(int ntiles) {
+  return ntiles <= 4 ? ntiles - 1 : ntiles == 8 ? 4 : 5;
+}
+
+/// B tiles (8 activation rows each) for `rows` rows: 1..4, then 8 or 16.
+int TilesFor(std::size_t rows) {
+  return rows <= 32 ? static_cast<int>((rows + 7) / 8) : rows <= 64 ? 8 : 16;
+}
+
 KernelFn Lookup(int format, int ntiles, int variant) {
-  static const KernelFn* table[3][4] = {
-      {Row<0, 1>::table, Row<0, 2>::table, Row<0, 3>::table, Row<0, 4>::table},
-      {Row<1, 1>::table, Row<1, 2>::table, Row<1, 3>::table, Row<1, 4>::table},
-      {Row<2, 1>::table, Row<2, 2>::table, Row<2, 3>::table, Row<2, 4>::table},
+  static const KernelFn* table[3][6] = {
+      {Row<0, 1>::table, Row<0, 2>::table, Row<0, 3>::table, Row<0, 4>::table,
+       Row<0, 8>::table, Row<0, 16>::table},
+      {Row<1, 1>::table, Row<1, 2>::table, Row<1, 3>::table, Row<1, 4>::table,
+       Row<1, 8>::table, Row<1, 16>::table},
+      {Row<2, 1>::table, Row<2, 2>::table, Row<2, 3>::table, Row<2, 4>::table,
+       Row<2, 8>::table, Row<2, 16>::table},
   };
-  return table[format][ntiles - 1][variant];
+  return table[format][TileIndex(ntiles)][variant];
 }
 
 std::atomic<bool> g_programmatic{true};
@@ -578,7 +608,7 @@ constexpr MeasuredPlan kStreamPlans[] = {
 ProductPlan StreamPlan(WeightFormat format, std::size_t rows, std::size_t in,
                        std::size_t out) {
   ProductPlan plan;
-  const int rows_class = rows == 1 ? 0 : rows <= 8 ? 1 : 2;
+  const int rows_class = RowsClass(rows);
   for (const MeasuredPlan& m : kStreamPlans) {
     if (m.format != format || m.rows_class != rows_class ||
         static_cast<std::size_t>(m.in) != in ||
@@ -588,7 +618,7 @@ ProductPlan StreamPlan(WeightFormat format, std::size_t rows, std::size_t in,
     plan.variant = m.variant;
     plan.splits = m.splits;
     plan.blocks_per_split = (k_blocks + m.splits - 1) / m.splits;
-    const int ntiles = static_cast<int>((std::min<std::size_t>(rows, 32) + 7) / 8);
+    const int ntiles = TilesFor(rows);
     if (FootprintOf(static_cast<int>(format), m.variant, ntiles,
                     plan.blocks_per_split).smem > kMaxProductSmem)
       return ProductPlan();
@@ -606,21 +636,21 @@ ProductPlan PlanProduct(WeightFormat format, std::size_t rows, std::size_t in,
   // math needs three or four MMAs per 16 x 16 step there).
   if (format == WeightFormat::kQ8Tiles && target_ctas == 0 &&
       g_tensor_core && rows >= kTensorCoreMinRows &&
-      rows <= kMaxProductRows) {
+      rows <= kTensorCoreMaxRows) {
     const ProductPlan tc = PlanTensorCoreProduct(rows, in, out, SmCount());
     if (tc.variant >= 0)
       return tc;
   }
   const int k_blocks = static_cast<int>(in / kTileColumns);
   if (target_ctas == 0) {
-    const int rows_class = rows == 1 ? 0 : rows <= 8 ? 1 : 2;
+    const int rows_class = RowsClass(rows);
     for (const MeasuredPlan& m : kMeasuredPlans) {
       if (m.format != format || m.rows_class != rows_class ||
           static_cast<std::size_t>(m.in) != in ||
           static_cast<std::size_t>(m.out) != out)
         continue;
       const int bps = (k_blocks + m.splits - 1) / m.splits;
-      const int ntiles = static_cast<int>((std::min<std::size_t>(rows, 32) + 7) / 8);
+      const int ntiles = TilesFor(rows);
       if ((k_blocks + bps - 1) / bps != m.splits ||
           bps * kTileColumns > kMaxSliceColumns ||
           FootprintOf(static_cast<int>(format), m.variant, ntiles, bps).smem >
@@ -632,16 +662,24 @@ ProductPlan PlanProduct(WeightFormat format, std::size_t rows, std::size_t in,
       return best;
     }
   }
+  // 33..128 rows in one launch pay off only for short reductions (measured:
+  // 1.3-2x faster than 32-row launches at in = 1024, slower at in >= 2048,
+  // where a wide launch is compute-bound on too few CTAs); longer ones get no
+  // plan, so the launcher runs 32-row launches.
+  if (rows > 32 && target_ctas == 0 && in > 1024)
+    return best;
   const int groups_total = static_cast<int>((out + 15) / 16);
   const int min_splits =
       (k_blocks * kTileColumns + kPlannedSliceColumns - 1) / kPlannedSliceColumns;
   const int sms = SmCount();
-  const int ntiles = static_cast<int>((std::min<std::size_t>(rows, 32) + 7) / 8);
+  const int ntiles = TilesFor(rows);
   // Candidates: every variant and split count; cost = the largest number of
   // weight blocks a CTA streams (one wave of CTAs), plus a small charge per
   // split for the activation slice and the cluster reduction.
   double best_cost = 1e30;
   for (int variant = 0; variant < kPlannerVariants; ++variant) {
+    if (ntiles > 4 && !WideVariant(variant))
+      continue;
     const VariantShape& v = kVariants[variant];
     const int rows_per_cta = 16 * v.cta_groups;
     const int panels = (groups_total * 16 + rows_per_cta - 1) / rows_per_cta;
@@ -703,6 +741,20 @@ int LaunchProduct(WeightFormat format, const std::uint16_t* x, const void* w,
     plan = StreamPlan(format, rows, in, out);
   if (plan.variant < 0)
     plan = PlanProduct(format, rows, in, out, 0);
+  if (plan.variant < 0 && plan_in == nullptr && rows > 32) {
+    // No one-launch plan for this many rows (the activation slice of a
+    // long reduction does not fit): launches of 32 rows each.
+    for (std::size_t first = 0; first < rows; first += 32) {
+      const std::size_t count = std::min<std::size_t>(32, rows - first);
+      const int status = LaunchProduct(
+          format, x + first * in, w, y != nullptr ? y + first * out : nullptr,
+          y_bf16 != nullptr ? y_bf16 + first * out : nullptr, count, in, out,
+          accumulate, nullptr, stream, independent);
+      if (status != kOk)
+        return status;
+    }
+    return kOk;
+  }
   if (plan.variant == kTensorCoreVariant) {
     if (format == WeightFormat::kQ8Tiles)
       return LaunchTensorCoreProduct(x, w, y, y_bf16, rows, in, out,
@@ -719,7 +771,9 @@ int LaunchProduct(WeightFormat format, const std::uint16_t* x, const void* w,
       (k_blocks + plan.blocks_per_split - 1) / plan.blocks_per_split !=
           plan.splits)
     return kUnsupported;
-  const int ntiles = static_cast<int>((rows + 7) / 8);
+  const int ntiles = TilesFor(rows);
+  if (ntiles > 4 && !WideVariant(plan.variant))
+    return kUnsupported;
   const Footprint fp =
       FootprintOf(f, plan.variant, ntiles, plan.blocks_per_split);
   if (fp.smem > kMaxProductSmem)
@@ -733,12 +787,13 @@ int LaunchProduct(WeightFormat format, const std::uint16_t* x, const void* w,
   // The dynamic shared-memory limit is per function and device.
   {
     static std::mutex mutex;
-    static std::size_t configured[8][3][4][kNumVariants] = {};
+    static std::size_t configured[8][3][6][kNumVariants] = {};
     int device = 0;
     if (cudaGetDevice(&device) != cudaSuccess)
       return kCudaError;
     std::lock_guard<std::mutex> lock(mutex);
-    std::size_t& have = configured[device & 7][f][ntiles - 1][plan.variant];
+    std::size_t& have =
+        configured[device & 7][f][TileIndex(ntiles)][plan.variant];
     if (have < fp.smem) {
       if (cudaFuncSetAttribute(kernel,
                                cudaFuncAttributeMaxDynamicSharedMemorySize,

@@ -26,8 +26,11 @@ constexpr int kTileRows = 16;
 constexpr int kTileColumns = 32;
 constexpr int kQ8TileBytes = 16 * 32 + 16 * 2;
 constexpr int kBf16TileBytes = 16 * 32 * 2;
-/// Most activation rows one launch takes (4 MMA column tiles of 8).
-constexpr int kMaxProductRows = 32;
+/// Most activation rows one launch takes (up to 16 MMA column tiles of 8;
+/// 33..128 rows on the small CTA shapes only).
+constexpr int kMaxProductRows = 128;
+/// Most activation rows the tensor-core kernel takes.
+constexpr int kTensorCoreMaxRows = 32;
 /// Longest reduction slice one CTA holds in shared memory (explicit plans).
 constexpr int kMaxSliceColumns = 2048;
 /// Longest slice the planner's cost model gives one CTA.

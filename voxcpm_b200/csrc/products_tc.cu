@@ -501,7 +501,7 @@ bool EncodeActivations(const std::uint16_t* x, std::size_t rows,
 ProductPlan PlanTensorCoreProduct(std::size_t rows, std::size_t in,
                                   std::size_t out, int sms) {
   ProductPlan plan;
-  if (rows < 1 || rows > kMaxProductRows || in == 0 ||
+  if (rows < 1 || rows > kTensorCoreMaxRows || in == 0 ||
       in % kTileColumns != 0 || out == 0)
     return plan;
   const int k_blocks = static_cast<int>(in / kTileColumns);
@@ -526,7 +526,7 @@ int LaunchTensorCoreProduct(const std::uint16_t* x, const void* w, float* y,
                             const ProductPlan& plan, cudaStream_t stream,
                             bool independent, bool programmatic) {
   const int k_blocks = static_cast<int>(in / kTileColumns);
-  if (rows < 1 || rows > kMaxProductRows || plan.splits < 1 ||
+  if (rows < 1 || rows > kTensorCoreMaxRows || plan.splits < 1 ||
       plan.splits > 8 || plan.blocks_per_split < 1 ||
       plan.blocks_per_split > kTensorCoreMaxBlocks ||
       (k_blocks + plan.blocks_per_split - 1) / plan.blocks_per_split !=
