@@ -38,6 +38,7 @@
 #include "products.cuh"
 #include "product_math.cuh"
 #include "tcgen05.cuh"
+#include "tensor_map.cuh"
 #include "vx_common.cuh"
 
 #include <cuda.h>
@@ -435,28 +436,6 @@ __global__ void __launch_bounds__(kTcThreads, 1)
   }
 }
 
-/// cuTensorMapEncodeTiled, reached through the runtime's driver entry
-/// point (no link against the driver library).
-using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType,
-                                   cuuint32_t, void*, const cuuint64_t*,
-                                   const cuuint64_t*, const cuuint32_t*,
-                                   const cuuint32_t*, CUtensorMapInterleave,
-                                   CUtensorMapSwizzle, CUtensorMapL2promotion,
-                                   CUtensorMapFloatOOBfill);
-
-EncodeTiledFn TensorMapEncoder() {
-  static const EncodeTiledFn fn = [] {
-    void* f = nullptr;
-    cudaDriverEntryPointQueryResult found;
-    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f,
-                                cudaEnableDefault, &found) != cudaSuccess ||
-        found != cudaDriverEntryPointSuccess)
-      return static_cast<EncodeTiledFn>(nullptr);
-    return reinterpret_cast<EncodeTiledFn>(f);
-  }();
-  return fn;
-}
-
 /// The tensor map of x [rows][in] bf16 for the B operand. Preferred: x
 /// viewed as 3-D {8 columns, rows, in / 8 chunks} (strides in*2 and 16
 /// bytes) with a box of {8, 32, 32}, which lands one part (32 chunks of all
@@ -465,35 +444,23 @@ EncodeTiledFn TensorMapEncoder() {
 /// rows, 32 requests per part (`*boxes` = 32).
 bool EncodeActivations(const std::uint16_t* x, std::size_t rows,
                        std::size_t in, CUtensorMap* map, int* boxes) {
-  const EncodeTiledFn encode = TensorMapEncoder();
-  if (encode == nullptr)
-    return false;
-  void* base = const_cast<std::uint16_t*>(x);
   {
-    const cuuint64_t dims[3] = {8, static_cast<cuuint64_t>(rows),
-                                static_cast<cuuint64_t>(in / 8)};
-    const cuuint64_t strides[2] = {static_cast<cuuint64_t>(in) * 2, 16};
-    const cuuint32_t box[3] = {8, static_cast<cuuint32_t>(kTcXRows),
-                               4 * kTcPartBlocks};
-    const cuuint32_t element_strides[3] = {1, 1, 1};
-    if (encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 3, base, dims, strides,
-               box, element_strides, CU_TENSOR_MAP_INTERLEAVE_NONE,
-               CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
-               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS) {
+    const std::uint64_t dims[3] = {8, rows, in / 8};
+    const std::uint64_t strides[2] = {in * 2, 16};
+    const std::uint32_t box[3] = {8, static_cast<std::uint32_t>(kTcXRows),
+                                  4 * kTcPartBlocks};
+    if (EncodeBf16TensorMap(map, x, 3, dims, strides, box,
+                            CU_TENSOR_MAP_SWIZZLE_NONE)) {
       *boxes = 1;
       return true;
     }
   }
-  const cuuint64_t dims[2] = {static_cast<cuuint64_t>(in),
-                              static_cast<cuuint64_t>(rows)};
-  const cuuint64_t strides[1] = {static_cast<cuuint64_t>(in) * 2};
-  const cuuint32_t box[2] = {8, static_cast<cuuint32_t>(kTcXRows)};
-  const cuuint32_t element_strides[2] = {1, 1};
+  const std::uint64_t dims[2] = {in, rows};
+  const std::uint64_t strides[1] = {in * 2};
+  const std::uint32_t box[2] = {8, static_cast<std::uint32_t>(kTcXRows)};
   *boxes = 32;
-  return encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, base, dims, strides,
-                box, element_strides, CU_TENSOR_MAP_INTERLEAVE_NONE,
-                CU_TENSOR_MAP_SWIZZLE_NONE, CU_TENSOR_MAP_L2_PROMOTION_NONE,
-                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
+  return EncodeBf16TensorMap(map, x, 2, dims, strides, box,
+                             CU_TENSOR_MAP_SWIZZLE_NONE);
 }
 
 }  // namespace
@@ -604,6 +571,56 @@ int LaunchTensorCoreProduct(const std::uint16_t* x, const void* w, float* y,
   if (cudaLaunchKernelEx(&config, kernel, args, x_map) != cudaSuccess)
     return kCudaError;
   return kOk;
+}
+
+namespace {
+
+/// cuTensorMapEncodeTiled through the runtime's driver entry point.
+using EncodeTiledFn = CUresult (*)(CUtensorMap*, CUtensorMapDataType,
+                                   cuuint32_t, void*, const cuuint64_t*,
+                                   const cuuint64_t*, const cuuint32_t*,
+                                   const cuuint32_t*, CUtensorMapInterleave,
+                                   CUtensorMapSwizzle, CUtensorMapL2promotion,
+                                   CUtensorMapFloatOOBfill);
+
+EncodeTiledFn TensorMapEncoder() {
+  static const EncodeTiledFn fn = [] {
+    void* f = nullptr;
+    cudaDriverEntryPointQueryResult found;
+    if (cudaGetDriverEntryPoint("cuTensorMapEncodeTiled", &f,
+                                cudaEnableDefault, &found) != cudaSuccess ||
+        found != cudaDriverEntryPointSuccess)
+      return static_cast<EncodeTiledFn>(nullptr);
+    return reinterpret_cast<EncodeTiledFn>(f);
+  }();
+  return fn;
+}
+
+}  // namespace
+
+bool EncodeBf16TensorMap(CUtensorMap* map, const void* base, int rank,
+                         const std::uint64_t* dims,
+                         const std::uint64_t* strides,
+                         const std::uint32_t* box, CUtensorMapSwizzle swizzle) {
+  const EncodeTiledFn encode = TensorMapEncoder();
+  if (encode == nullptr || rank < 1 || rank > 5)
+    return false;
+  cuuint64_t d[5];
+  cuuint64_t st[4];
+  cuuint32_t b[5];
+  cuuint32_t e[5];
+  for (int i = 0; i < rank; ++i) {
+    d[i] = dims[i];
+    b[i] = box[i];
+    e[i] = 1;
+    if (i + 1 < rank)
+      st[i] = strides[i];
+  }
+  return encode(map, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16,
+                static_cast<cuuint32_t>(rank), const_cast<void*>(base), d, st,
+                b, e, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
+                CU_TENSOR_MAP_L2_PROMOTION_NONE,
+                CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE) == CUDA_SUCCESS;
 }
 
 }  // namespace vx
