@@ -341,9 +341,10 @@ typedef struct vx_model_config {
  * factors 1 and vocab 0 (set them for real use). */
 VX_API void vx_model_config_released(vx_model_config* config);
 
-/* VoxCPM2's generator on the current device with seeded weights. Replaces
- * Generator::Create (generator.hpp:60-62, generator.cpp:82-174), whose file
- * readers are out of scope. Returns null on failure (vx_last_error). */
+/* VoxCPM2's generator on the current device with seeded weights (benchmarks
+ * and parity tests; vx_generator_create_from_files reads checkpoint files).
+ * Generator::Create (generator.hpp:60-62, generator.cpp:82-174) with a
+ * seeded weight source. Returns null on failure (vx_last_error). */
 typedef struct vx_generator vx_generator;
 VX_API vx_generator* vx_generator_create(const vx_model_config* config,
                                          uint64_t seed, int checkpoint,
@@ -427,12 +428,97 @@ VX_API size_t vx_generator_position(const vx_generator* generator);
 VX_API size_t vx_generator_weight_bytes(const vx_generator* generator);
 VX_API cudaStream_t vx_generator_stream(const vx_generator* generator);
 
+/* ------------------------------------------------------------ model files */
+
+/* Tensor element types (safetensors.hpp:18, same order). Q8_0 is GGML's
+ * 34-byte block: an fp16 scale, then 32 int8 values. */
+#define VX_DTYPE_F32 0
+#define VX_DTYPE_BF16 1
+#define VX_DTYPE_F16 2
+#define VX_DTYPE_I64 3
+#define VX_DTYPE_I32 4
+#define VX_DTYPE_U8 5
+#define VX_DTYPE_Q8_0 6
+
+/* Components of the files: the generator's tensors (model.safetensors names)
+ * and the AudioVAE's (read from a GGUF only; not used by the generator). */
+#define VX_COMPONENT_MODEL 0
+#define VX_COMPONENT_VAE 1
+
+/* One tensor (safetensors.hpp:23-34). `name` and `data` stay valid while
+ * the files are open; `data` is host memory in the mapped file; `shape` is
+ * outermost first; `offset` is the tensor's byte position in its file. */
+typedef struct vx_tensor_info {
+  const char* name;
+  int dtype;
+  int rank;
+  uint64_t shape[8];
+  const void* data;
+  uint64_t bytes;
+  uint64_t offset;
+} vx_tensor_info;
+
+/* The checkpoint files: a Hugging Face directory (config.json,
+ * model.safetensors, tokenizer.json when present) or an audio.cpp VoxCPM2
+ * GGUF file (GGUF v2/v3, config and tokenizer embedded, abbreviated tensor
+ * names resolved). Host only. Replaces ModelFiles::Open
+ * (model_files.hpp:45-51, model_files.cpp:111-180); null on failure
+ * (vx_last_error names the file and the problem). */
+typedef struct vx_model_files vx_model_files;
+VX_API vx_model_files* vx_model_files_open(const char* path);
+VX_API void vx_model_files_close(vx_model_files* files);
+/* ModelFiles::IsVoxCpm2Gguf (model_files.hpp:49-51): a .gguf file whose
+ * header names audio.cpp's VoxCPM2 layout. */
+VX_API int vx_model_files_is_voxcpm2_gguf(const char* path);
+VX_API int vx_model_files_is_gguf(const vx_model_files* files);
+/* config.json / tokenizer.json text (ModelFiles::config, ::tokenizer; the
+ * tokenizer is empty when a directory has none). */
+VX_API const char* vx_model_files_config(const vx_model_files* files);
+VX_API const char* vx_model_files_tokenizer(const vx_model_files* files);
+VX_API size_t vx_model_files_count(const vx_model_files* files, int component);
+VX_API vx_status vx_model_files_tensor(const vx_model_files* files,
+                                       int component, size_t index,
+                                       vx_tensor_info* info);
+/* ModelFiles::Model / ::Vae (model_files.hpp:60-63); VX_INVALID when
+ * absent. */
+VX_API vx_status vx_model_files_find(const vx_model_files* files,
+                                     int component, const char* name,
+                                     vx_tensor_info* info);
+
+/* Parses config.json text into the generator's configuration and checks
+ * that the kernels serve it. Replaces ParseConfig + IsSupported
+ * (config.hpp:89-98, config.cpp:144-323). `max_length` is config.json's
+ * max_length; the LongRoPE factors and scale are those the reference
+ * applies. VX_INVALID with the key named on failure. */
+VX_API vx_status vx_parse_config(const char* json, size_t length,
+                                 vx_model_config* config);
+
+/* The generator with the files' weights (Generator::Create(config, files),
+ * generator.hpp:60-62): every model tensor must be one the generator takes,
+ * with the expected shape (weights.cpp:187-197, :316-318). Matrices become
+ * Q8 tiles when Q8_0, bf16 tiles in the DiT and bf16 rows elsewhere
+ * (weights.cpp:44-144); F16/F32/Q8_0 vectors are converted to bf16 on the
+ * device. The files may be closed afterwards. Null on failure. */
+VX_API vx_generator* vx_generator_create_from_files(
+    const vx_model_config* config, const vx_model_files* files,
+    int cache_type);
+
+/* Device conversions to bf16, round to nearest even with NaN kept quiet
+ * (kernels/convert_kernels.hpp:12-23). Device arrays; `count` values (a
+ * multiple of 32 for Q8_0). */
+VX_API vx_status vx_half_to_bf16(const uint16_t* input, uint16_t* output,
+                                 size_t count, cudaStream_t stream);
+VX_API vx_status vx_float_to_bf16(const float* input, uint16_t* output,
+                                  size_t count, cudaStream_t stream);
+VX_API vx_status vx_q8_0_to_bf16(const uint8_t* blocks, uint16_t* output,
+                                 size_t count, cudaStream_t stream);
+
 /* ------------------------------------------------------------ synthetic weights */
 
 /* Host: GGML Q8_0 blocks [rows][in/32] of seeded random weights, a pure
  * function of (seed, tensor, index): q uniform in [-127, 127], one fp16
- * scale |N(0, scale_std)| per 32 values. Stands in for the checkpoint reader
- * (weights.cpp:26-327, out of scope: no checkpoint is available). */
+ * scale |N(0, scale_std)| per 32 values. The seeded checkpoint of
+ * vx_generator_create (no released checkpoint is available here). */
 VX_API vx_status vx_random_q8_0(uint64_t seed, uint64_t tensor, size_t rows,
                          size_t in, float scale_std, uint8_t* blocks);
 /* Host: `count` seeded bf16 values bf16(mean + N(0, std)). */

@@ -14,8 +14,8 @@ from __future__ import annotations
 import numpy as np
 
 from . import (BF16_ROWS, Q8_0, _f32, add_bias, assemble_dit, attention, bf16_bits, bf16_value,
-               concat_rows, euler_schedule, gather_rows, guided_euler, linear, prepend_special, quantize,
-               qkv_rope, random_bf16, random_q8_0, rms_norm, rope_table, sinusoid, swiglu, to_bf16)
+               concat_rows, euler_schedule, gather_rows, guided_euler, linear, prepend_special, q8_0_dequant,
+               quantize, qkv_rope, random_bf16, random_q8_0, rms_norm, rope_table, sinusoid, swiglu, to_bf16)
 
 Q8_SCALE_STD = 0.02 / 127
 MATRIX_STD = 0.02
@@ -51,8 +51,13 @@ def _stack_config(s) -> dict:
 class Weights:
     """weights.cpp:268-304: every tensor in the reference's order and names."""
 
-    def __init__(self, config, seed: int, q8: bool):
-        self.seed, self.q8 = seed, q8
+    def __init__(self, config, seed: int, q8: bool, source: dict | None = None):
+        """`source` (name -> ("Q8_0", GGML blocks) or ("BF16", bits)) stands
+        for checkpoint files: matrices follow the file rule of
+        weights.cpp:44-144 (Q8_0 blocks when every part is Q8_0 and, for
+        fused parts, fills whole 16-row tiles; bf16 rows otherwise, Q8_0
+        parts dequantized to bf16(scale * q))."""
+        self.seed, self.q8, self.source = seed, q8, source
         c = config
         hidden, local, dit, feat = c.lm.hidden, c.encoder.hidden, c.dit.hidden, c.feat_dim
         self.embed = self.vector("base_lm.embed_tokens.weight", c.vocab * hidden, 0.0, 0.5) if c.vocab else None
@@ -80,9 +85,21 @@ class Weights:
         self.stop_head = self.linear("stop_head", hidden, 2, False)
 
     def vector(self, name, count, mean, std):
+        if self.source is not None:
+            kind, values = self.source[name]
+            assert kind == "BF16" and values.size == count, name
+            return values
         return random_bf16(self.seed, tensor_id(name), count, mean, std)
 
-    def matrix(self, names, outs, n_in):
+    def matrix(self, names, outs, n_in, fused=True):
+        if self.source is not None:
+            parts = [self.source[n] for n in names]
+            whole = all(o % 16 == 0 for o in outs) or not fused
+            if all(kind == "Q8_0" for kind, _ in parts) and whole and n_in % 32 == 0:
+                return Q8_0, np.concatenate([v for _, v in parts])
+            rows = [v if kind == "BF16" else bf16_bits(q8_0_dequant(v, o, n_in))
+                    for (kind, v), o in zip(parts, outs)]
+            return BF16_ROWS, np.concatenate([r.reshape(-1) for r in rows])
         if self.q8:
             parts = [random_q8_0(self.seed, tensor_id(n), o, n_in, Q8_SCALE_STD) for n, o in zip(names, outs)]
             return Q8_0, np.concatenate(parts)
@@ -90,7 +107,7 @@ class Weights:
         return BF16_ROWS, np.concatenate(parts)
 
     def linear(self, prefix, n_in, n_out, bias):
-        fmt, w = self.matrix([prefix + ".weight"], [n_out], n_in)
+        fmt, w = self.matrix([prefix + ".weight"], [n_out], n_in, fused=False)
         b = self.vector(prefix + ".bias", n_out, 0.0, MATRIX_STD) if bias else None
         return Projection(fmt, w, b, n_in, n_out)
 
@@ -131,11 +148,12 @@ class Cache:
 class OracleGenerator:
     """generator.cpp:82-538 on the CPU."""
 
-    def __init__(self, config, seed: int = 0, q8: bool = True, bf16_cache: bool = False, threads: int = 0):
+    def __init__(self, config, seed: int = 0, q8: bool = True, bf16_cache: bool = False, threads: int = 0,
+                 source: dict | None = None):
         self.c = config
         self.threads = threads
         self.bf16_cache = bf16_cache
-        self.w = Weights(config, seed, q8)
+        self.w = Weights(config, seed, q8, source)
         positions = max(config.max_length, 64)
         factors = np.array(list(config.rope_factors)[: config.lm.head_dim // 2], np.float64)
         self.rope = rope_table(config.rope_theta, config.lm.head_dim, factors, config.rope_scaling, positions)

@@ -76,6 +76,19 @@ class ModelConfig(ctypes.Structure):
 CHECKPOINT_Q8 = 0
 CHECKPOINT_BF16 = 1
 
+# Tensor element types (safetensors.hpp:18) and file components.
+DTYPE_F32, DTYPE_BF16, DTYPE_F16, DTYPE_I64, DTYPE_I32, DTYPE_U8, DTYPE_Q8_0 = range(7)
+DTYPE_NAMES = ("F32", "BF16", "F16", "I64", "I32", "U8", "Q8_0")
+COMPONENT_MODEL = 0
+COMPONENT_VAE = 1
+
+
+class TensorInfo(ctypes.Structure):
+    """vx_tensor_info (safetensors.hpp:23-34)."""
+
+    _fields_ = [("name", c_char_p), ("dtype", c_int), ("rank", c_int), ("shape", c_uint64 * 8),
+                ("data", c_void_p), ("bytes", c_uint64), ("offset", c_uint64)]
+
 # name -> (restype, argtypes)
 SIGNATURES: dict[str, tuple] = {
     "vx_last_error": (c_char_p, []),
@@ -171,6 +184,20 @@ SIGNATURES: dict[str, tuple] = {
     "vx_generator_position": (c_size_t, [c_void_p]),
     "vx_generator_weight_bytes": (c_size_t, [c_void_p]),
     "vx_generator_stream": (c_void_p, [c_void_p]),
+    "vx_model_files_open": (c_void_p, [c_char_p]),
+    "vx_model_files_close": (None, [c_void_p]),
+    "vx_model_files_is_voxcpm2_gguf": (c_int, [c_char_p]),
+    "vx_model_files_is_gguf": (c_int, [c_void_p]),
+    "vx_model_files_config": (c_char_p, [c_void_p]),
+    "vx_model_files_tokenizer": (c_char_p, [c_void_p]),
+    "vx_model_files_count": (c_size_t, [c_void_p, c_int]),
+    "vx_model_files_tensor": (c_int, [c_void_p, c_int, c_size_t, POINTER(TensorInfo)]),
+    "vx_model_files_find": (c_int, [c_void_p, c_int, c_char_p, POINTER(TensorInfo)]),
+    "vx_parse_config": (c_int, [c_char_p, c_size_t, POINTER(ModelConfig)]),
+    "vx_generator_create_from_files": (c_void_p, [POINTER(ModelConfig), c_void_p, c_int]),
+    "vx_half_to_bf16": (c_int, [c_void_p, c_void_p, c_size_t, c_void_p]),
+    "vx_float_to_bf16": (c_int, [c_void_p, c_void_p, c_size_t, c_void_p]),
+    "vx_q8_0_to_bf16": (c_int, [c_void_p, c_void_p, c_size_t, c_void_p]),
     "vx_gemm_create": (c_void_p, [c_void_p]),
     "vx_gemm_destroy": (None, [c_void_p]),
     "vx_gemm_linear": (

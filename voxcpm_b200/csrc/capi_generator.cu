@@ -2,6 +2,7 @@
 // prefill, step, the DiT patch and state access. Exceptions of the model
 // layer become status codes with the thread's last error message.
 #include "model.cuh"
+#include "model_files.h"
 #include "vx_status.h"
 
 #include "../../include/voxcpm_b200.h"
@@ -60,6 +61,61 @@ vx_status Guard(vx_generator* g, const char* what, F&& body) {
 
 }  // namespace
 
+namespace {
+
+/// The C configuration as the model layer's; false (with the thread's error
+/// set) when the head size is out of range.
+bool ToModelConfig(const vx_model_config& config, vx::ModelConfig* out,
+                   const char* what) {
+  vx::ModelConfig c;
+  c.lm = FromC(config.lm);
+  c.residual_lm = FromC(config.residual_lm);
+  c.encoder = FromC(config.encoder);
+  c.dit = FromC(config.dit);
+  c.rope_theta = config.rope_theta;
+  c.rope_scaling = config.rope_scaling;
+  const int half = config.lm.head_dim / 2;
+  if (half <= 0 || half > 64) {
+    vx::Fail(vx::kInvalid, std::string(what) + ": head_dim must be in 2..128");
+    return false;
+  }
+  c.rope_factors.assign(config.rope_factors, config.rope_factors + half);
+  c.patch_size = config.patch_size;
+  c.feat_dim = config.feat_dim;
+  c.fsq_latent_dim = config.fsq_latent_dim;
+  c.fsq_scale = config.fsq_scale;
+  c.max_length = config.max_length;
+  c.vocab = config.vocab;
+  *out = std::move(c);
+  return true;
+}
+
+vx_generator* Create(const vx_model_config* config, uint64_t seed,
+                     int checkpoint, int cache_type,
+                     const vx_model_files* files, const char* what) {
+  if (config == nullptr ||
+      (checkpoint != VX_CHECKPOINT_Q8 && checkpoint != VX_CHECKPOINT_BF16) ||
+      (cache_type != VX_CACHE_F32 && cache_type != VX_CACHE_BF16)) {
+    vx::Fail(vx::kInvalid, std::string(what) + ": bad arguments");
+    return nullptr;
+  }
+  vx::ModelConfig c;
+  if (!ToModelConfig(*config, &c, what))
+    return nullptr;
+  std::string error;
+  auto impl = vx::Generator::Create(
+      c, seed, static_cast<vx::CheckpointKind>(checkpoint),
+      cache_type == VX_CACHE_BF16 ? vx::CacheType::kBf16 : vx::CacheType::kF32,
+      &error, vx::FilesOf(files));
+  if (!impl) {
+    vx::Fail(vx::kCudaError, std::string(what) + ": " + error);
+    return nullptr;
+  }
+  return new vx_generator{std::move(impl)};
+}
+
+}  // namespace
+
 extern "C" {
 
 void vx_model_config_released(vx_model_config* config) {
@@ -86,41 +142,19 @@ void vx_model_config_released(vx_model_config* config) {
 
 vx_generator* vx_generator_create(const vx_model_config* config, uint64_t seed,
                                   int checkpoint, int cache_type) {
-  if (config == nullptr ||
-      (checkpoint != VX_CHECKPOINT_Q8 && checkpoint != VX_CHECKPOINT_BF16) ||
-      (cache_type != VX_CACHE_F32 && cache_type != VX_CACHE_BF16)) {
-    vx::Fail(vx::kInvalid, "vx_generator_create: bad arguments");
+  return Create(config, seed, checkpoint, cache_type, nullptr,
+                "vx_generator_create");
+}
+
+vx_generator* vx_generator_create_from_files(const vx_model_config* config,
+                                             const vx_model_files* files,
+                                             int cache_type) {
+  if (vx::FilesOf(files) == nullptr) {
+    vx::Fail(vx::kInvalid, "vx_generator_create_from_files: null files");
     return nullptr;
   }
-  vx::ModelConfig c;
-  c.lm = FromC(config->lm);
-  c.residual_lm = FromC(config->residual_lm);
-  c.encoder = FromC(config->encoder);
-  c.dit = FromC(config->dit);
-  c.rope_theta = config->rope_theta;
-  c.rope_scaling = config->rope_scaling;
-  const int half = config->lm.head_dim / 2;
-  if (half <= 0 || half > 64) {
-    vx::Fail(vx::kInvalid, "vx_generator_create: head_dim must be in 2..128");
-    return nullptr;
-  }
-  c.rope_factors.assign(config->rope_factors, config->rope_factors + half);
-  c.patch_size = config->patch_size;
-  c.feat_dim = config->feat_dim;
-  c.fsq_latent_dim = config->fsq_latent_dim;
-  c.fsq_scale = config->fsq_scale;
-  c.max_length = config->max_length;
-  c.vocab = config->vocab;
-  std::string error;
-  auto impl = vx::Generator::Create(
-      c, seed, static_cast<vx::CheckpointKind>(checkpoint),
-      cache_type == VX_CACHE_BF16 ? vx::CacheType::kBf16 : vx::CacheType::kF32,
-      &error);
-  if (!impl) {
-    vx::Fail(vx::kCudaError, "vx_generator_create: " + error);
-    return nullptr;
-  }
-  return new vx_generator{std::move(impl)};
+  return Create(config, 0, VX_CHECKPOINT_Q8, cache_type, files,
+                "vx_generator_create_from_files");
 }
 
 void vx_generator_destroy(vx_generator* generator) { delete generator; }

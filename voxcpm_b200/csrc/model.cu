@@ -11,6 +11,8 @@
 // - every kernel is launched with programmatic dependent launch, so the
 //   products' weight streams start while the previous kernel drains.
 #include "model.cuh"
+#include "convert.cuh"
+#include "model_files.h"
 #include "vx_common.cuh"
 #include "vx_status.h"
 
@@ -91,44 +93,93 @@ void ThrowStatus(int status, const std::string& what) {
 constexpr float kQ8ScaleStd = 0.02f / 127.0f;  // |N(0, 0.02)| / 127
 constexpr float kMatrixStd = 0.02f;
 
-/// Takes every tensor of a seeded checkpoint in the reference's order
-/// (weights.cpp:268-304); without an arena it only counts bytes.
+/// Takes every tensor of the generator in the reference's order
+/// (weights.cpp:268-304), from a seeded checkpoint or from checkpoint files;
+/// without an arena it only counts bytes.
+///
+/// Files follow the reference's format rule (weights.cpp:47-144): a matrix
+/// of Q8_0 blocks becomes Q8 tiles; other matrices become bf16 tiles in the
+/// DiT stack and bf16 rows elsewhere; fused parts (qkv, gate_up) keep tiles
+/// only when every part is Q8_0 (for Q8 tiles) and fills whole 16-row tiles;
+/// a reduction that is not a multiple of 32 keeps bf16 rows. Vectors and the
+/// embedding table become bf16. F16, F32 and Q8_0 sources are converted on
+/// the device after the raw bytes are copied in.
 class Uploader {
  public:
-  Uploader(std::uint64_t seed, CheckpointKind kind, DeviceArena* arena,
-           cudaStream_t stream)
-      : seed_(seed), kind_(kind), arena_(arena), stream_(stream) {}
+  Uploader(std::uint64_t seed, CheckpointKind kind, const ModelFiles* files,
+           DeviceArena* arena, cudaStream_t stream)
+      : seed_(seed), kind_(kind), files_(files), arena_(arena),
+        stream_(stream) {}
   ~Uploader() {
+    cudaStreamSynchronize(stream_);
     if (pinned_ != nullptr)
       cudaFreeHost(pinned_);
+    for (int i = 0; i < 2; ++i) {
+      if (bounce_[i] != nullptr)
+        cudaFreeHost(bounce_[i]);
+      if (bounce_done_[i] != nullptr)
+        cudaEventDestroy(bounce_done_[i]);
+    }
     if (staging_ != nullptr)
       cudaFree(staging_);
+    if (rows_ != nullptr)
+      cudaFree(rows_);
   }
 
-  const std::uint16_t* Vector(const std::string& name, std::size_t count,
+  /// A vector (or the embedding table) as bf16; seeded values are
+  /// bf16(mean + N(0, std)).
+  const std::uint16_t* Vector(const std::string& name,
+                              std::initializer_list<std::size_t> shape,
                               float mean, float std) {
+    std::size_t count = 1;
+    for (const std::size_t d : shape)
+      count *= d;
+    const Tensor* tensor = files_ != nullptr ? &Find(name, shape) : nullptr;
     auto* target = arena_->Take<std::uint16_t>(count);
     if (target == nullptr)
       return nullptr;
-    auto* host = static_cast<std::uint16_t*>(Pinned(count * 2));
-    ThrowStatus(vx_random_bf16(seed_, TensorId(name), count, mean, std, host),
-                "seeded " + name);
-    ThrowCuda(cudaMemcpyAsync(target, host, count * 2, cudaMemcpyHostToDevice,
-                              stream_),
-              "upload " + name);
+    if (tensor != nullptr) {
+      ToBf16(*tensor, target);
+    } else {
+      auto* host = static_cast<std::uint16_t*>(Pinned(count * 2));
+      ThrowStatus(vx_random_bf16(seed_, TensorId(name), count, mean, std, host),
+                  "seeded " + name);
+      ThrowCuda(cudaMemcpyAsync(target, host, count * 2,
+                                cudaMemcpyHostToDevice, stream_),
+                "upload " + name);
+    }
     ThrowCuda(cudaStreamSynchronize(stream_), "upload " + name);
     return target;
   }
 
-  /// `names` ([outs[i]][in] each) side by side: Q8 tiles for a Q8
-  /// checkpoint, bf16 tiles for the DiT of a bf16 checkpoint, bf16 rows
-  /// otherwise (weights.cpp:100-132, :138-144).
+  /// `names` ([outs[i]][in] each) side by side as one matrix. A seeded
+  /// checkpoint uses Q8 tiles for kQ8, bf16 tiles for the DiT of kBf16 and
+  /// bf16 rows otherwise. `fused` applies the whole-tile rule of fused
+  /// matrices to files (weights.cpp:57-86); single matrices follow
+  /// TakeMatrix (:44-54).
   Projection Fused(const std::vector<std::string>& names,
-                   const std::vector<int>& outs, int in, bool dit) {
+                   const std::vector<int>& outs, int in, bool dit,
+                   bool fused = true) {
     Projection p;
-    p.format = kind_ == CheckpointKind::kQ8
-                   ? WeightFormat::kQ8Tiles
-                   : (dit ? WeightFormat::kBf16Tiles : WeightFormat::kBf16);
+    std::vector<const Tensor*> tensors;
+    if (files_ != nullptr) {
+      bool q8 = true;
+      bool whole = true;
+      for (std::size_t i = 0; i < names.size(); ++i) {
+        tensors.push_back(&Find(names[i], {static_cast<std::size_t>(outs[i]),
+                                           static_cast<std::size_t>(in)}));
+        q8 = q8 && tensors.back()->dtype == DType::kQ8_0;
+        whole = whole && (!fused || outs[i] % 16 == 0);
+      }
+      p.format = in % 32 != 0 ? WeightFormat::kBf16
+                 : q8 && whole ? WeightFormat::kQ8Tiles
+                 : dit && whole ? WeightFormat::kBf16Tiles
+                                : WeightFormat::kBf16;
+    } else {
+      p.format = kind_ == CheckpointKind::kQ8
+                     ? WeightFormat::kQ8Tiles
+                     : (dit ? WeightFormat::kBf16Tiles : WeightFormat::kBf16);
+    }
     p.in = in;
     p.out = std::accumulate(outs.begin(), outs.end(), 0);
     std::size_t total = 0;
@@ -139,7 +190,11 @@ class Uploader {
     if (target == nullptr)
       return p;
     for (std::size_t i = 0; i < names.size(); ++i) {
-      Write(names[i], p.format, outs[i], in, target);
+      if (files_ != nullptr)
+        WriteFile(*tensors[i], p.format, outs[i], in, target);
+      else
+        Write(names[i], p.format, outs[i], in, target);
+      ThrowCuda(cudaStreamSynchronize(stream_), "upload " + names[i]);
       target += Bytes(p.format, outs[i], in);
     }
     return p;
@@ -147,9 +202,10 @@ class Uploader {
 
   Projection Linear(const std::string& prefix, int in, int out, bool bias,
                     bool dit = false) {
-    Projection p = Fused({prefix + ".weight"}, {out}, in, dit);
+    Projection p = Fused({prefix + ".weight"}, {out}, in, dit, false);
     if (bias)
-      p.bias = Vector(prefix + ".bias", out, 0.0f, kMatrixStd);
+      p.bias = Vector(prefix + ".bias", {static_cast<std::size_t>(out)}, 0.0f,
+                      kMatrixStd);
     return p;
   }
 
@@ -158,20 +214,20 @@ class Uploader {
     StackWeights stack;
     stack.config = config;
     const int hidden = config.hidden;
+    const std::size_t h = static_cast<std::size_t>(hidden);
     const int q = config.heads * config.head_dim;
     const int kv = config.kv_heads * config.head_dim;
     for (int index = 0; index < config.layers; ++index) {
       const std::string layer = prefix + ".layers." + std::to_string(index);
       LayerWeights w;
-      w.input_norm =
-          Vector(layer + ".input_layernorm.weight", hidden, 1.0f, 0.05f);
+      w.input_norm = Vector(layer + ".input_layernorm.weight", {h}, 1.0f, 0.05f);
       const std::string attn = layer + ".self_attn.";
       w.qkv = Fused({attn + "q_proj.weight", attn + "k_proj.weight",
                      attn + "v_proj.weight"},
                     {q, kv, kv}, hidden, dit);
       w.o = Linear(attn + "o_proj", q, hidden, false, dit);
-      w.post_norm = Vector(layer + ".post_attention_layernorm.weight", hidden,
-                           1.0f, 0.05f);
+      w.post_norm =
+          Vector(layer + ".post_attention_layernorm.weight", {h}, 1.0f, 0.05f);
       w.gate_up = Fused(
           {layer + ".mlp.gate_proj.weight", layer + ".mlp.up_proj.weight"},
           {config.intermediate, config.intermediate}, hidden, dit);
@@ -179,9 +235,12 @@ class Uploader {
                       false, dit);
       stack.layers.push_back(w);
     }
-    stack.norm = Vector(prefix + ".norm.weight", hidden, 1.0f, 0.05f);
+    stack.norm = Vector(prefix + ".norm.weight", {h}, 1.0f, 0.05f);
     return stack;
   }
+
+  /// Tensors taken from the files so far.
+  std::size_t taken() const { return taken_; }
 
  private:
   static std::size_t Bytes(WeightFormat format, int out, int in) {
@@ -196,24 +255,145 @@ class Uploader {
     return static_cast<std::size_t>(out) * in * 2;
   }
 
+  /// The named tensor of the files with the expected shape
+  /// (weights.cpp:187-197).
+  const Tensor& Find(const std::string& name,
+                     std::initializer_list<std::size_t> shape) {
+    const Tensor* tensor = files_->Model(name);
+    if (tensor == nullptr)
+      throw std::runtime_error("the checkpoint lacks " + name);
+    if (!std::equal(tensor->shape.begin(), tensor->shape.end(), shape.begin(),
+                    shape.end()))
+      throw std::runtime_error(name + " has an unexpected shape");
+    ++taken_;
+    return *tensor;
+  }
+
   void* Pinned(std::size_t bytes) {
     if (bytes > pinned_bytes_) {
-      if (pinned_ != nullptr)
+      if (pinned_ != nullptr) {
+        ThrowCuda(cudaStreamSynchronize(stream_), "upload");
         cudaFreeHost(pinned_);
+        pinned_ = nullptr;
+      }
       ThrowCuda(cudaMallocHost(&pinned_, bytes), "cudaMallocHost");
       pinned_bytes_ = bytes;
     }
     return pinned_;
   }
 
-  void* Staging(std::size_t bytes) {
-    if (bytes > staging_bytes_) {
-      if (staging_ != nullptr)
-        cudaFree(staging_);
-      ThrowCuda(cudaMalloc(&staging_, bytes), "cudaMalloc staging");
-      staging_bytes_ = bytes;
+  static void* Grow(void*& buffer, std::size_t& size, std::size_t bytes,
+                    cudaStream_t stream) {
+    if (bytes > size) {
+      if (buffer != nullptr) {
+        ThrowCuda(cudaStreamSynchronize(stream), "upload");
+        cudaFree(buffer);
+        buffer = nullptr;
+      }
+      ThrowCuda(cudaMalloc(&buffer, bytes), "cudaMalloc staging");
+      size = bytes;
     }
-    return staging_;
+    return buffer;
+  }
+  void* Staging(std::size_t bytes) {
+    return Grow(staging_, staging_bytes_, bytes, stream_);
+  }
+  void* Rows(std::size_t bytes) {
+    return Grow(rows_, rows_bytes_, bytes, stream_);
+  }
+
+  /// Copies `bytes` of (pageable, possibly mapped) host memory to the device
+  /// through two pinned bounce buffers: the memcpy into one overlaps the DMA
+  /// out of the other.
+  void CopyIn(const void* host, std::size_t bytes, void* device) {
+    constexpr std::size_t kChunk = 32u << 20;
+    const auto* from = static_cast<const unsigned char*>(host);
+    auto* to = static_cast<unsigned char*>(device);
+    for (std::size_t done = 0, chunk = 0; done < bytes; done += kChunk, ++chunk) {
+      const int b = static_cast<int>(chunk % 2);
+      if (bounce_[b] == nullptr) {
+        ThrowCuda(cudaMallocHost(&bounce_[b], kChunk), "cudaMallocHost");
+        ThrowCuda(cudaEventCreateWithFlags(&bounce_done_[b],
+                                           cudaEventDisableTiming),
+                  "cudaEventCreate");
+      } else {
+        ThrowCuda(cudaEventSynchronize(bounce_done_[b]), "upload");
+      }
+      const std::size_t n = std::min(kChunk, bytes - done);
+      std::memcpy(bounce_[b], from + done, n);
+      ThrowCuda(cudaMemcpyAsync(to + done, bounce_[b], n,
+                                cudaMemcpyHostToDevice, stream_),
+                "upload");
+      ThrowCuda(cudaEventRecord(bounce_done_[b], stream_), "upload");
+    }
+  }
+
+  static void CheckQ8(const Tensor& tensor) {
+    const std::size_t elements = tensor.Elements();
+    if (elements % 32 != 0 || tensor.bytes != elements / 32 * 34)
+      throw std::runtime_error(tensor.name + " is not whole Q8_0 blocks");
+  }
+
+  /// bf16 of a file tensor at `target` (weights.cpp:215-246).
+  void ToBf16(const Tensor& tensor, std::uint16_t* target) {
+    const std::size_t elements = tensor.Elements();
+    switch (tensor.dtype) {
+      case DType::kBF16:
+        CopyIn(tensor.data, tensor.bytes, target);
+        return;
+      case DType::kF16:
+      case DType::kF32:
+      case DType::kQ8_0: {
+        if (tensor.dtype == DType::kQ8_0)
+          CheckQ8(tensor);
+        void* raw = Staging(tensor.bytes);
+        CopyIn(tensor.data, tensor.bytes, raw);
+        int status = kOk;
+        if (tensor.dtype == DType::kF16)
+          status = HalfToBf16(static_cast<const std::uint16_t*>(raw), target,
+                              elements, stream_);
+        else if (tensor.dtype == DType::kF32)
+          status = FloatToBf16(static_cast<const float*>(raw), target,
+                               elements, stream_);
+        else
+          status = Q8_0ToBf16(static_cast<const std::uint8_t*>(raw), target,
+                              elements, stream_);
+        ThrowStatus(status, "convert " + tensor.name);
+        return;
+      }
+      default:
+        throw std::runtime_error(tensor.name + " has an unsupported type " +
+                                 DTypeName(tensor.dtype));
+    }
+  }
+
+  /// A file tensor [out][in] in `format` at `target` (weights.cpp:159-185).
+  void WriteFile(const Tensor& tensor, WeightFormat format, int out, int in,
+                 unsigned char* target) {
+    switch (format) {
+      case WeightFormat::kBf16:
+        ToBf16(tensor, reinterpret_cast<std::uint16_t*>(target));
+        return;
+      case WeightFormat::kBf16Tiles: {
+        auto* rows = static_cast<std::uint16_t*>(
+            Rows(static_cast<std::size_t>(out) * in * 2));
+        ToBf16(tensor, rows);
+        ThrowStatus(Bf16ToTiles(rows, out, in,
+                                reinterpret_cast<std::uint16_t*>(target),
+                                stream_),
+                    "tiles " + tensor.name);
+        return;
+      }
+      case WeightFormat::kQ8Tiles: {
+        CheckQ8(tensor);
+        void* raw = Staging(tensor.bytes);
+        CopyIn(tensor.data, tensor.bytes, raw);
+        ThrowStatus(Q8_0ToTiles(static_cast<const std::uint8_t*>(raw), out, in,
+                                target, stream_),
+                    "tiles " + tensor.name);
+        return;
+      }
+    }
   }
 
   void Write(const std::string& name, WeightFormat format, int out, int in,
@@ -256,12 +436,18 @@ class Uploader {
 
   std::uint64_t seed_;
   CheckpointKind kind_;
+  const ModelFiles* files_;
   DeviceArena* arena_;
   cudaStream_t stream_;
+  std::size_t taken_ = 0;
   void* pinned_ = nullptr;
   std::size_t pinned_bytes_ = 0;
+  void* bounce_[2] = {nullptr, nullptr};
+  cudaEvent_t bounce_done_[2] = {nullptr, nullptr};
   void* staging_ = nullptr;
   std::size_t staging_bytes_ = 0;
+  void* rows_ = nullptr;
+  std::size_t rows_bytes_ = 0;
 };
 
 GeneratorWeights TakeAll(Uploader& take, const ModelConfig& c) {
@@ -272,12 +458,15 @@ GeneratorWeights TakeAll(Uploader& take, const ModelConfig& c) {
   const int feat = c.feat_dim;
   if (c.vocab > 0)
     w.embed = take.Vector("base_lm.embed_tokens.weight",
-                          static_cast<std::size_t>(c.vocab) * hidden, 0.0f,
-                          0.5f);
+                          {static_cast<std::size_t>(c.vocab),
+                           static_cast<std::size_t>(hidden)},
+                          0.0f, 0.5f);
   w.base_lm = take.Stack("base_lm", c.lm, false);
   w.residual_lm = take.Stack("residual_lm", c.residual_lm, false);
   w.encoder = take.Stack("feat_encoder.encoder", c.encoder, false);
-  w.special = take.Vector("feat_encoder.special_token", local, 0.0f, 1.0f);
+  w.special = take.Vector("feat_encoder.special_token",
+                          {1, 1, 1, static_cast<std::size_t>(local)}, 0.0f,
+                          1.0f);
   w.encoder_in = take.Linear("feat_encoder.in_proj", feat, local, true);
   w.dit = take.Stack("feat_decoder.estimator.decoder", c.dit, true);
   const std::string estimator = "feat_decoder.estimator.";
@@ -444,7 +633,8 @@ std::unique_ptr<Generator> Generator::Create(const ModelConfig& config,
                                              std::uint64_t seed,
                                              CheckpointKind kind,
                                              CacheType cache_type,
-                                             std::string* error) {
+                                             std::string* error,
+                                             const ModelFiles* files) {
   std::unique_ptr<Generator> g(new Generator());
   try {
     const ModelConfig& c = config;
@@ -467,12 +657,17 @@ std::unique_ptr<Generator> Generator::Create(const ModelConfig& config,
     // Count, allocate, upload (weights.cpp:308-327).
     {
       DeviceArena counter;
-      Uploader count(seed, kind, &counter, g->stream_);
+      Uploader count(seed, kind, files, &counter, g->stream_);
       (void)TakeAll(count, c);
+      if (files != nullptr && count.taken() != files->model_tensors().size())
+        throw std::runtime_error(
+            "the checkpoint holds tensors VoxCPM2 does not use");
       g->arena_ = std::make_unique<DeviceArena>(counter.used());
-      Uploader take(seed, kind, g->arena_.get(), g->stream_);
+      Uploader take(seed, kind, files, g->arena_.get(), g->stream_);
       g->w_ = TakeAll(take, c);
     }
+    if (files != nullptr)
+      files->ReleasePages();
 
     const int patch_values = c.patch_size * c.feat_dim;
     const int dit_rows = 2 * (3 + 2 * c.patch_size);
@@ -739,6 +934,12 @@ void Generator::SetupPersistent() {
   const WeightFormat format = w_.dit.layers[0].qkv.format;
   if (!DitPatchSupported(format))
     return;
+  // The kernel streams every layer in one format; checkpoint files may mix
+  // formats, and those run the per-kernel sequence.
+  for (const LayerWeights& layer : w_.dit.layers)
+    for (const Projection* m : {&layer.qkv, &layer.o, &layer.gate_up, &layer.down})
+      if (m->format != format)
+        return;
   std::vector<DitLayer> layers(d.layers);
   for (int i = 0; i < d.layers; ++i) {
     const LayerWeights& w = w_.dit.layers[i];

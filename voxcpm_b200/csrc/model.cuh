@@ -154,16 +154,20 @@ int ForwardStack(const StackWeights& stack, const float* rope,
                  cudaStream_t stream);
 
 class DeviceArena;
+class ModelFiles;
 
 /// VoxCPM2's generator on one GPU (generator.hpp:58-179): one sequence at a
 /// time on its own stream.
 class Generator {
  public:
+  /// Seeded weights when `files` is null, else the files' tensors (`seed`
+  /// and `kind` unused; generator.cpp:82-174, weights.cpp:308-327).
   static std::unique_ptr<Generator> Create(const ModelConfig& config,
                                            std::uint64_t seed,
                                            CheckpointKind kind,
                                            CacheType cache_type,
-                                           std::string* error);
+                                           std::string* error,
+                                           const ModelFiles* files = nullptr);
   ~Generator();
 
   const ModelConfig& config() const { return config_; }

@@ -46,8 +46,8 @@ def EulerSchedule(timesteps: int, sway: float = 1.0):
 
 
 class Generator:
-    """generator.hpp:58-179 with seeded weights (Create's file readers are out
-    of scope)."""
+    """generator.hpp:58-179: seeded weights from the constructor, checkpoint
+    files from Create."""
 
     def __init__(self, config: ModelConfig, seed: int = 0, checkpoint: int = _lib.CHECKPOINT_Q8,
                  cache_type: int = _lib.CACHE_F32):
@@ -56,6 +56,18 @@ class Generator:
         self._handle = self._lib.vx_generator_create(ctypes.byref(config), seed, checkpoint, cache_type)
         if not self._handle:
             raise _lib.VxError(_lib.VX_CUDA_ERROR, self._lib.vx_last_error().decode())
+
+    @classmethod
+    def Create(cls, config: ModelConfig, files, cache_type: int = _lib.CACHE_F32) -> "Generator":
+        """Generator::Create(config, files) (generator.hpp:60-62): the weights
+        of a ModelFiles (model_files.py)."""
+        self = cls.__new__(cls)
+        self._lib = load()
+        self.config = config
+        self._handle = self._lib.vx_generator_create_from_files(ctypes.byref(config), files.handle, cache_type)
+        if not self._handle:
+            raise _lib.VxError(_lib.VX_CUDA_ERROR, self._lib.vx_last_error().decode())
+        return self
 
     @property
     def patch_values(self) -> int:
