@@ -185,11 +185,13 @@ def test_file_errors(cuda, tmp_path):
 # ------------------------------------------------------------ conversions
 
 def special_floats(rng, n):
-    v = rng.normal(0, 3, n).astype(np.float32)
+    """n floats led by NaNs, infinities, zeros, subnormals, the largest
+    finite values and rounding ties (as many as fit)."""
+    v = rng.normal(0, 3, max(n, 20)).astype(np.float32)
     v[:12] = [np.nan, -np.nan, np.inf, -np.inf, 0.0, -0.0, 1e-40, -3e-39, 3.4e38, -3.39e38, 1.0, 1.00390625]
     bits = v.view(np.uint32)
     bits[12:20] = [0x7F800001, 0xFFC00001, 0x3F808000, 0x3F818000, 0x3F807FFF, 0x00008000, 0x7F7FFFFF, 0x80018000]
-    return v
+    return v[:n].copy()
 
 
 @pytest.mark.parametrize("count, offset", [(1, 0), (7, 1), (8, 0), (1000, 0), (1003, 3), (1 << 20, 0)])
@@ -207,8 +209,9 @@ def test_float_to_bf16(cuda, count, offset):
 @pytest.mark.parametrize("count, offset", [(1, 0), (9, 1), (4096, 0), (4099, 5)])
 def test_half_to_bf16(cuda, count, offset):
     rng = np.random.default_rng(count)
-    h = rng.integers(0, 1 << 16, count + offset).astype(np.uint16)
+    h = rng.integers(0, 1 << 16, max(count + offset, 6)).astype(np.uint16)
     h[:6] = [0x7C00, 0xFC00, 0x7E01, 0x0001, 0x8000, 0x03FF]
+    h = h[: count + offset].copy()
     out = torch.zeros(count + offset, dtype=torch.int16, device="cuda")
     src = to_dev(h)
     check(load().vx_half_to_bf16(src.data_ptr() + 2 * offset, out.data_ptr() + 2 * offset, count, None))
@@ -223,12 +226,16 @@ def test_q8_0_to_bf16(cuda, blocks, offset):
     raw = rng.integers(0, 256, (blocks, 34)).astype(np.uint8)
     scales = rng.normal(0, 0.02, blocks).astype(np.float16)
     scales[:1] = np.float16(6e-8)  # subnormal scale
+    scales[1:2] = np.array([0x7E55], np.uint16).view(np.float16)  # NaN scale with a payload
     raw[:, :2] = scales.view(np.uint8).reshape(blocks, 2)
     src = to_dev(raw.reshape(-1))
     out = torch.zeros(blocks * 32 + offset, dtype=torch.int16, device="cuda")
     check(load().vx_q8_0_to_bf16(src.data_ptr(), out.data_ptr() + 2 * offset, blocks * 32, None))
     torch.cuda.synchronize()
     q = raw[:, 2:].view(np.int8).astype(np.float32)
-    expect = oracle.bf16_bits((scales.astype(np.float32)[:, None] * q).reshape(-1))
+    wide = scales.astype(np.float32)[:, None]
+    # IEEE: a NaN operand propagates (payload kept).
+    products = np.where(np.isnan(wide), wide, wide * q)
+    expect = oracle.bf16_bits(products.reshape(-1))
     assert np.array_equal(bits16(out)[offset:], expect)
     assert load().vx_q8_0_to_bf16(src.data_ptr(), out.data_ptr(), 33, None) == _lib.VX_INVALID

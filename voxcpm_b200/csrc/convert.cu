@@ -1,9 +1,10 @@
 // Load-time conversion of checkpoint tensors to the bf16 the kernels read
 // (kernels/convert_kernels.hpp:9-24): fp16 -> bf16, fp32 -> bf16 and GGML
-// Q8_0 -> bf16 (bf16(scale * q)), each rounded to nearest even with NaN kept
-// quiet. HBM-bound byte work: grid-stride loops over eight values (fp16,
-// fp32) or one 32-value block (Q8_0) per thread, with 16-byte loads and
-// stores where the pointers allow, on a grid of a few CTAs per SM.
+// Q8_0 -> bf16 (bf16(scale * q)), each rounded to nearest even with NaN
+// kept quiet and the top bits of its payload kept. HBM-bound byte work:
+// grid-stride loops over eight values (fp16, fp32) or one 32-value block
+// (Q8_0) per thread, with 16-byte loads and stores where the pointers allow,
+// on a grid of a few CTAs per SM.
 #include "convert.cuh"
 #include "vx_common.cuh"
 #include "vx_status.h"
@@ -30,6 +31,23 @@ bool Aligned16(const void* p) {
   return (reinterpret_cast<std::uintptr_t>(p) & 15u) == 0;
 }
 
+/// IEEE 754 binary16 -> binary32 from the bit layout, exact, with NaN
+/// payloads kept (the reference widens with a plain _Float16 conversion,
+/// kernels/device_math.hpp:22-24, which keeps them; __half2float returns a
+/// canonical NaN).
+__device__ inline float HalfToFloatExact(std::uint16_t h) {
+  const std::uint32_t sign = static_cast<std::uint32_t>(h & 0x8000u) << 16;
+  const std::uint32_t exponent = (h >> 10) & 0x1Fu;
+  const std::uint32_t mantissa = h & 0x3FFu;
+  if (exponent == 0x1Fu)
+    return __uint_as_float(sign | 0x7F800000u | (mantissa << 13));
+  if (exponent != 0)
+    return __uint_as_float(sign | ((exponent + 112u) << 23) | (mantissa << 13));
+  // Zero or subnormal: mantissa * 2^-24, exact in binary32.
+  const float magnitude = static_cast<float>(mantissa) * 5.9604644775390625e-8f;
+  return sign != 0 ? -magnitude : magnitude;
+}
+
 __device__ inline std::uint32_t Pack(Bf16 lo, Bf16 hi) {
   return static_cast<std::uint32_t>(lo) | (static_cast<std::uint32_t>(hi) << 16);
 }
@@ -48,8 +66,8 @@ __global__ void ToBf16Kernel(const void* input, Bf16* output, std::size_t count,
       const uint4 raw = reinterpret_cast<const uint4*>(input)[g];
       const std::uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
       for (int i = 0; i < 4; ++i) {
-        v[2 * i] = HalfBitsToFloat(static_cast<std::uint16_t>(w[i] & 0xFFFFu));
-        v[2 * i + 1] = HalfBitsToFloat(static_cast<std::uint16_t>(w[i] >> 16));
+        v[2 * i] = HalfToFloatExact(static_cast<std::uint16_t>(w[i] & 0xFFFFu));
+        v[2 * i + 1] = HalfToFloatExact(static_cast<std::uint16_t>(w[i] >> 16));
       }
     } else {
       const float4 a = reinterpret_cast<const float4*>(input)[2 * g];
@@ -65,7 +83,7 @@ __global__ void ToBf16Kernel(const void* input, Bf16* output, std::size_t count,
     reinterpret_cast<uint4*>(output)[g] = out;
   }
   for (std::size_t i = groups * 8 + first; i < count; i += stride) {
-    const float v = kHalf ? HalfBitsToFloat(static_cast<const std::uint16_t*>(input)[i])
+    const float v = kHalf ? HalfToFloatExact(static_cast<const std::uint16_t*>(input)[i])
                           : static_cast<const float*>(input)[i];
     output[i] = FloatToBf16(v);
   }
@@ -79,11 +97,15 @@ __global__ void Q8_0ToBf16Kernel(const std::uint8_t* blocks, Bf16* output,
   for (std::size_t b = static_cast<std::size_t>(blockIdx.x) * blockDim.x + threadIdx.x;
        b < count_blocks; b += stride) {
     const std::uint8_t* block = blocks + b * 34;
-    const float scale = HalfBitsToFloat(
+    const float scale = HalfToFloatExact(
         static_cast<std::uint16_t>(block[0] | (block[1] << 8)));
+    // A NaN scale propagates with its payload (IEEE multiply), which the
+    // GPU's multiply would replace by its canonical NaN.
+    const bool nan_scale = scale != scale;
     Bf16 out[32];
     for (int i = 0; i < 32; ++i)
-      out[i] = FloatToBf16(scale * static_cast<float>(static_cast<std::int8_t>(block[2 + i])));
+      out[i] = FloatToBf16(nan_scale ? scale
+                                     : scale * static_cast<float>(static_cast<std::int8_t>(block[2 + i])));
     Bf16* target = output + b * 32;
     if (vector) {
       for (int i = 0; i < 4; ++i) {
