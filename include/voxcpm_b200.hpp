@@ -2,8 +2,10 @@
 // over the C ABI (voxcpm_b200.h): the names, argument meanings and error
 // behaviour of gemm.hpp, matrix.hpp, kernels/wmma_products.hpp,
 // kernels/skinny_gemm.hpp, kernels/generator_kernels.hpp, transformer.hpp
-// (RopeTable) and generator.hpp (Prompt, EulerStep, EulerSchedule,
-// Generator), so that code written against the reference keeps compiling.
+// (RopeTable), generator.hpp (Prompt, EulerStep, EulerSchedule, Generator),
+// model_files.hpp / safetensors.hpp (ModelFiles, Tensor) and config.hpp
+// (ParseConfig), so that code written against the reference keeps
+// compiling.
 //
 // Error behaviour: launchers that return bool in the reference return false
 // when the shape does not suit the kernels (VX_UNSUPPORTED, nothing
@@ -305,8 +307,101 @@ inline std::vector<EulerStep> EulerSchedule(std::size_t timesteps,
   return steps;
 }
 
-/// generator.hpp:58-179 with seeded weights (the reference's Create reads
-/// checkpoint files, which are out of scope here).
+/// safetensors.hpp:18-34: one tensor of the checkpoint files; `data` is
+/// host memory in the mapped file, valid while the files are open.
+enum class DType : int { kF32 = 0, kBF16, kF16, kI64, kI32, kU8, kQ8_0 };
+
+struct Tensor {
+  std::string name;
+  DType dtype = DType::kF32;
+  std::vector<std::size_t> shape;
+  const std::byte* data = nullptr;
+  std::size_t bytes = 0;
+  std::uint64_t offset = 0;
+
+  std::size_t Elements() const {
+    std::size_t n = 1;
+    for (const std::size_t d : shape)
+      n *= d;
+    return n;
+  }
+};
+
+/// model_files.hpp:45-83: a Hugging Face directory or an audio.cpp VoxCPM2
+/// GGUF file.
+class ModelFiles {
+ public:
+  static std::unique_ptr<ModelFiles> Open(const std::string& path,
+                                          std::string* error = nullptr) {
+    vx_model_files* f = vx_model_files_open(path.c_str());
+    if (f == nullptr) {
+      if (error != nullptr)
+        *error = vx_last_error();
+      return nullptr;
+    }
+    return std::unique_ptr<ModelFiles>(new ModelFiles(f));
+  }
+  static bool IsVoxCpm2Gguf(const std::string& path) {
+    return vx_model_files_is_voxcpm2_gguf(path.c_str()) != 0;
+  }
+  ~ModelFiles() { vx_model_files_close(f_); }
+  ModelFiles(const ModelFiles&) = delete;
+  ModelFiles& operator=(const ModelFiles&) = delete;
+
+  std::string config() const { return vx_model_files_config(f_); }
+  std::string tokenizer() const { return vx_model_files_tokenizer(f_); }
+  bool gguf() const { return vx_model_files_is_gguf(f_) != 0; }
+  const Tensor* Model(const std::string& name) const { return Find(model_, name); }
+  const Tensor* Vae(const std::string& name) const { return Find(vae_, name); }
+  const std::vector<Tensor>& model_tensors() const { return model_; }
+  const vx_model_files* handle() const { return f_; }
+
+ private:
+  explicit ModelFiles(vx_model_files* f) : f_(f) {
+    for (int component : {VX_COMPONENT_MODEL, VX_COMPONENT_VAE}) {
+      std::vector<Tensor>& out = component == VX_COMPONENT_MODEL ? model_ : vae_;
+      const std::size_t count = vx_model_files_count(f_, component);
+      for (std::size_t i = 0; i < count; ++i) {
+        vx_tensor_info info;
+        Check(vx_model_files_tensor(f_, component, i, &info), "ModelFiles");
+        Tensor t;
+        t.name = info.name;
+        t.dtype = static_cast<DType>(info.dtype);
+        t.shape.assign(info.shape, info.shape + info.rank);
+        t.data = static_cast<const std::byte*>(info.data);
+        t.bytes = static_cast<std::size_t>(info.bytes);
+        t.offset = info.offset;
+        out.push_back(std::move(t));
+      }
+    }
+  }
+  static const Tensor* Find(const std::vector<Tensor>& tensors,
+                            const std::string& name) {
+    for (const Tensor& t : tensors)
+      if (t.name == name)
+        return &t;
+    return nullptr;
+  }
+  vx_model_files* f_;
+  std::vector<Tensor> model_;
+  std::vector<Tensor> vae_;
+};
+
+/// config.hpp:92-98: config.json text -> the generator's configuration,
+/// false (and `error`) for a malformed or unsupported one (ParseConfig and
+/// IsSupported in one).
+inline bool ParseConfig(const std::string& text, vx_model_config* config,
+                        std::string* error = nullptr) {
+  if (vx_parse_config(text.data(), text.size(), config) != VX_OK) {
+    if (error != nullptr)
+      *error = vx_last_error();
+    return false;
+  }
+  return true;
+}
+
+/// generator.hpp:58-179: weights from checkpoint files (Create with
+/// ModelFiles) or seeded (Create with a seed, for benchmarks and tests).
 class Generator {
  public:
   static std::unique_ptr<Generator> Create(const vx_model_config& config,
@@ -314,6 +409,19 @@ class Generator {
                                            int cache_type,
                                            std::string* error = nullptr) {
     vx_generator* g = vx_generator_create(&config, seed, checkpoint, cache_type);
+    if (g == nullptr) {
+      if (error != nullptr)
+        *error = vx_last_error();
+      return nullptr;
+    }
+    return std::unique_ptr<Generator>(new Generator(g, config));
+  }
+  static std::unique_ptr<Generator> Create(const vx_model_config& config,
+                                           const ModelFiles& files,
+                                           std::string* error = nullptr,
+                                           int cache_type = VX_CACHE_F32) {
+    vx_generator* g =
+        vx_generator_create_from_files(&config, files.handle(), cache_type);
     if (g == nullptr) {
       if (error != nullptr)
         *error = vx_last_error();

@@ -2,11 +2,31 @@
 // include/voxcpm_b200.hpp, links libvoxcpm_b200.so and prints the Euler
 // schedule, a product plan and tile sizes for the Python test to check.
 #include <cstdio>
+#include <string>
 
 #include "voxcpm_b200.hpp"
 
-int main() {
+int main(int argc, char** argv) {
   namespace vb = voxcpm_b200;
+  if (argc > 1) {
+    // Checkpoint files: open, list, parse the embedded config.
+    std::string error;
+    const auto files = vb::ModelFiles::Open(argv[1], &error);
+    if (files == nullptr) {
+      std::printf("files error %s\n", error.c_str());
+      return 0;
+    }
+    std::printf("files %zu %d\n", files->model_tensors().size(), files->gguf() ? 1 : 0);
+    const vb::Tensor* t = files->Model("stop_head.weight");
+    if (t != nullptr)
+      std::printf("tensor %d %zu %zu %zu\n", static_cast<int>(t->dtype), t->shape[0], t->shape[1], t->bytes);
+    vx_model_config config;
+    if (vb::ParseConfig(files->config(), &config, &error))
+      std::printf("config %d %d %d %d\n", config.lm.hidden, config.dit.layers, config.vocab, config.max_length);
+    else
+      std::printf("config error %s\n", error.c_str());
+    return 0;
+  }
   for (const vb::EulerStep& s : vb::EulerSchedule(10))
     std::printf("step %.9g %.9g %d\n", s.t, s.dt, s.evaluate ? 1 : 0);
   const vb::kernels::WmmaPlan plan = vb::kernels::PlanWmma(22, 2048, 6144);

@@ -33,3 +33,27 @@ def test_cpp_shim_compiles_links_and_runs(tmp_path):
     rope = next(line for line in out if line.startswith("rope")).split()
     assert np.float32(float(rope[1])) == table[1, 1] and np.float32(float(rope[2])) == table[3, 64 + 5]
     assert "error ok" in out
+
+
+def test_cpp_shim_model_files(tmp_path):
+    """ModelFiles / ParseConfig through the C++ mirror on a GGUF written here."""
+    from _checkpoints import GGML_Q8_0, config_json, write_gguf
+    from voxcpm_b200.generator import small_config
+
+    _lib.load()
+    exe = tmp_path / "shim_host"
+    lib_dir = str(_lib.LIBRARY.parent)
+    subprocess.run(["g++", "-std=c++17", "-O1", "-I", str(ROOT / "include"), "-I", "/usr/local/cuda/include",
+                    str(ROOT / "tests" / "cpp" / "shim_host.cpp"), "-o", str(exe), "-L", lib_dir,
+                    "-l:libvoxcpm_b200.so", f"-Wl,-rpath,{lib_dir}"], check=True)
+    c = small_config(layers=3, max_length=128, vocab=77)
+    path = tmp_path / "m.gguf"
+    write_gguf(path, {"stop_head.weight": (GGML_Q8_0, [2048, 2], bytes(2 * 64 * 34))},
+               config_text=config_json(c), abbreviate=("stop_head.weight",))
+    out = subprocess.run([str(exe), str(path)], check=True, capture_output=True, text=True).stdout.split("\n")
+    assert out[0] == "files 1 1"
+    assert out[1] == f"tensor {_lib.DTYPE_Q8_0} 2 2048 {2 * 64 * 34}"
+    assert out[2] == "config 2048 3 77 128"
+    bad = subprocess.run([str(exe), str(tmp_path / "absent.gguf")], check=True, capture_output=True,
+                         text=True).stdout
+    assert bad.startswith("files error") and "absent.gguf" in bad
