@@ -428,6 +428,55 @@ VX_API size_t vx_generator_position(const vx_generator* generator);
 VX_API size_t vx_generator_weight_bytes(const vx_generator* generator);
 VX_API cudaStream_t vx_generator_stream(const vx_generator* generator);
 
+/* ------------------------------------------------------------ batched slots */
+
+typedef struct vx_model_files vx_model_files; /* checkpoint files, below */
+
+/* Several requests generated together on the current device: `slots`
+ * generators that share one set of weights and one stream, each with its own
+ * caches and state. A step advances every active slot by one patch: their
+ * DiT passes run as one pass of 22 rows per slot (the DiT's weights are read
+ * once per Euler evaluation for all of them) and their local encoder as one
+ * call; each slot's LMs advance on its own caches. No reference counterpart:
+ * it batches the per-request loop of synthesizer.cpp:283-307 (one
+ * Generator::Step per request). Seeded weights, or the files' with
+ * _from_files. Null on failure. */
+typedef struct vx_generator_batch vx_generator_batch;
+VX_API vx_generator_batch* vx_generator_batch_create(
+    const vx_model_config* config, uint64_t seed, int checkpoint,
+    int cache_type, size_t slots);
+VX_API vx_generator_batch* vx_generator_batch_create_from_files(
+    const vx_model_config* config, const vx_model_files* files,
+    int cache_type, size_t slots);
+VX_API void vx_generator_batch_destroy(vx_generator_batch* batch);
+VX_API size_t vx_generator_batch_slots(const vx_generator_batch* batch);
+/* A new request in `slot` (Generator::Prefill; the other slots keep their
+ * state). Synchronizes. */
+VX_API vx_status vx_generator_batch_prefill(vx_generator_batch* batch,
+                                            size_t slot, const int32_t* tokens,
+                                            const int32_t* text_mask,
+                                            const int32_t* audio_mask,
+                                            const float* feats, size_t rows);
+/* One patch for every slot with active[slot] != 0 (host arrays: active
+ * [slots], noise [slots][patch][feat]); writes those slots' latents
+ * [slots][patch][feat] (when not null) and stop logits [slots][2]. One CUDA
+ * graph per set of active slots. Synchronizes once. VX_INVALID when an
+ * active slot has no prefilled request or no room. */
+VX_API vx_status vx_generator_batch_step(vx_generator_batch* batch,
+                                         const int32_t* active,
+                                         const float* noise, size_t timesteps,
+                                         float cfg, float* latents,
+                                         float* stop_logits);
+VX_API size_t vx_generator_batch_position(const vx_generator_batch* batch,
+                                          size_t slot);
+/* vx_generator_state of one slot. */
+VX_API vx_status vx_generator_batch_state(vx_generator_batch* batch,
+                                          size_t slot, const char* name,
+                                          float* out, size_t count);
+VX_API vx_status vx_generator_batch_set_graphs(vx_generator_batch* batch,
+                                               int enabled);
+VX_API cudaStream_t vx_generator_batch_stream(const vx_generator_batch* batch);
+
 /* ------------------------------------------------------------ model files */
 
 /* Tensor element types (safetensors.hpp:18, same order). Q8_0 is GGML's
@@ -464,7 +513,6 @@ typedef struct vx_tensor_info {
  * names resolved). Host only. Replaces ModelFiles::Open
  * (model_files.hpp:45-51, model_files.cpp:111-180); null on failure
  * (vx_last_error names the file and the problem). */
-typedef struct vx_model_files vx_model_files;
 VX_API vx_model_files* vx_model_files_open(const char* path);
 VX_API void vx_model_files_close(vx_model_files* files);
 /* ModelFiles::IsVoxCpm2Gguf (model_files.hpp:49-51): a .gguf file whose

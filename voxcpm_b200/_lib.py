@@ -184,6 +184,16 @@ SIGNATURES: dict[str, tuple] = {
     "vx_generator_position": (c_size_t, [c_void_p]),
     "vx_generator_weight_bytes": (c_size_t, [c_void_p]),
     "vx_generator_stream": (c_void_p, [c_void_p]),
+    "vx_generator_batch_create": (c_void_p, [POINTER(ModelConfig), c_uint64, c_int, c_int, c_size_t]),
+    "vx_generator_batch_create_from_files": (c_void_p, [POINTER(ModelConfig), c_void_p, c_int, c_size_t]),
+    "vx_generator_batch_destroy": (None, [c_void_p]),
+    "vx_generator_batch_slots": (c_size_t, [c_void_p]),
+    "vx_generator_batch_prefill": (c_int, [c_void_p, c_size_t, c_void_p, c_void_p, c_void_p, c_void_p, c_size_t]),
+    "vx_generator_batch_step": (c_int, [c_void_p, c_void_p, c_void_p, c_size_t, c_float, c_void_p, c_void_p]),
+    "vx_generator_batch_position": (c_size_t, [c_void_p, c_size_t]),
+    "vx_generator_batch_state": (c_int, [c_void_p, c_size_t, c_char_p, c_void_p, c_size_t]),
+    "vx_generator_batch_set_graphs": (c_int, [c_void_p, c_int]),
+    "vx_generator_batch_stream": (c_void_p, [c_void_p]),
     "vx_model_files_open": (c_void_p, [c_char_p]),
     "vx_model_files_close": (None, [c_void_p]),
     "vx_model_files_is_voxcpm2_gguf": (c_int, [c_char_p]),

@@ -15,6 +15,10 @@ struct vx_generator {
   std::unique_ptr<vx::Generator> impl;
 };
 
+struct vx_generator_batch {
+  std::unique_ptr<vx::GeneratorBatch> impl;
+};
+
 namespace {
 
 vx::StackConfig FromC(const vx_stack_config& s) {
@@ -88,6 +92,44 @@ bool ToModelConfig(const vx_model_config& config, vx::ModelConfig* out,
   c.vocab = config.vocab;
   *out = std::move(c);
   return true;
+}
+
+template <typename F>
+vx_status BatchGuard(vx_generator_batch* b, const char* what, F&& body) {
+  if (b == nullptr || !b->impl)
+    return vx::Fail(vx::kInvalid, std::string(what) + ": null batch");
+  try {
+    body(*b->impl);
+  } catch (const std::logic_error& e) {
+    return vx::Fail(vx::kInvalid, std::string(what) + ": " + e.what());
+  } catch (const std::exception& e) {
+    return vx::Fail(vx::kCudaError, std::string(what) + ": " + e.what());
+  }
+  return vx::kOk;
+}
+
+vx_generator_batch* CreateBatch(const vx_model_config* config, uint64_t seed,
+                                int checkpoint, int cache_type, size_t slots,
+                                const vx_model_files* files, const char* what) {
+  if (config == nullptr || slots == 0 || slots > 64 ||
+      (checkpoint != VX_CHECKPOINT_Q8 && checkpoint != VX_CHECKPOINT_BF16) ||
+      (cache_type != VX_CACHE_F32 && cache_type != VX_CACHE_BF16)) {
+    vx::Fail(vx::kInvalid, std::string(what) + ": bad arguments");
+    return nullptr;
+  }
+  vx::ModelConfig c;
+  if (!ToModelConfig(*config, &c, what))
+    return nullptr;
+  std::string error;
+  auto impl = vx::GeneratorBatch::Create(
+      c, seed, static_cast<vx::CheckpointKind>(checkpoint),
+      cache_type == VX_CACHE_BF16 ? vx::CacheType::kBf16 : vx::CacheType::kF32,
+      static_cast<int>(slots), &error, vx::FilesOf(files));
+  if (!impl) {
+    vx::Fail(vx::kCudaError, std::string(what) + ": " + error);
+    return nullptr;
+  }
+  return new vx_generator_batch{std::move(impl)};
 }
 
 vx_generator* Create(const vx_model_config* config, uint64_t seed,
@@ -274,6 +316,79 @@ size_t vx_generator_weight_bytes(const vx_generator* generator) {
 cudaStream_t vx_generator_stream(const vx_generator* generator) {
   return generator != nullptr && generator->impl ? generator->impl->stream()
                                                  : nullptr;
+}
+
+vx_generator_batch* vx_generator_batch_create(const vx_model_config* config,
+                                              uint64_t seed, int checkpoint,
+                                              int cache_type, size_t slots) {
+  return CreateBatch(config, seed, checkpoint, cache_type, slots, nullptr,
+                     "vx_generator_batch_create");
+}
+
+vx_generator_batch* vx_generator_batch_create_from_files(
+    const vx_model_config* config, const vx_model_files* files, int cache_type,
+    size_t slots) {
+  if (vx::FilesOf(files) == nullptr) {
+    vx::Fail(vx::kInvalid, "vx_generator_batch_create_from_files: null files");
+    return nullptr;
+  }
+  return CreateBatch(config, 0, VX_CHECKPOINT_Q8, cache_type, slots, files,
+                     "vx_generator_batch_create_from_files");
+}
+
+void vx_generator_batch_destroy(vx_generator_batch* batch) { delete batch; }
+
+size_t vx_generator_batch_slots(const vx_generator_batch* batch) {
+  return batch != nullptr && batch->impl ? batch->impl->slots() : 0;
+}
+
+vx_status vx_generator_batch_prefill(vx_generator_batch* batch, size_t slot,
+                                     const int32_t* tokens,
+                                     const int32_t* text_mask,
+                                     const int32_t* audio_mask,
+                                     const float* feats, size_t rows) {
+  return BatchGuard(batch, "vx_generator_batch_prefill", [&](vx::GeneratorBatch& b) {
+    if (slot >= static_cast<size_t>(b.slots()))
+      throw std::invalid_argument("no such slot");
+    b.slot(static_cast<int>(slot)).Prefill(tokens, text_mask, audio_mask, feats,
+                                           static_cast<int>(rows));
+  });
+}
+
+vx_status vx_generator_batch_step(vx_generator_batch* batch,
+                                  const int32_t* active, const float* noise,
+                                  size_t timesteps, float cfg, float* latents,
+                                  float* stop_logits) {
+  return BatchGuard(batch, "vx_generator_batch_step", [&](vx::GeneratorBatch& b) {
+    b.Step(active, noise, static_cast<int>(timesteps), cfg, latents, stop_logits);
+  });
+}
+
+size_t vx_generator_batch_position(const vx_generator_batch* batch,
+                                   size_t slot) {
+  if (batch == nullptr || !batch->impl ||
+      slot >= static_cast<size_t>(batch->impl->slots()))
+    return 0;
+  return static_cast<size_t>(batch->impl->slot(static_cast<int>(slot)).position());
+}
+
+vx_status vx_generator_batch_state(vx_generator_batch* batch, size_t slot,
+                                   const char* name, float* out, size_t count) {
+  return BatchGuard(batch, "vx_generator_batch_state", [&](vx::GeneratorBatch& b) {
+    if (slot >= static_cast<size_t>(b.slots()) || name == nullptr || out == nullptr)
+      throw std::invalid_argument("bad argument");
+    b.slot(static_cast<int>(slot)).State(name, out, count);
+  });
+}
+
+vx_status vx_generator_batch_set_graphs(vx_generator_batch* batch, int enabled) {
+  return BatchGuard(batch, "vx_generator_batch_set_graphs", [&](vx::GeneratorBatch& b) {
+    b.set_graphs(enabled != 0);
+  });
+}
+
+cudaStream_t vx_generator_batch_stream(const vx_generator_batch* batch) {
+  return batch != nullptr && batch->impl ? batch->impl->stream() : nullptr;
 }
 
 }  // extern "C"

@@ -634,7 +634,9 @@ std::unique_ptr<Generator> Generator::Create(const ModelConfig& config,
                                              CheckpointKind kind,
                                              CacheType cache_type,
                                              std::string* error,
-                                             const ModelFiles* files) {
+                                             const ModelFiles* files,
+                                             const Generator* share,
+                                             cudaStream_t stream) {
   std::unique_ptr<Generator> g(new Generator());
   try {
     const ModelConfig& c = config;
@@ -651,11 +653,19 @@ std::unique_ptr<Generator> Generator::Create(const ModelConfig& config,
         c.feat_dim % 32 != 0 || c.patch_size < 1 || c.max_length < 2)
       throw std::runtime_error("unsupported configuration");
     g->config_ = config;
-    ThrowCuda(cudaStreamCreateWithFlags(&g->stream_, cudaStreamNonBlocking),
-              "cudaStreamCreate");
+    if (stream != nullptr) {
+      g->stream_ = stream;
+      g->owns_stream_ = false;
+    } else {
+      ThrowCuda(cudaStreamCreateWithFlags(&g->stream_, cudaStreamNonBlocking),
+                "cudaStreamCreate");
+    }
 
     // Count, allocate, upload (weights.cpp:308-327).
-    {
+    if (share != nullptr) {
+      g->arena_ = share->arena_;
+      g->w_ = share->w_;
+    } else {
       DeviceArena counter;
       Uploader count(seed, kind, files, &counter, g->stream_);
       (void)TakeAll(count, c);
@@ -820,7 +830,7 @@ Generator::~Generator() {
     cudaFreeHost(pinned_stop_);
   arena_.reset();
   work_.reset();
-  if (stream_ != nullptr)
+  if (stream_ != nullptr && owns_stream_)
     cudaStreamDestroy(stream_);
 }
 
@@ -835,6 +845,7 @@ void Generator::CheckCuda(cudaError_t error, const char* what) {
 }
 
 void Generator::DestroyGraphs() {
+  ++buffers_epoch_;
   if (step_graph_ != nullptr)
     cudaGraphExecDestroy(step_graph_);
   if (patch_graph_ != nullptr)
@@ -1273,8 +1284,7 @@ void Generator::EulerLoop(int timesteps, float cfg) {
   }
 }
 
-void Generator::StepBody(int timesteps, float cfg) {
-  // generator.cpp:424-513, with the host syncs replaced by device state.
+void Generator::PreDit() {
   const ModelConfig& c = config_;
   const int hidden = c.lm.hidden;
   const int dit = c.dit.hidden;
@@ -1290,7 +1300,10 @@ void Generator::StepBody(int timesteps, float cfg) {
   CheckCuda(cudaMemcpyAsync(x_, pinned_noise_, values * sizeof(float),
                             cudaMemcpyHostToDevice, stream_),
             "noise");
-  EulerLoop(timesteps, cfg);
+}
+
+void Generator::PatchOutputs() {
+  const int values = config_.patch_size * config_.feat_dim;
   CheckCuda(cudaMemcpyAsync(pinned_latent_, x_, values * sizeof(float),
                             cudaMemcpyDeviceToHost, stream_),
             "latent");
@@ -1298,9 +1311,12 @@ void Generator::StepBody(int timesteps, float cfg) {
   CheckCuda(cudaMemcpyAsync(pinned_stop_, stop_, 2 * sizeof(float),
                             cudaMemcpyDeviceToHost, stream_),
             "stop");
-  // The patch's embedding advances both LMs, one row at the device-held
-  // position (its rotary row and cache row coincide).
-  Encode(x_, 1, embed_);
+}
+
+void Generator::AdvanceLms() {
+  // One row at the device-held position (its rotary row and cache row
+  // coincide).
+  const int hidden = config_.lm.hidden;
   AttentionLayout layout;
   layout.positions = step_positions_;
   layout.cache_rows = step_positions_;
@@ -1318,6 +1334,16 @@ void Generator::StepBody(int timesteps, float cfg) {
   StepStack(1, layout, step_a_, residual_hidden_);
   Check(AdvancePosition(position_counter_, step_positions_, stream_),
         "advance");
+}
+
+void Generator::StepBody(int timesteps, float cfg) {
+  // generator.cpp:424-513, with the host syncs replaced by device state.
+  PreDit();
+  EulerLoop(timesteps, cfg);
+  PatchOutputs();
+  // The patch's embedding advances both LMs.
+  Encode(x_, 1, embed_);
+  AdvanceLms();
 }
 
 void Generator::Step(const float* noise, int timesteps, float cfg,

@@ -11,6 +11,7 @@
 #include <cstddef>
 #include <cstdint>
 #include <map>
+#include <tuple>
 #include <memory>
 #include <string>
 #include <vector>
@@ -162,12 +163,18 @@ class Generator {
  public:
   /// Seeded weights when `files` is null, else the files' tensors (`seed`
   /// and `kind` unused; generator.cpp:82-174, weights.cpp:308-327).
+  ///
+  /// With `share`, the weights are `share`'s (same configuration; nothing is
+  /// uploaded). With `stream`, the generator runs on that stream and does
+  /// not own it (the slots of a GeneratorBatch).
   static std::unique_ptr<Generator> Create(const ModelConfig& config,
                                            std::uint64_t seed,
                                            CheckpointKind kind,
                                            CacheType cache_type,
                                            std::string* error,
-                                           const ModelFiles* files = nullptr);
+                                           const ModelFiles* files = nullptr,
+                                           const Generator* share = nullptr,
+                                           cudaStream_t stream = nullptr);
   ~Generator();
 
   const ModelConfig& config() const { return config_; }
@@ -215,8 +222,16 @@ class Generator {
   float* device_x() const { return x_; }
 
  private:
+  friend class GeneratorBatch;
   Generator() = default;
   void Check(int status, const char* what);
+  /// StepBody's parts: the stop logits, mu and the DiT conditioning from
+  /// the LM states, and the patch's noise into x (generator.cpp:424-447);
+  /// the latent, stop logits and next prefix out (:465-476); both LMs
+  /// advanced by the patch's embedding in embed_ (:478-513).
+  void PreDit();
+  void PatchOutputs();
+  void AdvanceLms();
   void CheckCuda(cudaError_t error, const char* what);
   const float* TimeVector(float t);
   void EvaluateDit(const float* x, float t, float* velocity);
@@ -238,8 +253,12 @@ class Generator {
 
   ModelConfig config_;
   cudaStream_t stream_ = nullptr;
-  std::unique_ptr<DeviceArena> arena_;
+  std::shared_ptr<DeviceArena> arena_;  // the weights (shared by batch slots)
   std::unique_ptr<DeviceArena> work_;
+  bool owns_stream_ = true;
+  // Counts DestroyGraphs calls: every reallocation of a buffer that graphs
+  // capture goes through it, so a GeneratorBatch re-captures when it moves.
+  std::uint64_t buffers_epoch_ = 0;
   GeneratorWeights w_;
   float* rope_ = nullptr;
   KvCache base_cache_, residual_cache_, encoder_cache_, dit_cache_;
@@ -322,6 +341,66 @@ class Generator {
   LmLayer* lm_layers_ = nullptr;  // [LM layers | residual layers]
   void* lm_work_ = nullptr;
   LmStackParams lm_params_[2];
+};
+
+/// Several requests generated together on one GPU: the loop of
+/// synthesizer.cpp:283-307 over `slots` requests at once (no reference
+/// counterpart; the reference serves one sequence per generator). The slots
+/// are Generators that share one set of weights and one stream, each with its
+/// own caches and states. A step runs, for the active slots:
+/// - each slot's stop logits and DiT conditioning;
+/// - one DiT pass of 22 rows per slot (two CFG sequences of 11 per slot,
+///   attention block-diagonal per sequence) for every Euler evaluation, so
+///   the DiT's weights are read once per evaluation for all of them;
+/// - the local encoder over all their patches at once;
+/// - each slot's LM and residual LM on its own caches.
+/// A slot takes a new request through its Prefill while the others keep
+/// their state. One CUDA graph per set of active slots (and timesteps, cfg).
+class GeneratorBatch {
+ public:
+  static std::unique_ptr<GeneratorBatch> Create(const ModelConfig& config,
+                                                std::uint64_t seed,
+                                                CheckpointKind kind,
+                                                CacheType cache_type,
+                                                int slots, std::string* error,
+                                                const ModelFiles* files = nullptr);
+  ~GeneratorBatch();
+
+  int slots() const { return static_cast<int>(slots_.size()); }
+  Generator& slot(int index) { return *slots_.at(index); }
+  cudaStream_t stream() const { return stream_; }
+  void set_graphs(bool enabled) { graphs_enabled_ = enabled; }
+  /// One patch for every slot with active[i] != 0: noise [slots][patch][feat]
+  /// in; latents [slots][patch][feat] (may be null) and stop logits
+  /// [slots][2] out for those slots. Synchronizes once.
+  void Step(const std::int32_t* active, const float* noise, int timesteps,
+            float cfg, float* latents, float* stop_logits);
+
+ private:
+  GeneratorBatch() = default;
+  void Body(const std::vector<int>& members, int timesteps, float cfg);
+  void EvaluateDit(int count, float t);
+  void DestroyGraphs();
+
+  std::vector<std::unique_ptr<Generator>> slots_;
+  cudaStream_t stream_ = nullptr;
+  KvCache dit_cache_;
+  unsigned char* block_ = nullptr;
+  float* mu_ = nullptr;        // [slots][2][dit hidden]
+  float* cond_ = nullptr;      // [slots][patch][dit hidden]
+  float* x_ = nullptr;         // [slots][patch][feat]
+  float* velocity_ = nullptr;  // [slots][2][patch][feat]
+  float* x_rows_ = nullptr;    // [slots][patch][dit hidden]
+  float* hidden_ = nullptr;    // [slots * dit rows][dit hidden]
+  float* output_ = nullptr;    // [slots * dit rows][dit hidden]
+  std::uint16_t* bf16_ = nullptr;
+  float* embed_ = nullptr;     // [slots][lm hidden]
+  std::int32_t* positions_ = nullptr;
+  std::int32_t* rows_ = nullptr;
+  std::int32_t* outputs_ = nullptr;
+  bool graphs_enabled_ = true;
+  std::map<std::tuple<std::uint64_t, int, float>, cudaGraphExec_t> graphs_;
+  std::vector<std::uint64_t> epochs_;  // the slots' buffers_epoch_ at capture
 };
 
 /// The reference's released shapes (tests/config_test.cpp:36-67): LM 28 x

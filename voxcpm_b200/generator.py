@@ -145,3 +145,70 @@ class Generator:
             self.close()
         except Exception:
             pass
+
+
+class GeneratorBatch:
+    """Several requests per GPU (vx_generator_batch_*): `slots` generators
+    sharing one set of weights and one stream; a step advances every active
+    slot by one patch with one DiT pass for all of them. Batches the
+    per-request loop of synthesizer.cpp:283-307."""
+
+    def __init__(self, config: ModelConfig, slots: int, seed: int = 0, checkpoint: int = _lib.CHECKPOINT_Q8,
+                 cache_type: int = _lib.CACHE_F32, files=None):
+        self._lib = load()
+        self.config = config
+        if files is not None:
+            self._handle = self._lib.vx_generator_batch_create_from_files(ctypes.byref(config), files.handle,
+                                                                          cache_type, slots)
+        else:
+            self._handle = self._lib.vx_generator_batch_create(ctypes.byref(config), seed, checkpoint, cache_type,
+                                                               slots)
+        if not self._handle:
+            raise _lib.VxError(_lib.VX_CUDA_ERROR, self._lib.vx_last_error().decode())
+        self.slots = slots
+
+    @property
+    def patch_values(self) -> int:
+        return self.config.patch_size * self.config.feat_dim
+
+    def Prefill(self, slot: int, tokens, text_mask, audio_mask, feats) -> None:
+        tokens, text_mask, audio_mask = _i32(tokens), _i32(text_mask), _i32(audio_mask)
+        feats = _f32(feats)
+        check(self._lib.vx_generator_batch_prefill(self._handle, slot, tokens.ctypes.data, text_mask.ctypes.data,
+                                                   audio_mask.ctypes.data, feats.ctypes.data, tokens.size))
+
+    def Step(self, noise, active=None, timesteps: int = 10, cfg: float = 2.0):
+        """noise [slots][patch][feat]; returns (latents [slots][patch][feat],
+        stop logits [slots][2]); rows of inactive slots are zero."""
+        active = _i32(np.ones(self.slots) if active is None else active)
+        noise = _f32(noise)
+        latents = np.zeros((self.slots, self.config.patch_size, self.config.feat_dim), np.float32)
+        stop = np.zeros((self.slots, 2), np.float32)
+        check(self._lib.vx_generator_batch_step(self._handle, active.ctypes.data, noise.ctypes.data, timesteps, cfg,
+                                                latents.ctypes.data, stop.ctypes.data))
+        return latents, stop
+
+    def State(self, slot: int, name: str, count: int) -> np.ndarray:
+        out = np.empty(count, np.float32)
+        check(self._lib.vx_generator_batch_state(self._handle, slot, name.encode(), out.ctypes.data, count))
+        return out
+
+    def position(self, slot: int) -> int:
+        return self._lib.vx_generator_batch_position(self._handle, slot)
+
+    def SetGraphs(self, enabled: bool) -> None:
+        check(self._lib.vx_generator_batch_set_graphs(self._handle, int(enabled)))
+
+    def stream(self) -> int:
+        return self._lib.vx_generator_batch_stream(self._handle) or 0
+
+    def close(self) -> None:
+        if self._handle:
+            self._lib.vx_generator_batch_destroy(self._handle)
+            self._handle = None
+
+    def __del__(self):
+        try:
+            self.close()
+        except Exception:
+            pass
