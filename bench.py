@@ -498,6 +498,7 @@ STEP_BYTES_CONFIG3 = 4_034_512_896 + 18_874_368
 BOX_REQUESTS = 64        # independent requests over the box
 BOX_PATCHES = 63         # patches per request (about 10 s of audio)
 BOX_PER_RANK = 8         # requests each rank runs (a bounded sample of its share)
+BOX_SLOTS = 8            # requests generated together per GPU (GeneratorBatch slots)
 
 
 SWEEP_ROWS = (1, 2, 8, 22, 64, 128)
@@ -676,6 +677,7 @@ def measure_generator(rank: int, world=None, context: int = 512, patch_replays: 
     box_audio = len(mine) * BOX_PATCHES * PATCH_AUDIO_S
     weight_bytes = gen.weight_bytes()
     gen.close()
+    batched_s = max_over_ranks(world, measure_box_batched(c, mine))
     box_s_max = max_over_ranks(world, box_s)
     box_audio_all = sum_over_ranks(world, box_audio)
     box_patches_all = sum_over_ranks(world, len(mine) * BOX_PATCHES)
@@ -698,6 +700,13 @@ def measure_generator(rank: int, world=None, context: int = 512, patch_replays: 
                          else "per-kernel sequence",
                  "config": "LM 28x2048 + residual LM 8x2048 + encoder 12x1024 + DiT 12x1024, Q8_0, "
                            "one CUDA graph per patch"},
+        "box_batched": {"audio_s_per_s": box_audio_all / batched_s, "n_gpus": n_ranks,
+                        "slots": BOX_SLOTS, "device_s": batched_s,
+                        "hbm_gbs_per_gpu": STEP_BYTES_CONFIG3 * box_patches_all / n_ranks / batched_s / 1e9,
+                        "sample": f"the same {BOX_PER_RANK} requests per rank in {BOX_SLOTS} slots of one "
+                                  "GeneratorBatch (shared weights; one DiT pass for all active slots per "
+                                  "Euler evaluation); a slot takes the next request when its request ends",
+                        "config": "BASELINE config 4 (box throughput), batched request slots, no collectives"},
         "box": {"audio_s_per_s": box_audio_all / box_s_max, "n_gpus": n_ranks,
                 "requests": sum_over_ranks(world, len(mine)), "patches_per_request": BOX_PATCHES,
                 "device_s": box_s_max, "audio_s": box_audio_all,
@@ -707,6 +716,72 @@ def measure_generator(rank: int, world=None, context: int = 512, patch_replays: 
                           "prefill included; requests run one after another on each GPU",
                 "config": "BASELINE config 4 (box throughput), one request stream per GPU, no collectives"},
     }
+
+
+def box_request(c, req: int):
+    """Request `req` of config 4: a seeded prompt of 16..128 text tokens plus
+    the audio-start row, and its generator for the patches' noise."""
+    import numpy as np
+
+    rq = np.random.default_rng(10_000 + req)
+    rows = int(rq.integers(16, 129)) + 1
+    tokens = rq.integers(0, c.vocab, rows).astype(np.int32)
+    audio = np.zeros(rows, np.int32)
+    audio[-1] = 1
+    feats = np.zeros((rows, c.patch_size, c.feat_dim), np.float32)
+    feats[-1] = rq.normal(0, 1, (c.patch_size, c.feat_dim))
+    return (tokens, 1 - audio, audio, feats), rq
+
+
+def measure_box_batched(c, requests) -> float:
+    """Config 4 through a GeneratorBatch of BOX_SLOTS slots: the requests fill
+    the slots; every step advances all active slots by one patch; a slot that
+    has produced BOX_PATCHES patches takes the next request (prefill) while
+    the others continue. Device seconds on the batch's stream from the first
+    prefill to the last patch (a short warm-up first captures the graph).
+    With every request BOX_PATCHES long, slots finish together and refill
+    together."""
+    import numpy as np
+    import torch
+
+    from voxcpm_b200 import _lib
+    from voxcpm_b200.generator import GeneratorBatch
+
+    slots = min(BOX_SLOTS, len(requests))
+    batch = GeneratorBatch(c, slots, seed=100, checkpoint=_lib.CHECKPOINT_Q8, cache_type=_lib.CACHE_BF16)
+    stream = torch.cuda.ExternalStream(batch.stream())
+    values = (c.patch_size, c.feat_dim)
+
+    def run(reqs, patches):
+        queue = list(reqs)
+        left = [0] * slots
+        rngs = [None] * slots
+        while True:
+            for s in range(slots):
+                if left[s] == 0 and queue:
+                    prompt, rngs[s] = box_request(c, queue.pop(0))
+                    batch.Prefill(s, *prompt)
+                    left[s] = patches
+            active = np.array([1 if n > 0 else 0 for n in left], np.int32)
+            if not active.any():
+                return
+            noise = np.zeros((slots,) + values, np.float32)
+            for s in range(slots):
+                if active[s]:
+                    noise[s] = rngs[s].normal(0, 1, values)
+            batch.Step(noise, active, 10, 2.0)
+            left = [n - 1 if n > 0 else 0 for n in left]
+
+    run(requests[:slots], 3)  # captures the graph of all slots active
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    torch.cuda.synchronize()
+    a.record(stream)
+    run(requests, BOX_PATCHES)
+    b.record(stream)
+    b.synchronize()
+    batch.close()
+    return a.elapsed_time(b) / 1e3
 
 
 def profile_case(case: str) -> None:

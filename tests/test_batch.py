@@ -46,7 +46,12 @@ def noises(c, slots, seed):
 
 
 def test_one_active_slot_is_the_single_generator(cuda):
+    """The batch always runs the per-kernel DiT; the single generator does
+    too with SetPersistent(False), which also turns off its persistent LM
+    stacks. An LM FFN width the persistent LM kernel does not serve keeps
+    both sides on the same LM kernels as well."""
     c = config()
+    c.lm.intermediate = c.residual_lm.intermediate = 4096
     batch = GeneratorBatch(c, 3, seed=SEED)
     single = Generator(c, seed=SEED)
     single.SetPersistent(False)
