@@ -186,6 +186,15 @@ VX_API void vx_set_programmatic_launch(int enabled);
 #define VX_TENSOR_CORE_VARIANT 100
 VX_API void vx_set_tensor_core_products(int enabled);
 VX_API int vx_tensor_core_products(void);
+/* Q8_0 products of 33..128 rows on the tcgen05 kernel for many rows: one
+ * 128 x N MMA per K step (N = rows rounded up to 64, 96 or 128), every weight
+ * byte read once, per-block fp32 sums scaled in block order. A plan with
+ * variant VX_TENSOR_CORE_WIDE_VARIANT runs it for one call; the switch makes
+ * it the choice for such products launched without a plan. No reference
+ * counterpart (the reference takes 32 rows per launch, wmma_products.hip). */
+#define VX_TENSOR_CORE_WIDE_VARIANT 101
+VX_API void vx_set_wide_tensor_core_products(int enabled);
+VX_API int vx_wide_tensor_core_products(void);
 /* Number of product kernel shapes and the shape of one (benchmarks). */
 VX_API int vx_product_variants(void);
 VX_API void vx_product_variant_shape(int variant, int* warps, int* groups,

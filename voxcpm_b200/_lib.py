@@ -133,6 +133,8 @@ SIGNATURES: dict[str, tuple] = {
     "vx_set_programmatic_launch": (None, [c_int]),
     "vx_set_tensor_core_products": (None, [c_int]),
     "vx_tensor_core_products": (c_int, []),
+    "vx_set_wide_tensor_core_products": (None, [c_int]),
+    "vx_wide_tensor_core_products": (c_int, []),
     "vx_product_variants": (c_int, []),
     "vx_product_variant_shape": (
         None, [c_int, POINTER(c_int), POINTER(c_int), POINTER(c_int), POINTER(c_int)]

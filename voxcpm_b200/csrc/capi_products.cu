@@ -214,6 +214,14 @@ void vx_set_tensor_core_products(int enabled) {
 
 int vx_tensor_core_products(void) { return vx::TensorCoreProducts() ? 1 : 0; }
 
+void vx_set_wide_tensor_core_products(int enabled) {
+  vx::SetWideTensorCoreProducts(enabled != 0);
+}
+
+int vx_wide_tensor_core_products(void) {
+  return vx::WideTensorCoreProducts() ? 1 : 0;
+}
+
 int vx_product_variants(void) { return vx::NumProductVariants(); }
 
 void vx_product_variant_shape(int variant, int* warps, int* groups,

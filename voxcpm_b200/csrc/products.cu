@@ -739,6 +739,10 @@ int LaunchProduct(WeightFormat format, const std::uint16_t* x, const void* w,
     plan = *plan_in;
   else if (independent)
     plan = StreamPlan(format, rows, in, out);
+  if (plan.variant < 0 && format == WeightFormat::kQ8Tiles &&
+      rows >= static_cast<std::size_t>(kWideMinRows) &&
+      rows <= static_cast<std::size_t>(kWideMaxRows) && WideTensorCoreProducts())
+    plan = PlanWideProduct(rows, in, out, SmCount());
   if (plan.variant < 0)
     plan = PlanProduct(format, rows, in, out, 0);
   if (plan.variant < 0 && plan_in == nullptr && rows > 32) {
@@ -754,6 +758,12 @@ int LaunchProduct(WeightFormat format, const std::uint16_t* x, const void* w,
         return status;
     }
     return kOk;
+  }
+  if (plan.variant == kTensorCoreWideVariant) {
+    if (format == WeightFormat::kQ8Tiles)
+      return LaunchWideProduct(x, w, y, y_bf16, rows, in, out, accumulate,
+                               plan, stream, independent, g_programmatic);
+    plan = PlanProduct(format, rows, in, out, 0);
   }
   if (plan.variant == kTensorCoreVariant) {
     if (format == WeightFormat::kQ8Tiles)

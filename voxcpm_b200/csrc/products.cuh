@@ -99,6 +99,25 @@ bool ProgrammaticLaunch();
 void SetTensorCoreProducts(bool enabled);
 bool TensorCoreProducts();
 
+/// The tensor-core product for 33..128 rows of Q8_0 tiles
+/// (products_tc_wide.cu): one 128 x N MMA per K step (N = rows rounded up to
+/// 64, 96 or 128), weights streamed once through a two-stage ring, per-block
+/// fp32 sums scaled in block order. Plans carry kTensorCoreWideVariant.
+constexpr int kTensorCoreWideVariant = 101;
+constexpr int kWideMinRows = 33;
+constexpr int kWideMaxRows = 128;
+ProductPlan PlanWideProduct(std::size_t rows, std::size_t in, std::size_t out,
+                            int sms);
+int LaunchWideProduct(const std::uint16_t* x, const void* w, float* y,
+                      std::uint16_t* y_bf16, std::size_t rows, std::size_t in,
+                      std::size_t out, bool accumulate, const ProductPlan& plan,
+                      cudaStream_t stream, bool independent, bool programmatic);
+/// Whether products of 33..128 rows of Q8_0 tiles without a given plan run
+/// on the wide tensor-core kernel (else the mma.sync planner, or launches
+/// of 32 rows).
+void SetWideTensorCoreProducts(bool enabled);
+bool WideTensorCoreProducts();
+
 int NumProductVariants();
 /// Warps, row groups per warp, blocks per stage, stages of a variant.
 void ProductVariantShape(int variant, int* warps, int* groups, int* stage,

@@ -136,6 +136,21 @@ __device__ inline std::uint64_t SmemDescriptorNoSwizzle(const void* start,
          (1ull << 46);  // descriptor version for sm_100
 }
 
+/// Shared-memory matrix descriptor, 128-byte swizzle, K-major: rows of 128
+/// bytes (64 bf16 values) in 8-row, 1024-byte swizzle atoms, as the TMA's
+/// CU_TENSOR_MAP_SWIZZLE_128B writes them. `start` is a 1024-byte aligned
+/// atom base plus the K offset within the row in bytes (32 per 16-element
+/// K step); `group_stride` bytes between 8-row groups. The leading-dimension
+/// offset is unused for this layout (one MMA's K stays inside a row).
+__device__ inline std::uint64_t SmemDescriptorSw128(const void* start,
+                                                    std::uint32_t group_stride) {
+  return static_cast<std::uint64_t>((SmemAddr(start) >> 4) & 0x3FFFu) |
+         (1ull << 16) |
+         (static_cast<std::uint64_t>((group_stride >> 4) & 0x3FFFu) << 32) |
+         (1ull << 46) |  // descriptor version for sm_100
+         (2ull << 61);   // layout: 128-byte swizzle
+}
+
 /// D (TMEM) = A (TMEM) x B (shared memory) [+ D when `accumulate`]. One
 /// thread issues it; it completes asynchronously (see MmaCommit).
 __device__ inline void MmaBf16TmemA(std::uint32_t d, std::uint32_t a,

@@ -177,6 +177,19 @@ def TensorCoreProducts() -> bool:
     return bool(load().vx_tensor_core_products())
 
 
+TENSOR_CORE_WIDE_VARIANT = 101  # VX_TENSOR_CORE_WIDE_VARIANT
+
+
+def SetWideTensorCoreProducts(enabled: bool) -> None:
+    """Q8_0 products of 33..128 rows without a plan onto the wide tcgen05
+    kernel (one pass over the weights), or onto the mma.sync planner."""
+    load().vx_set_wide_tensor_core_products(int(enabled))
+
+
+def WideTensorCoreProducts() -> bool:
+    return bool(load().vx_wide_tensor_core_products())
+
+
 def ProductVariants() -> list[tuple[int, int, int, int]]:
     lib = load()
     shapes = []
