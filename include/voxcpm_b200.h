@@ -189,8 +189,10 @@ VX_API int vx_tensor_core_products(void);
 /* Q8_0 products of 33..128 rows on the tcgen05 kernel for many rows: one
  * 128 x N MMA per K step (N = rows rounded up to 64, 96 or 128), every weight
  * byte read once, per-block fp32 sums scaled in block order. A plan with
- * variant VX_TENSOR_CORE_WIDE_VARIANT runs it for one call; the switch makes
- * it the choice for such products launched without a plan. No reference
+ * variant VX_TENSOR_CORE_WIDE_VARIANT runs it for one call. With the switch
+ * on (default), products launched without a plan take it where it measured
+ * faster than the mma.sync kernels: more than 64 rows, in <= 1024 and
+ * out >= 3072 (the DiT's gate/up products of batched slots). No reference
  * counterpart (the reference takes 32 rows per launch, wmma_products.hip). */
 #define VX_TENSOR_CORE_WIDE_VARIANT 101
 VX_API void vx_set_wide_tensor_core_products(int enabled);

@@ -114,24 +114,24 @@ def test_wide_splits_and_repeat(cuda):
     assert K.DeviceError() == 0
 
 
-def test_wide_planner_switch(cuda):
-    """With the switch on, products of 33..128 rows launched without a plan
-    take the wide kernel (no 32-row launches); 129 rows are refused by the
-    product entry, 32 rows stay on the skinny kernels."""
-    rng = np.random.default_rng(5)
-    columns, out = 4096, 1024
+@pytest.mark.parametrize("columns,out", [(1024, 8192), (1024, 3072), (4096, 1024)])
+def test_wide_planner_switch(cuda, columns, out):
+    """Products launched without a plan, with the switch on (default: the
+    wide kernel where it pays, 65..128 rows of 1024 -> 3072 or more) and off
+    (the mma.sync planner or 32-row launches), match the oracle either way."""
+    rng = np.random.default_rng(5 + columns + out)
     blocks = make_q8_blocks(out, columns, rng)
     tiles = tiles_of(blocks, out, columns)
-    K.SetWideTensorCoreProducts(True)
+    assert K.WideTensorCoreProducts()
     try:
-        assert K.WideTensorCoreProducts()
-        for rows in (32, 33, 96, 128):
-            x = make_activations(rows, columns, rng)
-            y = torch.empty(rows, out, dtype=torch.float32, device="cuda")
-            assert run(to_dev(x), tiles, y, rows, columns, out)
-            exact = oracle.product_exact(x, oracle.Q8_0, blocks, rows, columns, out)
-            assert oracle.relative_error(y.cpu().numpy(), *exact) <= LIMIT, rows
+        for enabled in (True, False):
+            K.SetWideTensorCoreProducts(enabled)
+            for rows in (32, 33, 88, 128):
+                x = make_activations(rows, columns, rng)
+                y = torch.empty(rows, out, dtype=torch.float32, device="cuda")
+                assert run(to_dev(x), tiles, y, rows, columns, out)
+                exact = oracle.product_exact(x, oracle.Q8_0, blocks, rows, columns, out)
+                assert oracle.relative_error(y.cpu().numpy(), *exact) <= LIMIT, (enabled, rows)
     finally:
-        K.SetWideTensorCoreProducts(False)
-    assert not K.WideTensorCoreProducts()
+        K.SetWideTensorCoreProducts(True)
     assert K.DeviceError() == 0

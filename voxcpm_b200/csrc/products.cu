@@ -740,8 +740,7 @@ int LaunchProduct(WeightFormat format, const std::uint16_t* x, const void* w,
   else if (independent)
     plan = StreamPlan(format, rows, in, out);
   if (plan.variant < 0 && format == WeightFormat::kQ8Tiles &&
-      rows >= static_cast<std::size_t>(kWideMinRows) &&
-      rows <= static_cast<std::size_t>(kWideMaxRows) && WideTensorCoreProducts())
+      WideTensorCoreProducts() && WideProductPays(rows, in, out))
     plan = PlanWideProduct(rows, in, out, SmCount());
   if (plan.variant < 0)
     plan = PlanProduct(format, rows, in, out, 0);

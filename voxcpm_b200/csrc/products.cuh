@@ -112,11 +112,13 @@ int LaunchWideProduct(const std::uint16_t* x, const void* w, float* y,
                       std::uint16_t* y_bf16, std::size_t rows, std::size_t in,
                       std::size_t out, bool accumulate, const ProductPlan& plan,
                       cudaStream_t stream, bool independent, bool programmatic);
-/// Whether products of 33..128 rows of Q8_0 tiles without a given plan run
-/// on the wide tensor-core kernel (else the mma.sync planner, or launches
-/// of 32 rows).
+/// Whether Q8_0 products launched without a plan take the wide tensor-core
+/// kernel where WideProductPays (default on); else the mma.sync planner, or
+/// launches of 32 rows.
 void SetWideTensorCoreProducts(bool enabled);
 bool WideTensorCoreProducts();
+/// The shapes where the wide kernel measured faster than the mma.sync path.
+bool WideProductPays(std::size_t rows, std::size_t in, std::size_t out);
 
 int NumProductVariants();
 /// Warps, row groups per warp, blocks per stage, stages of a variant.

@@ -408,11 +408,22 @@ bool EncodeWideActivations(const std::uint16_t* x, std::size_t rows,
                              CU_TENSOR_MAP_SWIZZLE_128B);
 }
 
-bool g_wide = false;
+bool g_wide = true;
 
 }  // namespace
 
 void SetWideTensorCoreProducts(bool enabled) { g_wide = enabled; }
+
+bool WideProductPays(std::size_t rows, std::size_t in, std::size_t out) {
+  // Measured on B200 against the mma.sync path at 33..128 rows over the
+  // config-1 and DiT shapes: the wide kernel wins for more than 64 rows over
+  // short reductions into many outputs (1024 -> 8192 at 88..128 rows: 18-22
+  // against 48-52 us; 1024 -> 3072: 19-23 against 25-27 us), where the
+  // mma.sync kernels' activation slice leaves few CTAs; elsewhere the
+  // per-block read-back of its sums keeps it slower.
+  return rows > 64 && rows <= static_cast<std::size_t>(kWideMaxRows) &&
+         in <= 1024 && out >= 3072;
+}
 bool WideTensorCoreProducts() { return g_wide; }
 
 ProductPlan PlanWideProduct(std::size_t rows, std::size_t in, std::size_t out,

@@ -181,8 +181,9 @@ TENSOR_CORE_WIDE_VARIANT = 101  # VX_TENSOR_CORE_WIDE_VARIANT
 
 
 def SetWideTensorCoreProducts(enabled: bool) -> None:
-    """Q8_0 products of 33..128 rows without a plan onto the wide tcgen05
-    kernel (one pass over the weights), or onto the mma.sync planner."""
+    """Q8_0 products without a plan onto the wide tcgen05 kernel where it
+    measured faster (more than 64 rows, in <= 1024, out >= 3072; default on),
+    or always onto the mma.sync planner."""
     load().vx_set_wide_tensor_core_products(int(enabled))
 
 
