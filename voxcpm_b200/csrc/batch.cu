@@ -11,9 +11,14 @@
 //     the 8n output rows, dit_out, GuidedEuler per slot
 //   scatter the latents; each slot's outputs (Generator::PatchOutputs)
 //   the local encoder over the n patches (5n rows, n sequences)
-//   each slot: both LMs advanced by its embedding (Generator::AdvanceLms)
+//   both LMs advanced for all n slots as one pass of n rows: the slots' LM
+//   caches are slot-major ([layer][slot][kv_head][position][128]), so row i
+//   writes and reads slot s_i's cache through a cache row of
+//   s_i * kv_heads * positions + position and a first key row of
+//   s_i * kv_heads * positions, with its own past length
 // The products of 22n rows read each DiT weight once per evaluation for all
-// n requests; rows beyond 128 run in chunks of 32.
+// n requests (rows beyond 128 in chunks of 32), and the LM's weights are read
+// once per step for all n requests.
 #include "model.cuh"
 #include "vx_status.h"
 
@@ -41,6 +46,28 @@ void Ok(int status, const char* what) {
   }
 }
 
+/// The active slots of a step: their position counters and slot indices
+/// (kernel arguments, so a captured graph keeps its own list).
+struct SlotPositions {
+  int count;
+  int stride;  // cache rows per slot: kv_heads * positions
+  const std::int32_t* counter[64];
+  int slot[64];
+};
+
+__global__ void GatherPositionsKernel(const SlotPositions a,
+                                      std::int32_t* past,
+                                      std::int32_t* cache_rows,
+                                      std::int32_t* first_keys) {
+  const int i = static_cast<int>(threadIdx.x);
+  if (i < a.count) {
+    const std::int32_t position = *a.counter[i];
+    past[i] = position;
+    first_keys[i] = a.slot[i] * a.stride;
+    cache_rows[i] = a.slot[i] * a.stride + position;
+  }
+}
+
 }  // namespace
 
 std::unique_ptr<GeneratorBatch> GeneratorBatch::Create(
@@ -52,14 +79,21 @@ std::unique_ptr<GeneratorBatch> GeneratorBatch::Create(
     if (slots < 1 || slots > 64)
       throw std::invalid_argument("a batch holds 1 to 64 slots");
     std::string failure;
-    auto first = Generator::Create(config, seed, kind, cache_type, &failure, files);
+    b->base_caches_ = KvCache(config.lm, config.max_length, cache_type, slots);
+    b->residual_caches_ =
+        KvCache(config.residual_lm, config.max_length, cache_type, slots);
+    SlotCaches caches{&b->base_caches_, &b->residual_caches_, 0};
+    auto first = Generator::Create(config, seed, kind, cache_type, &failure,
+                                   files, nullptr, nullptr, &caches);
     if (!first)
       throw std::runtime_error(failure);
     b->stream_ = first->stream_;
     b->slots_.push_back(std::move(first));
     for (int i = 1; i < slots; ++i) {
+      caches.slot = i;
       auto g = Generator::Create(config, seed, kind, cache_type, &failure,
-                                 nullptr, b->slots_[0].get(), b->stream_);
+                                 nullptr, b->slots_[0].get(), b->stream_,
+                                 &caches);
       if (!g)
         throw std::runtime_error(failure);
       b->slots_.push_back(std::move(g));
@@ -85,8 +119,18 @@ std::unique_ptr<GeneratorBatch> GeneratorBatch::Create(
     const std::size_t x_rows_at = take(n * patch * dit * 4);
     const std::size_t hidden_at = take(n * dit_rows * dit * 4);
     const std::size_t output_at = take(n * dit_rows * dit * 4);
-    const std::size_t bf16_at = take(n * dit_rows * std::max(dit, c.feat_dim) * 2);
+    const std::size_t bf16_at = take(
+        n * std::max<std::size_t>(dit_rows * std::max(dit, c.feat_dim),
+                                  2 * c.lm.hidden) * 2);
     const std::size_t embed_at = take(n * c.lm.hidden * 4);
+    const std::size_t lm_a_at = take(n * c.lm.hidden * 4);
+    const std::size_t lm_b_at = take(n * c.lm.hidden * 4);
+    const std::size_t lm_hidden_at = take(n * c.lm.hidden * 4);
+    const std::size_t residual_at = take(n * c.lm.hidden * 4);
+    const std::size_t fsq_at = take(n * c.fsq_latent_dim * 4);
+    const std::size_t past_at = take(n * 4);
+    const std::size_t cache_rows_at = take(n * 4);
+    const std::size_t first_keys_at = take(n * 4);
     const std::size_t positions_at = take(n * dit_rows * 4);
     const std::size_t rows_at = take(n * dit_rows * 4);
     const std::size_t outputs_at = take(n * 2 * patch * 4);
@@ -101,6 +145,14 @@ std::unique_ptr<GeneratorBatch> GeneratorBatch::Create(
     b->output_ = reinterpret_cast<float*>(base + output_at);
     b->bf16_ = reinterpret_cast<std::uint16_t*>(base + bf16_at);
     b->embed_ = reinterpret_cast<float*>(base + embed_at);
+    b->lm_a_ = reinterpret_cast<float*>(base + lm_a_at);
+    b->lm_b_ = reinterpret_cast<float*>(base + lm_b_at);
+    b->lm_hidden_ = reinterpret_cast<float*>(base + lm_hidden_at);
+    b->residual_hidden_ = reinterpret_cast<float*>(base + residual_at);
+    b->fsq_ = reinterpret_cast<float*>(base + fsq_at);
+    b->past_ = reinterpret_cast<std::int32_t*>(base + past_at);
+    b->cache_rows_ = reinterpret_cast<std::int32_t*>(base + cache_rows_at);
+    b->first_keys_ = reinterpret_cast<std::int32_t*>(base + first_keys_at);
     b->positions_ = reinterpret_cast<std::int32_t*>(base + positions_at);
     b->rows_ = reinterpret_cast<std::int32_t*>(base + rows_at);
     b->outputs_ = reinterpret_cast<std::int32_t*>(base + outputs_at);
@@ -221,11 +273,65 @@ void GeneratorBatch::Body(const std::vector<int>& members, int timesteps,
     g.PatchOutputs();
   }
   g0.Encode(x_, count, embed_);
+  AdvanceLms(members);
+}
+
+void GeneratorBatch::AdvanceLms(const std::vector<int>& members) {
+  // Generator::AdvanceLms (generator.cpp:478-513) for every active slot as
+  // one pass of `count` rows over the slot-major caches.
+  Generator& g0 = *slots_[0];
+  const ModelConfig& c = g0.config_;
+  const GeneratorWeights& w = g0.w_;
+  const int hidden = c.lm.hidden;
+  const int count = static_cast<int>(members.size());
+  const int capacity = g0.capacity();
+  SlotPositions positions{};
+  positions.count = count;
+  positions.stride = c.lm.kv_heads * capacity;
+  for (int i = 0; i < count; ++i) {
+    positions.counter[i] = slots_[members[i]]->position_counter_;
+    positions.slot[i] = members[i];
+  }
+  GatherPositionsKernel<<<1, 64, 0, stream_>>>(positions, past_, cache_rows_,
+                                                first_keys_);
+  Cuda(cudaGetLastError(), "gather positions");
+  AttentionLayout layout;
+  layout.positions = past_;      // the rotary row is the position
+  layout.cache_rows = cache_rows_;
+  layout.rows_per_sequence = 1;
+  layout.keys_per_sequence = positions.stride;
+  layout.first_keys = first_keys_;  // row i reads slot members[i]
+  layout.past_device = past_;
+  layout.past_per_sequence = true;
+  layout.max_keys = capacity;
+  layout.causal = true;
+  const std::size_t rows_h = static_cast<std::size_t>(count) * hidden;
+  Ok(CopyFloats(embed_, lm_a_, rows_h, stream_), "copy");
+  Ok(ForwardStack(w.base_lm, g0.rope_, layout, base_caches_, lm_a_, lm_b_,
+                  count, g0.scratch_, stream_),
+     "base lm");
+  // FSQ (generator.cpp:239-250) over the rows.
+  Ok(ToBf16(lm_b_, bf16_, rows_h, false, stream_), "ToBf16");
+  Ok(Project(w.fsq_in, bf16_, fsq_, count, stream_), "fsq_in");
+  Ok(Quantize(fsq_, bf16_, static_cast<std::size_t>(count) * c.fsq_latent_dim,
+              c.fsq_scale, stream_),
+     "Quantize");
+  Ok(Project(w.fsq_out, bf16_, lm_hidden_, count, stream_), "fsq_out");
+  Ok(ConcatRows(lm_hidden_, nullptr, hidden, embed_, nullptr, hidden, bf16_,
+                count, stream_),
+     "ConcatRows");
+  Ok(Project(w.fusion, bf16_, lm_a_, count, stream_), "fusion");
+  Ok(ForwardStack(w.residual_lm, nullptr, layout, residual_caches_, lm_a_,
+                  residual_hidden_, count, g0.scratch_, stream_),
+     "residual lm");
   for (int i = 0; i < count; ++i) {
     Generator& g = *slots_[members[i]];
-    Ok(CopyFloats(embed_ + static_cast<std::size_t>(i) * hidden, g.embed_, hidden, stream_),
+    const std::size_t row = static_cast<std::size_t>(i) * hidden;
+    Ok(CopyFloats(lm_hidden_ + row, g.lm_hidden_, hidden, stream_), "copy");
+    Ok(CopyFloats(residual_hidden_ + row, g.residual_hidden_, hidden, stream_),
        "copy");
-    g.AdvanceLms();
+    Ok(AdvancePosition(g.position_counter_, g.step_positions_, stream_),
+       "advance");
   }
 }
 

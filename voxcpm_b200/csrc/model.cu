@@ -517,10 +517,12 @@ ModelConfig ReleasedConfig() {
 
 // ------------------------------------------------------------ KvCache
 
-KvCache::KvCache(const StackConfig& config, int capacity, CacheType type)
+KvCache::KvCache(const StackConfig& config, int capacity, CacheType type,
+                 int slots)
     : capacity_(capacity), type_(type) {
-  layer_bytes_ = static_cast<std::size_t>(config.kv_heads) * capacity *
-                 config.head_dim * CacheElementBytes(type);
+  slot_bytes_ = static_cast<std::size_t>(config.kv_heads) * capacity *
+                config.head_dim * CacheElementBytes(type);
+  layer_bytes_ = slot_bytes_ * static_cast<std::size_t>(std::max(slots, 1));
   bytes_ = layer_bytes_ * config.layers;
   ThrowCuda(cudaMalloc(reinterpret_cast<void**>(&keys_), bytes_),
             "cudaMalloc keys");
@@ -541,6 +543,8 @@ KvCache& KvCache::operator=(KvCache&& other) noexcept {
     Release();
     keys_ = other.keys_;
     values_ = other.values_;
+    owns_ = other.owns_;
+    slot_bytes_ = other.slot_bytes_;
     layer_bytes_ = other.layer_bytes_;
     bytes_ = other.bytes_;
     capacity_ = other.capacity_;
@@ -553,16 +557,31 @@ KvCache& KvCache::operator=(KvCache&& other) noexcept {
 }
 
 void KvCache::Release() {
-  if (keys_ != nullptr)
-    cudaFree(keys_);
-  if (values_ != nullptr)
-    cudaFree(values_);
+  if (owns_) {
+    if (keys_ != nullptr)
+      cudaFree(keys_);
+    if (values_ != nullptr)
+      cudaFree(values_);
+  }
   keys_ = values_ = nullptr;
 }
 
 void* KvCache::keys(int layer) const { return keys_ + layer * layer_bytes_; }
 void* KvCache::values(int layer) const {
   return values_ + layer * layer_bytes_;
+}
+
+KvCache KvCache::Slot(int slot) const {
+  KvCache view;
+  view.keys_ = keys_ + static_cast<std::size_t>(slot) * slot_bytes_;
+  view.values_ = values_ + static_cast<std::size_t>(slot) * slot_bytes_;
+  view.owns_ = false;
+  view.slot_bytes_ = slot_bytes_;
+  view.layer_bytes_ = layer_bytes_;
+  view.bytes_ = 0;
+  view.capacity_ = capacity_;
+  view.type_ = type_;
+  return view;
 }
 
 // ------------------------------------------------------------ stack loop
@@ -614,7 +633,8 @@ int ForwardStack(const StackWeights& stack, const float* rope,
                   s.attention, rows, layout.rows_per_sequence,
                   layout.keys_per_sequence, layout.past, layout.past_device,
                   layout.causal, c.heads, c.kv_heads, c.head_dim,
-                  cache.capacity(), layout.max_keys, stream));
+                  cache.capacity(), layout.max_keys, stream,
+                  layout.past_per_sequence, layout.first_keys));
     run(Linear(s.attention, layer.o, hidden, rows, true, stream));
     run(RmsNorm(hidden, layer.post_norm, s.normed, nullptr, rows, width,
                 c.rms_eps, stream));
@@ -636,7 +656,8 @@ std::unique_ptr<Generator> Generator::Create(const ModelConfig& config,
                                              std::string* error,
                                              const ModelFiles* files,
                                              const Generator* share,
-                                             cudaStream_t stream) {
+                                             cudaStream_t stream,
+                                             const SlotCaches* lm_caches) {
   std::unique_ptr<Generator> g(new Generator());
   try {
     const ModelConfig& c = config;
@@ -728,8 +749,13 @@ std::unique_ptr<Generator> Generator::Create(const ModelConfig& config,
                            cudaMemcpyHostToDevice),
                 "upload rope");
     }
-    g->base_cache_ = KvCache(c.lm, c.max_length, cache_type);
-    g->residual_cache_ = KvCache(c.residual_lm, c.max_length, cache_type);
+    if (lm_caches != nullptr) {
+      g->base_cache_ = lm_caches->base->Slot(lm_caches->slot);
+      g->residual_cache_ = lm_caches->residual->Slot(lm_caches->slot);
+    } else {
+      g->base_cache_ = KvCache(c.lm, c.max_length, cache_type);
+      g->residual_cache_ = KvCache(c.residual_lm, c.max_length, cache_type);
+    }
     g->dit_cache_ = KvCache(c.dit, dit_rows, cache_type);
     g->encoder_cache_ = KvCache(c.encoder, 64, cache_type);
     g->EnsureRows(std::max(dit_rows, c.patch_size + 1));

@@ -92,7 +92,12 @@ enum class CheckpointKind : int { kQ8 = 0, kBf16 = 1 };
 class KvCache {
  public:
   KvCache() = default;
-  KvCache(const StackConfig& config, int capacity, CacheType type);
+  /// [layer][kv_head][capacity][head_dim] keys and values; with `slots` > 1,
+  /// [layer][slot][kv_head][capacity][head_dim]: one cache per slot, each a
+  /// view (Slot) that the one-sequence kernels read as usual, while a kernel
+  /// given slot 0's pointers reaches slot s at s * kv_heads * capacity rows.
+  KvCache(const StackConfig& config, int capacity, CacheType type,
+          int slots = 1);
   ~KvCache();
   KvCache(const KvCache&) = delete;
   KvCache& operator=(const KvCache&) = delete;
@@ -104,11 +109,15 @@ class KvCache {
   void* keys(int layer) const;
   void* values(int layer) const;
   std::size_t bytes() const { return bytes_; }
+  /// A non-owning view of slot `slot` (valid while this cache lives).
+  KvCache Slot(int slot) const;
 
  private:
   void Release();
   unsigned char* keys_ = nullptr;
   unsigned char* values_ = nullptr;
+  bool owns_ = true;
+  std::size_t slot_bytes_ = 0;
   std::size_t layer_bytes_ = 0;
   std::size_t bytes_ = 0;
   int capacity_ = 0;
@@ -127,6 +136,8 @@ struct AttentionLayout {
   const std::int32_t* past_device = nullptr;
   int max_keys = 0;
   bool causal = true;
+  bool past_per_sequence = false;  // past_device holds one value per sequence
+  const std::int32_t* first_keys = nullptr;  // device: each sequence's first key row
 };
 
 /// Scratch shared by the stacks of one generator (transformer.hpp:50-58).
@@ -157,6 +168,14 @@ int ForwardStack(const StackWeights& stack, const float* rope,
 class DeviceArena;
 class ModelFiles;
 
+/// The LM caches of one GeneratorBatch slot: slot `slot` of slot-major caches
+/// (KvCache with slots) that outlive the generator.
+struct SlotCaches {
+  const KvCache* base = nullptr;
+  const KvCache* residual = nullptr;
+  int slot = 0;
+};
+
 /// VoxCPM2's generator on one GPU (generator.hpp:58-179): one sequence at a
 /// time on its own stream.
 class Generator {
@@ -166,7 +185,8 @@ class Generator {
   ///
   /// With `share`, the weights are `share`'s (same configuration; nothing is
   /// uploaded). With `stream`, the generator runs on that stream and does
-  /// not own it (the slots of a GeneratorBatch).
+  /// not own it; with `lm_caches`, its LM caches are views of those (the
+  /// slots of a GeneratorBatch).
   static std::unique_ptr<Generator> Create(const ModelConfig& config,
                                            std::uint64_t seed,
                                            CheckpointKind kind,
@@ -174,7 +194,8 @@ class Generator {
                                            std::string* error,
                                            const ModelFiles* files = nullptr,
                                            const Generator* share = nullptr,
-                                           cudaStream_t stream = nullptr);
+                                           cudaStream_t stream = nullptr,
+                                           const SlotCaches* lm_caches = nullptr);
   ~Generator();
 
   const ModelConfig& config() const { return config_; }
@@ -380,8 +401,13 @@ class GeneratorBatch {
   GeneratorBatch() = default;
   void Body(const std::vector<int>& members, int timesteps, float cfg);
   void EvaluateDit(int count, float t);
+  void AdvanceLms(const std::vector<int>& members);
   void DestroyGraphs();
 
+  // The slots' LM caches, slot-major (declared before the slots, released
+  // after them).
+  KvCache base_caches_;
+  KvCache residual_caches_;
   std::vector<std::unique_ptr<Generator>> slots_;
   cudaStream_t stream_ = nullptr;
   KvCache dit_cache_;
@@ -395,6 +421,14 @@ class GeneratorBatch {
   float* output_ = nullptr;    // [slots * dit rows][dit hidden]
   std::uint16_t* bf16_ = nullptr;
   float* embed_ = nullptr;     // [slots][lm hidden]
+  float* lm_a_ = nullptr;      // [slots][lm hidden] LM step rows
+  float* lm_b_ = nullptr;
+  float* lm_hidden_ = nullptr;       // [slots][lm hidden] after FSQ
+  float* residual_hidden_ = nullptr; // [slots][lm hidden]
+  float* fsq_ = nullptr;       // [slots][fsq latent]
+  std::int32_t* past_ = nullptr;        // [slots] each active slot's position
+  std::int32_t* cache_rows_ = nullptr;  // [slots] its cache row (slot-major)
+  std::int32_t* first_keys_ = nullptr;  // [slots] its first key row
   std::int32_t* positions_ = nullptr;
   std::int32_t* rows_ = nullptr;
   std::int32_t* outputs_ = nullptr;

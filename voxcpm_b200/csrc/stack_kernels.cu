@@ -237,6 +237,8 @@ struct AttentionArgs {
   const void* v_cache;
   Bf16* output;
   const std::int32_t* past_device;
+  int past_stride;  // 1: past_device holds one value per sequence
+  const std::int32_t* first_keys;  // per sequence; null: sequence * keys_per_sequence
   int rows_per_sequence;
   int keys_per_sequence;
   int past;
@@ -271,13 +273,17 @@ __global__ void __launch_bounds__(kAttentionWarps * 32)
   const int split = static_cast<int>(blockIdx.y);
   const int sequence = row / a.rows_per_sequence;
   const int local = row % a.rows_per_sequence;
-  const int past = a.past_device != nullptr ? *a.past_device : a.past;
+  const int past = a.past_device != nullptr
+                       ? a.past_device[a.past_stride * sequence]
+                       : a.past;
   const int count = past + (a.causal ? local + 1 : a.rows_per_sequence);
   const int per = (count + a.splits - 1) / a.splits;
   const int k0 = split * per;
   const int k1 = min(count, k0 + per);
   const std::size_t first_key =
-      static_cast<std::size_t>(sequence) * a.keys_per_sequence;
+      a.first_keys != nullptr
+          ? static_cast<std::size_t>(a.first_keys[sequence])
+          : static_cast<std::size_t>(sequence) * a.keys_per_sequence;
   const int kv_head = head / (a.heads / a.kv_heads);
   const CacheT* keys = static_cast<const CacheT*>(a.k_cache) +
                        (static_cast<std::size_t>(kv_head) * a.capacity +
@@ -615,7 +621,8 @@ int Attention(const float* q, const void* k_cache, const void* v_cache,
               std::size_t past, const std::int32_t* past_device, bool causal,
               std::size_t heads, std::size_t kv_heads, std::size_t head_dim,
               std::size_t capacity, std::size_t max_keys,
-              cudaStream_t stream) {
+              cudaStream_t stream, bool past_per_sequence,
+              const std::int32_t* first_keys) {
   if (rows == 0)
     return kOk;
   if (head_dim != 128 || kv_heads == 0 || heads % kv_heads != 0 ||
@@ -633,6 +640,8 @@ int Attention(const float* q, const void* k_cache, const void* v_cache,
   a.v_cache = v_cache;
   a.output = output;
   a.past_device = past_device;
+  a.past_stride = past_per_sequence ? 1 : 0;
+  a.first_keys = first_keys;
   a.rows_per_sequence = static_cast<int>(rows_per_sequence);
   a.keys_per_sequence = static_cast<int>(keys_per_sequence);
   a.past = static_cast<int>(past);

@@ -32,14 +32,18 @@ int QkvRope(const float* qkv, const float* cos_sin,
             std::size_t rows, std::size_t heads, std::size_t kv_heads,
             std::size_t head_dim, std::size_t capacity, cudaStream_t stream);
 /// `past` keys before each sequence's rows; when `past_device` is not null
-/// the kernel reads `past` from it (graph replays with a moving position)
-/// and `max_keys` bounds the keys a row may see.
+/// the kernel reads `past` from it (graph replays with a moving position),
+/// one value per sequence with `past_per_sequence`, and `max_keys` bounds the
+/// keys a row may see. A sequence's keys start at cache row
+/// sequence * keys_per_sequence, or at first_keys[sequence] when given.
 int Attention(const float* q, const void* k_cache, const void* v_cache,
               CacheType cache_type, std::uint16_t* output, std::size_t rows,
               std::size_t rows_per_sequence, std::size_t keys_per_sequence,
               std::size_t past, const std::int32_t* past_device, bool causal,
               std::size_t heads, std::size_t kv_heads, std::size_t head_dim,
-              std::size_t capacity, std::size_t max_keys, cudaStream_t stream);
+              std::size_t capacity, std::size_t max_keys, cudaStream_t stream,
+              bool past_per_sequence = false,
+              const std::int32_t* first_keys = nullptr);
 int SwiGlu(const float* gate_up, std::uint16_t* output, std::size_t rows,
            std::size_t width, cudaStream_t stream);
 int AddBias(float* data, const std::uint16_t* bias, std::size_t rows,
