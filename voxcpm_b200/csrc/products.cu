@@ -662,12 +662,40 @@ ProductPlan PlanProduct(WeightFormat format, std::size_t rows, std::size_t in,
       return best;
     }
   }
-  // 33..128 rows in one launch pay off only for short reductions (measured:
-  // 1.3-2x faster than 32-row launches at in = 1024, slower at in >= 2048,
-  // where a wide launch is compute-bound on too few CTAs); longer ones get no
-  // plan, so the launcher runs 32-row launches.
-  if (rows > 32 && target_ctas == 0 && in > 1024)
+  // 33..128 rows over reductions longer than 1024 columns: the cost model's
+  // wide plans were compute-bound on too few CTAs there. For Q8_0 tiles into
+  // at most 2560 outputs, one launch of variant 1 over slices of 22 (or 16)
+  // blocks, split across a cluster, measured
+  // 1.3-1.8x faster than 32-row launches (which re-read the weights) at
+  // 48..128 rows of 2048 / 4096 -> 1024 .. 2560. Into more outputs there are
+  // panels enough for 32-row launches to win (2048 -> 6144: 19.6 against
+  // 34 us at 64 rows); those, the slices that do not fit, and bf16 weights
+  // get no plan: the launcher runs 32-row launches.
+  if (rows > 32 && target_ctas == 0 && in > 1024) {
+    if (format != WeightFormat::kQ8Tiles || out > 2560)
+      return best;
+    constexpr int kLongVariant = 1;
+    if (!WideVariant(kLongVariant))
+      return best;
+    // Slices up to the launch limit (220 KB, as explicit plans): the 22-block
+    // slice of 88..128 rows needs it, and 16-block slices split 4096 / 2048
+    // -> 1024 / 2560 too finely (34 / 30 us against 21 / 20 us).
+    for (const int slice : {22, 16}) {
+      int splits = (k_blocks + slice - 1) / slice;
+      if (splits > 8)
+        return best;
+      const int bps = (k_blocks + splits - 1) / splits;
+      splits = (k_blocks + bps - 1) / bps;
+      if (FootprintOf(static_cast<int>(format), kLongVariant, TilesFor(rows), bps)
+              .smem > kMaxProductSmem)
+        continue;
+      best.variant = kLongVariant;
+      best.splits = splits;
+      best.blocks_per_split = bps;
+      return best;
+    }
     return best;
+  }
   const int groups_total = static_cast<int>((out + 15) / 16);
   const int min_splits =
       (k_blocks * kTileColumns + kPlannedSliceColumns - 1) / kPlannedSliceColumns;
