@@ -497,8 +497,8 @@ STEP_BYTES_CONFIG3 = 4_034_512_896 + 18_874_368
 
 BOX_REQUESTS = 64        # independent requests over the box
 BOX_PATCHES = 63         # patches per request (about 10 s of audio)
-BOX_PER_RANK = 8         # requests each rank runs (a bounded sample of its share)
-BOX_SLOTS = 8            # requests generated together per GPU (GeneratorBatch slots)
+BOX_PER_RANK = 16        # requests each rank runs (a bounded sample of its share)
+BOX_SLOTS = 16           # requests generated together per GPU (GeneratorBatch slots)
 
 
 SWEEP_ROWS = (1, 2, 8, 22, 64, 128)
