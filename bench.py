@@ -60,7 +60,7 @@ def parse():
     p.add_argument("--steps", type=int, default=400_000)
     p.add_argument("--warmup", type=int, default=20_000)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--case", choices=["product", "dit"], default=None,
+    p.add_argument("--case", choices=["product", "dit", "wide", "batch"], default=None,
                    help="run a few launches of one kernel for a profiler and exit (no JSON line)")
     return p.parse_args()
 
@@ -788,7 +788,11 @@ def profile_case(case: str) -> None:
     """A few launches of one kernel on a small case, for ncu captures:
     `product`: 8 config-0 products with the stream plan (independent), then 8
     with the planner's plan (dependent); `dit`: two eager DiT patches (the
-    persistent kernel) on the released DiT with one-layer LMs."""
+    persistent kernel) on the released DiT with one-layer LMs; `wide`: three
+    products of 88 rows of 1024 -> 8192 (the gate/up product of four batched
+    slots' DiT rows; the planner gives it to the wide tcgen05 kernel);
+    `batch`: two steps of a GeneratorBatch of 8 slots on the released shapes
+    (the first captures the step's graph)."""
     import numpy as np
     import torch
 
@@ -815,6 +819,34 @@ def profile_case(case: str) -> None:
             _lib.check(lib.vx_product(_lib.WEIGHTS_Q8_TILES, x.data_ptr(), tiles[8 + i].data_ptr(),
                                       ys[8 + i].data_ptr(), _lib.OUT_BF16, ROWS, IN, OUT, 0, None, None))
         torch.cuda.synchronize()
+    elif case == "wide":
+        rows, columns, out = 88, 1024, 8192
+        blocks = torch.from_numpy(K.RandomQ8_0(1000, 0, out, columns)).cuda()
+        t = torch.empty(K.Q8TilesBytes(out, columns), dtype=torch.uint8, device="cuda")
+        K.Q8_0ToTiles(blocks, out, columns, t)
+        x = torch.randn(rows, columns, device="cuda").to(torch.bfloat16)
+        y = torch.empty(rows, out, dtype=torch.float32, device="cuda")
+        for _ in range(3):
+            _lib.check(lib.vx_product(_lib.WEIGHTS_Q8_TILES, x.data_ptr(), t.data_ptr(), y.data_ptr(),
+                                      _lib.OUT_F32, rows, columns, out, 0, None, None))
+        torch.cuda.synchronize()
+    elif case == "batch":
+        from voxcpm_b200.generator import GeneratorBatch, released_config
+
+        c = released_config()
+        c.max_length = 256
+        slots, rows = 8, 16
+        rng = np.random.default_rng(0)
+        feats = rng.normal(0, 1, (rows, c.patch_size, c.feat_dim)).astype(np.float32)
+        audio = np.ones(rows, np.int32)
+        batch = GeneratorBatch(c, slots, seed=1)
+        for s in range(slots):
+            batch.Prefill(s, np.zeros(rows, np.int32), 1 - audio, audio, feats)
+        noise = rng.normal(0, 1, (slots, c.patch_size, c.feat_dim)).astype(np.float32)
+        for _ in range(2):
+            batch.Step(noise, None, 10, 2.0)
+        torch.cuda.synchronize()
+        batch.close()
     else:
         from voxcpm_b200.generator import Generator, released_config
 
