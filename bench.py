@@ -90,26 +90,24 @@ def barrier(world):
         dist.barrier()
 
 
-def max_over_ranks(world, value: float) -> float:
-    if world == 1:
-        return value
+def _all_reduce(value: float, op_name: str) -> float:
+    """One value reduced over the ranks (a CUDA tensor under NCCL, a host
+    tensor under gloo)."""
     import torch
     import torch.distributed as dist
 
-    t = torch.tensor([value], dtype=torch.float64, device="cuda")
-    dist.all_reduce(t, op=dist.ReduceOp.MAX)
+    device = "cpu" if dist.get_backend() == "gloo" else "cuda"
+    t = torch.tensor([value], dtype=torch.float64, device=device)
+    dist.all_reduce(t, op=getattr(dist.ReduceOp, op_name))
     return float(t.item())
+
+
+def max_over_ranks(world, value: float) -> float:
+    return value if world == 1 else _all_reduce(value, "MAX")
 
 
 def sum_over_ranks(world, value: float) -> float:
-    if world == 1:
-        return value
-    import torch
-    import torch.distributed as dist
-
-    t = torch.tensor([value], dtype=torch.float64, device="cuda")
-    dist.all_reduce(t, op=dist.ReduceOp.SUM)
-    return float(t.item())
+    return value if world == 1 else _all_reduce(value, "SUM")
 
 
 # ---------------------------------------------------------------- clocks
@@ -657,7 +655,7 @@ def measure_generator(rank: int, world=None, context: int = 512, patch_replays: 
     # BOX_PATCHES patches; device time on the generator's stream from the
     # first prefill to the last latent.
     n_ranks = world if world else 1
-    mine = list(range(rank, BOX_REQUESTS, n_ranks))[:BOX_PER_RANK]
+    mine = box_share(rank, n_ranks)
     torch.cuda.synchronize()
     a.record(stream)
     for req in mine:
@@ -718,6 +716,44 @@ def measure_generator(rank: int, world=None, context: int = 512, patch_replays: 
     }
 
 
+def box_share(rank: int, world: int) -> list:
+    """The config-4 requests rank `rank` of `world` runs: requests rank,
+    rank + world, ... of BOX_REQUESTS, the first BOX_PER_RANK of them (no
+    request on two ranks; no collective)."""
+    return list(range(rank, BOX_REQUESTS, max(world, 1)))[:BOX_PER_RANK]
+
+
+def drive_box(batch, c, requests, slots: int, patches: int) -> int:
+    """Runs `requests` through the slots of `batch` (GeneratorBatch-like:
+    Prefill(slot, ...), Step(noise, active, timesteps, cfg)): requests fill
+    free slots in order; every step advances all active slots by one patch;
+    a slot that has produced `patches` patches takes the next request.
+    Returns the number of steps."""
+    import numpy as np
+
+    values = (c.patch_size, c.feat_dim)
+    queue = list(requests)
+    left = [0] * slots
+    rngs = [None] * slots
+    steps = 0
+    while True:
+        for s in range(slots):
+            if left[s] == 0 and queue:
+                prompt, rngs[s] = box_request(c, queue.pop(0))
+                batch.Prefill(s, *prompt)
+                left[s] = patches
+        active = np.array([1 if n > 0 else 0 for n in left], np.int32)
+        if not active.any():
+            return steps
+        noise = np.zeros((slots,) + values, np.float32)
+        for s in range(slots):
+            if active[s]:
+                noise[s] = rngs[s].normal(0, 1, values)
+        batch.Step(noise, active, 10, 2.0)
+        steps += 1
+        left = [n - 1 if n > 0 else 0 for n in left]
+
+
 def box_request(c, req: int):
     """Request `req` of config 4: a seeded prompt of 16..128 text tokens plus
     the audio-start row, and its generator for the patches' noise."""
@@ -750,34 +786,12 @@ def measure_box_batched(c, requests) -> float:
     slots = min(BOX_SLOTS, len(requests))
     batch = GeneratorBatch(c, slots, seed=100, checkpoint=_lib.CHECKPOINT_Q8, cache_type=_lib.CACHE_BF16)
     stream = torch.cuda.ExternalStream(batch.stream())
-    values = (c.patch_size, c.feat_dim)
-
-    def run(reqs, patches):
-        queue = list(reqs)
-        left = [0] * slots
-        rngs = [None] * slots
-        while True:
-            for s in range(slots):
-                if left[s] == 0 and queue:
-                    prompt, rngs[s] = box_request(c, queue.pop(0))
-                    batch.Prefill(s, *prompt)
-                    left[s] = patches
-            active = np.array([1 if n > 0 else 0 for n in left], np.int32)
-            if not active.any():
-                return
-            noise = np.zeros((slots,) + values, np.float32)
-            for s in range(slots):
-                if active[s]:
-                    noise[s] = rngs[s].normal(0, 1, values)
-            batch.Step(noise, active, 10, 2.0)
-            left = [n - 1 if n > 0 else 0 for n in left]
-
-    run(requests[:slots], 3)  # captures the graph of all slots active
+    drive_box(batch, c, requests[:slots], slots, 3)  # captures the graph of all slots active
     a = torch.cuda.Event(enable_timing=True)
     b = torch.cuda.Event(enable_timing=True)
     torch.cuda.synchronize()
     a.record(stream)
-    run(requests, BOX_PATCHES)
+    drive_box(batch, c, requests, slots, BOX_PATCHES)
     b.record(stream)
     b.synchronize()
     batch.close()
