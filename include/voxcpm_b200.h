@@ -176,6 +176,32 @@ VX_API vx_status vx_product_ex(int format, const uint16_t* x, const void* w,
                                size_t out, unsigned flags,
                                const vx_wmma_plan* plan, cudaStream_t stream);
 
+/* A product whose activations and output live in page-locked host memory
+ * (cudaHostAlloc, or cudaHostRegister'd: reachable from the device at the
+ * same address): x_host [rows][in] bf16, y_host [rows][out] of out_dtype.
+ * Three launches on `stream`: x_host is staged into x_dev (rows * in bf16 of
+ * device memory), the product writes y_dev (rows * out of out_dtype, device
+ * memory; read first when accumulating), and y_dev is staged into y_host.
+ * The staging launches move 16-byte pieces with SM loads and stores over
+ * PCIe, not the copy engines (faster for transfers of a few hundred KB; see
+ * vx_stage). y_host holds the result once the stream has reached this
+ * point. Flags: VX_PRODUCT_ACCUMULATE only (VX_PRODUCT_INDEPENDENT is
+ * VX_INVALID: the product reads what the first launch wrote). Replaces the
+ * upload, Linear and download a caller of the reference's products makes
+ * (tests/products_test.cpp:100-110 around kernels/wmma_products.hpp:87-99). */
+VX_API vx_status vx_product_host(int format, const uint16_t* x_host,
+                                 uint16_t* x_dev, const void* w, void* y_dev,
+                                 void* y_host, int out_dtype, size_t rows,
+                                 size_t in, size_t out, unsigned flags,
+                                 const vx_wmma_plan* plan, cudaStream_t stream);
+/* Copies `bytes` from `src` to `dst`, either of which may be page-locked
+ * host memory, with one launch of SM loads and stores (16-byte pieces where
+ * both addresses and the size are multiples of 16). Ordered on `stream`
+ * like a kernel. Replaces hipMemcpy (tests/products_test.cpp:100-110) for
+ * transfers where the copy engines' per-copy cost dominates. */
+VX_API vx_status vx_stage(void* dst, const void* src, size_t bytes,
+                          cudaStream_t stream);
+
 /* Programmatic dependent launch for every kernel of the library (default on).
  * No reference counterpart (HIP has none). */
 VX_API void vx_set_programmatic_launch(int enabled);

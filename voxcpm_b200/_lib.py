@@ -130,6 +130,12 @@ SIGNATURES: dict[str, tuple] = {
         [c_int, c_void_p, c_void_p, c_void_p, c_int, c_size_t, c_size_t, c_size_t,
          c_uint, POINTER(WmmaPlan), c_void_p],
     ),
+    "vx_product_host": (
+        c_int,
+        [c_int, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_int, c_size_t, c_size_t,
+         c_size_t, c_uint, POINTER(WmmaPlan), c_void_p],
+    ),
+    "vx_stage": (c_int, [c_void_p, c_void_p, c_size_t, c_void_p]),
     "vx_set_programmatic_launch": (None, [c_int]),
     "vx_set_tensor_core_products": (None, [c_int]),
     "vx_tensor_core_products": (c_int, []),

@@ -204,6 +204,41 @@ vx_status vx_product_ex(int format, const uint16_t* x, const void* w, void* y,
                  "vx_product_ex", (flags & VX_PRODUCT_INDEPENDENT) != 0);
 }
 
+vx_status vx_product_host(int format, const uint16_t* x_host, uint16_t* x_dev,
+                          const void* w, void* y_dev, void* y_host,
+                          int out_dtype, size_t rows, size_t in, size_t out,
+                          unsigned flags, const vx_wmma_plan* plan,
+                          cudaStream_t stream) {
+  if ((flags & ~VX_PRODUCT_ACCUMULATE) != 0)
+    return vx::Fail(vx::kInvalid,
+                    "vx_product_host: only VX_PRODUCT_ACCUMULATE applies");
+  if (x_host == nullptr || x_dev == nullptr || y_dev == nullptr ||
+      y_host == nullptr)
+    return vx::Fail(vx::kInvalid, "vx_product_host: null buffer");
+  if (out_dtype != VX_OUT_F32 && out_dtype != VX_OUT_BF16)
+    return vx::Fail(vx::kInvalid, "vx_product_host: unknown out_dtype");
+  if (rows == 0)
+    return VX_OK;
+  const size_t y_bytes = rows * out * (out_dtype == VX_OUT_F32 ? 4 : 2);
+  vx_status status = vx::Checked(
+      vx::StageBytes(x_dev, x_host, rows * in * sizeof(uint16_t), stream),
+      "vx_product_host");
+  if (status != VX_OK)
+    return status;
+  status = Product(format, x_dev, w, y_dev, out_dtype, rows, in, out,
+                   (flags & VX_PRODUCT_ACCUMULATE) != 0 ? 1 : 0, plan, stream,
+                   "vx_product_host");
+  if (status != VX_OK)
+    return status;
+  return vx::Checked(vx::StageBytes(y_host, y_dev, y_bytes, stream),
+                     "vx_product_host");
+}
+
+vx_status vx_stage(void* dst, const void* src, size_t bytes,
+                   cudaStream_t stream) {
+  return vx::Checked(vx::StageBytes(dst, src, bytes, stream), "vx_stage");
+}
+
 void vx_set_programmatic_launch(int enabled) {
   vx::SetProgrammaticLaunch(enabled != 0);
 }

@@ -136,5 +136,10 @@ int Bf16TilesToRows(const std::uint16_t* tiles, std::size_t rows,
                     std::size_t in, std::uint16_t* out, cudaStream_t stream);
 int ReadProbe(const void* data, std::size_t pieces, unsigned blocks,
               unsigned* sink, cudaStream_t stream);
+// Copies `bytes` from `src` to `dst` with SM loads and stores (staging.cu):
+// either side may be page-locked host memory. 16- or 4-byte pieces where
+// both addresses and the size allow, else bytes.
+int StageBytes(void* dst, const void* src, std::size_t bytes,
+               cudaStream_t stream);
 
 }  // namespace vx

@@ -31,6 +31,22 @@ def _ptr(t: torch.Tensor | None) -> int | None:
     return t.data_ptr()
 
 
+def _any_ptr(t: torch.Tensor) -> int:
+    """A device tensor, or a page-locked host tensor (reachable from the
+    device at the same address)."""
+    if not t.is_contiguous():
+        raise ValueError("contiguous tensor expected")
+    if not t.is_cuda and not t.is_pinned():
+        raise ValueError("device or page-locked host tensor expected")
+    return t.data_ptr()
+
+
+def _host_ptr(t: torch.Tensor) -> int:
+    if t.is_cuda or not t.is_pinned():
+        raise ValueError("page-locked host tensor expected")
+    return _any_ptr(t)
+
+
 def _stream(stream=None) -> int:
     if stream is None:
         return torch.cuda.current_stream().cuda_stream
@@ -158,6 +174,34 @@ def ProductEx(fmt: int, x, w, y, rows, columns, out, flags: int = 0, plan=None, 
                              int(flags), _plan_arg(plan), _stream(stream)),
         unsupported_ok=True,
     )
+
+
+def ProductHost(fmt: int, x_host, x_dev, w, y_dev, y_host, rows, columns, out, flags: int = 0,
+                plan=None, stream=None) -> bool:
+    """vx_product_host: x_host and y_host page-locked host tensors, x_dev and
+    y_dev device tensors of the same shapes (staging and product output)."""
+    if y_dev.dtype != y_host.dtype:
+        raise ValueError("y_dev and y_host must have one dtype")
+    if y_dev.dtype == torch.float32:
+        out_dtype = _lib.OUT_F32
+    elif y_dev.dtype == torch.bfloat16:
+        out_dtype = _lib.OUT_BF16
+    else:
+        raise ValueError("y must be float32 or bfloat16")
+    return check(
+        load().vx_product_host(fmt, _host_ptr(x_host), _ptr(x_dev), _ptr(w), _ptr(y_dev), _host_ptr(y_host),
+                               out_dtype, rows, columns, out, int(flags), _plan_arg(plan),
+                               _stream(stream)),
+        unsupported_ok=True,
+    )
+
+
+def Stage(dst, src, nbytes: int, stream=None) -> None:
+    """vx_stage: copy `nbytes` between device or page-locked host tensors with
+    SM loads and stores, ordered on the stream."""
+    if nbytes > min(dst.numel() * dst.element_size(), src.numel() * src.element_size()):
+        raise ValueError("nbytes exceeds a tensor")
+    check(load().vx_stage(_any_ptr(dst), _any_ptr(src), nbytes, _stream(stream)))
 
 
 def SetProgrammaticLaunch(enabled: bool) -> None:
