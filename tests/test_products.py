@@ -260,6 +260,39 @@ def test_independent_launch_stream_plan(cuda):
     assert K.DeviceError() == 0
 
 
+@pytest.mark.parametrize("rows,splits", [(1, 1), (5, 1), (22, 1), (22, 4), (32, 2)])
+def test_half_tile_math_bit_equal(cuda, rows, splits):
+    """Variant 14 (fp16 tile math over activations scaled by a power of two
+    per row) gives variant 13's bf16 sums bit for bit, at row scales from
+    1e-30 to 1e30 and with a zero row; and the oracle's sums within the
+    limit. (Rows whose fp32 sums overflow may differ: an overflow inside
+    one bf16 MMA can give NaN where the scaled sum overflows only when
+    unscaled, to inf.)"""
+    rng = np.random.default_rng(59 + rows)
+    columns, out = 2048, 6144
+    blocks, q8_tiles, _, _ = prepare(out, columns, rng)
+    base = rng.normal(0.0, 1.0, size=(rows, columns)).astype(np.float32)
+    scales = np.array([1.0, 3e4, 1e-30, 0.0, 1e-3, 1e-20, 1.0, 1e30] * 4)[:rows]
+    x = (base * scales[:, None]).astype(np.float32)
+    x_bits = oracle.bf16_bits(x)
+    x_dev = to_dev(x_bits)
+    ys = {}
+    for variant in (13, 14):
+        # Split slices scale their own activations and unscale before the
+        # cluster adds them up.
+        plan = _lib.WmmaPlan(splits, columns // 32 // splits, 0, 0, variant)
+        y = torch.empty(rows, out, dtype=torch.float32, device="cuda")
+        assert K.ProductEx(_lib.WEIGHTS_Q8_TILES, x_dev, q8_tiles, y, rows, columns, out, 0,
+                           plan=plan)
+        ys[variant] = y
+    torch.cuda.synchronize()
+    assert torch.equal(ys[13], ys[14])
+    exact, mag = oracle.product_exact(x_bits, oracle.Q8_0, blocks, rows, columns, out)
+    err = np.abs(ys[14].cpu().numpy() - exact) / np.maximum(mag, 1e-300)
+    assert float(err.max()) <= LIMIT
+    assert K.DeviceError() == 0
+
+
 @pytest.mark.parametrize("columns,out", [(1024, 2560), (2048, 1024), (6144, 512)])
 def test_wide_rows(cuda, columns, out):
     """33..128 activation rows in one launch (8 or 16 B tiles per warp) on

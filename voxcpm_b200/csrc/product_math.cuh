@@ -25,6 +25,32 @@ __device__ inline void Mma16816(float (&d)[4], std::uint32_t a0,
         "f"(c[1]), "f"(c[2]), "f"(c[3]));
 }
 
+/// The same MMA on fp16 operands (both A and B fp16).
+__device__ inline void Mma16816Half(float (&d)[4], std::uint32_t a0,
+                                    std::uint32_t a1, std::uint32_t a2,
+                                    std::uint32_t a3, std::uint32_t b0,
+                                    std::uint32_t b1, const float (&c)[4]) {
+  asm(
+      "mma.sync.aligned.m16n8k16.row.col.f32.f16.f16.f32 {%0,%1,%2,%3}, "
+      "{%4,%5,%6,%7}, {%8,%9}, {%10,%11,%12,%13};"
+      : "=f"(d[0]), "=f"(d[1]), "=f"(d[2]), "=f"(d[3])
+      : "r"(a0), "r"(a1), "r"(a2), "r"(a3), "r"(b0), "r"(b1), "f"(c[0]),
+        "f"(c[1]), "f"(c[2]), "f"(c[3]));
+}
+
+/// Four biased int8 values (q + 128) -> two fp16 pairs (bytes 0,1 and 2,3),
+/// exactly: 0x64uu is 1024 + u as an fp16 (ten mantissa bits hold u), and
+/// one packed subtraction of 1152 leaves q. Two instructions per pair,
+/// against four for the bf16 route below.
+__device__ inline void DequantWordHalf(std::uint32_t w, std::uint32_t& pair01,
+                                       std::uint32_t& pair23) {
+  const std::uint32_t bias = 0x64806480u;  // fp16 1152 in both halves
+  const std::uint32_t a = Prmt(w, 0x64646464u, 0x5140u);
+  const std::uint32_t b = Prmt(w, 0x64646464u, 0x5342u);
+  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(pair01) : "r"(a), "r"(bias));
+  asm("sub.rn.f16x2 %0, %1, %2;" : "=r"(pair23) : "r"(b), "r"(bias));
+}
+
 /// Four biased int8 values (q + 128) -> two bf16 pairs (bytes 0,1 and 2,3),
 /// exactly: 0x4B0000uu is 2^23 + u as a float; subtracting 2^23 + 128
 /// leaves q, whose float has at most 8 significant bits, so its upper half
@@ -44,7 +70,9 @@ __device__ inline void DequantWord(std::uint32_t w, std::uint32_t& pair01,
 
 /// One 32-column block of one 16-row group: the block's partial sums for
 /// every activation tile, added into `acc` (Q8: scaled; bf16: directly).
-template <int kFormat, int kNTiles, int kRowStride>
+/// kHalf (Q8 only): the activation fragments `b` hold fp16 and the weights
+/// are dequantized to fp16 (the products and fp32 sums are the same).
+template <int kFormat, int kNTiles, int kRowStride, bool kHalf = false>
 __device__ __forceinline__ void BlockProduct(const unsigned char* base, int kb,
                                              int gid, int tig,
                                              const uint4 (&b)[kNTiles],
@@ -62,16 +90,28 @@ __device__ __forceinline__ void BlockProduct(const unsigned char* base, int kb,
         HalfBitsToFloat(static_cast<std::uint16_t>(sc & 0xFFFFu));
     const float s_hi = HalfBitsToFloat(static_cast<std::uint16_t>(sc >> 16));
     std::uint32_t a00, a02, a01, a03, a10, a12, a11, a13;
-    DequantWord(lo.x, a00, a02);
-    DequantWord(hi.x, a01, a03);
-    DequantWord(lo.y, a10, a12);
-    DequantWord(hi.y, a11, a13);
+    if constexpr (kHalf) {
+      DequantWordHalf(lo.x, a00, a02);
+      DequantWordHalf(hi.x, a01, a03);
+      DequantWordHalf(lo.y, a10, a12);
+      DequantWordHalf(hi.y, a11, a13);
+    } else {
+      DequantWord(lo.x, a00, a02);
+      DequantWord(hi.x, a01, a03);
+      DequantWord(lo.y, a10, a12);
+      DequantWord(hi.y, a11, a13);
+    }
     const float zero[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll
     for (int j = 0; j < kNTiles; ++j) {
       float part[4];
-      Mma16816(part, a00, a01, a02, a03, b[j].x, b[j].y, zero);
-      Mma16816(part, a10, a11, a12, a13, b[j].z, b[j].w, part);
+      if constexpr (kHalf) {
+        Mma16816Half(part, a00, a01, a02, a03, b[j].x, b[j].y, zero);
+        Mma16816Half(part, a10, a11, a12, a13, b[j].z, b[j].w, part);
+      } else {
+        Mma16816(part, a00, a01, a02, a03, b[j].x, b[j].y, zero);
+        Mma16816(part, a10, a11, a12, a13, b[j].z, b[j].w, part);
+      }
       const float2 lo2 =
           Fma2(make_float2(s_lo, s_lo), make_float2(part[0], part[1]),
                make_float2(acc[j][0], acc[j][1]));

@@ -75,6 +75,7 @@ struct VariantShape {
   int groups;      // 16-row groups per warp
   int stage;       // 32-column blocks per pipeline stage
   int depth;       // stages in flight per warp
+  bool half;       // Q8_0: fp16 tile math over exactly scaled activations
 };
 
 __host__ __device__ constexpr int WarpsOf(const VariantShape& v) {
@@ -101,6 +102,9 @@ constexpr VariantShape kVariants[] = {
     // A whole-reduction CTA without a cluster (streams of independent
     // launches: 16 CTAs per config-0 launch, several launches side by side).
     {24, 1, 1, 8, 1},  // 13: 384 rows, 24 warps, one 8-block stage per warp
+    // Variant 13 with the fp16 tile math (Q8_0; other formats run as 13):
+    // half the dequantization instructions per tile.
+    {24, 1, 1, 8, 1, true},  // 14
 };
 constexpr int kNumVariants = sizeof(kVariants) / sizeof(kVariants[0]);
 // The cost model chooses among the first eight shapes only: their plans fit
@@ -153,7 +157,7 @@ struct ProductArgs {
 
 /// All blocks of one landed stage. A full stage is unrolled without guards
 /// so the compiler can interleave the blocks' loads, conversions and MMAs.
-template <int kFormat, int kGroups, int kNTiles, int kStage>
+template <int kFormat, int kGroups, int kNTiles, int kStage, bool kHalf>
 __device__ __forceinline__ void StageProduct(
     const unsigned char* stage_base, int group_bytes, const unsigned char* xs,
     int x_stride, int column0, int nb, int my_groups, int gid, int tig,
@@ -169,8 +173,8 @@ __device__ __forceinline__ void StageProduct(
 #pragma unroll
     for (int g = 0; g < kGroups; ++g)
       if (g < my_groups)
-        BlockProduct<kFormat, kNTiles, kRowStride>(stage_base + g * group_bytes,
-                                                   kb, gid, tig, b, acc[g]);
+        BlockProduct<kFormat, kNTiles, kRowStride, kHalf>(
+            stage_base + g * group_bytes, kb, gid, tig, b, acc[g]);
   };
   if (nb == kStage) {
 #pragma unroll
@@ -185,8 +189,47 @@ __device__ __forceinline__ void StageProduct(
 
 // ------------------------------------------------------------ the kernel
 
+/// Rewrites one activation row in shared memory (bf16, `pieces` 16-byte
+/// pieces) as fp16 times a power of two that puts its largest magnitude in
+/// [2^15, 2^16): every bf16 value within 2^31 of the row's largest is then
+/// exact in fp16, so the fp16 tile math forms the same products and sums as
+/// the bf16 one, scaled by that power. Returns 2^-shift, the factor that
+/// undoes it. One warp per row.
+__device__ inline float ScaleRowToHalf(unsigned char* row, int pieces,
+                                       int lane) {
+  std::uint32_t largest = 0;  // largest |x| bits, per 16-bit half
+  for (int i = lane; i < pieces; i += 32) {
+    const uint4 v = *reinterpret_cast<const uint4*>(row + 16 * i);
+    largest = __vmaxu2(largest, v.x & 0x7FFF7FFFu);
+    largest = __vmaxu2(largest, v.y & 0x7FFF7FFFu);
+    largest = __vmaxu2(largest, v.z & 0x7FFF7FFFu);
+    largest = __vmaxu2(largest, v.w & 0x7FFF7FFFu);
+  }
+  largest = __reduce_max_sync(0xFFFFFFFFu,
+                              max(largest & 0xFFFFu, largest >> 16));
+  // Biased exponent of the largest magnitude (inf / NaN as the largest
+  // finite); the shift stays within the normal fp32 range both ways.
+  const int exponent = min(static_cast<int>(largest >> 7), 254);
+  const int shift = min(142 - exponent, 126);
+  const float factor = __int_as_float((shift + 127) << 23);
+  for (int i = lane; i < pieces; i += 32) {
+    uint4 v = *reinterpret_cast<const uint4*>(row + 16 * i);
+    std::uint32_t* words = reinterpret_cast<std::uint32_t*>(&v);
+#pragma unroll
+    for (int h = 0; h < 4; ++h) {
+      const float lo = __uint_as_float(words[h] << 16) * factor;
+      const float hi = __uint_as_float(words[h] & 0xFFFF0000u) * factor;
+      std::uint32_t packed;
+      asm("cvt.rn.f16x2.f32 %0, %1, %2;" : "=r"(packed) : "f"(hi), "f"(lo));
+      words[h] = packed;
+    }
+    *reinterpret_cast<uint4*>(row + 16 * i) = v;
+  }
+  return __int_as_float((127 - shift) << 23);
+}
+
 template <int kFormat, int kCtaGroups, int kWays, int kGroups, int kNTiles,
-          int kStage, int kDepth>
+          int kStage, int kDepth, bool kHalf>
 __global__ void __launch_bounds__(kCtaGroups / kGroups * kWays * 32)
     ProductKernel(const ProductArgs p) {
   constexpr int kWarps = kCtaGroups / kGroups * kWays;
@@ -196,8 +239,11 @@ __global__ void __launch_bounds__(kCtaGroups / kGroups * kWays * 32)
   constexpr bool kRows = kFormat == static_cast<int>(WeightFormat::kBf16);
   constexpr int kTileBytes = kQ8 ? kQ8TileBytes : kBf16TileBytes;
   constexpr int kRowStride = RowStrideBytes(kStage);
+  constexpr bool kHalfMath = kHalf && kQ8;
 
   extern __shared__ __align__(128) unsigned char smem[];
+  // Per activation row: the factor undoing its fp16 scaling (kHalfMath).
+  __shared__ float row_unscale[kHalfMath ? kNTiles * 8 : 1];
   const int lane = threadIdx.x & 31;
   const int warp = threadIdx.x >> 5;
   const int gid = lane >> 2;
@@ -226,6 +272,10 @@ __global__ void __launch_bounds__(kCtaGroups / kGroups * kWays * 32)
     for (int i = 0; i < kWarps * kDepth + 1; ++i)
       MbarInit(&bars[i], 1);
     FenceMbarInit();
+  }
+  if constexpr (kHalfMath) {
+    for (int i = threadIdx.x; i < kNTiles * 8; i += blockDim.x)
+      row_unscale[i] = 1.0f;
   }
   // Activation rows past `m` read as zeros.
   {
@@ -313,6 +363,23 @@ __global__ void __launch_bounds__(kCtaGroups / kGroups * kWays * 32)
 
   bool failed = false;
   int waited = 0;
+  if constexpr (kHalfMath) {
+    // Every warp waits for the activations; each converts rows warp,
+    // warp + kWarps, ...; the CTA then reads them as fp16 fragments.
+    if (nblocks > 0) {
+      if (!MbarWaitBounded(xbar, 0, &g_vx_device_error, kErrActivationWait)) {
+        failed = true;
+      } else {
+        for (int row = warp; row < p.m; row += kWarps) {
+          const float unscale =
+              ScaleRowToHalf(xs + row * p.x_stride, nblocks * 4, lane);
+          if (lane == 0)
+            row_unscale[row] = unscale;
+        }
+      }
+    }
+    __syncthreads();
+  }
   if (active) {
     if (!MbarWaitBounded(xbar, 0, &g_vx_device_error, kErrActivationWait))
       failed = true;
@@ -326,7 +393,7 @@ __global__ void __launch_bounds__(kCtaGroups / kGroups * kWays * 32)
       ++waited;
       const int st = way + i * kWays;
       const int nb = min(kStage, last - (first + st * kStage));
-      StageProduct<kFormat, kGroups, kNTiles, kStage>(
+      StageProduct<kFormat, kGroups, kNTiles, kStage, kHalfMath>(
           ring + slot * kGroups * kGroupBytes, kGroupBytes, xs, p.x_stride,
           st * kStage * 32, nb, my_groups, gid, tig, acc);
       // The slot's values are in registers (consumed above); refill it.
@@ -346,6 +413,15 @@ __global__ void __launch_bounds__(kCtaGroups / kGroups * kWays * 32)
     }
   }
   (void)kRowStride;
+  if constexpr (kHalfMath) {
+#pragma unroll
+    for (int g = 0; g < kGroups; ++g)
+#pragma unroll
+      for (int j = 0; j < kNTiles; ++j)
+#pragma unroll
+        for (int c = 0; c < 4; ++c)
+          acc[g][j][c] *= row_unscale[8 * j + 2 * tig + (c & 1)];
+  }
 
   // Ways of a group add up in way order through shared memory.
   float4* red = reinterpret_cast<float4*>(rings);
@@ -460,7 +536,7 @@ constexpr KernelFn KernelFor() {
     return ProductKernel<kFormat, kVariants[kVariant].cta_groups,
                          kVariants[kVariant].ways, kVariants[kVariant].groups,
                          kNTiles, kVariants[kVariant].stage,
-                         kVariants[kVariant].depth>;
+                         kVariants[kVariant].depth, kVariants[kVariant].half>;
   }
 }
 
@@ -471,7 +547,7 @@ struct VariantRow {
 
 template <int kFormat, int kNTiles>
 using Row = VariantRow<kFormat, kNTiles, 0, 1, 2, 3, 4, 5, 6, 7, 8, 9, 10, 11,
-                       12, 13>;
+                       12, 13, 14>;
 
 /// Row classes of the measured plan tables: 1, 2..8, 9..32, 33..128.
 int RowsClass(std::size_t rows) {
@@ -599,10 +675,11 @@ constexpr MeasuredPlan kMeasuredPlans[] = {
 
 // Measured plans for streams of independent launches (PRODUCT_INDEPENDENT
 // with no plan): a launch overlaps the ones before it, so fewer, larger
-// CTAs without clusters win (config 0: 3.2 us per product against 4.4 us
-// for the best clustered plan).
+// CTAs without clusters win (config 0: 3.13 us per product with variant 13
+// against 4.4 us for the best clustered plan; 2.94 us with variant 14's
+// fp16 tile math, bit-equal to 13).
 constexpr MeasuredPlan kStreamPlans[] = {
-    {WeightFormat::kQ8Tiles, 2, 2048, 6144, 13, 1},
+    {WeightFormat::kQ8Tiles, 2, 2048, 6144, 14, 1},
 };
 
 ProductPlan StreamPlan(WeightFormat format, std::size_t rows, std::size_t in,
