@@ -188,16 +188,19 @@ __device__ bool WaitCount(const Control& c, const unsigned* counter,
   bool aborted = false;
   if (threadIdx.x == 0) {
     if (*c.aborted == 0 && LoadAcquire(counter) < target) {
+      // Acquire polls; the abort flag and the time limit every 32 polls.
       const std::uint64_t start = GlobalTimerNs();
       unsigned spins = 0;
       while (LoadAcquire(counter) < target) {
-        if (LoadRelaxed(c.sync + kSyncAbort) != 0) {
-          *c.aborted = 1;
-          break;
-        }
-        if ((++spins & 63u) == 0 && GlobalTimerNs() - start > kWaitLimitNs) {
-          Abort(c, kErrBarrierWait);
-          break;
+        if ((++spins & 31u) == 0) {
+          if (LoadRelaxed(c.sync + kSyncAbort) != 0) {
+            *c.aborted = 1;
+            break;
+          }
+          if (GlobalTimerNs() - start > kWaitLimitNs) {
+            Abort(c, kErrBarrierWait);
+            break;
+          }
         }
       }
     }
