@@ -293,7 +293,7 @@ def test_half_tile_math_bit_equal(cuda, rows, splits):
     assert K.DeviceError() == 0
 
 
-@pytest.mark.parametrize("columns,out", [(1024, 2560), (2048, 1024), (6144, 512)])
+@pytest.mark.parametrize("columns,out", [(1024, 2560), (2048, 1024), (4096, 1024), (6144, 512)])
 def test_wide_rows(cuda, columns, out):
     """33..128 activation rows in one launch (8 or 16 B tiles per warp) on
     every weight format, plain and accumulating, fp32 and bf16 output; for a

@@ -105,6 +105,7 @@ constexpr VariantShape kVariants[] = {
     // Variant 13 with the fp16 tile math (Q8_0; other formats run as 13):
     // half the dequantization instructions per tile.
     {24, 1, 1, 8, 1, true},  // 14
+    {4, 2, 1, 4, 2},   // 15: 64 rows, 8 warps (2 ways), for 33..128 rows
 };
 constexpr int kNumVariants = sizeof(kVariants) / sizeof(kVariants[0]);
 // The cost model chooses among the first eight shapes only: their plans fit
@@ -525,7 +526,7 @@ using KernelFn = void (*)(const ProductArgs);
 // Variants that take 33..128 activation rows (8 or 16 B tiles per warp):
 // the small CTAs, whose registers and activation slices stay in bounds.
 __host__ __device__ constexpr bool WideVariant(int variant) {
-  return variant == 0 || variant == 1 || variant == 3;
+  return variant == 0 || variant == 1 || variant == 3 || variant == 15;
 }
 
 template <int kFormat, int kNTiles, int kVariant>
@@ -547,7 +548,7 @@ struct VariantRow {
 
 template <int kFormat, int kNTiles>
 using Row = VariantRow<kFormat, kNTiles, 0, 1, 2, 3, 4, 5, 6, 7, 8, 9, 10, 11,
-                       12, 13, 14>;
+                       12, 13, 14, 15>;
 
 /// Row classes of the measured plan tables: 1, 2..8, 9..32, 33..128.
 int RowsClass(std::size_t rows) {
@@ -631,7 +632,7 @@ void ProductVariantShape(int variant, int* warps, int* groups, int* stage,
 // Measured plans (B200, products launched back to back, each waiting for
 // the previous one, weights larger than L2) for the shapes of VoxCPM2's
 // generator and of the benchmark; other shapes use the cost model below.
-// Rows classes: 1, 2..8, 9..32.
+// Rows classes: 1, 2..8, 9..32, 33..128.
 struct MeasuredPlan {
   WeightFormat format;
   int rows_class;
@@ -666,6 +667,15 @@ constexpr MeasuredPlan kMeasuredPlans[] = {
     {WeightFormat::kQ8Tiles, 2, 2048, 1024, 3, 7},
     {WeightFormat::kQ8Tiles, 2, 1024, 8192, 7, 2},
     {WeightFormat::kQ8Tiles, 2, 4096, 1024, 3, 8},
+    // Q8_0 tiles, 33..128 rows (the DiT's rows of batched slots): variant
+    // 15, two ways of four warps over 64-row panels. Dependent chains, us
+    // at 48 / 128 rows against the plans before: 1024 -> 2560 7.7 / 13.5
+    // (9.2 / 14.4), 2048 -> 1024 10.1 / 14.7 (11.0 / 18.5), 4096 -> 1024
+    // 10.3 at 48 rows (11.9); at 65..128 rows its slices do not fit and the
+    // long-reduction plan runs.
+    {WeightFormat::kQ8Tiles, 3, 1024, 2560, 15, 2},
+    {WeightFormat::kQ8Tiles, 3, 2048, 1024, 15, 4},
+    {WeightFormat::kQ8Tiles, 3, 4096, 1024, 15, 6},
     // bf16 tiles and rows.
     {WeightFormat::kBf16Tiles, 2, 2048, 6144, 0, 2},
     {WeightFormat::kBf16, 2, 2048, 6144, 1, 4},
@@ -728,10 +738,13 @@ ProductPlan PlanProduct(WeightFormat format, std::size_t rows, std::size_t in,
         continue;
       const int bps = (k_blocks + m.splits - 1) / m.splits;
       const int ntiles = TilesFor(rows);
+      // Plans measured at 33..128 rows were measured up to the launch limit.
+      const std::size_t limit =
+          rows_class == 3 ? kMaxProductSmem : kPlannedProductSmem;
       if ((k_blocks + bps - 1) / bps != m.splits ||
           bps * kTileColumns > kMaxSliceColumns ||
           FootprintOf(static_cast<int>(format), m.variant, ntiles, bps).smem >
-              kPlannedProductSmem)
+              limit)
         break;  // not a valid plan for these rows: use the cost model
       best.variant = m.variant;
       best.splits = m.splits;
