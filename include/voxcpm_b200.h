@@ -624,6 +624,37 @@ VX_API vx_status vx_gemm_linear(vx_gemm* gemm, const uint16_t* x, int format,
                          const void* w, float* y, size_t rows, size_t in,
                          size_t out, int accumulate);
 
+/* A column-major (BLAS) product C[m][n] (+)= op(A)[m][k] * op(B)[k][n],
+ * optionally strided-batched (strides in elements, batch b at a + b *
+ * stride_a, ...). Replaces MatmulShape (gemm.hpp:16-38). */
+typedef struct vx_matmul_shape {
+  int transpose_a;
+  int transpose_b;
+  size_t m, n, k;
+  size_t lda, ldb, ldc;
+  int64_t stride_a, stride_b, stride_c;
+  size_t batch;
+  int accumulate;
+} vx_matmul_shape;
+/* bf16 A and B, float32 C and sums. `representative` (the shape a tuned
+ * algorithm is shared with) may be null: one kernel serves every shape.
+ * VX_INVALID for leading dimensions below the stored column heights, sizes
+ * above 2^30 or more than 65535 batches; nothing is launched for m, n or
+ * batch 0. Replaces Bf16Gemm::Matmul (gemm.hpp:62-63, gemm.cpp:338-361). */
+VX_API vx_status vx_matmul(const vx_matmul_shape* shape,
+                           const vx_matmul_shape* representative,
+                           const uint16_t* a, const uint16_t* b, float* c,
+                           cudaStream_t stream);
+/* vx_matmul on the gemm's stream. */
+VX_API vx_status vx_gemm_matmul(vx_gemm* gemm, const vx_matmul_shape* shape,
+                                const vx_matmul_shape* representative,
+                                const uint16_t* a, const uint16_t* b, float* c);
+/* Rounds up to a multiple of 128, the bucket size of shared shapes.
+ * Replaces TuningBucket (gemm.hpp:74-77). */
+static inline size_t vx_tuning_bucket(size_t size) {
+  return (size + 127) / 128 * 128;
+}
+
 #ifdef __cplusplus
 }
 #endif

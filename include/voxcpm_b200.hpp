@@ -245,6 +245,35 @@ inline void GuidedEuler(const float* velocity, float* x, std::size_t count,
 
 }  // namespace kernels
 
+/// gemm.hpp:16-38: a column-major (BLAS) product C[m][n] (+)= op(A)[m][k] *
+/// op(B)[k][n], optionally strided-batched.
+struct MatmulShape {
+  bool transpose_a = false;
+  bool transpose_b = false;
+  std::size_t m = 0;
+  std::size_t n = 0;
+  std::size_t k = 0;
+  std::size_t lda = 0;
+  std::size_t ldb = 0;
+  std::size_t ldc = 0;
+  std::int64_t stride_a = 0;
+  std::int64_t stride_b = 0;
+  std::int64_t stride_c = 0;
+  std::size_t batch = 1;
+  bool accumulate = false;
+
+  [[nodiscard]] vx_matmul_shape ToC() const {
+    return vx_matmul_shape{transpose_a ? 1 : 0, transpose_b ? 1 : 0, m, n, k,
+                           lda, ldb, ldc, stride_a, stride_b, stride_c, batch,
+                           accumulate ? 1 : 0};
+  }
+};
+
+/// gemm.hpp:74-77
+[[nodiscard]] constexpr std::size_t TuningBucket(std::size_t size) {
+  return (size + 127) / 128 * 128;
+}
+
 /// gemm.hpp:49-72. The reference's constructor also takes a hipBLAS handle
 /// for its library fallback; these products need none.
 class Bf16Gemm {
@@ -263,6 +292,17 @@ class Bf16Gemm {
                          static_cast<int>(w.format), w.data, y, rows, in, out,
                          accumulate ? 1 : 0),
           "Bf16Gemm::Linear");
+  }
+
+  /// gemm.hpp:60-63: bf16 a and b, float32 c. One kernel serves every
+  /// shape, so `representative` is not used for tuning.
+  void Matmul(const MatmulShape& shape, const MatmulShape& representative,
+              const void* a, const void* b, float* c) {
+    const vx_matmul_shape s = shape.ToC();
+    const vx_matmul_shape r = representative.ToC();
+    Check(vx_gemm_matmul(gemm_, &s, &r, static_cast<const std::uint16_t*>(a),
+                         static_cast<const std::uint16_t*>(b), c),
+          "Bf16Gemm::Matmul");
   }
 
  private:

@@ -171,6 +171,39 @@ def linear(x: np.ndarray, fmt: int, w: np.ndarray, rows: int, columns: int, out:
     return y
 
 
+def matmul_exact(a: np.ndarray, b: np.ndarray, c: np.ndarray | None, transpose_a: bool, transpose_b: bool,
+                 m: int, n: int, k: int, lda: int, ldb: int, ldc: int, stride_a: int = 0, stride_b: int = 0,
+                 stride_c: int = 0, batch: int = 1):
+    """(exact, magnitude) in double of the column-major BLAS product
+    C[m][n] (+)= op(A)[m][k] op(B)[k][n] per batch (gemm.hpp:16-38;
+    gemm.cpp:338-361 runs it with alpha 1 and beta = accumulate). `a`, `b`
+    are bf16 bits, `c` the float32 C before the call (None: beta 0). Both
+    results are flat arrays laid out as C: element (i, j) of batch t at
+    t * stride_c + i + j * ldc; entries outside the product are NaN."""
+    av, bv = bf16_value(a).astype(np.float64), bf16_value(b).astype(np.float64)
+    size = (batch - 1) * stride_c + (n - 1) * ldc + m if m and n and batch else 0
+    exact = np.full(max(size, 0 if c is None else c.size), np.nan)
+    magnitude = np.full_like(exact, np.nan)
+    i = np.arange(m)[:, None]
+    ll = np.arange(k)[None, :]
+    for t in range(batch):
+        ia = t * stride_a + (ll + i * lda if transpose_a else i + ll * lda)  # op(A)[i][l]
+        j = np.arange(n)[None, :]
+        lb = np.arange(k)[:, None]
+        ib = t * stride_b + (j + lb * ldb if transpose_b else lb + j * ldb)  # op(B)[l][j]
+        opa, opb = av[ia], bv[ib]
+        prod = opa @ opb
+        mag = np.abs(opa) @ np.abs(opb)
+        ic = t * stride_c + np.arange(m)[:, None] + np.arange(n)[None, :] * ldc
+        if c is not None:
+            before = c.astype(np.float64)[ic]
+            prod = prod + before
+            mag = mag + np.abs(before)
+        exact[ic] = prod
+        magnitude[ic] = mag
+    return exact, magnitude
+
+
 def relative_error(y: np.ndarray, exact: np.ndarray, magnitude: np.ndarray) -> float:
     """max |y - exact| / sum |x w| (tests/products_test.cpp:115-145)."""
     return float(np.max(np.abs(y.astype(np.float64) - exact) / np.maximum(magnitude, 1e-30)))

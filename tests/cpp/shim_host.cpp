@@ -36,6 +36,23 @@ int main(int argc, char** argv) {
               vb::kernels::Bf16TilesBytes(72, 1024));
   const std::vector<float> table = vb::RopeTable(10000.0, 128, std::vector<double>(64, 1.0), 1.0, 4);
   std::printf("rope %.9g %.9g\n", table[128 + 1], table[3 * 128 + 64 + 5]);
+  std::printf("bucket %zu %zu\n", vb::TuningBucket(129), vb::TuningBucket(128));
+  {
+    // Bf16Gemm::Matmul rejects a leading dimension below m before launching.
+    vb::Bf16Gemm gemm(nullptr);
+    vb::MatmulShape shape;
+    shape.m = 64;
+    shape.n = 8;
+    shape.k = 32;
+    shape.lda = 63;
+    shape.ldb = 32;
+    shape.ldc = 64;
+    try {
+      gemm.Matmul(shape, shape, nullptr, nullptr, nullptr);
+    } catch (const vb::GpuError& e) {
+      std::printf("matmul rejects ok\n");
+    }
+  }
   try {
     vb::Check(VX_INVALID, "forced");
   } catch (const vb::GpuError& e) {

@@ -33,6 +33,7 @@ def test_cpp_shim_compiles_links_and_runs(tmp_path):
     rope = next(line for line in out if line.startswith("rope")).split()
     assert np.float32(float(rope[1])) == table[1, 1] and np.float32(float(rope[2])) == table[3, 64 + 5]
     assert "error ok" in out
+    assert "bucket 256 128" in out and "matmul rejects ok" in out
 
 
 def test_cpp_shim_model_files(tmp_path):

@@ -46,6 +46,32 @@ class WmmaPlan(ctypes.Structure):
     ]
 
 
+class MatmulShape(ctypes.Structure):
+    """vx_matmul_shape (replaces MatmulShape, gemm.hpp:16-38): column-major
+    C[m][n] (+)= op(A)[m][k] * op(B)[k][n], strides in elements."""
+
+    _fields_ = [
+        ("transpose_a", c_int),
+        ("transpose_b", c_int),
+        ("m", c_size_t),
+        ("n", c_size_t),
+        ("k", c_size_t),
+        ("lda", c_size_t),
+        ("ldb", c_size_t),
+        ("ldc", c_size_t),
+        ("stride_a", ctypes.c_int64),
+        ("stride_b", ctypes.c_int64),
+        ("stride_c", ctypes.c_int64),
+        ("batch", c_size_t),
+        ("accumulate", c_int),
+    ]
+
+
+def TuningBucket(size: int) -> int:
+    """Rounds up to a multiple of 128 (gemm.hpp:74-77)."""
+    return (size + 127) // 128 * 128
+
+
 class SplitScratch(ctypes.Structure):
     """vx_split_scratch (kernels/wmma_products.hpp:62-68)."""
 
@@ -222,6 +248,8 @@ SIGNATURES: dict[str, tuple] = {
         c_int,
         [c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_size_t, c_size_t, c_size_t, c_int],
     ),
+    "vx_matmul": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
+    "vx_gemm_matmul": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
 }
 
 _lib: ctypes.CDLL | None = None

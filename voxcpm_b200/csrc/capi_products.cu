@@ -301,4 +301,12 @@ vx_status vx_gemm_linear(vx_gemm* gemm, const uint16_t* x, int format,
   return VX_OK;
 }
 
+vx_status vx_gemm_matmul(vx_gemm* gemm, const vx_matmul_shape* shape,
+                         const vx_matmul_shape* representative,
+                         const uint16_t* a, const uint16_t* b, float* c) {
+  if (gemm == nullptr)
+    return vx::Fail(vx::kInvalid, "vx_gemm_matmul: null gemm");
+  return vx_matmul(shape, representative, a, b, c, gemm->stream);
+}
+
 }  // extern "C"

@@ -3,9 +3,11 @@ over the C ABI (vx_gemm_*)."""
 
 from __future__ import annotations
 
+import ctypes
+
 import torch
 
-from ._lib import check, load
+from ._lib import MatmulShape, TuningBucket, check, load  # noqa: F401 (re-exported)
 from .kernels import _ptr, _stream
 
 
@@ -31,6 +33,14 @@ class Bf16Gemm:
         """y[rows][out] (+)= x[rows][columns] * w^T (gemm.hpp:51-58)."""
         check(self._lib.vx_gemm_linear(self._handle, _ptr(x), w.format, _ptr(w.data), _ptr(y),
                                        rows, columns, out, int(accumulate)))
+
+    def Matmul(self, shape, representative, a: torch.Tensor, b: torch.Tensor, c: torch.Tensor) -> None:
+        """Column-major C (+)= op(A) op(B) of bf16 a and b into float32 c
+        (gemm.hpp:60-63). `shape` and `representative` are MatmulShape; the
+        representative may be None (one kernel serves every shape)."""
+        rep = ctypes.byref(representative) if representative is not None else None
+        check(self._lib.vx_gemm_matmul(self._handle, ctypes.byref(shape), rep, _ptr(a), _ptr(b),
+                                       _ptr(c)))
 
     def close(self) -> None:
         if self._handle:
