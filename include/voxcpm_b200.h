@@ -462,6 +462,14 @@ VX_API vx_status vx_generator_set_persistent(vx_generator* generator,
 VX_API int vx_generator_persistent(const vx_generator* generator);
 /* Rows in the caches (Generator::position, generator.hpp:69-70). */
 VX_API size_t vx_generator_position(const vx_generator* generator);
+/* The last patch's latent [patch][feat] in device memory, valid until the
+ * step after next (two slots alternate), ready once the event of
+ * vx_generator_latent_event completes; null before the first step of a
+ * sequence. Replaces Generator::latent (generator.hpp:78-84). */
+VX_API const float* vx_generator_latent(const vx_generator* generator);
+/* The event recorded on the generator's stream after the last step's
+ * launches. Replaces Generator::latent_event (generator.hpp:84). */
+VX_API cudaEvent_t vx_generator_latent_event(const vx_generator* generator);
 VX_API size_t vx_generator_weight_bytes(const vx_generator* generator);
 VX_API cudaStream_t vx_generator_stream(const vx_generator* generator);
 

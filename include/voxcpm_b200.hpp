@@ -475,6 +475,9 @@ class Generator {
 
   std::size_t capacity() const { return static_cast<std::size_t>(config_.max_length); }
   std::size_t position() const { return vx_generator_position(g_); }
+  /// generator.hpp:83-84
+  const float* latent() const { return vx_generator_latent(g_); }
+  cudaEvent_t latent_event() const { return vx_generator_latent_event(g_); }
 
   void Prefill(const Prompt& prompt) {
     Check(vx_generator_prefill(g_, prompt.tokens.data(),

@@ -143,6 +143,48 @@ def test_prefill_and_steps_small(cuda, cache_type):
     eager.close()
 
 
+def test_device_latent(cuda):
+    """Generator::latent() / latent_event() (generator.hpp:78-84): each
+    patch's latent stays in device memory until the step after next (two
+    slots alternate), equal to the host copy Step returns; the event has
+    completed when Step returns; no latent before a sequence's first step."""
+    import ctypes
+
+    c = small_config()
+    values = c.patch_size * c.feat_dim
+    cudart = ctypes.CDLL("libcudart.so.12")  # the runtime the library links
+
+    def read(ptr):
+        out = np.empty(values, np.float32)
+        status = cudart.cudaMemcpy(ctypes.c_void_p(out.ctypes.data), ctypes.c_void_p(ptr),
+                                   ctypes.c_size_t(out.nbytes), 2)  # device to host
+        assert status == 0
+        return out.reshape(c.patch_size, c.feat_dim)
+
+    gen = Generator(c, seed=5)
+    assert gen.latent() == 0
+    gen.Prefill(*prompt(c, 3))
+    assert gen.latent() == 0
+    rng = np.random.default_rng(4)
+    latents, ptrs = [], []
+    for k in range(3):
+        noise = rng.normal(0, 1, (c.patch_size, c.feat_dim)).astype(np.float32)
+        latent, _ = gen.Step(noise, 10, 2.0)
+        ptr = gen.latent()
+        assert ptr and gen.latent_event()
+        assert cudart.cudaEventQuery(ctypes.c_void_p(gen.latent_event())) == 0
+        assert np.array_equal(read(ptr), latent)
+        if k >= 1:
+            assert ptr != ptrs[-1]
+            assert np.array_equal(read(ptrs[-1]), latents[-1])
+        latents.append(latent)
+        ptrs.append(ptr)
+    assert ptrs[2] == ptrs[0]
+    gen.Prefill(*prompt(c, 3))
+    assert gen.latent() == 0
+    gen.close()
+
+
 def test_step_errors(cuda):
     """A step without a prefilled sequence is rejected (generator.cpp:426-427)."""
     c = small_config()

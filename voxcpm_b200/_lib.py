@@ -216,6 +216,8 @@ SIGNATURES: dict[str, tuple] = {
     "vx_generator_set_persistent": (c_int, [c_void_p, c_int]),
     "vx_generator_persistent": (c_int, [c_void_p]),
     "vx_generator_position": (c_size_t, [c_void_p]),
+    "vx_generator_latent": (c_void_p, [c_void_p]),
+    "vx_generator_latent_event": (c_void_p, [c_void_p]),
     "vx_generator_weight_bytes": (c_size_t, [c_void_p]),
     "vx_generator_stream": (c_void_p, [c_void_p]),
     "vx_generator_batch_create": (c_void_p, [POINTER(ModelConfig), c_uint64, c_int, c_int, c_size_t]),

@@ -393,6 +393,8 @@ void GeneratorBatch::Step(const std::int32_t* active, const float* noise,
     }
     Cuda(cudaGraphLaunch(found->second, stream_), "batch graph");
   }
+  for (const int s : members)
+    Cuda(cudaEventRecord(slots_[s]->latent_event_, stream_), "latent event");
   Cuda(cudaStreamSynchronize(stream_), "batch step");
   for (const int s : members) {
     Generator& g = *slots_[s];
@@ -403,6 +405,7 @@ void GeneratorBatch::Step(const std::int32_t* active, const float* noise,
       std::memcpy(stop_logits + 2 * static_cast<std::size_t>(s), g.pinned_stop_,
                   2 * sizeof(float));
     ++g.position_;
+    g.latent_ready_ = true;
   }
 }
 

@@ -307,6 +307,17 @@ size_t vx_generator_position(const vx_generator* generator) {
              : 0;
 }
 
+const float* vx_generator_latent(const vx_generator* generator) {
+  return generator != nullptr && generator->impl ? generator->impl->latent()
+                                                 : nullptr;
+}
+
+cudaEvent_t vx_generator_latent_event(const vx_generator* generator) {
+  return generator != nullptr && generator->impl
+             ? generator->impl->latent_event()
+             : nullptr;
+}
+
 size_t vx_generator_weight_bytes(const vx_generator* generator) {
   return generator != nullptr && generator->impl
              ? generator->impl->weight_bytes()

@@ -711,6 +711,7 @@ std::unique_ptr<Generator> Generator::Create(const ModelConfig& config,
       g->residual_hidden_ = a.Take<float>(c.lm.hidden);
       g->prefix_cond_ = a.Take<float>(patch_values);
       g->x_ = a.Take<float>(2 * patch_values);  // x and the patch's noise
+      g->latent_slots_ = a.Take<float>(2 * patch_values);
       g->velocity_ = a.Take<float>(2 * patch_values);
       g->mu_ = a.Take<float>(2 * c.dit.hidden);
       g->cond_rows_ = a.Take<float>(static_cast<std::size_t>(c.patch_size) * c.dit.hidden);
@@ -781,6 +782,8 @@ std::unique_ptr<Generator> Generator::Create(const ModelConfig& config,
     }
     ThrowCuda(cudaMemset(g->position_counter_, 0, 4), "cudaMemset");
     ThrowCuda(cudaMemset(g->step_positions_, 0, 4), "cudaMemset");
+    ThrowCuda(cudaEventCreateWithFlags(&g->latent_event_, cudaEventDisableTiming),
+              "cudaEventCreate");
     ThrowCuda(cudaMallocHost(reinterpret_cast<void**>(&g->pinned_noise_),
                              patch_values * sizeof(float)), "cudaMallocHost");
     ThrowCuda(cudaMallocHost(reinterpret_cast<void**>(&g->pinned_latent_),
@@ -854,6 +857,8 @@ Generator::~Generator() {
     cudaFreeHost(pinned_latent_);
   if (pinned_stop_ != nullptr)
     cudaFreeHost(pinned_stop_);
+  if (latent_event_ != nullptr)
+    cudaEventDestroy(latent_event_);
   arena_.reset();
   work_.reset();
   if (stream_ != nullptr && owns_stream_)
@@ -1333,6 +1338,10 @@ void Generator::PatchOutputs() {
   CheckCuda(cudaMemcpyAsync(pinned_latent_, x_, values * sizeof(float),
                             cudaMemcpyDeviceToHost, stream_),
             "latent");
+  // The device copy behind latent(): the slot of this patch's position
+  // (the device counter still holds it; the LMs advance it afterwards).
+  Check(CopyToParitySlot(x_, latent_slots_, values, position_counter_, stream_),
+        "latent slot");
   Check(CopyFloats(x_, prefix_cond_, values, stream_), "prefix");
   CheckCuda(cudaMemcpyAsync(pinned_stop_, stop_, 2 * sizeof(float),
                             cudaMemcpyDeviceToHost, stream_),
@@ -1409,12 +1418,21 @@ void Generator::Step(const float* noise, int timesteps, float cfg,
     }
     CheckCuda(cudaGraphLaunch(step_graph_, stream_), "step graph");
   }
+  CheckCuda(cudaEventRecord(latent_event_, stream_), "latent event");
   CheckCuda(cudaStreamSynchronize(stream_), "step");
   if (latent != nullptr)
     std::memcpy(latent, pinned_latent_, values * sizeof(float));
   if (stop_logits != nullptr)
     std::memcpy(stop_logits, pinned_stop_, 2 * sizeof(float));
   ++position_;
+  latent_ready_ = true;
+}
+
+const float* Generator::latent() const {
+  if (!latent_ready_ || position_ < 1)
+    return nullptr;
+  const int values = config_.patch_size * config_.feat_dim;
+  return latent_slots_ + static_cast<std::size_t>((position_ - 1) & 1) * values;
 }
 
 void Generator::Velocity(const float* mu, const float* cond, const float* x,
@@ -1655,6 +1673,7 @@ void Generator::Prefill(const std::int32_t* tokens,
     throw;
   }
   position_ = rows;
+  latent_ready_ = false;
 }
 
 namespace {

@@ -211,6 +211,12 @@ class Generator {
   /// graph when graphs are enabled.
   void Step(const float* noise, int timesteps, float cfg, float* latent,
             float* stop_logits);
+  /// generator.hpp:83-84: the last patch's latent [patch][feat] on the
+  /// device, valid until the step after next (two slots alternate by
+  /// position), ready once latent_event() completes; null before the first
+  /// step of a sequence.
+  const float* latent() const;
+  cudaEvent_t latent_event() const { return latent_event_; }
   /// generator.cpp:515-538: one DiT evaluation's velocity pair.
   void Velocity(const float* mu, const float* cond, const float* x, float t,
                 float* velocity);
@@ -291,6 +297,11 @@ class Generator {
   std::size_t prefill_bytes_ = 0;
   int position_ = 0;
   bool graphs_ = true;
+  // Latents of the last two patches ([2][patch][feat], slot = position & 1)
+  // and the event after the last step's launches.
+  float* latent_slots_ = nullptr;
+  cudaEvent_t latent_event_ = nullptr;
+  bool latent_ready_ = false;
 
   // Sequence state.
   float* lm_hidden_ = nullptr;

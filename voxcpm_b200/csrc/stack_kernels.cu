@@ -551,6 +551,17 @@ __global__ void AdvancePositionKernel(std::int32_t* counter,
   }
 }
 
+/// output[(*position & 1) * count + i] = input[i]: the patch's latent into
+/// the slot of its position's parity (one block).
+__global__ void CopyToParitySlotKernel(const float* input, float* slots,
+                                       std::size_t count,
+                                       const std::int32_t* position) {
+  Prologue();
+  float* output = slots + static_cast<std::size_t>(*position & 1) * count;
+  for (std::size_t i = threadIdx.x; i < count; i += blockDim.x)
+    output[i] = input[i];
+}
+
 }  // namespace
 
 int Embed(const std::uint16_t* table, const std::int32_t* ids,
@@ -751,6 +762,14 @@ int CopyFloats(const float* input, float* output, std::size_t count,
     return kOk;
   return LaunchKernel(CopyFloatsKernel, dim3(Blocks(count)), dim3(kThreads), 0,
                       stream, kNoCluster, input, output, count);
+}
+
+int CopyToParitySlot(const float* input, float* slots, std::size_t count,
+                     const std::int32_t* position, cudaStream_t stream) {
+  if (count == 0)
+    return kOk;
+  return LaunchKernel(CopyToParitySlotKernel, dim3(1), dim3(kThreads), 0,
+                      stream, kNoCluster, input, slots, count, position);
 }
 
 int AdvancePosition(std::int32_t* counter, std::int32_t* positions,

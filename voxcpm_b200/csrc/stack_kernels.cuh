@@ -70,6 +70,10 @@ int GuidedEuler(const float* velocity, float* x, std::size_t count, float cfg,
 /// programmatic dependent launch).
 int CopyFloats(const float* input, float* output, std::size_t count,
                cudaStream_t stream);
+/// Copies `count` floats into slot (*position & 1) of `slots` ([2][count]):
+/// a two-slot ring indexed by the device-held decode position, graph-safe.
+int CopyToParitySlot(const float* input, float* slots, std::size_t count,
+                     const std::int32_t* position, cudaStream_t stream);
 /// *counter += 1 and positions[0] = *counter (the decode step's moving
 /// position, graph-safe).
 int AdvancePosition(std::int32_t* counter, std::int32_t* positions,

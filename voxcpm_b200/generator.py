@@ -129,6 +129,16 @@ class Generator:
     def position(self) -> int:
         return self._lib.vx_generator_position(self._handle)
 
+    def latent(self) -> int:
+        """Device address of the last patch's latent [patch][feat], valid
+        until the step after next; 0 before the first step of a sequence
+        (generator.hpp:78-84)."""
+        return self._lib.vx_generator_latent(self._handle) or 0
+
+    def latent_event(self) -> int:
+        """The cudaEvent_t recorded after the last step (generator.hpp:84)."""
+        return self._lib.vx_generator_latent_event(self._handle) or 0
+
     def weight_bytes(self) -> int:
         return self._lib.vx_generator_weight_bytes(self._handle)
 
