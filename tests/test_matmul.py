@@ -78,7 +78,9 @@ def test_matmul_rejects_bad_shapes():
 CASES = [
     # (ta, tb, m, n, k, pads, batch)
     (False, False, 200, 72, 300, (3, 1, 5), 1),
-    (True, False, 130, 64, 96, (0, 2, 0), 2),
+    (True, False, 130, 64, 96, (0, 2, 0), 2),    # ldb not a multiple of 8: general kernel
+    (True, False, 200, 72, 296, (8, 0, 5), 2),   # reduction-contiguous kernel, ragged tiles
+    (True, False, 257, 300, 1024, (0, 0, 3), 1),  # reduction-contiguous kernel, several tiles
     (False, True, 64, 129, 33, (1, 0, 2), 3),
     (True, True, 77, 50, 1024, (4, 4, 4), 1),
     (True, False, 1, 1, 1, (0, 0, 0), 1),
@@ -94,7 +96,10 @@ def test_matmul_against_oracle(cuda, ta, tb, m, n, k, pads, batch):
     ldb = (n if tb else k) + pads[1]
     ldc = m + pads[2]
     cols_a, cols_b = (m if ta else k), (k if tb else n)
-    sa, sb, sc = lda * cols_a + 3, ldb * cols_b + 1, ldc * n + 7
+    # Batch gaps of 8 elements keep the reduction-contiguous layout's 16-byte
+    # alignment; odd gaps elsewhere.
+    gap = 8 if (ta and not tb) else 3
+    sa, sb, sc = lda * cols_a + gap, ldb * cols_b + gap, ldc * n + 7
     a = oracle.bf16_bits(rng.normal(0, 1, size=max(1, sa * batch)).astype(np.float32))
     b = oracle.bf16_bits(rng.normal(0, 1, size=max(1, sb * batch)).astype(np.float32))
     c0 = rng.normal(0, 1, size=sc * batch).astype(np.float32)
