@@ -218,6 +218,50 @@ def cpu_sample(threads: int, budget_s: float):
         f"{elapsed:.1f} s")
 
 
+def cpu_host_baselines() -> dict:
+    """The other host-side references the path's tests check against, timed
+    once each on this box's host cores (reported only):
+    - the scalar double-precision product of config 0 on one thread
+      (tests/products_test.cpp:117-134);
+    - one DiT patch of config 2 (12 layers, 10 Euler steps, 9 evaluations,
+      CFG 2.0, seeded Q8_0 weights) through the oracle's restatement on all
+      cores (generator.cpp:297-324, 424-460)."""
+    import numpy as np
+
+    import oracle
+    from oracle.model import OracleGenerator
+    from voxcpm_b200.generator import released_config
+
+    rng = np.random.default_rng(0)
+    blocks = oracle.random_q8_0(1, 0, OUT, IN)
+    x = oracle.bf16_bits(rng.normal(0, 1, (ROWS, IN)).astype(np.float32))
+    start = time.perf_counter()
+    oracle.product_exact(x, oracle.Q8_0, blocks, ROWS, IN, OUT, threads=1)
+    product_s = time.perf_counter() - start
+
+    c = released_config()
+    c.lm.layers = 1  # the DiT patch reads no LM weights; keeps set-up short
+    c.residual_lm.layers = 1
+    c.max_length = 64
+    threads = os.cpu_count() or 1
+    ref = OracleGenerator(c, seed=7, threads=threads)
+    mu = rng.normal(0, 1, 2 * c.dit.hidden).astype(np.float32)
+    cond = rng.normal(0, 1, (c.patch_size, c.feat_dim)).astype(np.float32)
+    noise = rng.normal(0, 1, (c.patch_size, c.feat_dim)).astype(np.float32)
+    start = time.perf_counter()
+    ref.dit_patch(mu, cond, noise, 10, 2.0)
+    patch_s = time.perf_counter() - start
+    return {
+        "double_sum_product": {"us": product_s * 1e6, "gbs": STEP_BYTES / product_s / 1e9, "cores": 1,
+                               "kind": "port",
+                               "sample": f"one full config-0 product (M={ROWS}, K={IN}, N={OUT}), "
+                                         "double-precision sums, one thread"},
+        "dit_patch": {"us": patch_s * 1e6, "cores": threads, "kind": "port",
+                      "sample": "one config-2 DiT patch (10 Euler steps, CFG 2.0) through the oracle's "
+                                "restatement, all host cores"},
+    }
+
+
 # ---------------------------------------------------------------- reference arm
 
 def run_reference(args, world, rank):
@@ -441,6 +485,7 @@ def run_ours(args, world, rank, local):
     peak, peak_kind = measured_peak()
     sweep = measure_sweep(peak)
     cpu_value, cpu_desc = cpu_sample(os.cpu_count() or 1, 10.0)
+    host_baselines = cpu_host_baselines() if (world or 1) == 1 else None
     plan = K.PlanWmma(ROWS, IN, OUT, 0)
     line = {
         "metric": METRIC, "value": value, "unit": "GB/s", "n_gpus": world, "steps": args.steps,
@@ -469,6 +514,7 @@ def run_ours(args, world, rank, local):
                      "algorithmic_bytes_per_launch": STEP_BYTES},
         "cpu_baseline": {"value": cpu_value, "unit": "GB/s", "cores": os.cpu_count() or 1,
                          "kind": "port", "sample": cpu_desc},
+        "cpu_baselines": host_baselines,
         "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": X_BYTES,
                 "d2h_bytes_per_step": Y_BYTES, "steps": e2e_steps, "streams": E2E_STREAMS,
                 "api": "vx_product_host (default plan): pinned host x staged in and y staged out "
