@@ -60,7 +60,7 @@ def parse():
     p.add_argument("--steps", type=int, default=400_000)
     p.add_argument("--warmup", type=int, default=20_000)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--case", choices=["product", "dit", "wide", "batch"], default=None,
+    p.add_argument("--case", choices=["product", "dit", "wide", "batch", "matmul"], default=None,
                    help="run a few launches of one kernel for a profiler and exit (no JSON line)")
     return p.parse_args()
 
@@ -856,7 +856,9 @@ def profile_case(case: str) -> None:
     products of 88 rows of 1024 -> 8192 (the gate/up product of four batched
     slots' DiT rows; the planner gives it to the wide tcgen05 kernel);
     `batch`: two steps of a GeneratorBatch of 8 slots on the released shapes
-    (the first captures the step's graph)."""
+    (the first captures the step's graph); `matmul`: three Bf16Gemm::Matmul
+    calls of 4096 x 4096 x 4096 in the reduction-contiguous layout, timed
+    with CUDA events (96 MB of operands and C)."""
     import numpy as np
     import torch
 
@@ -865,6 +867,26 @@ def profile_case(case: str) -> None:
 
     lib = _lib.load()
     torch.cuda.set_device(0)
+    if case == "matmul":
+        from voxcpm_b200.gemm import Bf16Gemm, MatmulShape
+
+        n = 4096
+        gen = torch.Generator(device="cuda").manual_seed(0)
+        a = torch.randn(n * n, device="cuda", generator=gen).to(torch.bfloat16).view(torch.int16)
+        b = torch.randn(n * n, device="cuda", generator=gen).to(torch.bfloat16).view(torch.int16)
+        c = torch.empty(n * n, device="cuda")
+        gemm = Bf16Gemm()
+        shape = MatmulShape(1, 0, n, n, n, n, n, n, 0, 0, 0, 1, 0)
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        for _ in range(3):
+            start.record()
+            gemm.Matmul(shape, None, a, b, c)
+            end.record()
+            end.synchronize()
+            print(f"matmul {n}^3: {start.elapsed_time(end) * 1e3:.1f} us, "
+                  f"{2 * n ** 3 / (start.elapsed_time(end) * 1e-3) / 1e12:.1f} TFLOP/s")
+        gemm.close()
+        return
     if case == "product":
         tiles, ys = [], []
         for c in range(COPIES):
