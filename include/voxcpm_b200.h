@@ -353,6 +353,89 @@ typedef struct vx_stack_config {
   int rope;
 } vx_stack_config;
 
+/* ------------------------------------------------------------ transformer */
+
+/* A linear layer y = x W^T (+ b): `format` one of VX_WEIGHTS_*, `weight` in
+ * that layout, `bias` bf16 [out] or null. Replaces Projection
+ * (weights.hpp:20-26). */
+typedef struct vx_projection {
+  int format;
+  const void* weight;
+  const uint16_t* bias;
+  size_t in, out;
+} vx_projection;
+/* One pre-norm layer: bf16 norm weights, fused [q | k | v] and [gate | up].
+ * Replaces LayerWeights (weights.hpp:28-36). */
+typedef struct vx_layer_weights {
+  const uint16_t* input_norm;
+  vx_projection qkv, o;
+  const uint16_t* post_norm;
+  vx_projection gate_up, down;
+} vx_layer_weights;
+/* `config.layers` layers (host array) and the final norm. Replaces
+ * StackWeights (weights.hpp:38-42). */
+typedef struct vx_stack_weights {
+  vx_stack_config config;
+  const vx_layer_weights* layers;
+  const uint16_t* norm;
+} vx_stack_weights;
+/* Which keys each row attends to; `positions` (rotary table rows) and
+ * `cache_rows` are device arrays of one entry per row. Replaces
+ * AttentionLayout (transformer.hpp:38-48). */
+typedef struct vx_attention_layout {
+  const int32_t* positions;
+  const int32_t* cache_rows;
+  size_t rows_per_sequence;
+  size_t keys_per_sequence;
+  size_t past;
+  int causal;
+} vx_attention_layout;
+/* Device work buffers of ForwardStack, sized by vx_stack_scratch_elements.
+ * Replaces StackScratch (transformer.hpp:50-58). */
+typedef struct vx_stack_scratch {
+  uint16_t* normed;
+  float* qkv;
+  float* q;
+  uint16_t* attention;
+  float* gate_up;
+  uint16_t* activation;
+} vx_stack_scratch;
+/* Elements each vx_stack_scratch buffer needs for `rows` rows of `config`,
+ * in field order (normed, qkv, q, attention, gate_up, activation). */
+VX_API vx_status vx_stack_scratch_elements(const vx_stack_config* config,
+                                           size_t rows, size_t counts[6]);
+
+/* Keys and values of one stack, [layer][kv_head][capacity][head_dim] each,
+ * float32 (VX_CACHE_F32) or bf16 (VX_CACHE_BF16); zeroed at creation.
+ * Replaces KvCache (transformer.hpp:17-36). Null on failure
+ * (vx_last_error). */
+typedef struct vx_kv_cache vx_kv_cache;
+VX_API vx_kv_cache* vx_kv_cache_create(const vx_stack_config* config,
+                                       size_t capacity, int cache_type);
+VX_API void vx_kv_cache_destroy(vx_kv_cache* cache);
+VX_API size_t vx_kv_cache_capacity(const vx_kv_cache* cache);
+/* Layer `layer`'s keys / values (null for a layer out of range). */
+VX_API void* vx_kv_cache_keys(const vx_kv_cache* cache, size_t layer);
+VX_API void* vx_kv_cache_values(const vx_kv_cache* cache, size_t layer);
+
+/* One MiniCPM4 stack over `rows` rows of the float32 residual stream
+ * `hidden` (updated in place); the final norm's float32 output goes to
+ * `output`. `rope` is the device rotary table ([position][cos | sin]), null
+ * for a stack without rotary embedding. Replaces ForwardStack
+ * (transformer.hpp:68-71, transformer.cpp:55-100). */
+VX_API vx_status vx_forward_stack(const vx_stack_weights* stack,
+                                  const float* rope,
+                                  const vx_attention_layout* layout,
+                                  vx_kv_cache* cache, float* hidden,
+                                  float* output, size_t rows,
+                                  const vx_stack_scratch* scratch,
+                                  cudaStream_t stream);
+/* y[rows][out] = x[rows][in] W^T + b for bf16 x. Replaces Project
+ * (transformer.hpp:73-76, transformer.cpp:47-53). */
+VX_API vx_status vx_project(const vx_projection* projection,
+                            const uint16_t* x, float* y, size_t rows,
+                            cudaStream_t stream);
+
 /* The generator's configuration (config.hpp:78-92). */
 typedef struct vx_model_config {
   vx_stack_config lm, residual_lm, encoder, dit;

@@ -309,6 +309,48 @@ class Bf16Gemm {
   vx_gemm* gemm_;
 };
 
+/// transformer.hpp:17-36: keys and values of one stack, zeroed.
+class KvCache {
+ public:
+  KvCache(const vx_stack_config& config, std::size_t capacity,
+          int cache_type = VX_CACHE_F32)
+      : cache_(vx_kv_cache_create(&config, capacity, cache_type)) {
+    if (cache_ == nullptr)
+      throw GpuError(std::string("KvCache: ") + vx_last_error());
+  }
+  ~KvCache() { vx_kv_cache_destroy(cache_); }
+  KvCache(const KvCache&) = delete;
+  KvCache& operator=(const KvCache&) = delete;
+
+  std::size_t capacity() const { return vx_kv_cache_capacity(cache_); }
+  void* keys(std::size_t layer) const { return vx_kv_cache_keys(cache_, layer); }
+  void* values(std::size_t layer) const {
+    return vx_kv_cache_values(cache_, layer);
+  }
+  vx_kv_cache* get() const { return cache_; }
+
+ private:
+  vx_kv_cache* cache_;
+};
+
+/// transformer.hpp:68-71. The products run on the library's own kernels, so
+/// no Bf16Gemm is passed.
+inline void ForwardStack(const vx_stack_weights& stack, const float* rope,
+                         const vx_attention_layout& layout, KvCache& cache,
+                         float* hidden, float* output, std::size_t rows,
+                         const vx_stack_scratch& scratch,
+                         cudaStream_t stream) {
+  Check(vx_forward_stack(&stack, rope, &layout, cache.get(), hidden, output,
+                         rows, &scratch, stream),
+        "ForwardStack");
+}
+
+/// transformer.hpp:73-76
+inline void Project(const vx_projection& projection, const Bf16* x, float* y,
+                    std::size_t rows, cudaStream_t stream) {
+  Check(vx_project(&projection, x, y, rows, stream), "Project");
+}
+
 /// transformer.hpp:63-66 (factors per frequency; the reference derives them
 /// from its RopeConfig).
 inline std::vector<float> RopeTable(double theta, std::size_t dim,

@@ -90,6 +90,40 @@ class StackConfig(ctypes.Structure):
                 ("kv_heads", c_int), ("head_dim", c_int), ("rms_eps", c_float), ("rope", c_int)]
 
 
+class ProjectionC(ctypes.Structure):
+    """vx_projection (weights.hpp:20-26)."""
+
+    _fields_ = [("format", c_int), ("weight", c_void_p), ("bias", c_void_p), ("in_", c_size_t),
+                ("out", c_size_t)]
+
+
+class LayerWeightsC(ctypes.Structure):
+    """vx_layer_weights (weights.hpp:28-36)."""
+
+    _fields_ = [("input_norm", c_void_p), ("qkv", ProjectionC), ("o", ProjectionC), ("post_norm", c_void_p),
+                ("gate_up", ProjectionC), ("down", ProjectionC)]
+
+
+class StackWeightsC(ctypes.Structure):
+    """vx_stack_weights (weights.hpp:38-42)."""
+
+    _fields_ = [("config", StackConfig), ("layers", POINTER(LayerWeightsC)), ("norm", c_void_p)]
+
+
+class AttentionLayoutC(ctypes.Structure):
+    """vx_attention_layout (transformer.hpp:38-48)."""
+
+    _fields_ = [("positions", c_void_p), ("cache_rows", c_void_p), ("rows_per_sequence", c_size_t),
+                ("keys_per_sequence", c_size_t), ("past", c_size_t), ("causal", c_int)]
+
+
+class StackScratchC(ctypes.Structure):
+    """vx_stack_scratch (transformer.hpp:50-58)."""
+
+    _fields_ = [("normed", c_void_p), ("qkv", c_void_p), ("q", c_void_p), ("attention", c_void_p),
+                ("gate_up", c_void_p), ("activation", c_void_p)]
+
+
 class ModelConfig(ctypes.Structure):
     """vx_model_config (config.hpp:78-92)."""
 
@@ -252,6 +286,15 @@ SIGNATURES: dict[str, tuple] = {
     ),
     "vx_matmul": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
     "vx_gemm_matmul": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
+    "vx_stack_scratch_elements": (c_int, [c_void_p, c_size_t, c_void_p]),
+    "vx_kv_cache_create": (c_void_p, [c_void_p, c_size_t, c_int]),
+    "vx_kv_cache_destroy": (None, [c_void_p]),
+    "vx_kv_cache_capacity": (c_size_t, [c_void_p]),
+    "vx_kv_cache_keys": (c_void_p, [c_void_p, c_size_t]),
+    "vx_kv_cache_values": (c_void_p, [c_void_p, c_size_t]),
+    "vx_forward_stack": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_size_t,
+                                 c_void_p, c_void_p]),
+    "vx_project": (c_int, [c_void_p, c_void_p, c_void_p, c_size_t, c_void_p]),
 }
 
 _lib: ctypes.CDLL | None = None
