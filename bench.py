@@ -6,21 +6,26 @@ Workload (the headline metric's configuration): one
 Q8_0 x bf16 skinny product, M = 22 activation rows, K = 2048, N = 6144,
 fp32 accumulation, bf16 output. A step is one product on one of 16 rotating
 seeded weight copies (214 MB, larger than the 126 MB L2, so every step reads
-its weights from HBM) into that copy's own output. Steps are replayed from
-CUDA graphs of 100 launches so the host's launch rate does not bound the
-device. With N > 1 (torchrun, one process per GPU) every rank runs its own
-products (replicas, weak scaling); the value is all ranks' bytes over the
-slowest rank's time.
+its weights from HBM) into that copy's own output, through the product path a
+caller of the reference's gemm.hpp takes: Bf16Gemm::Linear on one stream
+(vx_gemm_linear_ex), which plans the product itself. Every launch waits for
+the previous one (a dependent chain, the reference's own benchmark method);
+programmatic dependent launch lets a launch start its weight stream before
+the previous one ends. Steps are replayed from CUDA graphs of up to 100
+launches (any --steps), so the host's launch rate does not bound the device.
+With N > 1 (torchrun, one process per GPU) every rank runs its own products
+(replicas, weak scaling); the value is all ranks' bytes over the slowest
+rank's time.
 
 `value` is the sustained HBM throughput in GB/s of algorithmic bytes
-(weights + activations + bf16 output) of a stream of independent products:
-each launch skips the programmatic-launch wait, so a product's ramp overlaps
-its predecessor's tail. `dependent` is the same products as a chain in which
-every launch waits for the previous one (the generator's case). `e2e` is the same metric through the C ABI with
-host buffers: each step copies x from pinned memory, runs the product and
-reads y back. `--impl reference` times the reference's arithmetic on the host
-cores: the reference (HIP, AMD-only) cannot be built here, so the CPU oracle
-port (oracle/, a float32 transcription of its product kernel) stands in.
+(weights + activations + bf16 output) of that chain. `stream` is the same
+products as independent launches (each skips the programmatic wait, so one
+overlaps the next) on the measured stream plan. `e2e` is the same metric
+through the C ABI with host buffers: each step copies x from pinned memory,
+runs the product and reads y back. `--impl reference` times the reference's
+arithmetic on the host cores: the reference (HIP, AMD-only) cannot be built
+here, so the CPU oracle port (oracle/, a float32 transcription of its product
+kernel) stands in.
 """
 
 from __future__ import annotations
@@ -344,94 +349,127 @@ def run_ours(args, world, rank, local):
     x_ptr = x.data_ptr()
     y_ptrs = [t.data_ptr() for t in ys]
     tile_ptrs = [t.data_ptr() for t in tiles]
-    # Stream plan: measured best for independent launches of this shape.
+    # The product path a caller of the reference's gemm.hpp takes:
+    # Bf16Gemm::Linear on the stream (vx_gemm_linear_ex, bf16 output), which
+    # plans the product itself (the spread kernel through the gemm's own split
+    # scratch); every launch waits for the previous one (a dependent chain).
+    gemm = lib.vx_gemm_create(s)
+    if not gemm:
+        raise RuntimeError(lib.vx_last_error().decode())
+    # Beside it, the measured plan for streams of independent launches.
     stream_plan = _lib.WmmaPlan(STREAM_SPLITS, -(-(IN // 32) // STREAM_SPLITS), 0, 0, STREAM_VARIANT)
 
-    def launch(i, independent=False, x_at=x_ptr, on=s):
-        if independent:
+    def launch(i, mode, x_at=x_ptr, on=s):
+        if mode == "chain":
+            st = lib.vx_gemm_linear_ex(gemm, x_at, _lib.WEIGHTS_Q8_TILES, tile_ptrs[i % COPIES],
+                                       y_ptrs[i % COPIES], _lib.OUT_BF16, ROWS, IN, OUT, 0)
+        else:
             st = lib.vx_product_ex(_lib.WEIGHTS_Q8_TILES, x_at, tile_ptrs[i % COPIES], y_ptrs[i % COPIES],
                                    _lib.OUT_BF16, ROWS, IN, OUT, _lib.PRODUCT_INDEPENDENT,
                                    ctypes.byref(stream_plan), on)
-        else:
-            st = lib.vx_product(_lib.WEIGHTS_Q8_TILES, x_at, tile_ptrs[i % COPIES], y_ptrs[i % COPIES],
-                                _lib.OUT_BF16, ROWS, IN, OUT, 0, None, on)
         if st != 0:
             raise RuntimeError(lib.vx_last_error().decode())
 
-    # Graphs of GRAPH_LAUNCHES products over the rotating copies: the
-    # independent stream (the value) and the dependent chain.
+    # CUDA graphs of the launches (any step count: graphs of GRAPH_LAUNCHES
+    # launches and one of the remainder), captured before any timing.
     graphs = {}
-    with torch.cuda.stream(stream):
-        for independent in (True, False):
-            for i in range(3):
-                launch(i, independent)
-            stream.synchronize()
-            g = torch.cuda.CUDAGraph()
-            with torch.cuda.graph(g, stream=stream):
-                for i in range(GRAPH_LAUNCHES):
-                    launch(i, independent)
-            graphs[independent] = g
-    torch.cuda.synchronize()
 
-    def run_steps(n, independent=True):
+    def graph(mode, count):
+        key = (mode, count)
+        if key not in graphs:
+            with torch.cuda.stream(stream):
+                for i in range(3):
+                    launch(i, mode)
+                stream.synchronize()
+                g = torch.cuda.CUDAGraph()
+                with torch.cuda.graph(g, stream=stream):
+                    for i in range(count):
+                        launch(i, mode)
+            graphs[key] = g
+        return graphs[key]
+
+    def run_steps(n, mode):
+        full, rest = divmod(n, GRAPH_LAUNCHES)
         with torch.cuda.stream(stream):
-            for _ in range(n // GRAPH_LAUNCHES):
-                graphs[independent].replay()
-            for i in range(n % GRAPH_LAUNCHES):
-                launch(i, independent)
+            for _ in range(full):
+                graph(mode, GRAPH_LAUNCHES).replay()
+            if rest:
+                graph(mode, rest).replay()
 
-    run_steps(max(args.warmup, 3))
+    warmup = max(args.warmup, 3)
+    for mode in ("chain", "stream"):
+        for n in (warmup, args.steps):
+            full, rest = divmod(n, GRAPH_LAUNCHES)
+            if full:
+                graph(mode, GRAPH_LAUNCHES)
+            if rest:
+                graph(mode, rest)
     torch.cuda.synchronize()
 
     start = torch.cuda.Event(enable_timing=True)
     stop = torch.cuda.Event(enable_timing=True)
-    visible = os.environ.get("CUDA_VISIBLE_DEVICES")
-    sampler = ClockSampler(int(visible.split(",")[local]) if visible else local)
-    barrier(world)
-    torch.cuda.synchronize()
-    with sampler:
+
+    def timed(mode):
+        run_steps(warmup, mode)
+        torch.cuda.synchronize()
+        barrier(world)
+        torch.cuda.synchronize()
+        with torch.cuda.stream(stream):
+            # A device-side pause before the start event, so the host has
+            # enqueued the timed graphs by the time the stream reaches it and
+            # host submission stays out of the timed region.
+            torch.cuda._sleep(200_000)
         start.record(stream)
-        run_steps(args.steps)
+        run_steps(args.steps, mode)
         stop.record(stream)
         torch.cuda.synchronize()
-    barrier(world)
-    ms = start.elapsed_time(stop)
+        barrier(world)
+        return start.elapsed_time(stop)
+
+    visible = os.environ.get("CUDA_VISIBLE_DEVICES")
+    sampler = ClockSampler(int(visible.split(",")[local]) if visible else local)
+    with sampler:
+        ms = timed("chain")
     ms_max = max_over_ranks(world, ms)
     total_bytes = sum_over_ranks(world, STEP_BYTES * args.steps)
     value = total_bytes / (ms_max / 1e3) / 1e9
     per_launch_s = ms / 1e3 / max(args.steps, 1)
     achieved = STEP_BYTES / per_launch_s / 1e9
-    # The dependent chain, same steps.
-    run_steps(max(args.warmup, 3), independent=False)
-    torch.cuda.synchronize()
-    barrier(world)
-    start.record(stream)
-    run_steps(args.steps, independent=False)
-    stop.record(stream)
-    torch.cuda.synchronize()
-    dep_ms = max_over_ranks(world, start.elapsed_time(stop))
-    dep_value = sum_over_ranks(world, STEP_BYTES * args.steps) / (dep_ms / 1e3) / 1e9
+    # The same steps as a stream of independent launches (each skips the
+    # programmatic wait, so one overlaps the next) on the measured stream
+    # plan.
+    extra = {}
+    for mode in ("stream",):
+        m_ms = max_over_ranks(world, timed(mode))
+        extra[mode] = (m_ms, sum_over_ranks(world, STEP_BYTES * args.steps) / (m_ms / 1e3) / 1e9)
+    lib.vx_gemm_destroy(gemm)
+    graphs.clear()
     bits = K.DeviceError()
     if bits:
         raise RuntimeError(f"device wait timed out: bits {bits:#x}")
 
     # e2e through the C ABI with host buffers: every step is one
-    # vx_product_host call, which stages x in from pinned memory, runs the
-    # product (the default plan) and stages y out to pinned memory, the
-    # transfers by SM loads and stores over PCIe. Steps rotate over E2E_STREAMS streams, each with its own
-    # x and pinned y, so one step's copies overlap other steps' products;
-    # each stream replays a CUDA graph of its E2E_GRAPH_STEPS steps (the
-    # copies and the product of every step are in the graph), so the host's
-    # per-call cost stays out of the timed region as in the value above.
+    # vx_gemm_linear_host call (Bf16Gemm::Linear with host activations and
+    # output), which stages x in from pinned memory, runs the product on the
+    # same plan as the value above and stages y out to pinned memory, the
+    # transfers by SM loads and stores over PCIe. Steps rotate over
+    # E2E_STREAMS streams, each with its own gemm, x and pinned y, so one
+    # step's copies overlap other steps' products; each stream replays a CUDA
+    # graph of its E2E_GRAPH_STEPS steps (the copies and the product of every
+    # step are in the graph), so the host's per-call cost stays out of the
+    # timed region as in the value above.
     lanes = [torch.cuda.Stream(device) for _ in range(E2E_STREAMS)]
+    lane_gemms = [lib.vx_gemm_create(lane.cuda_stream) for lane in lanes]
+    if not all(lane_gemms):
+        raise RuntimeError(lib.vx_last_error().decode())
     x_lanes = [torch.empty_like(x) for _ in range(E2E_STREAMS)]
     x_pinned = x_host.pin_memory()
     y_pinned = [torch.empty(ROWS, OUT, dtype=torch.bfloat16).pin_memory() for _ in range(E2E_STREAMS)]
 
     def e2e_step(i, k):
-        st = lib.vx_product_host(_lib.WEIGHTS_Q8_TILES, x_pinned.data_ptr(), x_lanes[k].data_ptr(),
-                                 tile_ptrs[i % COPIES], y_ptrs[i % COPIES], y_pinned[k].data_ptr(),
-                                 _lib.OUT_BF16, ROWS, IN, OUT, 0, None, lanes[k].cuda_stream)
+        st = lib.vx_gemm_linear_host(lane_gemms[k], x_pinned.data_ptr(), x_lanes[k].data_ptr(),
+                                     _lib.WEIGHTS_Q8_TILES, tile_ptrs[i % COPIES], y_ptrs[i % COPIES],
+                                     y_pinned[k].data_ptr(), _lib.OUT_BF16, ROWS, IN, OUT, 0)
         if st != 0:
             raise RuntimeError(lib.vx_last_error().decode())
 
@@ -477,6 +515,9 @@ def run_ours(args, world, rank, local):
         if not torch.equal(y_pinned[k], ys[(k + E2E_STREAMS * (E2E_GRAPH_STEPS - 1)) % COPIES].cpu()):
             raise RuntimeError("end-to-end output copy differs from the device output")
     del e2e_graphs
+    torch.cuda.synchronize()
+    for g in lane_gemms:
+        lib.vx_gemm_destroy(g)
 
     clocks = sampler.summary()
     generator = measure_generator(rank, world)
@@ -497,16 +538,26 @@ def run_ours(args, world, rank, local):
                    "out": OUT, "accumulate": "fp32", "weight_copies": COPIES,
                    "l2": f"inputs larger than L2: {COPIES} rotating weight copies "
                          f"({COPIES * WEIGHT_BYTES / 1e6:.0f} MB)",
-                   "launch": f"CUDA graphs of {GRAPH_LAUNCHES} independent products (no programmatic "
-                             f"wait; each its own weight copy and output)",
-                   "plan": {"splits": stream_plan.splits, "blocks_per_split": stream_plan.blocks_per_split,
-                            "variant": stream_plan.variant},
+                   "api": "Bf16Gemm::Linear (vx_gemm_linear_ex, bf16 output) on one stream: the "
+                          "library plans each product itself",
+                   "launch": f"a dependent chain (each product waits for the previous one; programmatic "
+                             f"dependent launch lets its weight stream start early), replayed from CUDA "
+                             f"graphs of up to {GRAPH_LAUNCHES} launches; each product its own weight "
+                             f"copy and output",
+                   "plan": {"variant": plan.variant, "splits": plan.splits,
+                            "blocks_per_split": plan.blocks_per_split,
+                            "kernel": "ProductKernel, whole-reduction CTAs of 48 weight rows (12 warps: "
+                                      "3 groups x 4 ways), mma.sync tile math, no cluster, no scratch"},
+                   "timed_region": "a device-side sleep before the start event keeps host graph "
+                                   "submission out of it",
                    "parallelism": f"replicas x{world}"},
-        "dependent": {"value": dep_value, "unit": "GB/s", "ms_per_step": dep_ms / max(args.steps, 1),
-                      "frac": dep_value / world / peak,
-                      "launch": "each product waits for the previous one (programmatic dependent launch)",
-                      "plan": {"splits": plan.splits, "blocks_per_split": plan.blocks_per_split,
-                               "variant": plan.variant}},
+        "stream": {"value": extra["stream"][1], "unit": "GB/s",
+                   "ms_per_step": extra["stream"][0] / max(args.steps, 1),
+                   "frac": extra["stream"][1] / world / peak,
+                   "launch": "independent products (no programmatic wait: each overlaps the one "
+                             "before), measured stream plan",
+                   "plan": {"splits": stream_plan.splits, "blocks_per_split": stream_plan.blocks_per_split,
+                            "variant": stream_plan.variant}},
         "roofline": {"bound": "hbm", "achieved": achieved, "peak": peak, "unit": "GB/s",
                      "frac": achieved / peak, "traffic": profiled_traffic(),
                      "peak_source": f"{peak_kind} hbm_gbs (copy rate)",
@@ -517,15 +568,16 @@ def run_ours(args, world, rank, local):
         "cpu_baselines": host_baselines,
         "e2e": {"value": e2e_value, "unit": "GB/s", "h2d_bytes_per_step": X_BYTES,
                 "d2h_bytes_per_step": Y_BYTES, "steps": e2e_steps, "streams": E2E_STREAMS,
-                "api": "vx_product_host (default plan): pinned host x staged in and y staged out "
-                       "by SM loads and stores over PCIe every step",
+                "api": "vx_gemm_linear_host (Bf16Gemm::Linear with host buffers, the value's plan): "
+                       "pinned host x staged in and y staged out by SM loads and stores over PCIe "
+                       "every step",
                 "launch": f"one CUDA graph of {E2E_GRAPH_STEPS} steps per stream (the three "
                           f"launches of every step inside), replayed {e2e_reps} times"},
         "sweep": {"rows": sweep, "metric": "GB/s of algorithmic bytes (weights + x + fp32 y) per "
                   "Bf16Gemm::Linear call; err = max |y - exact| / sum |x w| (limit 1e-5)",
                   "launch": "dependent chain over rotating weight copies (more than L2), CUDA graph",
                   "config": "BASELINE config 1"},
-        "gpu_launches": 2 * args.steps,
+        "gpu_launches": args.steps,
         "clocks": clocks,
         **generator,
     }

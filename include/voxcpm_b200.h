@@ -91,9 +91,13 @@ VX_API vx_status vx_bf16_tiles_to_rows(const uint16_t* tiles, size_t rows, size_
 /* ------------------------------------------------------------ products */
 
 /* How a product is split. Replaces WmmaPlan (kernels/wmma_products.hpp:
- * 74-81). `splits` CTAs of one thread-block cluster share each panel of
- * weight rows and reduce on chip, so partial_floats and counters are always
- * 0 (no scratch). `variant` selects the kernel shape. */
+ * 74-81). For the cluster plans (vx_plan_wmma) `splits` CTAs of one
+ * thread-block cluster share each panel of weight rows and reduce on chip,
+ * so partial_floats and counters are 0 (no scratch). For a spread plan
+ * (variant VX_SPREAD_VARIANT, vx_plan_spread) `splits` is the CTA count,
+ * `blocks_per_split` the longest run of (panel, block) units of one CTA, and
+ * partial_floats / counters the split scratch the launch needs.
+ * `variant` selects the kernel shape. */
 typedef struct vx_wmma_plan {
   size_t splits;
   size_t blocks_per_split;
@@ -102,8 +106,11 @@ typedef struct vx_wmma_plan {
   int variant;
 } vx_wmma_plan;
 
-/* Replaces SplitScratch (kernels/wmma_products.hpp:62-68); accepted for
- * interface parity and not used (may be all zero). */
+/* Replaces SplitScratch (kernels/wmma_products.hpp:62-68): fp32 partial
+ * sums and one counter per 128-row panel, owned by the caller. The counters
+ * must be zero before the first launch that uses them; every launch leaves
+ * them zero. Launches that share one scratch must be ordered on one stream
+ * (the reference's rule). Cluster plans ignore it (may be all zero). */
 typedef struct vx_split_scratch {
   float* partials;
   size_t partial_floats;
@@ -118,11 +125,28 @@ typedef struct vx_split_scratch {
 VX_API vx_wmma_plan vx_plan_wmma(size_t rows, size_t in, size_t out,
                           size_t target_waves);
 
+/* The spread plan of a product of `rows` (at most 32) rows in the weight
+ * format `format`: the product's (128-row panel, 32-column block) units cut
+ * evenly over at most one CTA per SM, panels cut between CTAs added in part
+ * order by the CTA that finishes last, through split scratch of
+ * `partial_floats` floats and `counters` counters. splits 0 when the shape is
+ * not served. Extends PlanWmma (kernels/wmma_products.hpp:83-85). */
+#define VX_SPREAD_VARIANT 102
+VX_API vx_wmma_plan vx_plan_spread(int format, size_t rows, size_t in,
+                                   size_t out);
+/* Whether products launched without a plan, with split scratch at hand
+ * (vx_gemm_linear, or vx_wmma_q8 / vx_wmma_bf16 given scratch), take the
+ * spread kernel (default off: in dependent chains it measured slower than
+ * the planner's whole-reduction plans). No reference counterpart. */
+VX_API void vx_set_spread_products(int enabled);
+VX_API int vx_spread_products(void);
+
 /* y[rows][out] (+)= x[rows][in] * W^T for bf16 x and Q8 tiles W, at most
  * 128 rows (the reference's kernel takes 32 per launch; 33..128 run in one
- * launch here), `in` a multiple of 32 (at most 8192). `plan` may be null (planner's
- * choice), `scratch` may be null. Replaces WmmaQ8
- * (kernels/wmma_products.hpp:87-93). */
+ * launch here), `in` a multiple of 32 (at most 8192). `plan` may be null
+ * (the planner's choice: with `scratch` given and large enough, the spread
+ * plan for up to 32 rows; else a cluster plan); `scratch` may be null except
+ * for a spread plan. Replaces WmmaQ8 (kernels/wmma_products.hpp:87-93). */
 VX_API vx_status vx_wmma_q8(const uint16_t* x, const uint8_t* w, float* y,
                      size_t rows, size_t in, size_t out, int accumulate,
                      const vx_wmma_plan* plan, const vx_split_scratch* scratch,
@@ -133,10 +157,11 @@ VX_API vx_status vx_wmma_bf16(const uint16_t* x, const uint16_t* w, float* y,
                        size_t rows, size_t in, size_t out, int accumulate,
                        const vx_wmma_plan* plan,
                        const vx_split_scratch* scratch, cudaStream_t stream);
-/* y (+)= x * W^T for bf16 rows W ([out][in]), at most 32 rows (as the
- * reference's SkinnyGemm), `in` a
- * multiple of 8 (the kernels need a multiple of 32; other sizes return
- * VX_UNSUPPORTED). Replaces SkinnyGemm (kernels/skinny_gemm.hpp:18-24). */
+/* y (+)= x * W^T for bf16 rows W ([out][in]), at most 32 rows, `in` a
+ * multiple of 8 and at most 8192 (the reference's SkinnyGemm contract);
+ * other shapes return VX_UNSUPPORTED. Multiples of 32 run on the skinny
+ * product kernels, other multiples of 8 on the general product (vx_matmul).
+ * Replaces SkinnyGemm (kernels/skinny_gemm.hpp:18-24). */
 VX_API vx_status vx_skinny_gemm(const uint16_t* x, const uint16_t* w, float* y,
                          size_t rows, size_t in, size_t out, int accumulate,
                          cudaStream_t stream);
@@ -494,7 +519,8 @@ VX_API vx_status vx_generator_velocity(vx_generator* generator,
                                        float* velocity);
 /* The DiT part of a step with the conditioning given (host mu, prefix cond,
  * noise): dit_cond, then the Euler/CFG steps (generator.cpp:448-463);
- * writes the latent when `latent` is not null (synchronizing). */
+ * writes the latent when `latent` is not null (synchronizing; then
+ * VX_DEVICE_TIMEOUT when the persistent kernel's launch aborted). */
 VX_API vx_status vx_generator_dit_patch(vx_generator* generator,
                                         const float* mu, const float* cond,
                                         const float* noise, size_t timesteps,
@@ -511,14 +537,24 @@ VX_API vx_status vx_generator_dit_patch(vx_generator* generator,
  * vx_generator_dit_patch or vx_generator_step with the same `timesteps`
  * (else VX_INVALID). The first call on a device looks the array's address up
  * (make that first call before any stream capture). Calls that overlap on
- * the GPU, from any generator, share the array and race. Synchronizes the
- * generator's stream. */
+ * the GPU, from any generator, share the array and race. The inputs are
+ * copied on the generator's own stream, which is not ordered after the
+ * caller's streams: mu, cond and noise must be completely written before the
+ * call (synchronize the stream that produced them). Synchronizes the
+ * generator's stream. Returns VX_DEVICE_TIMEOUT (the latent is not valid)
+ * when one of the kernel's bounded waits gave up and the launch aborted. */
 VX_API vx_status vx_generator_dit_patch_static(vx_generator* generator,
                                                const float* mu,
                                                const float* cond,
                                                const float* noise,
                                                size_t timesteps, float cfg,
                                                float* latent);
+/* Test hook: every later persistent DiT launch of this process first makes
+ * one thread wait for a device word that nothing sets, for at most
+ * `limit_ns` nanoseconds, then abort the launch as a real time-out would, so
+ * tests can check that the entries report VX_DEVICE_TIMEOUT without a GPU
+ * fault (0: off, the default). No reference counterpart. */
+VX_API void vx_set_dit_stall_for_tests(uint64_t limit_ns);
 /* Replays the last DiT patch (its captured graph) on the generator's stream
  * without synchronizing (benchmarks). */
 VX_API vx_status vx_generator_replay_dit_patch(vx_generator* generator);
@@ -708,12 +744,40 @@ VX_API vx_status vx_random_bf16(uint64_t seed, uint64_t tensor, size_t count,
 typedef struct vx_gemm vx_gemm;
 VX_API vx_gemm* vx_gemm_create(cudaStream_t stream);
 VX_API void vx_gemm_destroy(vx_gemm* gemm);
-/* y[rows][out] (+)= x[rows][in] * w[out][in]^T, float32 y. Rows beyond 32
- * run in chunks of 32 (every chunk re-reads W). Replaces Bf16Gemm::Linear
- * (gemm.hpp:51-58, gemm.cpp:259-313). */
+/* y[rows][out] (+)= x[rows][in] * w[out][in]^T, float32 y. Up to 128 rows
+ * run in one launch on the planner's plan (the spread product through the
+ * gemm's own split scratch when vx_set_spread_products is on), more in
+ * chunks of 128.
+ * bf16 rows with `in` not a multiple of 32 run on the general product, as
+ * the reference's LinearRows falls back to Matmul. Replaces Bf16Gemm::Linear
+ * (gemm.hpp:51-58, gemm.cpp:259-336). vx_gemm_create allocates the scratch
+ * (about 5 MB); where it cannot (no device), the gemm serves every shape on
+ * the cluster plans, which need none. */
 VX_API vx_status vx_gemm_linear(vx_gemm* gemm, const uint16_t* x, int format,
                          const void* w, float* y, size_t rows, size_t in,
                          size_t out, int accumulate);
+
+/* vx_gemm_linear with the output type `out_dtype` (VX_OUT_F32 or
+ * VX_OUT_BF16: bf16 of the fp32 sum, BASELINE config 0's epilogue) and
+ * flags (VX_PRODUCT_ACCUMULATE). bf16 output needs `in` a multiple of 32.
+ * Extends Bf16Gemm::Linear (gemm.hpp:51-58). */
+VX_API vx_status vx_gemm_linear_ex(vx_gemm* gemm, const uint16_t* x, int format,
+                                   const void* w, void* y, int out_dtype,
+                                   size_t rows, size_t in, size_t out,
+                                   unsigned flags);
+
+/* vx_gemm_linear_ex with activations and output in page-locked host memory
+ * (as vx_product_host): x_host is staged into x_dev (rows * in bf16 of
+ * device memory), the product writes y_dev (read first when accumulating)
+ * and y_dev is staged into y_host, all on the gemm's stream by SM loads and
+ * stores. Replaces the upload, Bf16Gemm::Linear and download a caller of the
+ * reference's products makes (tests/products_test.cpp:100-110 around
+ * gemm.hpp:51-58). */
+VX_API vx_status vx_gemm_linear_host(vx_gemm* gemm, const uint16_t* x_host,
+                                     uint16_t* x_dev, int format, const void* w,
+                                     void* y_dev, void* y_host, int out_dtype,
+                                     size_t rows, size_t in, size_t out,
+                                     unsigned flags);
 
 /* A column-major (BLAS) product C[m][n] (+)= op(A)[m][k] * op(B)[k][n],
  * optionally strided-batched (strides in elements, batch b at a + b *

@@ -57,7 +57,7 @@ def test_host_queries():
 
 
 def test_planner():
-    # Every plan covers the reduction with nonempty splits of at most 1024
+    # Every plan covers the reduction with nonempty splits of at most 2048
     # columns and at most 8 CTAs per cluster.
     for rows in (1, 2, 5, 8, 11, 22, 32):
         for columns, out in ((1024, 2560), (2048, 1024), (4096, 1024), (1024, 8192), (6144, 2048),
@@ -66,12 +66,37 @@ def test_planner():
                 plan = K.PlanWmma(rows, columns, out, target)
                 kb = columns // 32
                 assert 1 <= plan.splits <= 8
-                assert plan.blocks_per_split * 32 <= 1024
+                assert plan.blocks_per_split * 32 <= 2048
                 assert plan.splits * plan.blocks_per_split >= kb
                 assert (plan.splits - 1) * plan.blocks_per_split < kb
                 assert plan.partial_floats == 0 and plan.counters == 0
     assert K.PlanWmma(22, 2048, 6144, 1).splits == 2  # fewest allowed splits
     assert K.PlanWmma(22, 48, 16).splits == 0          # in not a multiple of 32
+
+
+def test_spread_planner():
+    """Spread plans (host only; without a device the SM count is B200's 148):
+    one CTA per panel at least, at most one per SM, every run at most one
+    panel's reduction, scratch for two ends of every CTA's run and one
+    counter per 128-row panel."""
+    for fmt in (_lib.WEIGHTS_BF16, _lib.WEIGHTS_BF16_TILES, _lib.WEIGHTS_Q8_TILES):
+        for rows in (1, 5, 22, 32):
+            for columns, out in ((1024, 2560), (2048, 1024), (4096, 1024), (1024, 8192), (6144, 2048),
+                                 (2048, 6144), (2048, 12288), (64, 1024), (2048, 2), (1024, 72)):
+                plan = K.PlanSpread(fmt, rows, columns, out)
+                kb = columns // 32
+                panels = -(-out // 128)
+                assert plan.variant == _lib.SPREAD_VARIANT, (fmt, rows, columns, out)
+                assert panels <= plan.splits <= 148
+                assert plan.blocks_per_split == -(-(panels * kb) // plan.splits) <= kb
+                assert plan.counters == panels
+                assert plan.partial_floats == plan.splits * 2 * 8 * 32 * 16
+    # Config 0: 48 panels x 64 blocks over 148 CTAs, runs of 21 units.
+    plan = K.PlanSpread(_lib.WEIGHTS_Q8_TILES, 22, 2048, 6144)
+    assert (plan.splits, plan.blocks_per_split) == (148, 21)
+    assert K.PlanSpread(_lib.WEIGHTS_Q8_TILES, 33, 2048, 6144).splits == 0  # more than 32 rows
+    assert K.PlanSpread(_lib.WEIGHTS_Q8_TILES, 22, 48, 16).splits == 0      # in not a multiple of 32
+    assert K.PlanSpread(7, 22, 2048, 6144).splits == 0                      # unknown format
 
 
 def test_library_weights_match_the_oracle_restatement():

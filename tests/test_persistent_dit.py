@@ -186,3 +186,30 @@ def test_persistent_stacks_match_per_kernel_steps(cuda, cache_type):
     assert DeviceError() == 0
     fast.close()
     slow.close()
+
+
+def test_aborted_patch_reports_device_timeout(cuda):
+    """The regular DiT patch entry reports a launch whose bounded wait ran
+    out (the stall test hook: one thread waits 20 ms for a word nothing
+    sets, then aborts the launch) as VX_DEVICE_TIMEOUT; the error state is
+    cleared and the next patch gives the same latent as before."""
+    c = dit_config()
+    gen = Generator(c, seed=11)
+    gen.SetGraphs(False)  # the hook is read at launch, not baked into a graph
+    rng = np.random.default_rng(8)
+    mu = rng.normal(0, 1, 2 * c.dit.hidden).astype(np.float32)
+    cond = rng.normal(0, 1, (c.patch_size, c.feat_dim)).astype(np.float32)
+    noise = rng.normal(0, 1, (c.patch_size, c.feat_dim)).astype(np.float32)
+    before = gen.DitPatch(mu, cond, noise, 10, 2.0)
+    lib = _lib.load()
+    try:
+        lib.vx_set_dit_stall_for_tests(20_000_000)
+        with pytest.raises(_lib.VxError) as failure:
+            gen.DitPatch(mu, cond, noise, 10, 2.0)
+    finally:
+        lib.vx_set_dit_stall_for_tests(0)
+    assert failure.value.status == _lib.VX_DEVICE_TIMEOUT
+    assert DeviceError() == 0
+    after = gen.DitPatch(mu, cond, noise, 10, 2.0)
+    assert np.array_equal(after, before)
+    gen.close()

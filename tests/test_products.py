@@ -141,7 +141,7 @@ def test_every_variant(cuda):
     y = torch.empty(rows, out, dtype=torch.float32, device="cuda")
     ran = {fmt: 0 for fmt in (_lib.WEIGHTS_Q8_TILES, _lib.WEIGHTS_BF16_TILES, _lib.WEIGHTS_BF16)}
     for variant in range(len(K.ProductVariants())):
-        for splits in (2, 3, 4, 8):
+        for splits in (1, 2, 3, 4, 8):
             bps = -(-columns // 32 // splits)
             if -(-(columns // 32) // bps) != splits:
                 continue

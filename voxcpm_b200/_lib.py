@@ -30,6 +30,8 @@ OUT_BF16 = 1
 PRODUCT_ACCUMULATE = 1
 PRODUCT_INDEPENDENT = 2
 
+SPREAD_VARIANT = 102
+
 CACHE_F32 = 0
 CACHE_BF16 = 1
 
@@ -244,6 +246,7 @@ SIGNATURES: dict[str, tuple] = {
     "vx_generator_dit_patch": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_float, c_void_p]),
     "vx_generator_dit_patch_static": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_float, c_void_p]),
     "vx_generator_replay_dit_patch": (c_int, [c_void_p]),
+    "vx_set_dit_stall_for_tests": (None, [c_uint64]),
     "vx_generator_state": (c_int, [c_void_p, c_char_p, c_void_p, c_size_t]),
     "vx_generator_set_state": (c_int, [c_void_p, c_char_p, c_void_p, c_size_t]),
     "vx_generator_set_graphs": (c_int, [c_void_p, c_int]),
@@ -278,11 +281,23 @@ SIGNATURES: dict[str, tuple] = {
     "vx_half_to_bf16": (c_int, [c_void_p, c_void_p, c_size_t, c_void_p]),
     "vx_float_to_bf16": (c_int, [c_void_p, c_void_p, c_size_t, c_void_p]),
     "vx_q8_0_to_bf16": (c_int, [c_void_p, c_void_p, c_size_t, c_void_p]),
+    "vx_plan_spread": (WmmaPlan, [c_int, c_size_t, c_size_t, c_size_t]),
+    "vx_set_spread_products": (None, [c_int]),
+    "vx_spread_products": (c_int, []),
     "vx_gemm_create": (c_void_p, [c_void_p]),
     "vx_gemm_destroy": (None, [c_void_p]),
     "vx_gemm_linear": (
         c_int,
         [c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_size_t, c_size_t, c_size_t, c_int],
+    ),
+    "vx_gemm_linear_ex": (
+        c_int,
+        [c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_int, c_size_t, c_size_t, c_size_t, c_uint],
+    ),
+    "vx_gemm_linear_host": (
+        c_int,
+        [c_void_p, c_void_p, c_void_p, c_int, c_void_p, c_void_p, c_void_p, c_int, c_size_t, c_size_t,
+         c_size_t, c_uint],
     ),
     "vx_matmul": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),
     "vx_gemm_matmul": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_void_p, c_void_p]),

@@ -53,6 +53,8 @@ vx_status Guard(vx_generator* g, const char* what, F&& body) {
     return vx::Fail(vx::kInvalid, std::string(what) + ": null generator");
   try {
     body(*g->impl);
+  } catch (const vx::DeviceTimeout& e) {
+    return vx::Fail(vx::kDeviceTimeout, std::string(what) + ": " + e.what());
   } catch (const std::invalid_argument& e) {
     return vx::Fail(vx::kInvalid, std::string(what) + ": " + e.what());
   } catch (const std::logic_error& e) {
@@ -252,6 +254,10 @@ vx_status vx_generator_dit_patch_static(vx_generator* generator,
                  g.DitPatchStatic(mu, cond, noise, static_cast<int>(timesteps),
                                   cfg, latent);
                });
+}
+
+void vx_set_dit_stall_for_tests(uint64_t limit_ns) {
+  vx::SetDitStall(limit_ns);
 }
 
 vx_status vx_generator_replay_dit_patch(vx_generator* generator) {

@@ -1506,6 +1506,13 @@ void Generator::DitPatch(const float* mu, const float* cond,
     CheckCuda(cudaMemcpyAsync(latent, x_, values * sizeof(float),
                               cudaMemcpyDeviceToHost, stream_), "latent");
     CheckCuda(cudaStreamSynchronize(stream_), "patch");
+    if (persistent_ && dit_evaluations_ > 0) {
+      bool aborted = false;
+      Check(DitLaunchAborted(dit_params_, stream_, &aborted),
+            "persistent DiT patch");
+      if (aborted)
+        ThrowAborted("persistent DiT patch");
+    }
   }
 }
 
@@ -1540,6 +1547,22 @@ void Generator::DitPatchStatic(const float* mu, const float* cond,
   CheckCuda(cudaMemcpyAsync(latent, x_, values * sizeof(float),
                             cudaMemcpyDeviceToDevice, stream_), "latent");
   CheckCuda(cudaStreamSynchronize(stream_), "patch");
+  if (dit_evaluations_ > 0) {
+    bool aborted = false;
+    Check(DitStaticLaunchAborted(stream_, &aborted),
+          "allocation-free DiT patch");
+    if (aborted)
+      ThrowAborted("allocation-free DiT patch");
+  }
+}
+
+void Generator::ThrowAborted(const char* what) {
+  unsigned bits = 0;
+  (void)ReadDeviceError(&bits);  // reads and clears the device error word
+  throw DeviceTimeout(std::string(what) +
+                      ": a bounded device wait gave up and the launch "
+                      "aborted (device error bits " +
+                      std::to_string(bits) + "); the latent is not valid");
 }
 
 void Generator::ReplayDitPatch() {

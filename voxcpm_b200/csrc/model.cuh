@@ -13,6 +13,7 @@
 #include <map>
 #include <tuple>
 #include <memory>
+#include <stdexcept>
 #include <string>
 #include <vector>
 
@@ -168,6 +169,13 @@ int ForwardStack(const StackWeights& stack, const float* rope,
 class DeviceArena;
 class ModelFiles;
 
+/// A persistent kernel's bounded wait gave up and the launch aborted: its
+/// outputs are not valid (the C ABI returns VX_DEVICE_TIMEOUT).
+class DeviceTimeout : public std::runtime_error {
+ public:
+  using std::runtime_error::runtime_error;
+};
+
 /// The LM caches of one GeneratorBatch slot: slot `slot` of slot-major caches
 /// (KvCache with slots) that outlive the generator.
 struct SlotCaches {
@@ -252,6 +260,8 @@ class Generator {
   friend class GeneratorBatch;
   Generator() = default;
   void Check(int status, const char* what);
+  /// Reads and clears the device error word and throws DeviceTimeout.
+  [[noreturn]] void ThrowAborted(const char* what);
   /// StepBody's parts: the stop logits, mu and the DiT conditioning from
   /// the LM states, and the patch's noise into x (generator.cpp:424-447);
   /// the latent, stop logits and next prefix out (:465-476); both LMs

@@ -11,6 +11,7 @@
 #include "persistent_dit.cuh"
 
 #include <cmath>
+#include <atomic>
 #include <mutex>
 #include <string>
 
@@ -55,6 +56,7 @@ constexpr int kGroups = kHidden / 16;               // 64
 // groups folded; the count of assembled evaluations; per chunk of the
 // SwiGLU activation the count of gate/up units done. One thread per CTA
 // polls a counter, so the polling load on L2 stays small.
+constexpr int kSyncNever = 8;       // set by no CTA (the stall test hook)
 constexpr int kSyncQ = 32;          // [16]
 constexpr int kSyncKv = 48;         // [2]
 constexpr int kSyncAtt = 64;        // [2]
@@ -978,6 +980,17 @@ __global__ void __launch_bounds__(kThreads, 1)
               pub_empty, c);
     return;
   }
+  if (p.stall_limit_ns != 0 && blockIdx.x == 0 && threadIdx.x == 0) {
+    // The test hook: a bounded wait that runs out, then the abort every
+    // other wait of the launch watches for.
+    const std::uint64_t start = GlobalTimerNs();
+    while (LoadAcquire(p.sync + kSyncNever) == 0u) {
+      if (GlobalTimerNs() - start > p.stall_limit_ns) {
+        Abort(c, kErrBarrierWait);
+        break;
+      }
+    }
+  }
   Consume<kFormat>(p, smem, c);
   // Teardown: neither CTA of the pair exits while its peer may still write
   // into its shared memory. Each signals the other, then waits (bounded)
@@ -1108,7 +1121,66 @@ namespace {
 constexpr std::size_t kDitStaticScratchBytes = std::size_t{1} << 20;
 static __device__ __align__(256) unsigned char g_dit_static_scratch[kDitStaticScratchBytes];
 
+/// The static array's device address on the current device, looked up once
+/// per device (with that device current) on the first call there.
+int StaticScratchAddress(void** scratch) {
+  int device = 0;
+  if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= 64)
+    return Fail(kCudaError, "allocation-free DiT patch: no current device");
+  static std::mutex mutex;
+  static void* addresses[64] = {};
+  std::lock_guard<std::mutex> lock(mutex);
+  if (addresses[device] == nullptr) {
+    void* address = nullptr;
+    const cudaError_t error =
+        cudaGetSymbolAddress(&address, g_dit_static_scratch);
+    if (error != cudaSuccess || address == nullptr)
+      return Fail(kCudaError,
+                  std::string("allocation-free DiT patch: static scratch "
+                              "address: ") +
+                      cudaGetErrorString(error));
+    addresses[device] = address;
+  }
+  *scratch = addresses[device];
+  return kOk;
+}
+
+std::atomic<std::uint64_t> g_dit_stall_ns{0};
+
 }  // namespace
+
+void SetDitStall(std::uint64_t limit_ns) { g_dit_stall_ns = limit_ns; }
+
+int DitLaunchAborted(const DitPatchParams& params, cudaStream_t stream,
+                     bool* aborted) {
+  *aborted = false;
+  if (params.sync == nullptr)
+    return kOk;
+  unsigned word = 0;
+  if (cudaMemcpyAsync(&word, params.sync + kSyncAbort, sizeof(word),
+                      cudaMemcpyDeviceToHost, stream) != cudaSuccess ||
+      cudaStreamSynchronize(stream) != cudaSuccess)
+    return Fail(kCudaError, "persistent DiT: reading the abort word");
+  if (word != 0) {
+    *aborted = true;
+    if (cudaMemsetAsync(params.sync + kSyncAbort, 0, sizeof(unsigned),
+                        stream) != cudaSuccess ||
+        cudaStreamSynchronize(stream) != cudaSuccess)
+      return Fail(kCudaError, "persistent DiT: clearing the abort word");
+  }
+  return kOk;
+}
+
+int DitStaticLaunchAborted(cudaStream_t stream, bool* aborted) {
+  *aborted = false;
+  void* scratch = nullptr;
+  const int status = StaticScratchAddress(&scratch);
+  if (status != kOk)
+    return status;
+  DitPatchParams p;
+  DitWorkLayout(scratch, p);
+  return DitLaunchAborted(p, stream, aborted);
+}
 
 int LaunchDitPatchStatic(const DitPatchParams& base, cudaStream_t stream) {
   if (DitWorkBytes() > kDitStaticScratchBytes)
@@ -1117,29 +1189,10 @@ int LaunchDitPatchStatic(const DitPatchParams& base, cudaStream_t stream) {
                     std::to_string(DitWorkBytes()) + " bytes, more than the " +
                     std::to_string(kDitStaticScratchBytes) +
                     "-byte static scratch");
-  int device = 0;
-  if (cudaGetDevice(&device) != cudaSuccess || device < 0 || device >= 64)
-    return Fail(kCudaError, "allocation-free DiT patch: no current device");
-  // The array's device address, looked up once per device (with that device
-  // current) on the first call there.
-  static std::mutex mutex;
-  static void* addresses[64] = {};
   void* scratch = nullptr;
-  {
-    std::lock_guard<std::mutex> lock(mutex);
-    if (addresses[device] == nullptr) {
-      void* address = nullptr;
-      const cudaError_t error =
-          cudaGetSymbolAddress(&address, g_dit_static_scratch);
-      if (error != cudaSuccess || address == nullptr)
-        return Fail(kCudaError,
-                    std::string("allocation-free DiT patch: static scratch "
-                                "address: ") +
-                        cudaGetErrorString(error));
-      addresses[device] = address;
-    }
-    scratch = addresses[device];
-  }
+  const int status = StaticScratchAddress(&scratch);
+  if (status != kOk)
+    return status;
   DitPatchParams p = base;
   DitWorkLayout(scratch, p);  // the sync words are zeroed by LaunchDitPatch
   return LaunchDitPatch(p, stream);
@@ -1171,8 +1224,11 @@ int LaunchDitPatch(const DitPatchParams& p, cudaStream_t stream) {
   cudaLaunchAttribute attribute[2];
   const cudaLaunchConfig_t config =
       DitConfig(q8, static_cast<unsigned>(ctas), stream, attribute);
-  return FromCuda(cudaLaunchKernelEx(&config, DitKernel(q8), p, error_word),
-                  "persistent DiT launch");
+  DitPatchParams launch = p;
+  launch.stall_limit_ns = g_dit_stall_ns;
+  return FromCuda(
+      cudaLaunchKernelEx(&config, DitKernel(q8), launch, error_word),
+      "persistent DiT launch");
 }
 
 }  // namespace vx

@@ -83,7 +83,21 @@ struct DitPatchParams {
   std::uint16_t* att = nullptr; // [22][2048]
   std::uint16_t* act = nullptr; // [22][4096]
   unsigned* sync = nullptr;     // [kDitSyncWords]
+  // Test hook (0: off): CTA 0 first waits for a sync word that no CTA ever
+  // sets, gives up after this many nanoseconds and aborts the launch, so a
+  // test can run the bounded-wait error path without a GPU fault.
+  std::uint64_t stall_limit_ns = 0;
 };
+
+/// The test hook above for every later launch of this process (0: off).
+void SetDitStall(std::uint64_t limit_ns);
+/// Whether the last launch that used `params.sync` aborted (sync word 0 set
+/// by a CTA whose bounded wait gave up); clears the word. Synchronizes
+/// `stream` first.
+int DitLaunchAborted(const DitPatchParams& params, cudaStream_t stream,
+                     bool* aborted);
+/// The same for the allocation-free launch's sync words.
+int DitStaticLaunchAborted(cudaStream_t stream, bool* aborted);
 
 /// Device bytes of the work buffers above (hidden .. sync), laid out
 /// in that order with 256-byte alignment by DitWorkLayout.

@@ -106,6 +106,15 @@ constexpr VariantShape kVariants[] = {
     // half the dequantization instructions per tile.
     {24, 1, 1, 8, 1, true},  // 14
     {4, 2, 1, 4, 2},   // 15: 64 rows, 8 warps (2 ways), for 33..128 rows
+    // Whole-reduction CTAs for dependent launches: a few groups per CTA,
+    // split over the reduction by ways, so one launch fills the SMs without
+    // a cluster and without scratch.
+    {3, 4, 1, 8, 2},   // 16: 48 rows, 12 warps (4 ways)
+    {2, 4, 1, 8, 2},   // 17: 32 rows, 8 warps (4 ways)
+    {3, 2, 1, 8, 4},   // 18: 48 rows, 6 warps (2 ways)
+    {4, 4, 1, 8, 2},   // 19: 64 rows, 16 warps (4 ways)
+    {2, 4, 1, 4, 2},   // 20: 32 rows, 8 warps (4 ways), 4-block stages
+    {1, 4, 1, 8, 2},   // 21: 16 rows, 4 warps (4 ways)
 };
 constexpr int kNumVariants = sizeof(kVariants) / sizeof(kVariants[0]);
 // The cost model chooses among the first eight shapes only: their plans fit
@@ -548,7 +557,7 @@ struct VariantRow {
 
 template <int kFormat, int kNTiles>
 using Row = VariantRow<kFormat, kNTiles, 0, 1, 2, 3, 4, 5, 6, 7, 8, 9, 10, 11,
-                       12, 13, 14, 15>;
+                       12, 13, 14, 15, 16, 17, 18, 19, 20, 21>;
 
 /// Row classes of the measured plan tables: 1, 2..8, 9..32, 33..128.
 int RowsClass(std::size_t rows) {
@@ -642,31 +651,93 @@ struct MeasuredPlan {
   int splits;
 };
 constexpr MeasuredPlan kMeasuredPlans[] = {
+    // Whole-reduction CTAs (variants 16-21; clusters only for reductions
+    // beyond 2048 columns), measured on B200 in dependent chains of CUDA
+    // graph launches over rotating weight copies larger than L2, at 1, 8 and
+    // 22 rows for classes 0, 1 and 2; in comments the time and the cluster
+    // plan's time before them.
+    // Q8_0 tiles, one row.
+    {WeightFormat::kQ8Tiles, 0, 1024, 1024, 21, 1},  // 2.24 us (3.34)
+    {WeightFormat::kQ8Tiles, 0, 1024, 2560, 16, 1},  // 2.59 us (4.38)
+    {WeightFormat::kQ8Tiles, 0, 1024, 3072, 16, 1},  // 2.61 us (4.43)
+    {WeightFormat::kQ8Tiles, 0, 1024, 8192, 17, 1},  // 3.39 us (5.37)
+    {WeightFormat::kQ8Tiles, 0, 2048, 1024, 21, 1},  // 2.87 us (3.83)
+    {WeightFormat::kQ8Tiles, 0, 2048, 2048, 21, 1},  // 3.15 us (4.43)
+    {WeightFormat::kQ8Tiles, 0, 2048, 2560, 16, 1},  // 3.69 us (4.44)
+    {WeightFormat::kQ8Tiles, 0, 2048, 6144, 21, 1},  // 4.52 us (9.93)
+    {WeightFormat::kQ8Tiles, 0, 2048, 12288, 20, 1},  // 7.02 us (10.33)
+    {WeightFormat::kQ8Tiles, 0, 4096, 1024, 17, 2},  // 4.20 us (5.05)
+    {WeightFormat::kQ8Tiles, 0, 6144, 2048, 17, 3},  // 5.83 us (7.47)
+    // Q8_0 tiles, 2..8 rows.
+    {WeightFormat::kQ8Tiles, 1, 1024, 1024, 21, 1},  // 2.46 us (4.10)
+    {WeightFormat::kQ8Tiles, 1, 1024, 2560, 16, 1},  // 2.94 us (4.27)
+    {WeightFormat::kQ8Tiles, 1, 1024, 3072, 16, 1},  // 3.06 us (4.90)
+    {WeightFormat::kQ8Tiles, 1, 1024, 8192, 17, 1},  // 3.60 us (5.39)
+    {WeightFormat::kQ8Tiles, 1, 2048, 1024, 21, 1},  // 3.14 us (3.99)
+    {WeightFormat::kQ8Tiles, 1, 2048, 2048, 16, 1},  // 4.11 us (5.39)
+    {WeightFormat::kQ8Tiles, 1, 2048, 2560, 16, 1},  // 4.03 us (5.75)
+    {WeightFormat::kQ8Tiles, 1, 2048, 6144, 21, 1},  // 4.93 us (10.11)
+    {WeightFormat::kQ8Tiles, 1, 2048, 12288, 20, 1},  // 7.47 us (15.97)
+    {WeightFormat::kQ8Tiles, 1, 4096, 1024, 17, 2},  // 4.68 us (5.66)
+    {WeightFormat::kQ8Tiles, 1, 6144, 2048, 17, 3},  // 6.24 us (7.93)
+    // Q8_0 tiles, 9..32 rows.
+    {WeightFormat::kQ8Tiles, 2, 1024, 1024, 21, 1},  // 3.58 us (5.57)
+    {WeightFormat::kQ8Tiles, 2, 1024, 2560, 21, 1},  // 3.74 us (5.41)
+    {WeightFormat::kQ8Tiles, 2, 1024, 3072, 21, 1},  // 3.79 us (6.99)
+    {WeightFormat::kQ8Tiles, 2, 1024, 8192, 20, 1},  // 5.38 us (7.27)
+    {WeightFormat::kQ8Tiles, 2, 2048, 1024, 21, 1},  // 4.16 us (6.06)
+    {WeightFormat::kQ8Tiles, 2, 2048, 2048, 21, 1},  // 4.35 us (7.40)
+    {WeightFormat::kQ8Tiles, 2, 2048, 2560, 17, 1},  // 5.32 us (8.05)
+    {WeightFormat::kQ8Tiles, 2, 2048, 6144, 16, 1},  // 6.95 us (8.41)
+    {WeightFormat::kQ8Tiles, 2, 2048, 12288, 16, 1},  // 13.74 us (21.28)
+    {WeightFormat::kQ8Tiles, 2, 4096, 1024, 21, 2},  // 5.34 us (7.43)
+    {WeightFormat::kQ8Tiles, 2, 6144, 2048, 20, 4},  // 8.03 us (11.59)
+    // bf16 rows, one row.
+    {WeightFormat::kBf16, 0, 1024, 1024, 21, 1},  // 1.91 us (3.17)
+    {WeightFormat::kBf16, 0, 1024, 2560, 21, 1},  // 2.42 us (5.44)
+    {WeightFormat::kBf16, 0, 1024, 3072, 21, 1},  // 2.53 us (8.72)
+    {WeightFormat::kBf16, 0, 1024, 8192, 20, 1},  // 4.39 us (6.75)
+    {WeightFormat::kBf16, 0, 2048, 1024, 21, 1},  // 2.35 us (5.02)
+    {WeightFormat::kBf16, 0, 2048, 2048, 21, 1},  // 2.51 us (5.91)
+    {WeightFormat::kBf16, 0, 2048, 2560, 21, 1},  // 3.35 us (5.54)
+    {WeightFormat::kBf16, 0, 2048, 6144, 20, 1},  // 6.38 us (17.53)
+    {WeightFormat::kBf16, 0, 2048, 12288, 21, 1},  // 11.83 us (17.91)
+    {WeightFormat::kBf16, 0, 4096, 1024, 17, 2},  // 3.53 us (9.54)
+    {WeightFormat::kBf16, 0, 6144, 2048, 20, 4},  // 7.30 us (18.87)
+    // bf16 rows, 2..8 rows.
+    {WeightFormat::kBf16, 1, 1024, 1024, 21, 1},  // 2.33 us (3.59)
+    {WeightFormat::kBf16, 1, 1024, 2560, 21, 1},  // 2.57 us (5.59)
+    {WeightFormat::kBf16, 1, 1024, 3072, 21, 1},  // 2.62 us (9.11)
+    {WeightFormat::kBf16, 1, 1024, 8192, 20, 1},  // 4.50 us (6.89)
+    {WeightFormat::kBf16, 1, 2048, 1024, 21, 1},  // 2.86 us (5.22)
+    {WeightFormat::kBf16, 1, 2048, 2048, 17, 1},  // 3.17 us (6.03)
+    {WeightFormat::kBf16, 1, 2048, 2560, 21, 1},  // 3.53 us (6.83)
+    {WeightFormat::kBf16, 1, 2048, 6144, 20, 1},  // 6.65 us (17.98)
+    {WeightFormat::kBf16, 1, 2048, 12288, 21, 1},  // 12.63 us (32.36)
+    {WeightFormat::kBf16, 1, 4096, 1024, 17, 2},  // 3.96 us (9.94)
+    {WeightFormat::kBf16, 1, 6144, 2048, 20, 4},  // 7.38 us (19.17)
+    // bf16 rows, 9..32 rows.
+    {WeightFormat::kBf16, 2, 1024, 1024, 21, 1},  // 3.20 us (4.88)
+    {WeightFormat::kBf16, 2, 1024, 2560, 17, 1},  // 3.88 us (6.99)
+    {WeightFormat::kBf16, 2, 1024, 3072, 17, 1},  // 4.00 us (11.51)
+    {WeightFormat::kBf16, 2, 1024, 8192, 17, 1},  // 8.27 us (8.67)
+    {WeightFormat::kBf16, 2, 2048, 1024, 21, 1},  // 3.99 us (6.83)
+    {WeightFormat::kBf16, 2, 2048, 2048, 21, 1},  // 4.86 us (7.45)
+    {WeightFormat::kBf16, 2, 2048, 2560, 20, 1},  // 6.81 us (8.39)
+    {WeightFormat::kBf16, 2, 2048, 6144, 20, 1},  // 13.65 us (14.83)
+    {WeightFormat::kBf16, 2, 2048, 12288, 20, 1},  // 21.74 us (39.84)
+    {WeightFormat::kBf16, 2, 4096, 1024, 21, 2},  // 5.86 us (12.99)
+    {WeightFormat::kBf16, 2, 6144, 2048, 17, 4},  // 13.84 us (24.31)
+    // Earlier measurements (shapes not re-measured).
     // Q8_0 tiles, one row (LM, residual LM, FSQ, projections).
-    {WeightFormat::kQ8Tiles, 0, 2048, 2560, 3, 5},
-    {WeightFormat::kQ8Tiles, 0, 2048, 2048, 3, 7},
-    {WeightFormat::kQ8Tiles, 0, 2048, 12288, 0, 2},
-    {WeightFormat::kQ8Tiles, 0, 6144, 2048, 7, 8},
     {WeightFormat::kQ8Tiles, 0, 2048, 512, 7, 8},
     {WeightFormat::kQ8Tiles, 0, 512, 2048, 3, 1},
     {WeightFormat::kQ8Tiles, 0, 4096, 2048, 3, 8},
-    {WeightFormat::kQ8Tiles, 0, 2048, 1024, 3, 5},
     {WeightFormat::kQ8Tiles, 0, 2048, 2, 7, 5},
-    {WeightFormat::kQ8Tiles, 0, 1024, 1024, 3, 5},
     {WeightFormat::kQ8Tiles, 0, 1024, 2048, 3, 5},
     // Q8_0 tiles, 2..8 rows (encoder of a patch, DiT in/out).
-    {WeightFormat::kQ8Tiles, 1, 1024, 2560, 7, 5},
-    {WeightFormat::kQ8Tiles, 1, 2048, 1024, 3, 5},
-    {WeightFormat::kQ8Tiles, 1, 1024, 8192, 7, 2},
-    {WeightFormat::kQ8Tiles, 1, 4096, 1024, 7, 6},
     {WeightFormat::kQ8Tiles, 1, 64, 1024, 1, 1},
     {WeightFormat::kQ8Tiles, 1, 1024, 64, 4, 5},
-    // Q8_0 tiles, 9..32 rows (the DiT's 22 rows, benchmark config 0).
-    {WeightFormat::kQ8Tiles, 2, 2048, 6144, 1, 4},
-    {WeightFormat::kQ8Tiles, 2, 1024, 2560, 7, 2},
-    {WeightFormat::kQ8Tiles, 2, 2048, 1024, 3, 7},
-    {WeightFormat::kQ8Tiles, 2, 1024, 8192, 7, 2},
-    {WeightFormat::kQ8Tiles, 2, 4096, 1024, 3, 8},
     // Q8_0 tiles, 33..128 rows (the DiT's rows of batched slots): variant
     // 15, two ways of four warps over 64-row panels. Dependent chains, us
     // at 48 / 128 rows against the plans before: 1024 -> 2560 7.7 / 13.5
@@ -678,9 +749,6 @@ constexpr MeasuredPlan kMeasuredPlans[] = {
     {WeightFormat::kQ8Tiles, 3, 4096, 1024, 15, 6},
     // bf16 tiles and rows.
     {WeightFormat::kBf16Tiles, 2, 2048, 6144, 0, 2},
-    {WeightFormat::kBf16, 2, 2048, 6144, 1, 4},
-    {WeightFormat::kBf16, 0, 2048, 2560, 0, 4},
-    {WeightFormat::kBf16, 0, 2048, 12288, 1, 2},
 };
 
 // Measured plans for streams of independent launches (PRODUCT_INDEPENDENT
@@ -738,9 +806,8 @@ ProductPlan PlanProduct(WeightFormat format, std::size_t rows, std::size_t in,
         continue;
       const int bps = (k_blocks + m.splits - 1) / m.splits;
       const int ntiles = TilesFor(rows);
-      // Plans measured at 33..128 rows were measured up to the launch limit.
-      const std::size_t limit =
-          rows_class == 3 ? kMaxProductSmem : kPlannedProductSmem;
+      // Measured plans were measured up to the launch limit.
+      const std::size_t limit = kMaxProductSmem;
       if ((k_blocks + bps - 1) / bps != m.splits ||
           bps * kTileColumns > kMaxSliceColumns ||
           FootprintOf(static_cast<int>(format), m.variant, ntiles, bps).smem >
@@ -839,7 +906,7 @@ int LaunchProduct(WeightFormat format, const std::uint16_t* x, const void* w,
                   float* y, std::uint16_t* y_bf16, std::size_t rows,
                   std::size_t in, std::size_t out, bool accumulate,
                   const ProductPlan* plan_in, cudaStream_t stream,
-                  bool independent) {
+                  bool independent, const SplitScratch* scratch) {
   if (rows == 0 || rows > kMaxProductRows || in == 0 || out == 0 ||
       in % kTileColumns != 0)
     return kUnsupported;
@@ -857,6 +924,22 @@ int LaunchProduct(WeightFormat format, const std::uint16_t* x, const void* w,
     plan = *plan_in;
   else if (independent)
     plan = StreamPlan(format, rows, in, out);
+  if (plan.variant < 0 && scratch != nullptr &&
+      SpreadProductPays(format, rows, in, out)) {
+    const SpreadNeeds needs = SpreadScratchNeeds(format, rows, in, out);
+    if (needs.ok && scratch->partials != nullptr &&
+        scratch->counters != nullptr &&
+        scratch->partial_floats >= needs.partial_floats &&
+        scratch->counter_count >= needs.counters)
+      plan.variant = kSpreadVariant;
+  }
+  if (plan.variant == kSpreadVariant) {
+    if (scratch == nullptr)
+      return kInvalid;
+    return LaunchSpreadProduct(format, x, w, y, y_bf16, rows, in, out,
+                               accumulate, *scratch, stream, independent,
+                               g_programmatic);
+  }
   if (plan.variant < 0 && format == WeightFormat::kQ8Tiles &&
       WideTensorCoreProducts() && WideProductPays(rows, in, out))
     plan = PlanWideProduct(rows, in, out, SmCount());
@@ -870,7 +953,7 @@ int LaunchProduct(WeightFormat format, const std::uint16_t* x, const void* w,
       const int status = LaunchProduct(
           format, x + first * in, w, y != nullptr ? y + first * out : nullptr,
           y_bf16 != nullptr ? y_bf16 + first * out : nullptr, count, in, out,
-          accumulate, nullptr, stream, independent);
+          accumulate, nullptr, stream, independent, scratch);
       if (status != kOk)
         return status;
     }
@@ -901,8 +984,17 @@ int LaunchProduct(WeightFormat format, const std::uint16_t* x, const void* w,
   const int ntiles = TilesFor(rows);
   if (ntiles > 4 && !WideVariant(plan.variant))
     return kUnsupported;
-  const Footprint fp =
-      FootprintOf(f, plan.variant, ntiles, plan.blocks_per_split);
+  Footprint fp = FootprintOf(f, plan.variant, ntiles, plan.blocks_per_split);
+  if (fp.smem > kMaxProductSmem && plan_in != nullptr) {
+    // A plan made for another weight format whose stages do not fit this
+    // one's shared memory (the reference's PlanWmma plans serve Q8_0 and
+    // bf16 tiles alike): this format's own plan for the shape.
+    plan = PlanProduct(format, rows, in, out, 0);
+    if (plan.variant < 0 || plan.variant >= kNumVariants ||
+        (ntiles > 4 && !WideVariant(plan.variant)))
+      return kUnsupported;
+    fp = FootprintOf(f, plan.variant, ntiles, plan.blocks_per_split);
+  }
   if (fp.smem > kMaxProductSmem)
     return kUnsupported;
   const VariantShape& v = kVariants[plan.variant];

@@ -79,17 +79,72 @@ int LaunchTensorCoreProduct(const std::uint16_t* x, const void* w, float* y,
 ProductPlan PlanProduct(WeightFormat format, std::size_t rows, std::size_t in,
                         std::size_t out, std::size_t target_ctas = 0);
 
+/// Caller-owned scratch of products whose panels are cut between CTAs (the
+/// reference's SplitScratch, kernels/wmma_products.hpp:62-68): fp32 partial
+/// sums, and one counter per 128-row panel that must be zero before the
+/// first launch; every launch leaves the counters zero again. Launches that
+/// share a scratch must be ordered (one stream), as in the reference.
+struct SplitScratch {
+  float* partials = nullptr;
+  std::size_t partial_floats = 0;
+  unsigned* counters = nullptr;
+  std::size_t counter_count = 0;
+};
+
+/// Plan variant of the spread product (products_spread.cu): the product's
+/// (128-row panel, 32-column block) units cut evenly over at most one CTA
+/// per SM, panels cut between CTAs added in part order through a
+/// SplitScratch. Plans carry the CTA count in `splits` and the longest run
+/// of units in `blocks_per_split`.
+constexpr int kSpreadVariant = 102;
+constexpr int kSpreadMaxRows = 32;
+constexpr int kSpreadMaxPanels = 1024;
+
+struct SpreadNeeds {
+  bool ok = false;
+  int ctas = 0;
+  int run = 0;
+  std::size_t partial_floats = 0;
+  std::size_t counters = 0;
+};
+/// Whether the spread kernel serves this shape, and the scratch it needs.
+SpreadNeeds SpreadScratchNeeds(WeightFormat format, std::size_t rows,
+                               std::size_t in, std::size_t out);
+/// Scratch floats that serve every spread shape of at most `ctas` CTAs.
+std::size_t SpreadScratchFloatsFor(int ctas);
+/// CTAs of the widest spread launch on the current device (its SM count).
+int MaxSpreadCtas();
+/// Whether products launched without a plan may take the spread kernel
+/// (default off: it measured slower than the whole-reduction plans).
+void SetSpreadProducts(bool enabled);
+bool SpreadProducts();
+/// Whether a product launched without a plan takes the spread kernel when
+/// the caller gave scratch (the shapes where it measured faster).
+bool SpreadProductPays(WeightFormat format, std::size_t rows, std::size_t in,
+                       std::size_t out);
+/// Launches the spread kernel. Returns kOk, kUnsupported (shape not served),
+/// kInvalid (scratch missing or too small) or kCudaError.
+int LaunchSpreadProduct(WeightFormat format, const std::uint16_t* x,
+                        const void* w, float* y, std::uint16_t* y_bf16,
+                        std::size_t rows, std::size_t in, std::size_t out,
+                        bool accumulate, const SplitScratch& scratch,
+                        cudaStream_t stream, bool independent,
+                        bool programmatic);
+
 /// Launches one product of at most kMaxProductRows rows. Returns kOk,
 /// kUnsupported (nothing launched) or kInvalid / kCudaError.
 /// `independent`: the launch reads nothing that the kernels before it on
 /// the stream write, so it skips the programmatic-launch wait and may overlap
 /// them (streams of independent products); with no plan it takes the
 /// measured stream plan for its shape where there is one.
+/// `scratch` (may be null): split scratch the launch may use; with no plan,
+/// shapes where SpreadProductPays take the spread kernel through it.
 int LaunchProduct(WeightFormat format, const std::uint16_t* x, const void* w,
                   float* y, std::uint16_t* y_bf16, std::size_t rows,
                   std::size_t in, std::size_t out, bool accumulate,
                   const ProductPlan* plan, cudaStream_t stream,
-                  bool independent = false);
+                  bool independent = false,
+                  const SplitScratch* scratch = nullptr);
 
 /// Whether kernels are launched with programmatic dependent launch.
 void SetProgrammaticLaunch(bool enabled);

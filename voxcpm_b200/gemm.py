@@ -34,6 +34,16 @@ class Bf16Gemm:
         check(self._lib.vx_gemm_linear(self._handle, _ptr(x), w.format, _ptr(w.data), _ptr(y),
                                        rows, columns, out, int(accumulate)))
 
+    def LinearEx(self, x: torch.Tensor, w: Matrix, y: torch.Tensor, rows: int, columns: int, out: int,
+                 flags: int = 0) -> None:
+        """Linear with the output type of `y` (float32 or bfloat16) and
+        flags (PRODUCT_ACCUMULATE): vx_gemm_linear_ex."""
+        from ._lib import OUT_BF16, OUT_F32
+
+        dtype = OUT_BF16 if y.dtype == torch.bfloat16 else OUT_F32
+        check(self._lib.vx_gemm_linear_ex(self._handle, _ptr(x), w.format, _ptr(w.data), _ptr(y), dtype,
+                                          rows, columns, out, flags))
+
     def Matmul(self, shape, representative, a: torch.Tensor, b: torch.Tensor, c: torch.Tensor) -> None:
         """Column-major C (+)= op(A) op(B) of bf16 a and b into float32 c
         (gemm.hpp:60-63). `shape` and `representative` are MatmulShape; the

@@ -90,12 +90,35 @@ def PlanWmma(rows: int, columns: int, out: int, target_waves: int = 0) -> WmmaPl
     return load().vx_plan_wmma(rows, columns, out, target_waves)
 
 
+def PlanSpread(fmt: int, rows: int, columns: int, out: int) -> WmmaPlan:
+    """The spread plan (vx_plan_spread): CTA count, longest run and the split
+    scratch it needs (kernels/wmma_products.hpp:83-85 extended)."""
+    return load().vx_plan_spread(fmt, rows, columns, out)
+
+
+class SpreadScratch:
+    """Device split scratch for spread plans (kernels/wmma_products.hpp:62-68):
+    zeroed counters; kernels leave them zero."""
+
+    def __init__(self, plan: WmmaPlan, device="cuda"):
+        import torch
+
+        self.partials = torch.empty(max(int(plan.partial_floats), 1), dtype=torch.float32, device=device)
+        self.counters = torch.zeros(max(int(plan.counters), 1), dtype=torch.int32, device=device)
+        self.c = SplitScratch(self.partials.data_ptr(), int(plan.partial_floats),
+                              self.counters.data_ptr(), int(plan.counters))
+
+
 def _plan_arg(plan: WmmaPlan | None):
     return ctypes.byref(plan) if plan is not None else None
 
 
-def _scratch_arg(scratch: SplitScratch | None):
-    return ctypes.byref(scratch) if scratch is not None else None
+def _scratch_arg(scratch):
+    if scratch is None:
+        return None
+    if isinstance(scratch, SpreadScratch):
+        scratch = scratch.c
+    return ctypes.byref(scratch)
 
 
 def WmmaQ8(x, w, y, rows, columns, out, accumulate, plan=None, scratch=None, stream=None) -> bool:
