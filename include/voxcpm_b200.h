@@ -560,7 +560,10 @@ VX_API void vx_set_dit_stall_for_tests(uint64_t limit_ns);
 VX_API vx_status vx_generator_replay_dit_patch(vx_generator* generator);
 /* Host copies of internal state (tests, benchmarks): names "lm_hidden",
  * "residual_hidden", "prefix_cond", "x", "mu", "stop", "embed", "cond_rows",
- * "velocity", "delta_time", "lm_output" (the LM's last row before FSQ); set_state takes "lm_hidden", "residual_hidden",
+ * "velocity", "delta_time", "lm_output" (the LM's last row before FSQ), and
+ * the LM caches "base_cache_k", "base_cache_v", "residual_cache_k",
+ * "residual_cache_v" ([layer][kv_head][capacity][head_dim] as float, bf16
+ * caches widened); set_state takes "lm_hidden", "residual_hidden",
  * "prefix_cond", "mu" and "position" (one value). Stands in for
  * Generator::set_trace (generator.hpp:93-94). */
 VX_API vx_status vx_generator_state(vx_generator* generator, const char* name,

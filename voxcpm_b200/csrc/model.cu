@@ -1710,6 +1710,41 @@ struct StateBuffer {
 
 void Generator::State(const std::string& name, float* out, std::size_t count) {
   const ModelConfig& c = config_;
+  // The LM caches: [layer][kv_head][capacity][head_dim], bf16 widened.
+  const KvCache* cache = name == "base_cache_k" || name == "base_cache_v"
+                             ? &base_cache_
+                             : (name == "residual_cache_k" ||
+                                        name == "residual_cache_v"
+                                    ? &residual_cache_
+                                    : nullptr);
+  if (cache != nullptr) {
+    const StackConfig& s = cache == &base_cache_ ? c.lm : c.residual_lm;
+    const bool keys = name.back() == 'k';
+    const std::size_t per_layer = static_cast<std::size_t>(s.kv_heads) *
+                                  cache->capacity() * s.head_dim;
+    if (count > per_layer * s.layers)
+      throw std::invalid_argument("count too large: " + name);
+    CheckCuda(cudaStreamSynchronize(stream_), "sync");
+    const bool bf16 = cache->type() == CacheType::kBf16;
+    std::vector<std::uint16_t> bits(bf16 ? per_layer : 0);
+    for (int layer = 0; layer < s.layers && count > 0; ++layer) {
+      const std::size_t n = std::min(count, per_layer);
+      const void* src = keys ? cache->keys(layer) : cache->values(layer);
+      if (bf16) {
+        CheckCuda(cudaMemcpy(bits.data(), src, n * 2, cudaMemcpyDeviceToHost),
+                  "state");
+        for (std::size_t i = 0; i < n; ++i) {
+          const std::uint32_t word = static_cast<std::uint32_t>(bits[i]) << 16;
+          std::memcpy(out + i, &word, 4);
+        }
+      } else {
+        CheckCuda(cudaMemcpy(out, src, n * 4, cudaMemcpyDeviceToHost), "state");
+      }
+      out += n;
+      count -= n;
+    }
+    return;
+  }
   const std::map<std::string, StateBuffer> buffers = {
       {"lm_hidden", {lm_hidden_, static_cast<std::size_t>(c.lm.hidden)}},
       {"residual_hidden", {residual_hidden_, static_cast<std::size_t>(c.lm.hidden)}},
