@@ -85,7 +85,7 @@ bool IsDirectory(const std::string& path) {
   return ::stat(path.c_str(), &info) == 0 && S_ISDIR(info.st_mode);
 }
 
-/// Tensors sorted by offset must not overlap.
+/// No two tensors may share a byte of the file (checked in file order).
 void CheckOverlap(const std::vector<Tensor>& tensors) {
   std::vector<const Tensor*> order;
   for (const Tensor& t : tensors)
@@ -95,7 +95,8 @@ void CheckOverlap(const std::vector<Tensor>& tensors) {
   });
   for (std::size_t i = 1; i < order.size(); ++i)
     if (order[i - 1]->offset + order[i - 1]->bytes > order[i]->offset)
-      throw FormatError(order[i - 1]->name + " overlaps " + order[i]->name);
+      throw FormatError("tensors " + order[i - 1]->name + " and " +
+                        order[i]->name + " share bytes of the file");
 }
 
 }  // namespace
@@ -155,58 +156,89 @@ void MappedFile::ReleasePages() const {
 }
 
 // ------------------------------------------------------------ safetensors
+//
+// The safetensors layout (huggingface/safetensors, the format's README):
+//   u64 little-endian N | N bytes of UTF-8 JSON | the data buffer.
+// The JSON is an object: "__metadata__" (optional, a string map) and one
+// entry per tensor, {"dtype": "F32" | ..., "shape": [d0, d1, ...],
+// "data_offsets": [begin, end]} with the offsets relative to the data
+// buffer. The format caps N at 100,000,000 bytes.
+//
+// Reading happens in two passes: the header's entries become declarations
+// (name, element type, dimensions, byte range) with each entry checked on
+// its own; then the declarations are checked against each other and the
+// buffer (ranges inside it, sizes that match, no shared bytes, no repeated
+// name) before any becomes a Tensor.
 
 namespace {
 
-std::optional<DType> SafetensorsDType(const std::string& name) {
-  if (name == "F32") return DType::kF32;
-  if (name == "BF16") return DType::kBF16;
-  if (name == "F16") return DType::kF16;
-  if (name == "I64") return DType::kI64;
-  if (name == "I32") return DType::kI32;
-  if (name == "U8") return DType::kU8;
-  return std::nullopt;
-}
+constexpr std::uint64_t kSafetensorsHeaderCap = 100'000'000;
 
-Tensor SafetensorsEntry(const std::string& name, const json::Value& entry,
-                        const unsigned char* payload, std::uint64_t payload_at,
-                        std::uint64_t payload_bytes) {
-  if (!entry.is_object())
-    throw FormatError(name + " is not a JSON object");
-  const json::Value* dtype = entry.find("dtype");
-  const json::Value* shape = entry.find("shape");
-  const json::Value* offsets = entry.find("data_offsets");
-  if (dtype == nullptr || !dtype->is_string() || shape == nullptr ||
-      !shape->is_array() || offsets == nullptr || !offsets->is_array() ||
-      offsets->items().size() != 2)
-    throw FormatError(name + " lacks dtype, shape or data_offsets");
-  const auto type = SafetensorsDType(dtype->str());
-  if (!type.has_value())
-    throw FormatError(name + " has the unsupported dtype " + dtype->str());
-  Tensor tensor;
-  tensor.name = name;
-  tensor.dtype = *type;
-  std::size_t elements = 1;
-  for (const json::Value& dim : shape->items()) {
-    std::uint64_t size = 0;
-    if (!dim.as_unsigned(&size) || !Multiply(elements, size, &elements))
-      throw FormatError(name + " has a bad shape");
-    tensor.shape.push_back(size);
-  }
+/// The element types this library reads from safetensors files.
+struct SafetensorsType {
+  const char* code;
+  DType dtype;
+};
+constexpr SafetensorsType kSafetensorsTypes[] = {
+    {"BF16", DType::kBF16}, {"F16", DType::kF16}, {"F32", DType::kF32},
+    {"I32", DType::kI32},   {"I64", DType::kI64}, {"U8", DType::kU8},
+};
+
+struct Declared {
+  std::string name;
+  DType dtype = DType::kU8;
+  std::vector<std::size_t> dims;
   std::uint64_t begin = 0;
   std::uint64_t end = 0;
-  if (!offsets->items()[0].as_unsigned(&begin) ||
-      !offsets->items()[1].as_unsigned(&end) || begin > end ||
-      end > payload_bytes)
-    throw FormatError(name + " has data_offsets outside the payload");
-  std::size_t bytes = 0;
-  if (!Multiply(elements, DTypeSize(*type), &bytes) || bytes != end - begin)
-    throw FormatError(name + " has " + std::to_string(end - begin) +
-                      " bytes for its shape and dtype");
-  tensor.data = payload + begin;
-  tensor.bytes = bytes;
-  tensor.offset = payload_at + begin;
-  return tensor;
+};
+
+[[noreturn]] void BadEntry(const std::string& name, const std::string& why) {
+  throw FormatError("safetensors entry \"" + name + "\" " + why);
+}
+
+Declared Declare(const std::string& name, const json::Value& entry) {
+  if (!entry.is_object())
+    BadEntry(name, "must be an object");
+  const json::Value* code = entry.find("dtype");
+  const json::Value* dims = entry.find("shape");
+  const json::Value* range = entry.find("data_offsets");
+  if (code == nullptr || dims == nullptr || range == nullptr)
+    BadEntry(name, "needs all of dtype, shape and data_offsets");
+  Declared d;
+  d.name = name;
+  const SafetensorsType* type = nullptr;
+  if (code->is_string())
+    for (const SafetensorsType& t : kSafetensorsTypes)
+      if (code->str() == t.code)
+        type = &t;
+  if (type == nullptr)
+    BadEntry(name, "stores elements of type " +
+                       (code->is_string() ? code->str() : std::string("?")) +
+                       ", which this library does not read");
+  d.dtype = type->dtype;
+  if (!dims->is_array())
+    BadEntry(name, "has a shape that is not a list of sizes");
+  for (const json::Value& dim : dims->items()) {
+    std::uint64_t extent = 0;
+    if (!dim.as_unsigned(&extent))
+      BadEntry(name, "has a shape that is not a list of sizes");
+    d.dims.push_back(static_cast<std::size_t>(extent));
+  }
+  if (!range->is_array() || range->items().size() != 2 ||
+      !range->items()[0].as_unsigned(&d.begin) ||
+      !range->items()[1].as_unsigned(&d.end))
+    BadEntry(name, "needs data_offsets of two byte positions");
+  return d;
+}
+
+/// Bytes a declaration's dimensions and element type take, or false on
+/// overflow.
+bool DeclaredBytes(const Declared& d, std::size_t* bytes) {
+  std::size_t count = 1;
+  for (const std::size_t extent : d.dims)
+    if (!Multiply(count, extent, &count))
+      return false;
+  return Multiply(count, DTypeSize(d.dtype), bytes);
 }
 
 }  // namespace
@@ -215,39 +247,76 @@ std::vector<Tensor> ReadSafetensors(const MappedFile& file) {
   const unsigned char* bytes = file.data();
   const std::size_t size = file.size();
   if (size < 8)
-    throw FormatError("file is shorter than its header length");
-  std::uint64_t header_bytes = 0;
-  for (int i = 7; i >= 0; --i)
-    header_bytes = (header_bytes << 8) | bytes[i];
-  // The format caps headers at 100 MB.
-  if (header_bytes == 0 || header_bytes > 100'000'000 ||
-      header_bytes > size - 8)
-    throw FormatError("implausible header length");
+    throw FormatError("safetensors file of " + std::to_string(size) +
+                      " bytes is shorter than its 8-byte header length");
+  std::uint64_t json_bytes = 0;
+  for (int i = 0; i < 8; ++i)
+    json_bytes |= static_cast<std::uint64_t>(bytes[i]) << (8 * i);
+  if (json_bytes == 0 || json_bytes > kSafetensorsHeaderCap ||
+      json_bytes > size - 8)
+    throw FormatError("safetensors header length " +
+                      std::to_string(json_bytes) +
+                      " is implausible: it must be 1..100,000,000 and fit "
+                      "in the file");
   json::Value header;
   try {
     header = json::Parse(std::string_view(
-        reinterpret_cast<const char*>(bytes + 8), header_bytes));
+        reinterpret_cast<const char*>(bytes + 8), json_bytes));
   } catch (const json::Error& failure) {
-    throw FormatError(std::string("header: ") + failure.what());
+    throw FormatError(std::string("safetensors header is not valid JSON (") +
+                      failure.what() + ")");
   }
   if (!header.is_object())
-    throw FormatError("header is not a JSON object");
-  const std::uint64_t payload_at = 8 + header_bytes;
+    throw FormatError("safetensors header must be a JSON object");
+  const std::uint64_t buffer_at = 8 + json_bytes;
+  const std::uint64_t buffer_bytes = size - buffer_at;
+
+  // Pass 1: each entry on its own.
+  std::vector<Declared> declared;
+  for (const auto& [name, entry] : header.members())
+    if (name != "__metadata__")
+      declared.push_back(Declare(name, entry));
+  if (declared.empty())
+    throw FormatError("safetensors header declares no tensors");
+
+  // Pass 2: against the buffer and each other, in byte order.
+  std::sort(declared.begin(), declared.end(),
+            [](const Declared& a, const Declared& b) {
+              return a.begin != b.begin ? a.begin < b.begin : a.end < b.end;
+            });
   std::vector<Tensor> tensors;
-  for (const auto& [name, entry] : header.members()) {
-    if (name == "__metadata__")
-      continue;
-    tensors.push_back(SafetensorsEntry(name, entry, bytes + payload_at,
-                                       payload_at, size - payload_at));
+  tensors.reserve(declared.size());
+  for (std::size_t i = 0; i < declared.size(); ++i) {
+    const Declared& d = declared[i];
+    if (d.begin > d.end || d.end > buffer_bytes)
+      BadEntry(d.name, "spans bytes " + std::to_string(d.begin) + ".." +
+                           std::to_string(d.end) + ", outside the payload of " +
+                           std::to_string(buffer_bytes) + " bytes");
+    std::size_t need = 0;
+    if (!DeclaredBytes(d, &need))
+      BadEntry(d.name, "has a shape too large to address");
+    if (need != d.end - d.begin)
+      BadEntry(d.name, "spans " + std::to_string(d.end - d.begin) +
+                           " bytes, but its shape and dtype need " +
+                           std::to_string(need));
+    if (i > 0 && declared[i - 1].end > d.begin)
+      throw FormatError("safetensors entries \"" + declared[i - 1].name +
+                        "\" and \"" + d.name + "\" share bytes (their ranges "
+                        "overlap)");
+    Tensor t;
+    t.name = d.name;
+    t.dtype = d.dtype;
+    t.shape = d.dims;
+    t.data = bytes + buffer_at + d.begin;
+    t.bytes = need;
+    t.offset = buffer_at + d.begin;
+    tensors.push_back(std::move(t));
   }
-  if (tensors.empty())
-    throw FormatError("no tensors");
-  CheckOverlap(tensors);
   std::sort(tensors.begin(), tensors.end(),
             [](const Tensor& a, const Tensor& b) { return a.name < b.name; });
   for (std::size_t i = 1; i < tensors.size(); ++i)
     if (tensors[i - 1].name == tensors[i].name)
-      throw FormatError("the header names " + tensors[i].name + " twice");
+      BadEntry(tensors[i].name, "appears twice in the header");
   return tensors;
 }
 
