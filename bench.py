@@ -223,47 +223,87 @@ def cpu_sample(threads: int, budget_s: float):
         f"{elapsed:.1f} s")
 
 
+def cpu_model() -> str:
+    """The host CPU's model name (from /proc/cpuinfo), or the platform's."""
+    try:
+        for line in open("/proc/cpuinfo"):
+            if line.startswith("model name"):
+                return line.split(":", 1)[1].strip()
+    except OSError:
+        pass
+    import platform
+
+    return platform.processor() or platform.machine()
+
+
 def cpu_host_baselines() -> dict:
-    """The other host-side references the path's tests check against, timed
-    once each on this box's host cores (reported only):
+    """The host-side references the path's tests check against, timed on
+    this box's host cores (reported only):
     - the scalar double-precision product of config 0 on one thread
       (tests/products_test.cpp:117-134);
+    - the fp32 per-block transcription of the reference's Q8_0 product
+      (kernels/wmma_products.hip:201-214) on a slice of config 0, on one
+      thread and on all host threads;
     - one DiT patch of config 2 (12 layers, 10 Euler steps, 9 evaluations,
       CFG 2.0, seeded Q8_0 weights) through the oracle's restatement on all
-      cores (generator.cpp:297-324, 424-460)."""
+      cores (generator.cpp:297-324, 424-460);
+    - one full per-patch step of config 3 (28-layer LM, 8-layer residual
+      LM, 12-layer encoder and DiT, context 512, bf16 cache) through the
+      oracle's restatement on all cores (generator.cpp:424-513)."""
     import numpy as np
 
     import oracle
     from oracle.model import OracleGenerator
     from voxcpm_b200.generator import released_config
 
+    threads = os.cpu_count() or 1
     rng = np.random.default_rng(0)
     blocks = oracle.random_q8_0(1, 0, OUT, IN)
     x = oracle.bf16_bits(rng.normal(0, 1, (ROWS, IN)).astype(np.float32))
     start = time.perf_counter()
     oracle.product_exact(x, oracle.Q8_0, blocks, ROWS, IN, OUT, threads=1)
     product_s = time.perf_counter() - start
+    one_value, one_desc = cpu_sample(1, 3.0)
+    all_value, all_desc = cpu_sample(threads, 3.0)
 
     c = released_config()
-    c.lm.layers = 1  # the DiT patch reads no LM weights; keeps set-up short
-    c.residual_lm.layers = 1
-    c.max_length = 64
-    threads = os.cpu_count() or 1
-    ref = OracleGenerator(c, seed=7, threads=threads)
+    c.max_length = 640
+    c.vocab = 1024
+    ref = OracleGenerator(c, seed=7, threads=threads, bf16_cache=True)
     mu = rng.normal(0, 1, 2 * c.dit.hidden).astype(np.float32)
     cond = rng.normal(0, 1, (c.patch_size, c.feat_dim)).astype(np.float32)
     noise = rng.normal(0, 1, (c.patch_size, c.feat_dim)).astype(np.float32)
     start = time.perf_counter()
     ref.dit_patch(mu, cond, noise, 10, 2.0)
     patch_s = time.perf_counter() - start
+    # The step at context 512: caches hold seeded keys and values for the
+    # 512 prompt positions (the step's work does not depend on their values).
+    for cache in (ref.base_cache, ref.residual_cache):
+        cache.k[:, :, :512] = rng.normal(0, 1, cache.k[:, :, :512].shape).astype(np.float32)
+        cache.v[:, :, :512] = rng.normal(0, 1, cache.v[:, :, :512].shape).astype(np.float32)
+    ref.position = 512
+    ref.lm_hidden = rng.normal(0, 1, c.lm.hidden).astype(np.float32)
+    ref.residual_hidden = rng.normal(0, 1, c.lm.hidden).astype(np.float32)
+    start = time.perf_counter()
+    ref.step(noise, 10, 2.0)
+    step_s = time.perf_counter() - start
+    host = {"cores": threads, "cpu": cpu_model()}
     return {
+        "host": host,
         "double_sum_product": {"us": product_s * 1e6, "gbs": STEP_BYTES / product_s / 1e9, "cores": 1,
                                "kind": "port",
                                "sample": f"one full config-0 product (M={ROWS}, K={IN}, N={OUT}), "
                                          "double-precision sums, one thread"},
+        "fp32_product_one_thread": {"gbs": one_value, "cores": 1, "kind": "port", "sample": one_desc},
+        "fp32_product_all_threads": {"gbs": all_value, "cores": threads, "kind": "port",
+                                     "sample": all_desc},
         "dit_patch": {"us": patch_s * 1e6, "cores": threads, "kind": "port",
                       "sample": "one config-2 DiT patch (10 Euler steps, CFG 2.0) through the oracle's "
                                 "restatement, all host cores"},
+        "step": {"ms": step_s * 1e3, "audio_s_per_s": PATCH_AUDIO_S / step_s, "cores": threads,
+                 "kind": "port",
+                 "sample": "one config-3 per-patch step at context 512 (bf16 cache) through the "
+                           "oracle's restatement, all host cores"},
     }
 
 
@@ -597,8 +637,7 @@ STEP_BYTES_CONFIG3 = 4_034_512_896 + 18_874_368
 
 BOX_REQUESTS = 64        # independent requests over the box
 BOX_PATCHES = 63         # patches per request (about 10 s of audio)
-BOX_PER_RANK = 16        # requests each rank runs (a bounded sample of its share)
-BOX_SLOTS = 16           # requests generated together per GPU (GeneratorBatch slots)
+BOX_SLOTS = 16           # requests generated together per GPU (GeneratorBatch slots, at most)
 
 
 SWEEP_ROWS = (1, 2, 8, 22, 64, 128)
@@ -758,6 +797,10 @@ def measure_generator(rank: int, world=None, context: int = 512, patch_replays: 
     # first prefill to the last latent.
     n_ranks = world if world else 1
     mine = box_share(rank, n_ranks)
+    visible = os.environ.get("CUDA_VISIBLE_DEVICES")
+    gpu_index = int(visible.split(",")[torch.cuda.current_device()]) if visible else torch.cuda.current_device()
+    box_clocks = ClockSampler(gpu_index)
+    box_clocks.__enter__()
     torch.cuda.synchronize()
     a.record(stream)
     for req in mine:
@@ -777,7 +820,10 @@ def measure_generator(rank: int, world=None, context: int = 512, patch_replays: 
     box_audio = len(mine) * BOX_PATCHES * PATCH_AUDIO_S
     weight_bytes = gen.weight_bytes()
     gen.close()
-    batched_s = max_over_ranks(world, measure_box_batched(c, mine))
+    box_clocks.__exit__(None, None, None)
+    batched_clocks = ClockSampler(gpu_index)
+    with batched_clocks:
+        batched_s = max_over_ranks(world, measure_box_batched(c, mine))
     box_s_max = max_over_ranks(world, box_s)
     box_audio_all = sum_over_ranks(world, box_audio)
     box_patches_all = sum_over_ranks(world, len(mine) * BOX_PATCHES)
@@ -801,28 +847,32 @@ def measure_generator(rank: int, world=None, context: int = 512, patch_replays: 
                  "config": "LM 28x2048 + residual LM 8x2048 + encoder 12x1024 + DiT 12x1024, Q8_0, "
                            "one CUDA graph per patch"},
         "box_batched": {"audio_s_per_s": box_audio_all / batched_s, "n_gpus": n_ranks,
-                        "slots": BOX_SLOTS, "device_s": batched_s,
+                        "slots_per_gpu": min(BOX_SLOTS, len(mine)), "device_s": batched_s,
+                        "requests": sum_over_ranks(world, len(mine)),
                         "hbm_gbs_per_gpu": STEP_BYTES_CONFIG3 * box_patches_all / n_ranks / batched_s / 1e9,
-                        "sample": f"the same {BOX_PER_RANK} requests per rank in {BOX_SLOTS} slots of one "
-                                  "GeneratorBatch (shared weights; one DiT pass for all active slots per "
-                                  "Euler evaluation); a slot takes the next request when its request ends",
+                        "sample": f"each rank's share of the {BOX_REQUESTS} requests in min({BOX_SLOTS}, share) "
+                                  "slots of one GeneratorBatch (shared weights; one DiT pass for all active "
+                                  "slots per Euler evaluation); a slot takes the next request when its "
+                                  "request ends",
+                        "clocks": batched_clocks.summary(),
                         "config": "BASELINE config 4 (box throughput), batched request slots, no collectives"},
         "box": {"audio_s_per_s": box_audio_all / box_s_max, "n_gpus": n_ranks,
                 "requests": sum_over_ranks(world, len(mine)), "patches_per_request": BOX_PATCHES,
                 "device_s": box_s_max, "audio_s": box_audio_all,
                 "hbm_gbs_per_gpu": box_gbs_per_gpu, "hbm_frac_per_gpu": box_gbs_per_gpu / peak_gbs,
-                "sample": f"{BOX_PER_RANK} of each rank's share of {BOX_REQUESTS} requests "
+                "sample": f"all {BOX_REQUESTS} requests split over the ranks "
                           f"(prompts of 16..128 text tokens, per-request seeds), {BOX_PATCHES} patches each, "
                           "prefill included; requests run one after another on each GPU",
+                "clocks": box_clocks.summary(),
                 "config": "BASELINE config 4 (box throughput), one request stream per GPU, no collectives"},
     }
 
 
 def box_share(rank: int, world: int) -> list:
     """The config-4 requests rank `rank` of `world` runs: requests rank,
-    rank + world, ... of BOX_REQUESTS, the first BOX_PER_RANK of them (no
-    request on two ranks; no collective)."""
-    return list(range(rank, BOX_REQUESTS, max(world, 1)))[:BOX_PER_RANK]
+    rank + world, ... of BOX_REQUESTS (every request on exactly one rank; no
+    collective)."""
+    return list(range(rank, BOX_REQUESTS, max(world, 1)))
 
 
 def drive_box(batch, c, requests, slots: int, patches: int) -> int:

@@ -190,7 +190,11 @@ VX_API vx_status vx_product(int format, const uint16_t* x, const void* w, void* 
 /* The launch reads nothing that earlier kernels on the stream write (x, w
  * and, when accumulating, y are ready before it is enqueued): it may overlap
  * them instead of waiting for their completion. With a null plan it takes
- * the library's measured plan for such streams where it has one. */
+ * the library's measured plan for such streams where it has one. That plan
+ * (config 0's shape) does its tile math in fp16 over rows scaled by a power
+ * of two: bit-equal to the bf16 math for activations within 2^31 of their
+ * row's largest magnitude; smaller ones are rounded to fp16 there, which can
+ * change the last bits of a sum (within the products' 1e-5 limit). */
 #define VX_PRODUCT_INDEPENDENT 2u
 
 /* vx_product with flags (VX_PRODUCT_ACCUMULATE, VX_PRODUCT_INDEPENDENT).

@@ -1,10 +1,13 @@
 """The C++ mirror header (include/voxcpm_b200.hpp) compiles with g++, links
-the library and gives the same host results as the oracle (no GPU)."""
+the library and gives the same host results as the oracle (no GPU); and, on
+a B200, the products and the generator called from C++ through it match the
+oracle (tests/cpp/shim_device.cpp)."""
 
 import subprocess
 from pathlib import Path
 
 import numpy as np
+import pytest
 
 import oracle
 from voxcpm_b200 import _lib
@@ -58,3 +61,74 @@ def test_cpp_shim_model_files(tmp_path):
     bad = subprocess.run([str(exe), str(tmp_path / "absent.gguf")], check=True, capture_output=True,
                          text=True).stdout
     assert bad.startswith("files error") and "absent.gguf" in bad
+
+
+def _build_device_shim(tmp_path):
+    """Compiles tests/cpp/shim_device.cpp against include/voxcpm_b200.hpp
+    and links the library and the CUDA runtime."""
+    _lib.load()
+    exe = tmp_path / "shim_device"
+    lib_dir = str(_lib.LIBRARY.parent)
+    cuda = "/usr/local/cuda"
+    subprocess.run(["g++", "-std=c++17", "-O1", "-I", str(ROOT / "include"),
+                    "-I", f"{cuda}/include", str(ROOT / "tests" / "cpp" / "shim_device.cpp"), "-o", str(exe),
+                    "-L", lib_dir, "-l:libvoxcpm_b200.so", f"-Wl,-rpath,{lib_dir}", "-L", f"{cuda}/lib64",
+                    "-lcudart", f"-Wl,-rpath,{cuda}/lib64"], check=True)
+    return exe
+
+
+def test_cpp_device_shim_compiles(tmp_path):
+    """The device program of the C++ mirror compiles and links on any host."""
+    assert _build_device_shim(tmp_path).exists()
+
+
+@pytest.mark.gpu
+def test_cpp_mirror_on_device(tmp_path, cuda):
+    """Bf16Gemm::Linear (Q8_0 tiles and bf16 rows) and a seeded Generator's
+    Prefill and two Steps, called from C++ through include/voxcpm_b200.hpp,
+    against the oracle: products within 1e-5 of sum |x w|
+    (tests/products_test.cpp:115-145), latents relative L2 2e-2 and stop
+    logits within 5e-3 (the generator tests' limits)."""
+    from _checkpoints import config_json
+    from oracle.model import OracleGenerator
+    from voxcpm_b200.generator import small_config
+
+    exe = _build_device_shim(tmp_path)
+    rng = np.random.default_rng(5)
+    rows, columns, out = 22, 1024, 2560
+    x = oracle.bf16_bits(rng.normal(0, 1, (rows, columns)).astype(np.float32))
+    blocks = oracle.random_q8_0(3, 1, out, columns)
+    w = oracle.bf16_bits(rng.normal(0, 0.02, (out, columns)).astype(np.float32))
+    c = small_config()
+    p_rows, steps = 9, 2
+    tokens = rng.integers(0, c.vocab, p_rows).astype(np.int32)
+    audio = np.zeros(p_rows, np.int32)
+    audio[-1] = 1
+    feats = np.zeros((p_rows, c.patch_size * c.feat_dim), np.float32)
+    feats[-1] = rng.normal(0, 1, c.patch_size * c.feat_dim)
+    noise = rng.normal(0, 1, (steps, c.patch_size * c.feat_dim)).astype(np.float32)
+    (tmp_path / "dims.txt").write_text(f"{rows} {columns} {out} {steps} {p_rows}\n")
+    for name, array in (("x.u16", x), ("blocks.u8", blocks), ("w.u16", w), ("tokens.i32", tokens),
+                        ("text.i32", (1 - audio).astype(np.int32)), ("audio.i32", audio),
+                        ("feats.f32", feats), ("noise.f32", noise)):
+        array.tofile(tmp_path / name)
+    (tmp_path / "config.json").write_text(config_json(c))
+    run = subprocess.run([str(exe), str(tmp_path)], capture_output=True, text=True)
+    assert run.returncode == 0, run.stderr
+    assert f"positions {p_rows + steps}" in run.stdout
+
+    for file, fmt, weights in (("y_q8.f32", oracle.Q8_0, blocks), ("y_bf16.f32", oracle.BF16_ROWS, w)):
+        y = np.fromfile(tmp_path / file, np.float32).reshape(rows, out)
+        exact, mag = oracle.product_exact(x, fmt, weights, rows, columns, out)
+        err = oracle.relative_error(y, exact, mag)
+        print(f"{file}: {err:.3e}")
+        assert err <= 1e-5, file
+    ref = OracleGenerator(c, seed=7)
+    ref.prefill(tokens, 1 - audio, audio, feats.reshape(p_rows, c.patch_size, c.feat_dim))
+    latents = np.fromfile(tmp_path / "latents.f32", np.float32).reshape(steps, -1)
+    stops = np.fromfile(tmp_path / "stops.f32", np.float32).reshape(steps, 2)
+    for s in range(steps):
+        latent_r, stop_r = ref.step(noise[s].reshape(c.patch_size, c.feat_dim), 10, 2.0)
+        e = float(np.linalg.norm(latents[s] - latent_r.reshape(-1)) / np.linalg.norm(latent_r))
+        print(f"step {s}: latent {e:.3e} stop {np.abs(stops[s] - stop_r).max():.3e}")
+        assert e < 2e-2 and float(np.abs(stops[s] - stop_r).max()) < 5e-3

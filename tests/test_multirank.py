@@ -3,8 +3,8 @@ processes (the scaling run launches one process per GPU the same way, over
 NCCL). Replicas only: no data-path collective, so what needs checking is
 - the reductions the bench takes over ranks (max of times, sum of work),
   here on host tensors;
-- each rank's share of the config-4 requests: disjoint, the first
-  BOX_PER_RANK of rank, rank + N, ...;
+- each rank's share of the config-4 requests: rank, rank + N, ...,
+  disjoint, and together all of them;
 - the batched box's slot scheduling on each rank's share, against a
   stand-in batch that records its calls: every request is prefilled once
   into a free slot and advanced by exactly its patches, the slots refilling
@@ -64,12 +64,12 @@ def _rank(rank, world, port, out_dir):
         assert bench.max_over_ranks(world, 1.5 + rank) == 1.5 + world - 1
         assert bench.sum_over_ranks(world, 1.0 + rank) == sum(1.0 + r for r in range(world))
         share = bench.box_share(rank, world)
-        assert share == list(range(rank, bench.BOX_REQUESTS, world))[: bench.BOX_PER_RANK]
-        # Every rank's share, gathered: disjoint.
+        assert share == list(range(rank, bench.BOX_REQUESTS, world))
+        # Every rank's share, gathered: disjoint, and all the requests.
         gathered = [None] * world
         dist.all_gather_object(gathered, share)
         flat = [r for s in gathered for r in s]
-        assert len(flat) == len(set(flat))
+        assert len(flat) == len(set(flat)) == bench.BOX_REQUESTS
         # The batched box's schedule on this rank's share.
         c = SimpleNamespace(vocab=64, patch_size=4, feat_dim=64)
         slots, patches = 4, 3
@@ -108,5 +108,5 @@ def test_one_rank_needs_no_process_group():
     import bench
 
     assert bench.max_over_ranks(1, 3.0) == 3.0 and bench.sum_over_ranks(1, 2.0) == 2.0
-    assert bench.box_share(0, 1) == list(range(bench.BOX_PER_RANK))
+    assert bench.box_share(0, 1) == list(range(bench.BOX_REQUESTS))
     assert bench.box_share(7, 8) == list(range(7, bench.BOX_REQUESTS, 8))

@@ -328,3 +328,35 @@ def test_wide_rows(cuda, columns, out):
         assert np.array_equal(y16.cpu().view(torch.int16).numpy().view(np.uint16),
                               oracle.bf16_bits(y32.cpu().numpy()))
     assert K.DeviceError() == 0
+
+
+@pytest.mark.parametrize("rows", [1, 22])
+def test_half_tile_math_wide_rows(cuda, rows):
+    """Variant 14 on rows whose values span far more than 2^31: every
+    element N(0, 1) * 2^e with e uniform in [-60, 0]. Values more than about
+    2^32 below their row's largest fall below fp16's subnormal step once the
+    row is scaled and are rounded there (variant 13 forms them exactly), so
+    the bits may differ from variant 13; the sums stay within the products'
+    limit of the double-precision result, since each such rounding moves a
+    product by less than 2^-40 of the row's largest one."""
+    rng = np.random.default_rng(71 + rows)
+    columns, out = 2048, 2560
+    blocks, q8_tiles, _, _ = prepare(out, columns, rng)
+    x = (rng.normal(0.0, 1.0, size=(rows, columns)) *
+         np.exp2(rng.uniform(-60.0, 0.0, size=(rows, columns)))).astype(np.float32)
+    x_bits = oracle.bf16_bits(x)
+    x_dev = to_dev(x_bits)
+    exact, mag = oracle.product_exact(x_bits, oracle.Q8_0, blocks, rows, columns, out)
+    ys = {}
+    for variant in (13, 14):
+        plan = _lib.WmmaPlan(1, columns // 32, 0, 0, variant)
+        y = torch.empty(rows, out, dtype=torch.float32, device="cuda")
+        assert K.ProductEx(_lib.WEIGHTS_Q8_TILES, x_dev, q8_tiles, y, rows, columns, out, 0, plan=plan)
+        ys[variant] = y
+    torch.cuda.synchronize()
+    for variant, y in ys.items():
+        err = oracle.relative_error(y.cpu().numpy(), exact, mag)
+        assert err <= LIMIT, f"variant {variant}: {err:.3e}"
+    differ = int((ys[13] != ys[14]).sum())
+    print(f"rows {rows}: {differ} of {rows * out} sums differ from variant 13's bits")
+    assert K.DeviceError() == 0

@@ -755,7 +755,12 @@ constexpr MeasuredPlan kMeasuredPlans[] = {
 // with no plan): a launch overlaps the ones before it, so fewer, larger
 // CTAs without clusters win (config 0: 3.13 us per product with variant 13
 // against 4.4 us for the best clustered plan; 2.94 us with variant 14's
-// fp16 tile math, bit-equal to 13).
+// fp16 tile math). Variant 14 equals variant 13 bit for bit when every
+// activation lies within 2^31 of its row's largest magnitude; elements
+// further below are rounded to fp16's subnormal step after the row's
+// scaling (variant 13 forms their products exactly), which moves each such
+// product by less than 2^-40 of the row's largest: the sums can differ in
+// their last bits, within the products' 1e-5 limit of the exact result.
 constexpr MeasuredPlan kStreamPlans[] = {
     {WeightFormat::kQ8Tiles, 2, 2048, 6144, 14, 1},
 };
