@@ -65,7 +65,7 @@ def parse():
     p.add_argument("--steps", type=int, default=400_000)
     p.add_argument("--warmup", type=int, default=20_000)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--case", choices=["product", "dit", "wide", "batch", "matmul"], default=None,
+    p.add_argument("--case", choices=["product", "dit", "wide", "batch", "matmul", "vae"], default=None,
                    help="run a few launches of one kernel for a profiler and exit (no JSON line)")
     return p.parse_args()
 
@@ -635,6 +635,74 @@ PATCH_AUDIO_S = 0.16  # 4 latent frames x 640 samples at 16 kHz
 STEP_BYTES_CONFIG3 = 4_034_512_896 + 18_874_368
 
 
+def measure_vae(gen, c, tokens, audio, feats, noises, warm: int, rank: int, decodes: int = 20) -> dict:
+    """The AudioVAE decode on its own stream (vae.cpp:382-516): one patch of
+    latents (4 frames -> 7680 samples at 48 kHz) per decoding on the
+    released decoder with seeded weights; then the config-3 step loop with
+    each patch's latent decoded behind the next step, as synthesizer.cpp:
+    283-307 drives it (Step, Collect the previous patch, Enqueue this one on
+    the latent event)."""
+    import numpy as np
+    import torch
+
+    from voxcpm_b200.vae import AudioVae, default_vae_config
+
+    vae = AudioVae(default_vae_config(), seed=200 + rank)
+    vae_stream = torch.cuda.ExternalStream(vae.stream())
+    frames = c.patch_size
+    x = torch.randn(frames, c.feat_dim, device="cuda")
+    torch.cuda.synchronize()
+    a = torch.cuda.Event(enable_timing=True)
+    b = torch.cuda.Event(enable_timing=True)
+    times = []
+    for i in range(decodes + 3):
+        a.record(vae_stream)
+        vae.Enqueue(x.data_ptr(), frames)
+        b.record(vae_stream)
+        samples = vae.Collect()
+        if i >= 3:
+            times.append(a.elapsed_time(b) * 1e3)
+    decode_us = float(np.median(times))
+    # Steps with the decode behind them.
+    vae.Reset()
+    gen.Prefill(tokens, 1 - audio, audio, feats)
+    wall_ms, decoded = [], 0
+    for n in noises:
+        t0 = time.perf_counter()
+        gen.Step(n, 10, 2.0)
+        decoded += vae.Collect().size
+        vae.Enqueue(gen.latent(), frames, gen.latent_event())
+        wall_ms.append((time.perf_counter() - t0) * 1e3)
+    decoded += vae.Collect().size
+    if decoded != len(noises) * frames * vae.decode_hop or samples.size != frames * vae.decode_hop:
+        raise RuntimeError("AudioVAE returned the wrong number of samples")
+    with_vae_ms = float(np.median(wall_ms[warm:]))
+    patch_audio_s = frames * vae.decode_hop / 48000
+    vae.close()
+    return {"decode_us_per_patch": decode_us, "audio_s_per_s_decode_only": patch_audio_s / (decode_us / 1e6),
+            "step_wall_ms_with_vae": with_vae_ms,
+            "audio_s_per_s_with_vae": patch_audio_s / (with_vae_ms / 1e3),
+            "hbm_floor_us": VAE_WEIGHT_BYTES / (measured_peak()[0] * 1e9) * 1e6,
+            "fp32_floor_us": VAE_FLOPS_PER_FRAME * frames / 74.4e12 * 1e6,
+            "fp32_peak_note": "74.4 TFLOP/s: 148 SMs x 128 fp32 lanes x 2 x 1.965 GHz (nominal)",
+            "config": "AudioVAE V2 decoder: latent 64, decoder 2048, rates 8 6 5 2 2 2, 48 kHz, float32, "
+                      "seeded weights; its own stream, fed by the generator's latent event",
+            "timing": f"device events around Enqueue on the AudioVAE stream, median of {decodes}; with "
+                      "steps: wall time per config-3 step including Collect + Enqueue"}
+
+
+# The released decoder's product weights in float32 (read once per
+# decoding: input pointwise, per block the transposed convolution and three
+# unit pointwise matrices) and its product flops per latent frame (2 x the
+# multiply-adds; a block's input has `hop` frames per latent frame).
+VAE_RATES = (8, 6, 5, 2, 2, 2)
+VAE_WEIGHT_BYTES = 4 * (2048 * 64 + sum(
+    (2048 >> b) * (1024 >> b) * 2 * r + 3 * (1024 >> b) ** 2 for b, r in enumerate(VAE_RATES)))
+VAE_FLOPS_PER_FRAME = 2 * (64 * 2048 + sum(
+    hop * 2 * (2048 >> b) * r * (1024 >> b) + 3 * hop * r * (1024 >> b) ** 2
+    for b, (r, hop) in enumerate(zip(VAE_RATES, (1, 8, 48, 240, 480, 960)))))
+
+
 BOX_REQUESTS = 64        # BASELINE config 4: independent requests over the box
 BOX_PATCHES = 63         # patches per request (about 10 s of audio)
 BOX_SLOTS = 16           # requests generated together per GPU (GeneratorBatch slots, at most)
@@ -786,6 +854,7 @@ def measure_generator(rank: int, world=None, context: int = 512, patch_replays: 
         return float(np.median(device_ms[warm:])), float(np.median(wall_ms[warm:])), prefill
 
     step_ms, step_wall_ms, prefill_s = time_steps()
+    vae = measure_vae(gen, c, tokens, audio, feats, noises, warm, rank)
     # The same steps from the same prompt on the per-kernel path.
     gen.SetPersistent(False)
     per_kernel_step_ms, _, _ = time_steps()
@@ -846,6 +915,7 @@ def measure_generator(rank: int, world=None, context: int = 512, patch_replays: 
                          else "per-kernel sequence",
                  "config": "LM 28x2048 + residual LM 8x2048 + encoder 12x1024 + DiT 12x1024, Q8_0, "
                            "one CUDA graph per patch"},
+        "vae": vae,
         "box_batched": {"audio_s_per_s": box_audio_all / batched_s, "n_gpus": n_ranks,
                         "slots_per_gpu": min(BOX_SLOTS, len(mine)), "device_s": batched_s,
                         "requests": sum_over_ranks(world, len(mine)),
@@ -960,7 +1030,9 @@ def profile_case(case: str) -> None:
     `batch`: two steps of a GeneratorBatch of 8 slots on the released shapes
     (the first captures the step's graph); `matmul`: three Bf16Gemm::Matmul
     calls of 4096 x 4096 x 4096 in the reduction-contiguous layout, timed
-    with CUDA events (96 MB of operands and C)."""
+    with CUDA events (96 MB of operands and C); `vae`: six AudioVAE decodings
+    of one patch (4 latent frames) on the released decoder, timed with CUDA
+    events on its stream (183 MB of float32 weights)."""
     import numpy as np
     import torch
 
@@ -969,6 +1041,22 @@ def profile_case(case: str) -> None:
 
     lib = _lib.load()
     torch.cuda.set_device(0)
+    if case == "vae":
+        from voxcpm_b200.vae import AudioVae, default_vae_config
+
+        vae = AudioVae(default_vae_config(), seed=200)
+        stream = torch.cuda.ExternalStream(vae.stream())
+        x = torch.randn(4, 64, device="cuda")
+        torch.cuda.synchronize()
+        start, end = torch.cuda.Event(enable_timing=True), torch.cuda.Event(enable_timing=True)
+        for _ in range(6):
+            start.record(stream)
+            vae.Enqueue(x.data_ptr(), 4)
+            end.record(stream)
+            samples = vae.Collect()
+            print(f"vae decode of 4 frames: {start.elapsed_time(end) * 1e3:.1f} us, {samples.size} samples")
+        vae.close()
+        return
     if case == "matmul":
         from voxcpm_b200.gemm import Bf16Gemm, MatmulShape
 

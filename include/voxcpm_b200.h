@@ -648,6 +648,62 @@ VX_API vx_status vx_generator_batch_set_graphs(vx_generator_batch* batch,
                                                int enabled);
 VX_API cudaStream_t vx_generator_batch_stream(const vx_generator_batch* batch);
 
+/* ------------------------------------------------------------ AudioVAE */
+
+/* The decoder fields of AudioVaeConfig (config.hpp:53-72): latent frames of
+ * `latent_dim` to mono audio at `out_sample_rate`, through one block per
+ * decoder rate (each halves the channels and multiplies the frames by its
+ * rate), conditioned on the rate's bucket among `sr_bin_boundaries`. */
+typedef struct vx_vae_config {
+  size_t latent_dim;
+  size_t decoder_dim;
+  size_t decoder_rates[8];
+  size_t decoder_rate_count;
+  size_t out_sample_rate;
+  size_t sr_bin_boundaries[8];
+  size_t sr_bin_boundary_count;
+} vx_vae_config;
+/* The released AudioVAE V2: latent 64, decoder 2048, rates 8 6 5 2 2 2,
+ * 48 kHz out, boundaries 20000 30000 40000. */
+VX_API void vx_vae_config_default(vx_vae_config* config);
+
+/* The AudioVAE V2 decoder in float32 on its own stream, chunk by chunk with
+ * the state of every causal convolution carried between calls (decoding a
+ * stream in chunks gives the samples of decoding it at once, up to float32
+ * rounding; the same chunks give the same samples bit for bit). Weights are
+ * the seeded AudioVAE checkpoint of `seed` (bf16 values of the seeded
+ * hash, tensor ids FNV-1a of "audio_vae." + name), packed as the decoder
+ * reads them. Replaces AudioVae (vae.hpp:25-79) for decoding; null on
+ * failure (vx_last_error). */
+typedef struct vx_audio_vae vx_audio_vae;
+VX_API vx_audio_vae* vx_audio_vae_create(const vx_vae_config* config,
+                                         uint64_t seed);
+VX_API void vx_audio_vae_destroy(vx_audio_vae* vae);
+/* Output samples per latent frame (AudioVaeConfig::decode_hop). */
+VX_API size_t vx_audio_vae_decode_hop(const vx_audio_vae* vae);
+VX_API cudaStream_t vx_audio_vae_stream(const vx_audio_vae* vae);
+/* A new stream: zero history (AudioVae::Reset, vae.cpp:363-368). */
+VX_API vx_status vx_audio_vae_reset(vx_audio_vae* vae);
+/* Decodes `frames` host latent frames [frames][latent_dim] into
+ * frames * decode_hop host samples (AudioVae::Decode, vae.cpp:382-393).
+ * VX_INVALID while an enqueued decoding is pending. */
+VX_API vx_status vx_audio_vae_decode(vx_audio_vae* vae, const float* latents,
+                                     size_t frames, float* audio);
+/* Queues the decoding of `frames` device latent frames on the AudioVAE's
+ * stream once `ready` (may be null; e.g. vx_generator_latent_event) has
+ * completed; the latents are copied before anything else, so the generator
+ * may overwrite them afterwards. One decoding may be pending: VX_INVALID
+ * while one is (the reference would overwrite it). AudioVae::Enqueue
+ * (vae.cpp:395-407). */
+VX_API vx_status vx_audio_vae_enqueue(vx_audio_vae* vae, const float* latents,
+                                      size_t frames, cudaEvent_t ready);
+/* Waits for the pending decoding and copies its samples (frames *
+ * decode_hop, 0 when none is pending) into `audio`; `*samples` is how many.
+ * VX_INVALID when `capacity` is smaller. AudioVae::Collect (vae.cpp:409-
+ * 413). */
+VX_API vx_status vx_audio_vae_collect(vx_audio_vae* vae, float* audio,
+                                      size_t capacity, size_t* samples);
+
 /* ------------------------------------------------------------ model files */
 
 /* Tensor element types (safetensors.hpp:18, same order). Q8_0 is GGML's

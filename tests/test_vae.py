@@ -1,0 +1,216 @@
+"""AudioVAE V2 decoder (vae.hpp:25-79, vae.cpp:382-516): the library's CUDA
+decoder against the oracle restatement (oracle/vae.py), and the oracle
+pinned against torch's convolutions on the checkpoint-layout weights.
+
+The reference checks its decoder against a golden decoded stream with a
+relative L2 limit of 1e-4, decoding streamed in patches and at once
+(tests/vae_test.cpp:122-132); the same limit and the same two forms are used
+here, on the seeded checkpoint (the released weights are not available).
+"""
+
+import ctypes
+
+import numpy as np
+import pytest
+
+from oracle.vae import DILATIONS, KERNEL, OracleVae, VaeConfig
+
+SMALL = dict(latent_dim=8, decoder_dim=32, decoder_rates=(2, 3), out_sample_rate=24000)
+RELEASED = dict(latent_dim=64, decoder_dim=2048, decoder_rates=(8, 6, 5, 2, 2, 2), out_sample_rate=48000)
+LIMIT = 1e-4  # relative L2, tests/vae_test.cpp:127,132
+# Chunked against whole decodings: float32 rounding through 26 convolutions
+# (the released decoder measured 1.3e-5); the reference holds both forms to
+# LIMIT against its golden stream.
+CHUNKING = 1e-4
+
+
+def relative(actual, expected) -> float:
+    a = np.asarray(actual, np.float64)
+    e = np.asarray(expected, np.float64)
+    return float(np.sqrt(((a - e) ** 2).sum() / max((e ** 2).sum(), 1e-30)))
+
+
+def latents(frames: int, dim: int, seed: int = 3) -> np.ndarray:
+    return np.random.default_rng(seed).normal(0.0, 1.0, (frames, dim)).astype(np.float32)
+
+
+# ---------------------------------------------------------------- oracle (CPU)
+
+def torch_decoder(w, x: np.ndarray) -> np.ndarray:
+    """The decoder as torch layers on the checkpoint-layout weights, in
+    float64, over the whole input with zero history (causal padding)."""
+    import torch
+    import torch.nn.functional as F
+
+    d = lambda a: torch.as_tensor(np.asarray(a, np.float64))
+
+    def snake(y, alpha):
+        alpha = d(alpha)[None, :, None]
+        return y + (1.0 / (alpha + 1e-9)) * torch.sin(alpha * y) ** 2
+
+    def causal(y, weight, bias, dilation=1, groups=1):
+        pad = (weight.shape[-1] - 1) * dilation
+        return F.conv1d(F.pad(y, (pad, 0)), weight, bias, dilation=dilation, groups=groups)
+
+    h = d(x).T[None]  # [1][latent][frames]
+    latent = h.shape[1]
+    h = causal(h, d(w.in_depthwise)[:, None, :], d(w.in_depthwise_bias), groups=latent)
+    h = F.conv1d(h, d(w.in_pointwise)[:, :, None], d(w.in_pointwise_bias))
+    for block in w.blocks:
+        s, out = block["stride"], block["out"]
+        y = snake(h * d(block["scale"])[None, :, None] + d(block["bias"])[None, :, None], block["alpha"])
+        frames = y.shape[-1]
+        h = F.conv_transpose1d(y, d(block["up_weight"]), d(block["up_bias"][:out]), stride=s)[:, :, :frames * s]
+        for unit in block["units"]:
+            y = snake(h, unit["alpha_in"])
+            y = causal(y, d(unit["depthwise"])[:, None, :], d(unit["depthwise_bias"]), unit["dilation"], groups=out)
+            y = snake(y, unit["alpha_out"])
+            h = h + F.conv1d(y, d(unit["pointwise"])[:, :, None], d(unit["pointwise_bias"]))
+    y = snake(h, w.out_alpha)
+    y = causal(y, d(w.out_conv)[None], torch.tensor([float(w.out_bias)], dtype=torch.float64))
+    return torch.tanh(y)[0, 0].numpy()
+
+
+def test_oracle_matches_torch_convolutions():
+    c = VaeConfig(**SMALL)
+    vae = OracleVae(c, seed=11)
+    x = latents(9, c.latent_dim)
+    out = vae.decode(x)
+    assert out.shape == (9 * c.decode_hop(),)
+    assert relative(out, torch_decoder(vae.w, x)) < 1e-5
+
+
+def test_oracle_streams_like_decoding_at_once():
+    c = VaeConfig(**SMALL)
+    vae = OracleVae(c, seed=11)
+    x = latents(12, c.latent_dim)
+    whole = vae.decode(x)
+    vae.reset()
+    streamed = np.concatenate([vae.decode(x[a:b]) for a, b in ((0, 3), (3, 4), (4, 11), (11, 12))])
+    assert relative(streamed, whole) < 1e-6
+    vae.reset()
+    assert relative(vae.decode(x), whole) == 0.0
+
+
+def test_rate_bucket_is_torch_bucketize():
+    import torch
+
+    boundaries = torch.tensor([20000, 30000, 40000])
+    for rate in (8000, 16000, 20000, 24000, 30000, 44100, 48000):
+        c = VaeConfig(out_sample_rate=rate)
+        assert c.rate_bucket() == int(torch.bucketize(torch.tensor(rate), boundaries, right=False))
+    assert VaeConfig().decode_hop() == 1920
+
+
+def test_state_sizes_follow_the_decoding_order():
+    c = VaeConfig(**SMALL)
+    vae = OracleVae(c, seed=1)
+    rows = [s.shape[0] for s in vae.states]
+    assert rows == [KERNEL - 1] + ([1] + [(KERNEL - 1) * d for d in DILATIONS]) * 2 + [KERNEL - 1]
+
+
+# ---------------------------------------------------------------- library (GPU)
+
+def library_vae(config: dict, seed: int):
+    from voxcpm_b200.vae import AudioVae, vae_config
+
+    return AudioVae(vae_config(**config), seed)
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("config", [SMALL, RELEASED], ids=["small", "released"])
+def test_decode_matches_oracle_streamed_and_at_once(cuda, config):
+    vae = library_vae(config, seed=5)
+    oracle = OracleVae(VaeConfig(**config), seed=5)
+    patch = 4
+    x = latents(12, config["latent_dim"], seed=8)
+    expected = oracle.decode(x)
+    streamed = np.concatenate([vae.Decode(x[f:f + patch]) for f in range(0, len(x), patch)])
+    assert streamed.shape == expected.shape
+    assert relative(streamed, expected) <= LIMIT
+    vae.Reset()
+    whole = vae.Decode(x)
+    assert relative(whole, expected) <= LIMIT
+    # A product may run on another kernel at another row count: streaming
+    # equals decoding at once up to float32 rounding.
+    assert relative(streamed, whole) <= CHUNKING
+    # The same chunks from the same state: the same samples, bit for bit.
+    vae.Reset()
+    again = np.concatenate([vae.Decode(x[f:f + patch]) for f in range(0, len(x), patch)])
+    np.testing.assert_array_equal(again, streamed)
+    vae.close()
+
+
+@pytest.mark.gpu
+def test_ragged_chunks_and_reset(cuda):
+    vae = library_vae(SMALL, seed=9)
+    x = latents(40, SMALL["latent_dim"], seed=2)
+    whole = vae.Decode(x)
+    vae.Reset()
+    parts = [vae.Decode(x[a:b]) for a, b in ((0, 1), (1, 1), (1, 7), (7, 33), (33, 40))]
+    assert relative(np.concatenate(parts), whole) <= CHUNKING
+    assert parts[1].size == 0
+    vae.Reset()
+    np.testing.assert_array_equal(vae.Decode(x), whole)
+    oracle = OracleVae(VaeConfig(**SMALL), seed=9)
+    assert relative(whole, oracle.decode(x)) <= LIMIT
+    vae.close()
+
+
+@pytest.mark.gpu
+def test_enqueue_after_generator_steps(cuda):
+    """The latent hand-off of generator.cpp:464-469: each step's device
+    latent decoded on the AudioVAE's stream once the step's event has
+    completed, equal to decoding the latents the steps returned."""
+    from voxcpm_b200 import _lib
+    from voxcpm_b200.generator import Generator, small_config
+
+    c = small_config(layers=1, max_length=64, vocab=64)
+    generator = Generator(c, seed=4, checkpoint=_lib.CHECKPOINT_Q8)
+    rng = np.random.default_rng(6)
+    n = 5
+    tokens = rng.integers(0, c.vocab, n).astype(np.int32)
+    text = np.ones(n, np.int32)
+    audio = np.zeros(n, np.int32)
+    feats = np.zeros((n, c.patch_size * c.feat_dim), np.float32)
+    generator.Prefill(tokens, text, audio, feats)
+    config = dict(RELEASED, latent_dim=c.feat_dim)
+    streamed = library_vae(config, seed=5)
+    host = library_vae(config, seed=5)
+    got, returned = [], []
+    for _ in range(3):
+        latent, _stop = generator.Step(rng.normal(0, 1, (c.patch_size, c.feat_dim)).astype(np.float32), 10, 2.0)
+        streamed.Enqueue(generator.latent(), c.patch_size, generator.latent_event())
+        got.append(streamed.Collect())
+        returned.append(latent)
+    expected = np.concatenate([host.Decode(l) for l in returned])
+    np.testing.assert_array_equal(np.concatenate(got), expected)
+    assert expected.size == 3 * c.patch_size * streamed.decode_hop
+    generator.close()
+    streamed.close()
+    host.close()
+
+
+@pytest.mark.gpu
+def test_pending_decoding_rules(cuda):
+    from voxcpm_b200 import _lib
+
+    import torch
+
+    vae = library_vae(SMALL, seed=1)
+    assert vae.Collect().size == 0  # nothing pending
+    x = torch.randn(3, SMALL["latent_dim"], device="cuda")
+    torch.cuda.synchronize()
+    vae.Enqueue(x.data_ptr(), 3)
+    with pytest.raises(_lib.VxError) as failure:
+        vae.Enqueue(x.data_ptr(), 3)
+    assert failure.value.status == _lib.VX_INVALID
+    lib = _lib.load()
+    small = np.empty(4, np.float32)
+    samples = ctypes.c_size_t(0)
+    assert lib.vx_audio_vae_collect(vae._handle, small.ctypes.data, small.size, ctypes.byref(samples)) == \
+        _lib.VX_INVALID
+    out = vae.Collect()  # the pending decoding is still there
+    vae.Reset()
+    np.testing.assert_array_equal(out, vae.Decode(x.cpu().numpy()))
+    vae.close()

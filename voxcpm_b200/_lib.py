@@ -48,6 +48,20 @@ class WmmaPlan(ctypes.Structure):
     ]
 
 
+class VaeConfig(ctypes.Structure):
+    """vx_vae_config: the decoder fields of AudioVaeConfig (config.hpp:53-72)."""
+
+    _fields_ = [
+        ("latent_dim", c_size_t),
+        ("decoder_dim", c_size_t),
+        ("decoder_rates", c_size_t * 8),
+        ("decoder_rate_count", c_size_t),
+        ("out_sample_rate", c_size_t),
+        ("sr_bin_boundaries", c_size_t * 8),
+        ("sr_bin_boundary_count", c_size_t),
+    ]
+
+
 class MatmulShape(ctypes.Structure):
     """vx_matmul_shape (replaces MatmulShape, gemm.hpp:16-38): column-major
     C[m][n] (+)= op(A)[m][k] * op(B)[k][n], strides in elements."""
@@ -267,6 +281,15 @@ SIGNATURES: dict[str, tuple] = {
     "vx_generator_batch_state": (c_int, [c_void_p, c_size_t, c_char_p, c_void_p, c_size_t]),
     "vx_generator_batch_set_graphs": (c_int, [c_void_p, c_int]),
     "vx_generator_batch_stream": (c_void_p, [c_void_p]),
+    "vx_vae_config_default": (None, [POINTER(VaeConfig)]),
+    "vx_audio_vae_create": (c_void_p, [POINTER(VaeConfig), c_uint64]),
+    "vx_audio_vae_destroy": (None, [c_void_p]),
+    "vx_audio_vae_decode_hop": (c_size_t, [c_void_p]),
+    "vx_audio_vae_stream": (c_void_p, [c_void_p]),
+    "vx_audio_vae_reset": (c_int, [c_void_p]),
+    "vx_audio_vae_decode": (c_int, [c_void_p, c_void_p, c_size_t, c_void_p]),
+    "vx_audio_vae_enqueue": (c_int, [c_void_p, c_void_p, c_size_t, c_void_p]),
+    "vx_audio_vae_collect": (c_int, [c_void_p, c_void_p, c_size_t, POINTER(c_size_t)]),
     "vx_model_files_open": (c_void_p, [c_char_p]),
     "vx_model_files_close": (None, [c_void_p]),
     "vx_model_files_is_voxcpm2_gguf": (c_int, [c_char_p]),

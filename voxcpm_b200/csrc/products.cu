@@ -767,6 +767,11 @@ constexpr MeasuredPlan kMeasuredPlans[] = {
     {WeightFormat::kBf16, 2, 2048, 12288, 20, 1},  // 21.74 us (39.84)
     {WeightFormat::kBf16, 2, 4096, 1024, 21, 2},  // 5.86 us (12.99)
     {WeightFormat::kBf16, 2, 6144, 2048, 17, 4},  // 13.84 us (24.31)
+    // Where the entry above does not fit 25..32 rows (its CTA's activation
+    // slice too large), the best plan measured at 32 rows.
+    {WeightFormat::kQ8Tiles, 2, 2048, 6144, 1, 4},    // 9.65 us (v17: 12.16)
+    {WeightFormat::kQ8Tiles, 2, 2048, 12288, 17, 1},  // 19.19 us (34.65)
+    {WeightFormat::kBf16, 2, 6144, 2048, 20, 4},      // 15.92 us (26.41)
     // Earlier measurements (shapes not re-measured).
     // Q8_0 tiles, one row (LM, residual LM, FSQ, projections).
     {WeightFormat::kQ8Tiles, 0, 2048, 512, 7, 8},
@@ -856,7 +861,7 @@ ProductPlan PlanProduct(WeightFormat format, std::size_t rows, std::size_t in,
           bps * kTileColumns > kMaxSliceColumns ||
           FootprintOf(static_cast<int>(format), m.variant, ntiles, bps).smem >
               limit)
-        break;  // not a valid plan for these rows: use the cost model
+        continue;  // does not fit these rows: a later entry, or the cost model
       best.variant = m.variant;
       best.splits = m.splits;
       best.blocks_per_split = bps;
