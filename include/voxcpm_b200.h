@@ -806,6 +806,8 @@ VX_API vx_status vx_random_bf16(uint64_t seed, uint64_t tensor, size_t count,
  * (gemm.hpp:49-72); one instance per stream. */
 typedef struct vx_gemm vx_gemm;
 VX_API vx_gemm* vx_gemm_create(cudaStream_t stream);
+/* Synchronizes the gemm's stream (launches may still use its scratch), so
+ * the stream must outlive the gemm. */
 VX_API void vx_gemm_destroy(vx_gemm* gemm);
 /* y[rows][out] (+)= x[rows][in] * w[out][in]^T, float32 y. Up to 128 rows
  * run in one launch on the planner's plan (the spread product through the

@@ -546,6 +546,60 @@ class Generator {
   vx_model_config config_;
 };
 
+/// vae.hpp:25-79, decoding: the AudioVAE V2 decoder on its own stream, with
+/// the seeded AudioVAE checkpoint of `seed` (no audiovae.pth reader).
+class AudioVae {
+ public:
+  static std::unique_ptr<AudioVae> Create(const vx_vae_config& config,
+                                          std::uint64_t seed,
+                                          std::string* error = nullptr) {
+    vx_audio_vae* v = vx_audio_vae_create(&config, seed);
+    if (v == nullptr) {
+      if (error != nullptr)
+        *error = vx_last_error();
+      return nullptr;
+    }
+    return std::unique_ptr<AudioVae>(new AudioVae(v, config));
+  }
+  ~AudioVae() { vx_audio_vae_destroy(v_); }
+  AudioVae(const AudioVae&) = delete;
+  AudioVae& operator=(const AudioVae&) = delete;
+
+  /// vae.hpp:39-52
+  void Reset() { Check(vx_audio_vae_reset(v_), "AudioVae::Reset"); }
+  void Decode(const float* latents, std::size_t frames,
+              std::vector<float>* audio) {
+    const std::size_t at = audio->size();
+    audio->resize(at + frames * decode_hop());
+    Check(vx_audio_vae_decode(v_, latents, frames, audio->data() + at),
+          "AudioVae::Decode");
+  }
+  void Enqueue(const float* latents, std::size_t frames, cudaEvent_t ready) {
+    Check(vx_audio_vae_enqueue(v_, latents, frames, ready),
+          "AudioVae::Enqueue");
+    pending_ = frames * decode_hop();
+  }
+  void Collect(std::vector<float>* audio) {
+    const std::size_t at = audio->size();
+    audio->resize(at + pending_);
+    std::size_t samples = 0;
+    Check(vx_audio_vae_collect(v_, audio->data() + at, pending_, &samples),
+          "AudioVae::Collect");
+    audio->resize(at + samples);
+    pending_ = 0;
+  }
+  std::size_t output_rate() const { return config_.out_sample_rate; }
+  std::size_t decode_hop() const { return vx_audio_vae_decode_hop(v_); }
+  cudaStream_t stream() const { return vx_audio_vae_stream(v_); }
+
+ private:
+  AudioVae(vx_audio_vae* v, const vx_vae_config& config)
+      : v_(v), config_(config) {}
+  vx_audio_vae* v_;
+  vx_vae_config config_;
+  std::size_t pending_ = 0;
+};
+
 }  // namespace voxcpm_b200
 
 #endif  // VOXCPM_B200_HPP_

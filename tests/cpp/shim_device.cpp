@@ -1,7 +1,8 @@
 // Device use of the C++ mirror header, as a caller of the reference's
 // gemm.hpp and generator.hpp writes it (tests/products_test.cpp,
 // synthesizer.cpp:262,290): Bf16Gemm::Linear on Q8_0 tiles and on bf16 rows,
-// then a seeded Generator's Prefill and Steps. Inputs come from raw files
+// then a seeded Generator's Prefill and Steps, then the AudioVae decoding the
+// last latent. Inputs come from raw files
 // the Python test writes into <dir>; outputs go back there for it to check
 // against the oracle.
 //
@@ -11,8 +12,10 @@
 // blocks.u8 [out][in/32] GGML Q8_0 blocks; w.u16 [out][in] bf16 bits;
 // config.json; tokens.i32, text.i32, audio.i32 [prompt_rows];
 // feats.f32 [prompt_rows][patch * feat]; noise.f32 [steps][patch * feat].
-// Writes y_q8.f32, y_bf16.f32 [rows][out], latents.f32 [steps][patch * feat]
-// and stops.f32 [steps][2].
+// Writes y_q8.f32, y_bf16.f32 [rows][out], latents.f32 [steps][patch * feat],
+// stops.f32 [steps][2], and the last latent decoded by a seeded AudioVae
+// (latent = feat, decoder 64, rates 2 3, seed 11) from the device latent after
+// the step's event (vae_enqueued.f32) and from the host (vae_decoded.f32).
 #include <cuda_runtime.h>
 
 #include <cstdio>
@@ -86,6 +89,8 @@ int main(int argc, char** argv) {
                              static_cast<std::uint8_t*>(tiles), stream);
     float* y = nullptr;
     Cuda(cudaMalloc(&y, rows * out * sizeof(float)), "y");
+    {
+    // The gemm synchronizes its stream when destroyed: it goes first.
     vb::Bf16Gemm gemm(stream);
     std::vector<float> y_host(rows * out);
     const struct {
@@ -100,6 +105,7 @@ int main(int argc, char** argv) {
                       cudaMemcpyDeviceToHost),
            "download");
       Write(dir + run.file, y_host);
+    }
     }
 
     // A seeded Generator: Prefill, then Steps (generator.hpp:58-94).
@@ -133,6 +139,29 @@ int main(int argc, char** argv) {
     Write(dir + "/latents.f32", latents);
     Write(dir + "/stops.f32", stops);
     std::printf("positions %zu\n", generator->position());
+
+    // AudioVae (vae.hpp:25-79): the last step's device latent decoded on the
+    // AudioVAE's stream after the step's event, and the same latent from the
+    // host, each from a new stream.
+    vx_vae_config vae_config;
+    vx_vae_config_default(&vae_config);
+    vae_config.latent_dim = config.feat_dim;
+    vae_config.decoder_dim = 64;
+    vae_config.decoder_rate_count = 2;
+    vae_config.decoder_rates[0] = 2;
+    vae_config.decoder_rates[1] = 3;
+    const auto streamed = vb::AudioVae::Create(vae_config, 11, &error);
+    const auto host = vb::AudioVae::Create(vae_config, 11, &error);
+    if (streamed == nullptr || host == nullptr)
+      throw vb::GpuError("AudioVae::Create: " + error);
+    std::vector<float> enqueued, decoded;
+    streamed->Enqueue(generator->latent(), config.patch_size,
+                      generator->latent_event());
+    streamed->Collect(&enqueued);
+    host->Decode(latents.data() + (steps - 1) * values, config.patch_size,
+                 &decoded);
+    Write(dir + "/vae_enqueued.f32", enqueued);
+    Write(dir + "/vae_decoded.f32", decoded);
     cudaFree(x);
     cudaFree(block_dev);
     cudaFree(w);

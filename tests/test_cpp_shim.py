@@ -84,8 +84,9 @@ def test_cpp_device_shim_compiles(tmp_path):
 
 @pytest.mark.gpu
 def test_cpp_mirror_on_device(tmp_path, cuda):
-    """Bf16Gemm::Linear (Q8_0 tiles and bf16 rows) and a seeded Generator's
-    Prefill and two Steps, called from C++ through include/voxcpm_b200.hpp,
+    """Bf16Gemm::Linear (Q8_0 tiles and bf16 rows), a seeded Generator's
+    Prefill and two Steps and the AudioVae decoding the last latent, called
+    from C++ through include/voxcpm_b200.hpp,
     against the oracle: products within 1e-5 of sum |x w|
     (tests/products_test.cpp:115-145), latents relative L2 2e-2 and stop
     logits within 5e-3 (the generator tests' limits)."""
@@ -132,3 +133,16 @@ def test_cpp_mirror_on_device(tmp_path, cuda):
         e = float(np.linalg.norm(latents[s] - latent_r.reshape(-1)) / np.linalg.norm(latent_r))
         print(f"step {s}: latent {e:.3e} stop {np.abs(stops[s] - stop_r).max():.3e}")
         assert e < 2e-2 and float(np.abs(stops[s] - stop_r).max()) < 5e-3
+
+    # AudioVae: Enqueue(latent, latent_event) + Collect equals Decode of the
+    # same latent from the host, and both match the oracle decoder
+    # (tests/vae_test.cpp:127's 1e-4 relative L2).
+    from oracle.vae import OracleVae, VaeConfig
+
+    enqueued = np.fromfile(tmp_path / "vae_enqueued.f32", np.float32)
+    decoded = np.fromfile(tmp_path / "vae_decoded.f32", np.float32)
+    np.testing.assert_array_equal(enqueued, decoded)
+    vae = OracleVae(VaeConfig(latent_dim=c.feat_dim, decoder_dim=64, decoder_rates=(2, 3)), seed=11)
+    expected = vae.decode(latents[-1].reshape(c.patch_size, c.feat_dim))
+    assert decoded.shape == expected.shape
+    assert float(np.linalg.norm(decoded - expected) / np.linalg.norm(expected)) <= 1e-4

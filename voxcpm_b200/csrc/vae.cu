@@ -32,6 +32,7 @@
 // library's seeded hash, widened to float32, in the packed layouts.
 #include "model.cuh"
 #include "vx_common.cuh"
+#include "vx_launch.cuh"
 #include "vx_status.h"
 
 #include "../../include/voxcpm_b200.h"
@@ -131,12 +132,22 @@ __global__ void __launch_bounds__(128)
     for (int c = 0; c < kCols; ++c)
       acc[r][c] = 0.0f;
   const int groups = k / 4;
-#pragma unroll 1
-  for (int g = lane; g < groups; g += 32) {
-    float4 wv[kCols];
+  // The first weights are in flight before the wait for the previous
+  // launch (they do not depend on it).
+  float4 wv[kCols];
+  if (lane < groups) {
 #pragma unroll
     for (int c = 0; c < kCols; ++c)
-      wv[c] = LoadStreamed(wr[c] + g);
+      wv[c] = LoadStreamed(wr[c] + lane);
+  }
+  GridDependencyWait();
+#pragma unroll 1
+  for (int g = lane; g < groups; g += 32) {
+    if (g != lane) {
+#pragma unroll
+      for (int c = 0; c < kCols; ++c)
+        wv[c] = LoadStreamed(wr[c] + g);
+    }
 #pragma unroll
     for (int r = 0; r < kRows; ++r) {
       if (r < rows) {
@@ -149,6 +160,7 @@ __global__ void __launch_bounds__(128)
       }
     }
   }
+  GridLaunchDependents();
 #pragma unroll
   for (int r = 0; r < kRows; ++r)
 #pragma unroll
@@ -200,9 +212,9 @@ __global__ void __launch_bounds__(kThreads)
   const int k_end = min(k, k_begin + k_split);
   const int stages_total = max(0, (k_end - k_begin + kDepth - 1) / kDepth);
 
-  auto load = [&](int stage, int index) {
+  // 8 chunks of 4 floats per staged row.
+  auto load_x = [&](int stage, int index) {
     const int k0 = k_begin + index * kDepth;
-    // 8 chunks of 4 floats per staged row.
     for (int c = tid; c < kTileRows * 8; c += kThreads) {
       const int r = c / 8, kk = k0 + (c % 8) * 4;
       const bool valid = row0 + r < rows && kk < k_end;
@@ -210,6 +222,9 @@ __global__ void __launch_bounds__(kThreads)
                 valid ? x + static_cast<long long>(row0 + r) * ldx + kk : x,
                 valid);
     }
+  };
+  auto load_w = [&](int stage, int index) {
+    const int k0 = k_begin + index * kDepth;
     for (int c = tid; c < kTileCols * 8; c += kThreads) {
       const int r = c / 8, kk = k0 + (c % 8) * 4;
       const bool valid = col0 + r < out && kk < k_end;
@@ -220,17 +235,27 @@ __global__ void __launch_bounds__(kThreads)
   };
 
   float acc[kRowsPerThread][kColsPerThread] = {};
+  // The first stages' weights are copied before the wait for the previous
+  // launch (they do not depend on it; they join the first copy group), the
+  // activations after it.
+#pragma unroll
+  for (int s = 0; s < kStages - 1; ++s)
+    if (s < stages_total)
+      load_w(s, s);
+  GridDependencyWait();
 #pragma unroll
   for (int s = 0; s < kStages - 1; ++s) {
     if (s < stages_total)
-      load(s, s);
+      load_x(s, s);
     CommitChunks();
   }
   for (int index = 0; index < stages_total; ++index) {
     WaitChunks<kStages - 2>();
     __syncthreads();  // stage `index` landed; stage index - 1 is free
-    if (index + kStages - 1 < stages_total)
-      load((index + kStages - 1) % kStages, index + kStages - 1);
+    if (index + kStages - 1 < stages_total) {
+      load_x((index + kStages - 1) % kStages, index + kStages - 1);
+      load_w((index + kStages - 1) % kStages, index + kStages - 1);
+    }
     CommitChunks();
     const int stage = index % kStages;
     const float* xt = xs + stage * kTileRows * kPitch;
@@ -252,6 +277,7 @@ __global__ void __launch_bounds__(kThreads)
     }
   }
   WaitChunks<0>();
+  GridLaunchDependents();
   if (splits > 1) {
     // The partial sums, 4 at a time, interleaved by thread.
     float4* part = reinterpret_cast<float4*>(smem);
@@ -342,6 +368,7 @@ __global__ void VaeWindowKernel(const float4* __restrict__ in,
                                 float4* __restrict__ state_new, int t,
                                 int rows, int channels4, const float4* alpha,
                                 const float4* scale, const float4* bias) {
+  GridDependencyWait();
   const long long i =
       static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
   if (i >= static_cast<long long>(rows + t) * channels4)
@@ -355,56 +382,83 @@ __global__ void VaeWindowKernel(const float4* __restrict__ in,
     state_new[static_cast<long long>(row - t) * channels4 + c] = v;
 }
 
-/// A causal depthwise convolution (kernel 7, `dilation`) over the window
-/// [state_old | f(in)] formed on the fly (kernels/vae_kernels.hip:35-50):
-/// out[t][c] = bias[c] + sum_j w[c][j] window[t + j * dilation][c], then
-/// Snake with alpha_out when it is not null. Items past the t x channels4
-/// outputs write state_new, the window's last `rows` frames. Four channels
-/// per thread.
-__global__ void VaeWindowDepthwiseKernel(
+/// Channel groups (of four) of one VaeWindowDepthwiseKernel CTA.
+__host__ __device__ constexpr int DepthwiseGroups(int channels4) {
+  return channels4 < 32 ? channels4 : 32;
+}
+
+/// A causal depthwise convolution (kernel 7, `dilation` d) over the window
+/// [state_old | f(in)] (kernels/vae_kernels.hip:35-50): out[f][c] = bias[c]
+/// + sum_j w[c][j] window[f + j d][c], then Snake with alpha_out when it is
+/// not null. A CTA takes `frames` frames of up to 32 channel groups: it
+/// forms their window rows (frames + 6 d) once in shared memory, then each
+/// thread sums the taps of its outputs there. The CTAs of the last grid
+/// column write state_new instead, the window's last `rows` frames.
+__global__ void __launch_bounds__(kThreads) VaeWindowDepthwiseKernel(
     const float4* __restrict__ in, const float4* __restrict__ state_old,
     float4* __restrict__ state_new, float4* __restrict__ out, int t, int rows,
-    int channels4, int dilation, const float4* alpha_in,
+    int channels4, int dilation, int frames, const float4* alpha_in,
     const float* __restrict__ w, const float* __restrict__ bias,
     const float4* alpha_out) {
-  const long long i =
-      static_cast<long long>(blockIdx.x) * blockDim.x + threadIdx.x;
-  const long long outputs = static_cast<long long>(t) * channels4;
-  if (i >= outputs + static_cast<long long>(rows) * channels4)
-    return;
-  if (i >= outputs) {
-    const long long j = i - outputs;
-    const int row = t + static_cast<int>(j / channels4);
-    const int c = static_cast<int>(j % channels4);
-    state_new[j] = WindowRow(in, state_old, row, rows, c, channels4, alpha_in,
-                             nullptr, nullptr);
+  extern __shared__ float4 window[];  // [frames + 6 d][groups]
+  GridDependencyWait();
+  const int groups = DepthwiseGroups(channels4);
+  const int c0 = blockIdx.y * groups;
+  const int tid = threadIdx.x;
+  if (blockIdx.x == gridDim.x - 1) {
+    for (int e = tid; e < rows * groups; e += kThreads) {
+      const int j = e / groups, c = c0 + e % groups;
+      if (c < channels4)
+        state_new[static_cast<long long>(j) * channels4 + c] =
+            WindowRow(in, state_old, t + j, rows, c, channels4, alpha_in,
+                      nullptr, nullptr);
+    }
     return;
   }
-  const int f = static_cast<int>(i / channels4);
-  const int c = static_cast<int>(i % channels4);
-  float sum[4];
+  const int f0 = blockIdx.x * frames;
+  const int span = frames + (kVaeKernel - 1) * dilation;
+  for (int e = tid; e < span * groups; e += kThreads) {
+    const int row = f0 + e / groups, c = c0 + e % groups;
+    window[e] = c < channels4 && row < rows + t
+                    ? WindowRow(in, state_old, row, rows, c, channels4,
+                                alpha_in, nullptr, nullptr)
+                    : make_float4(0.0f, 0.0f, 0.0f, 0.0f);
+  }
+  __syncthreads();
+  const int per_pass = kThreads / groups;
+  const int cg = tid % groups, fg = tid / groups;
+  const int c = c0 + cg;
+  if (fg >= per_pass || c >= channels4)
+    return;
+  float taps[4][kVaeKernel];
 #pragma unroll
   for (int q = 0; q < 4; ++q)
-    sum[q] = bias[4 * c + q];
 #pragma unroll
-  for (int j = 0; j < kVaeKernel; ++j) {
-    const float4 v = WindowRow(in, state_old, f + j * dilation, rows, c,
-                               channels4, alpha_in, nullptr, nullptr);
-    sum[0] += w[(4 * c + 0) * kVaeKernel + j] * v.x;
-    sum[1] += w[(4 * c + 1) * kVaeKernel + j] * v.y;
-    sum[2] += w[(4 * c + 2) * kVaeKernel + j] * v.z;
-    sum[3] += w[(4 * c + 3) * kVaeKernel + j] * v.w;
+    for (int j = 0; j < kVaeKernel; ++j)
+      taps[q][j] = w[(4 * c + q) * kVaeKernel + j];
+  const float4 b = reinterpret_cast<const float4*>(bias)[c];
+  for (int f = fg; f < frames && f0 + f < t; f += per_pass) {
+    float sum[4] = {b.x, b.y, b.z, b.w};
+#pragma unroll
+    for (int j = 0; j < kVaeKernel; ++j) {
+      const float4 v = window[(f + j * dilation) * groups + cg];
+      sum[0] += taps[0][j] * v.x;
+      sum[1] += taps[1][j] * v.y;
+      sum[2] += taps[2][j] * v.z;
+      sum[3] += taps[3][j] * v.w;
+    }
+    float4 v = make_float4(sum[0], sum[1], sum[2], sum[3]);
+    if (alpha_out != nullptr)
+      v = SnakeOf(v, alpha_out[c]);
+    out[static_cast<long long>(f0 + f) * channels4 + c] = v;
   }
-  float4 v = make_float4(sum[0], sum[1], sum[2], sum[3]);
-  if (alpha_out != nullptr)
-    v = SnakeOf(v, alpha_out[c]);
-  out[i] = v;
 }
 
 /// samples[t] = tanh(bias + sum_{c, j} w[c][j] in[t + j][c]); one warp per
 /// output frame.
 __global__ void VaeToMonoKernel(const float* in, const float* w, float bias,
                                 float* samples, int frames, int channels) {
+  GridDependencyWait();
   const int warp = static_cast<int>((blockIdx.x * blockDim.x + threadIdx.x) / 32);
   const int lane = threadIdx.x % 32;
   if (warp >= frames)
@@ -420,6 +474,17 @@ __global__ void VaeToMonoKernel(const float* in, const float* w, float bias,
     sum += __shfl_xor_sync(0xFFFFFFFFu, sum, o);
   if (lane == 0)
     samples[warp] = tanhf(sum + bias);
+}
+
+constexpr int kDepthwiseSmemMax = 64 << 10;
+
+int DepthwiseSmem(int frames, int dilation, int groups) {
+  return (frames + (kVaeKernel - 1) * dilation) * groups * 16;
+}
+
+void Launched(int status, const char* what) {
+  if (status != kOk)
+    CudaCheck(cudaGetLastError(), what);
 }
 
 unsigned BlocksOf(long long count, int threads = kThreads) {
@@ -579,6 +644,10 @@ class AudioVae {
       channels /= 2;
     }
     layout_ = SeededVaeWeights(config, seed);
+    CudaCheck(cudaFuncSetAttribute(VaeWindowDepthwiseKernel,
+                                   cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                   kDepthwiseSmemMax),
+              "AudioVAE depthwise");
     SetSmem(VaeProductKernel<64, 64>, ProductSmem<64, 64>());
     SetSmem(VaeProductKernel<64, 32>, ProductSmem<64, 32>());
     SetSmem(VaeProductKernel<32, 64>, ProductSmem<32, 64>());
@@ -771,13 +840,12 @@ class AudioVae {
     const float* b = at(bias);
     const int acc = accumulate ? 1 : 0;
     if (rows <= 8) {
-      const unsigned ctas = (out + 7) / 8;  // 4 warps of 2 columns
-      if (rows <= 4)
-        VaeSkinnyKernel<4, 2><<<ctas, 128, 0, stream_>>>(x, ldx, w, b, y, rows,
-                                                          k, out, acc);
-      else
-        VaeSkinnyKernel<8, 2><<<ctas, 128, 0, stream_>>>(x, ldx, w, b, y, rows,
-                                                          k, out, acc);
+      const dim3 ctas((out + 7) / 8);  // 4 warps of 2 columns
+      Launched(LaunchKernel(rows <= 4 ? VaeSkinnyKernel<4, 2>
+                                      : VaeSkinnyKernel<8, 2>,
+                            ctas, dim3(128), 0, stream_, dim3(1), x, ldx, w, b,
+                            y, rows, k, out, acc),
+               "AudioVAE product");
       return;
     }
     struct Tile {
@@ -805,22 +873,13 @@ class AudioVae {
         break;
     }
     const int k_split = (k / splits + kDepth - 1) / kDepth * kDepth;
-    cudaLaunchConfig_t launch = {};
-    launch.gridDim = dim3((out + pick->cols - 1) / pick->cols,
-                          (rows + pick->rows - 1) / pick->rows, splits);
-    launch.blockDim = dim3(kThreads);
-    launch.dynamicSmemBytes = pick->smem;
-    launch.stream = stream_;
-    cudaLaunchAttribute cluster[1];
-    cluster[0].id = cudaLaunchAttributeClusterDimension;
-    cluster[0].val.clusterDim.x = 1;
-    cluster[0].val.clusterDim.y = 1;
-    cluster[0].val.clusterDim.z = splits;
-    launch.attrs = cluster;
-    launch.numAttrs = splits > 1 ? 1 : 0;
-    CudaCheck(cudaLaunchKernelEx(&launch, pick->kernel, x, ldx, w, b, y, rows,
-                                 k, out, acc, k_split),
-              "AudioVAE product");
+    Launched(LaunchKernel(pick->kernel,
+                          dim3((out + pick->cols - 1) / pick->cols,
+                               (rows + pick->rows - 1) / pick->rows, splits),
+                          dim3(kThreads), pick->smem, stream_,
+                          dim3(1, 1, splits), x, ldx, w, b, y, rows, k, out,
+                          acc, k_split),
+             "AudioVAE product");
   }
 
   /// The block's window (Snake of the rate-conditioned input after one
@@ -830,14 +889,16 @@ class AudioVae {
     const State& s = states_[state++];
     const int rows = static_cast<int>(s.rows);
     const long long count4 = static_cast<long long>(rows + t) * width / 4;
-    VaeWindowKernel<<<BlocksOf(count4), kThreads, 0, stream_>>>(
-        reinterpret_cast<const float4*>(in),
+    Launched(LaunchKernel(
+        VaeWindowKernel, dim3(BlocksOf(count4)), dim3(kThreads), 0, stream_,
+        dim3(1), reinterpret_cast<const float4*>(in),
         reinterpret_cast<const float4*>(s.data[phase_]),
         reinterpret_cast<float4*>(work_),
         reinterpret_cast<float4*>(s.data[phase_ ^ 1]), t, rows, width / 4,
         reinterpret_cast<const float4*>(alpha),
         reinterpret_cast<const float4*>(scale),
-        reinterpret_cast<const float4*>(bias));
+        reinterpret_cast<const float4*>(bias)),
+             "AudioVAE window");
   }
 
   /// A depthwise convolution over its window, formed on the fly from the
@@ -849,14 +910,29 @@ class AudioVae {
                        const float* alpha_out) {
     const State& s = states_[state++];
     const int rows = static_cast<int>(s.rows);
-    const long long items = static_cast<long long>(t + rows) * width / 4;
-    VaeWindowDepthwiseKernel<<<BlocksOf(items), kThreads, 0, stream_>>>(
+    const int channels4 = width / 4;
+    const int groups = DepthwiseGroups(channels4);
+    const int per_pass = kThreads / groups;
+    const int channel_tiles = (channels4 + groups - 1) / groups;
+    // Frames per CTA: as many passes as keep the launch at a wave or more,
+    // within the shared memory of the window.
+    int frames = per_pass;
+    while (frames < 64 &&
+           static_cast<long long>((t + 2 * frames - 1) / (2 * frames)) *
+                   channel_tiles >= kSms &&
+           DepthwiseSmem(2 * frames, dilation, groups) <= kDepthwiseSmemMax)
+      frames *= 2;
+    const dim3 grid((t + frames - 1) / frames + 1, channel_tiles);
+    Launched(LaunchKernel(
+        VaeWindowDepthwiseKernel, grid, dim3(kThreads),
+        DepthwiseSmem(frames, dilation, groups), stream_, dim3(1),
         reinterpret_cast<const float4*>(in),
         reinterpret_cast<const float4*>(s.data[phase_]),
         reinterpret_cast<float4*>(s.data[phase_ ^ 1]),
-        reinterpret_cast<float4*>(scratch_), t, rows, width / 4, dilation,
-        reinterpret_cast<const float4*>(alpha_in), at(weight), at(bias),
-        reinterpret_cast<const float4*>(alpha_out));
+        reinterpret_cast<float4*>(scratch_), t, rows, channels4, dilation,
+        frames, reinterpret_cast<const float4*>(alpha_in), at(weight),
+        at(bias), reinterpret_cast<const float4*>(alpha_out)),
+             "AudioVAE depthwise");
   }
 
   /// vae.cpp:415-516 (Run): latents_ -> samples_ -> pinned_, as launches on
@@ -890,9 +966,13 @@ class AudioVae {
     }
     const int c = layout_.out_channels;
     Window(state, hidden_, t, c, at(layout_.out_alpha), nullptr, nullptr);
-    VaeToMonoKernel<<<BlocksOf(static_cast<long long>(t) * 32), kThreads, 0,
-                      stream_>>>(work_, at(layout_.out_conv), layout_.out_bias,
-                                 samples_, t, c);
+    Launched(LaunchKernel(VaeToMonoKernel,
+                          dim3(BlocksOf(static_cast<long long>(t) * 32)),
+                          dim3(kThreads), 0, stream_, dim3(1),
+                          static_cast<const float*>(work_),
+                          at(layout_.out_conv), layout_.out_bias, samples_, t,
+                          c),
+             "AudioVAE output");
     CudaCheck(cudaMemcpyAsync(pinned_, samples_, t * sizeof(float),
                               cudaMemcpyDeviceToHost, stream_),
               "AudioVAE samples");
