@@ -65,8 +65,13 @@ def parse():
     p.add_argument("--steps", type=int, default=400_000)
     p.add_argument("--warmup", type=int, default=20_000)
     p.add_argument("--impl", choices=["ours", "reference"], default="ours")
-    p.add_argument("--case", choices=["product", "dit", "wide", "batch", "matmul", "vae"], default=None,
+    p.add_argument("--case", choices=["product", "dit", "wide", "batch", "matmul", "vae", "step"], default=None,
                    help="run a few launches of one kernel for a profiler and exit (no JSON line)")
+    p.add_argument("--max-ctas", type=int, default=0,
+                   help="with --case: cap the persistent kernels' CTAs (vx_set_persistent_max_ctas)")
+    p.add_argument("--non-cooperative", action="store_true",
+                   help="with --case: launch the persistent kernels without the cooperative attribute "
+                        "(vx_set_persistent_cooperative(0)), for profilers")
     return p.parse_args()
 
 
@@ -1020,11 +1025,13 @@ def measure_box_batched(c, requests) -> float:
     return a.elapsed_time(b) / 1e3
 
 
-def profile_case(case: str) -> None:
+def profile_case(case: str, max_ctas: int = 0, cooperative: bool = True) -> None:
     """A few launches of one kernel on a small case, for ncu captures:
     `product`: 8 config-0 products with the stream plan (independent), then 8
     with the planner's plan (dependent); `dit`: two eager DiT patches (the
-    persistent kernel) on the released DiT with one-layer LMs; `wide`: three
+    persistent kernel) on the released DiT with one-layer LMs; `step`: two
+    eager steps at context 512 (bf16 cache) with a 4-layer LM and a 2-layer
+    residual LM (the persistent stack kernel at the released widths); `wide`: three
     products of 88 rows of 1024 -> 8192 (the gate/up product of four batched
     slots' DiT rows; the planner gives it to the wide tcgen05 kernel);
     `batch`: two steps of a GeneratorBatch of 8 slots on the released shapes
@@ -1041,6 +1048,31 @@ def profile_case(case: str) -> None:
 
     lib = _lib.load()
     torch.cuda.set_device(0)
+    lib.vx_set_persistent_max_ctas(max_ctas)
+    lib.vx_set_persistent_cooperative(int(cooperative))
+    if case == "step":
+        from voxcpm_b200.generator import Generator, released_config
+
+        c = released_config()
+        c.lm.layers, c.residual_lm.layers = 4, 2
+        c.max_length = 600
+        c.vocab = 1024
+        gen = Generator(c, seed=7, cache_type=_lib.CACHE_BF16)
+        gen.SetGraphs(False)
+        rng = np.random.default_rng(0)
+        rows = 512
+        audio = np.zeros(rows, np.int32)
+        audio[-1] = 1
+        feats = np.zeros((rows, c.patch_size, c.feat_dim), np.float32)
+        feats[-1] = rng.normal(0, 1, (c.patch_size, c.feat_dim))
+        gen.Prefill(rng.integers(0, c.vocab, rows).astype(np.int32), 1 - audio, audio, feats)
+        for _ in range(2):
+            gen.Step(rng.normal(0, 1, (c.patch_size, c.feat_dim)).astype(np.float32), 10, 2.0)
+        gen.close()
+        if K.DeviceError():
+            raise RuntimeError("a bounded device wait expired")
+        print(f"case {case}: ok", flush=True)
+        return
     if case == "vae":
         from voxcpm_b200.vae import AudioVae, default_vae_config
 
@@ -1147,7 +1179,7 @@ def profile_case(case: str) -> None:
 def main():
     args = parse()
     if args.case is not None:
-        profile_case(args.case)
+        profile_case(args.case, args.max_ctas, not args.non_cooperative)
         return
     world, rank, local = init_dist(args.gpus)
     try:

@@ -586,6 +586,19 @@ VX_API vx_status vx_generator_set_persistent(vx_generator* generator,
                                              int enabled);
 /* 1 when the DiT patch runs as the persistent kernel. */
 VX_API int vx_generator_persistent(const vx_generator* generator);
+/* Caps the CTAs of the persistent DiT and stack kernels launched from now on
+ * (0: no cap, the default: as many as the occupancy query says co-reside;
+ * below a kernel's minimum of 128 CTAs the minimum). Graphs captured before
+ * keep their grids. For tuning and for profilers that hold back resources.
+ * No reference counterpart. */
+VX_API void vx_set_persistent_max_ctas(size_t ctas);
+/* Whether the persistent kernels launch with the cooperative attribute
+ * (default 1). With 0 their CTAs' co-residency rests on the grid fitting
+ * an idle GPU (one CTA per SM); when it does not, the kernels' bounded waits
+ * end the step with VX_DEVICE_TIMEOUT instead of waiting for good. For
+ * profilers that cannot replay cooperative launches with thread-block
+ * clusters. No reference counterpart. */
+VX_API void vx_set_persistent_cooperative(int enabled);
 /* Rows in the caches (Generator::position, generator.hpp:69-70). */
 VX_API size_t vx_generator_position(const vx_generator* generator);
 /* The last patch's latent [patch][feat] in device memory, valid until the

@@ -213,3 +213,71 @@ def test_aborted_patch_reports_device_timeout(cuda):
     after = gen.DitPatch(mu, cond, noise, 10, 2.0)
     assert np.array_equal(after, before)
     gen.close()
+
+
+def test_persistent_kernels_at_fewer_ctas(cuda):
+    """The persistent DiT and stack kernels split their work by the grid
+    they get: capped at their minimum of 128 CTAs, a patch and steps match
+    the oracle with the same limits and the uncapped kernels within the
+    paths' limit."""
+    lib = _lib.load()
+    c = small_config()
+    hidden = c.lm.hidden
+    full = Generator(c, seed=31)
+    lib.vx_set_persistent_max_ctas(128)
+    try:
+        capped = Generator(c, seed=31)
+        ref = OracleGenerator(c, seed=31)
+        mu, cond, noise = inputs(c, 9)
+        latent_c = capped.DitPatch(mu, cond, noise, 10, 2.0)
+        latent_f = full.DitPatch(mu, cond, noise, 10, 2.0)
+        e_ref = rel_l2(latent_c, ref.dit_patch(mu, cond, noise, 10, 2.0))
+        e_paths = rel_l2(latent_c, latent_f)
+        print(f"patch at 128 CTAs: vs oracle {e_ref:.3e}, vs full grid {e_paths:.3e}")
+        assert e_ref < LATENT_LIMIT and e_paths < PATHS_LIMIT
+        p = prompt(c, 4, rows=10, audio=(9,))
+        for g in (capped, full):
+            g.Prefill(*p)
+        ref.prefill(*p)
+        rng = np.random.default_rng(8)
+        for k in range(2):
+            step_noise = rng.normal(0, 1, (c.patch_size, c.feat_dim)).astype(np.float32)
+            latent_c, stop_c = capped.Step(step_noise, 10, 2.0)
+            latent_f, _ = full.Step(step_noise, 10, 2.0)
+            latent_r, stop_r = ref.step(step_noise, 10, 2.0)
+            e_lm = rel_l2(capped.State("lm_output", hidden), ref.lm_output)
+            print(f"step {k} at 128 CTAs: latent vs oracle {rel_l2(latent_c, latent_r):.3e} "
+                  f"vs full grid {rel_l2(latent_c, latent_f):.3e}, lm output vs oracle {e_lm:.3e}")
+            assert rel_l2(latent_c, latent_r) < LATENT_LIMIT and rel_l2(latent_c, latent_f) < PATHS_LIMIT
+            assert e_lm < STATE_LIMIT and float(np.max(np.abs(stop_c - stop_r))) < STOP_ATOL
+        assert DeviceError() == 0
+        capped.close()
+    finally:
+        lib.vx_set_persistent_max_ctas(0)
+    full.close()
+
+
+def test_persistent_kernels_without_the_cooperative_attribute(cuda):
+    """Launched without the cooperative attribute (for profilers), the same
+    grid on an idle GPU gives the same bits as the cooperative launch."""
+    lib = _lib.load()
+    c = small_config()
+    mu, cond, noise = inputs(c, 12)
+    coop = Generator(c, seed=41)
+    p = prompt(c, 5, rows=10, audio=(9,))
+    coop.Prefill(*p)
+    step_noise = np.random.default_rng(2).normal(0, 1, (c.patch_size, c.feat_dim)).astype(np.float32)
+    expected_patch = coop.DitPatch(mu, cond, noise, 10, 2.0)
+    expected_step = coop.Step(step_noise, 10, 2.0)
+    lib.vx_set_persistent_cooperative(0)
+    try:
+        plain = Generator(c, seed=41)
+        plain.Prefill(*p)
+        assert np.array_equal(plain.DitPatch(mu, cond, noise, 10, 2.0), expected_patch)
+        latent, stop = plain.Step(step_noise, 10, 2.0)
+        assert np.array_equal(latent, expected_step[0]) and np.array_equal(stop, expected_step[1])
+        assert DeviceError() == 0
+        plain.close()
+    finally:
+        lib.vx_set_persistent_cooperative(1)
+    coop.close()

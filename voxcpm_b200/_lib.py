@@ -261,6 +261,8 @@ SIGNATURES: dict[str, tuple] = {
     "vx_generator_dit_patch_static": (c_int, [c_void_p, c_void_p, c_void_p, c_void_p, c_size_t, c_float, c_void_p]),
     "vx_generator_replay_dit_patch": (c_int, [c_void_p]),
     "vx_set_dit_stall_for_tests": (None, [c_uint64]),
+    "vx_set_persistent_max_ctas": (None, [c_size_t]),
+    "vx_set_persistent_cooperative": (None, [c_int]),
     "vx_generator_state": (c_int, [c_void_p, c_char_p, c_void_p, c_size_t]),
     "vx_generator_set_state": (c_int, [c_void_p, c_char_p, c_void_p, c_size_t]),
     "vx_generator_set_graphs": (c_int, [c_void_p, c_int]),

@@ -260,6 +260,14 @@ void vx_set_dit_stall_for_tests(uint64_t limit_ns) {
   vx::SetDitStall(limit_ns);
 }
 
+void vx_set_persistent_max_ctas(size_t ctas) {
+  vx::SetPersistentMaxCtas(ctas > 4096 ? 4096 : static_cast<int>(ctas));
+}
+
+void vx_set_persistent_cooperative(int enabled) {
+  vx::SetPersistentCooperative(enabled != 0);
+}
+
 vx_status vx_generator_replay_dit_patch(vx_generator* generator) {
   return Guard(generator, "vx_generator_replay_dit_patch",
                [&](vx::Generator& g) { g.ReplayDitPatch(); });

@@ -263,4 +263,18 @@ __device__ inline void PrefetchL2(const void* p, int bytes, int tid) {
 }
 
 }  // namespace
+
+/// The most CTAs a persistent kernel launches (0: no cap; below a kernel's
+/// minimum the minimum). A tuning and profiling knob: a profiler may hold
+/// back resources, so fewer CTAs than the occupancy query gives co-reside.
+void SetPersistentMaxCtas(int ctas);
+int PersistentMaxCtas();
+/// Whether the persistent kernels launch with the cooperative attribute
+/// (default on). Off, their co-residency rests on the grid fitting an idle
+/// GPU (one CTA per SM); if it does not, the bounded waits end the launch
+/// with the abort word set. For profilers that cannot replay cooperative
+/// cluster launches.
+void SetPersistentCooperative(bool enabled);
+bool PersistentCooperative();
+
 }  // namespace vx

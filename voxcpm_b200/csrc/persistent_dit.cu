@@ -11,6 +11,7 @@
 #include "persistent_dit.cuh"
 
 #include <cmath>
+#include <algorithm>
 #include <atomic>
 #include <mutex>
 #include <string>
@@ -1098,6 +1099,9 @@ int DitCtas(bool q8) {
       return 0;
     state.ctas[which] = clusters >= kGroups ? 2 * clusters : 0;
   }
+  const int cap = PersistentMaxCtas();
+  if (cap > 0 && state.ctas[which] > 0)
+    return std::min(state.ctas[which], std::max(cap / 2 * 2, 2 * kGroups));
   return state.ctas[which];
 }
 
@@ -1150,6 +1154,16 @@ std::atomic<std::uint64_t> g_dit_stall_ns{0};
 }  // namespace
 
 void SetDitStall(std::uint64_t limit_ns) { g_dit_stall_ns = limit_ns; }
+
+namespace {
+std::atomic<int> g_persistent_max_ctas{0};
+std::atomic<bool> g_persistent_cooperative{true};
+}  // namespace
+
+void SetPersistentMaxCtas(int ctas) { g_persistent_max_ctas = ctas > 0 ? ctas : 0; }
+int PersistentMaxCtas() { return g_persistent_max_ctas; }
+void SetPersistentCooperative(bool enabled) { g_persistent_cooperative = enabled; }
+bool PersistentCooperative() { return g_persistent_cooperative; }
 
 int DitLaunchAborted(const DitPatchParams& params, cudaStream_t stream,
                      bool* aborted) {
@@ -1224,10 +1238,13 @@ int LaunchDitPatch(const DitPatchParams& p, cudaStream_t stream) {
   cudaLaunchAttribute attribute[2];
   const cudaLaunchConfig_t config =
       DitConfig(q8, static_cast<unsigned>(ctas), stream, attribute);
+  cudaLaunchConfig_t launch_config = config;
+  if (!PersistentCooperative())
+    launch_config.numAttrs = 1;  // the cluster shape only
   DitPatchParams launch = p;
   launch.stall_limit_ns = g_dit_stall_ns;
   return FromCuda(
-      cudaLaunchKernelEx(&config, DitKernel(q8), launch, error_word),
+      cudaLaunchKernelEx(&launch_config, DitKernel(q8), launch, error_word),
       "persistent DiT launch");
 }
 

@@ -91,6 +91,10 @@ struct DitPatchParams {
 
 /// The test hook above for every later launch of this process (0: off).
 void SetDitStall(std::uint64_t limit_ns);
+/// The CTA cap and the cooperative attribute of the persistent kernels
+/// (persistent_common.cuh).
+void SetPersistentMaxCtas(int ctas);
+void SetPersistentCooperative(bool enabled);
 /// Whether the last launch that used `params.sync` aborted (sync word 0 set
 /// by a CTA whose bounded wait gave up); clears the word. Synchronizes
 /// `stream` first.

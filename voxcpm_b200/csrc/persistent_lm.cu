@@ -10,6 +10,7 @@
 #include "persistent_lm.cuh"
 
 #include <cmath>
+#include <algorithm>
 #include <mutex>
 #include <string>
 
@@ -788,6 +789,9 @@ int LmCtas() {
       return 0;
     ctas[device] = sms >= kTasks ? sms : 0;
   }
+  const int cap = PersistentMaxCtas();
+  if (cap > 0 && ctas[device] > 0)
+    return std::min(ctas[device], std::max(cap, kTasks));
   return ctas[device];
 }
 
@@ -845,7 +849,7 @@ int LaunchLmStack(const LmStackParams& p, cudaStream_t stream) {
   attribute[0].id = cudaLaunchAttributeCooperative;
   attribute[0].val.cooperative = 1;
   config.attrs = attribute;
-  config.numAttrs = 1;
+  config.numAttrs = PersistentCooperative() ? 1 : 0;
   return FromCuda(cudaLaunchKernelEx(&config, LmStackKernel, p, error_word),
                   "persistent stack launch");
 }
