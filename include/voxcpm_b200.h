@@ -234,6 +234,11 @@ VX_API vx_status vx_stage(void* dst, const void* src, size_t bytes,
 /* Programmatic dependent launch for every kernel of the library (default on).
  * No reference counterpart (HIP has none). */
 VX_API void vx_set_programmatic_launch(int enabled);
+/* Dependent product launches (the default) with more CTAs than a
+ * same-shaped launch leaves SMs free start their first CTAs while the
+ * previous product runs; with this on (default 1) those CTAs prefetch the
+ * other CTAs' weights into L2. No reference counterpart. */
+VX_API void vx_set_product_l2_prefetch(int enabled);
 /* Whether the planner gives Q8_0 products of 9..32 rows to the tensor-core
  * (tcgen05) kernel, plan variant VX_TENSOR_CORE_VARIANT, or (default) to the
  * mma.sync kernels. A plan with that variant runs it either way. No reference counterpart (the reference has one

@@ -360,3 +360,34 @@ def test_half_tile_math_wide_rows(cuda, rows):
     differ = int((ys[13] != ys[14]).sum())
     print(f"rows {rows}: {differ} of {rows * out} sums differ from variant 13's bits")
     assert K.DeviceError() == 0
+
+
+def test_global_activation_variants(cuda):
+    """The variants that read activation fragments from global memory
+    (22-24) at every row count of their tile classes (rows past `m` read as
+    zeros), accumulating and not, against the exact sums."""
+    rng = np.random.default_rng(23)
+    columns, out = 1024, 640
+    blocks, q8_tiles, dequant, bf16_tiles = prepare(out, columns, rng)
+    for rows in (1, 5, 8, 9, 17, 22, 32):
+        x = make_activations(rows, columns, rng)
+        x_dev = to_dev(x)
+        before = rng.normal(0, 1, (rows, out)).astype(np.float32)
+        for accumulate in (False, True):
+            exact = oracle.product_exact(x, oracle.Q8_0, blocks, rows, columns, out,
+                                         before if accumulate else None)
+            exact_rows = oracle.product_exact(x, oracle.BF16_ROWS, from_dev_u16(dequant), rows, columns, out,
+                                              before if accumulate else None)
+            for variant in (22, 23, 24):
+                for splits in (1, 2):
+                    plan = _lib.WmmaPlan(splits, columns // 32 // splits, 0, 0, variant)
+                    for fmt, w, ex in ((_lib.WEIGHTS_Q8_TILES, q8_tiles, exact),
+                                       (_lib.WEIGHTS_BF16_TILES, bf16_tiles, exact_rows),
+                                       (_lib.WEIGHTS_BF16, dequant, exact_rows)):
+                        y = torch.from_numpy(before).cuda() if accumulate else \
+                            torch.zeros(rows, out, dtype=torch.float32, device="cuda")
+                        assert K.Product(fmt, x_dev, w, y, rows, columns, out, accumulate, plan)
+                        torch.cuda.synchronize()
+                        err = oracle.relative_error(y.cpu().numpy(), *ex)
+                        assert err <= LIMIT, f"rows {rows} variant {variant} splits {splits} format {fmt}"
+    assert K.DeviceError() == 0

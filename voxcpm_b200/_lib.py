@@ -213,6 +213,7 @@ SIGNATURES: dict[str, tuple] = {
     ),
     "vx_stage": (c_int, [c_void_p, c_void_p, c_size_t, c_void_p]),
     "vx_set_programmatic_launch": (None, [c_int]),
+    "vx_set_product_l2_prefetch": (None, [c_int]),
     "vx_set_tensor_core_products": (None, [c_int]),
     "vx_tensor_core_products": (c_int, []),
     "vx_set_wide_tensor_core_products": (None, [c_int]),

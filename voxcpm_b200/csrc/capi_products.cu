@@ -321,6 +321,10 @@ void vx_set_programmatic_launch(int enabled) {
   vx::SetProgrammaticLaunch(enabled != 0);
 }
 
+void vx_set_product_l2_prefetch(int enabled) {
+  vx::SetProductL2Prefetch(enabled != 0);
+}
+
 void vx_set_tensor_core_products(int enabled) {
   vx::SetTensorCoreProducts(enabled != 0);
 }

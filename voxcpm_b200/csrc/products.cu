@@ -76,6 +76,8 @@ struct VariantShape {
   int stage;       // 32-column blocks per pipeline stage
   int depth;       // stages in flight per warp
   bool half;       // Q8_0: fp16 tile math over exactly scaled activations
+  bool x_global;   // activation fragments read from global memory (L1/L2),
+                   // not staged in shared memory
 };
 
 __host__ __device__ constexpr int WarpsOf(const VariantShape& v) {
@@ -115,6 +117,14 @@ constexpr VariantShape kVariants[] = {
     {4, 4, 1, 8, 2},   // 19: 64 rows, 16 warps (4 ways)
     {2, 4, 1, 4, 2},   // 20: 32 rows, 8 warps (4 ways), 4-block stages
     {1, 4, 1, 8, 2},   // 21: 16 rows, 4 warps (4 ways)
+    // Variants 16, 17 and 19 with the activation fragments read from global
+    // memory (through L1) instead of a shared-memory copy: a CTA then holds
+    // only its weight rings (104 KB for 48 Q8_0 rows of 2048), so a
+    // dependent launch's CTAs fit beside the running ones and stream their
+    // weights while those finish.
+    {3, 4, 1, 8, 2, false, true},  // 22: 48 rows, 12 warps (4 ways)
+    {2, 4, 1, 8, 2, false, true},  // 23: 32 rows, 8 warps (4 ways)
+    {4, 4, 1, 8, 2, false, true},  // 24: 64 rows, 16 warps (4 ways)
 };
 constexpr int kNumVariants = sizeof(kVariants) / sizeof(kVariants[0]);
 // The cost model chooses among the first eight shapes only: their plans fit
@@ -163,23 +173,41 @@ struct ProductArgs {
   int x_stride;     // bytes per activation row in shared memory
   int rings_bytes;  // bytes of all warps' rings (>= the reduction buffers)
   int wait;         // wait for the preceding kernel before reading x / y
+  // Dependent launches whose CTAs outnumber the SMs a same-shaped launch
+  // leaves free: the first `prefetch_ctas` CTAs (they start while the
+  // previous product runs) ask L2 for the weights of the CTAs after them,
+  // `panel_bytes` per CTA of the `w_bytes` in all.
+  int prefetch_ctas;
+  long long panel_bytes;
+  long long w_bytes;
 };
 
 /// All blocks of one landed stage. A full stage is unrolled without guards
 /// so the compiler can interleave the blocks' loads, conversions and MMAs.
-template <int kFormat, int kGroups, int kNTiles, int kStage, bool kHalf>
+template <int kFormat, int kGroups, int kNTiles, int kStage, bool kHalf,
+          bool kXGlobal = false>
 __device__ __forceinline__ void StageProduct(
     const unsigned char* stage_base, int group_bytes, const unsigned char* xs,
     int x_stride, int column0, int nb, int my_groups, int gid, int tig,
-    float (&acc)[kGroups][kNTiles][4]) {
+    float (&acc)[kGroups][kNTiles][4], int m = 0) {
   constexpr int kRowStride = RowStrideBytes(kStage);
   auto block = [&](int kb) {
     uint4 b[kNTiles];
     const int column = column0 + kb * 32 + 8 * tig;
 #pragma unroll
-    for (int j = 0; j < kNTiles; ++j)
-      b[j] = *reinterpret_cast<const uint4*>(xs + (8 * j + gid) * x_stride +
-                                             column * 2);
+    for (int j = 0; j < kNTiles; ++j) {
+      if constexpr (kXGlobal) {
+        // Rows past `m` are not in the activations: zeros.
+        b[j] = 8 * j + gid < m
+                   ? *reinterpret_cast<const uint4*>(
+                         xs + static_cast<std::size_t>(8 * j + gid) * x_stride +
+                         column * 2)
+                   : make_uint4(0, 0, 0, 0);
+      } else {
+        b[j] = *reinterpret_cast<const uint4*>(xs + (8 * j + gid) * x_stride +
+                                               column * 2);
+      }
+    }
 #pragma unroll
     for (int g = 0; g < kGroups; ++g)
       if (g < my_groups)
@@ -264,9 +292,10 @@ __device__ inline void CopyRowsAsync(unsigned char* dst, int dst_stride,
 }
 
 template <int kFormat, int kCtaGroups, int kWays, int kGroups, int kNTiles,
-          int kStage, int kDepth, bool kHalf>
+          int kStage, int kDepth, bool kHalf, bool kXGlobal>
 __global__ void __launch_bounds__(kCtaGroups / kGroups * kWays * 32)
     ProductKernel(const ProductArgs p) {
+  static_assert(!(kHalf && kXGlobal), "fp16 tile math rescales a shared copy");
   constexpr int kWarps = kCtaGroups / kGroups * kWays;
   constexpr int kGroupBytes = GroupStageBytes(kFormat, kStage);
   constexpr int kRingBytes = kDepth * kGroups * kGroupBytes;
@@ -296,7 +325,8 @@ __global__ void __launch_bounds__(kCtaGroups / kGroups * kWays * 32)
   const int my_groups = max(0, min(kGroups, groups_total - group0));
 
   unsigned char* xs = smem;
-  unsigned char* rings = smem + ((x_rows * p.x_stride + 127) / 128) * 128;
+  unsigned char* rings =
+      kXGlobal ? smem : smem + ((x_rows * p.x_stride + 127) / 128) * 128;
   std::uint64_t* bars =
       reinterpret_cast<std::uint64_t*>(rings + p.rings_bytes);
   std::uint64_t* xbar = bars + kWarps * kDepth;
@@ -313,7 +343,7 @@ __global__ void __launch_bounds__(kCtaGroups / kGroups * kWays * 32)
       row_unscale[i] = 1.0f;
   }
   // Activation rows past `m` read as zeros.
-  {
+  if constexpr (!kXGlobal) {
     uint4* pad = reinterpret_cast<uint4*>(xs + p.m * p.x_stride);
     const int count = (x_rows - p.m) * p.x_stride / 16;
     for (int i = threadIdx.x; i < count; i += blockDim.x)
@@ -372,6 +402,19 @@ __global__ void __launch_bounds__(kCtaGroups / kGroups * kWays * 32)
     for (; issued < min(kDepth, my_stages); ++issued)
       issue(issued);
   }
+  if (p.prefetch_ctas > 0 && static_cast<int>(blockIdx.x) < p.prefetch_ctas &&
+      threadIdx.x == 0) {
+    constexpr long long kChunk = 64 << 10;
+    const long long begin = p.prefetch_ctas * p.panel_bytes;
+    const long long share =
+        ((p.w_bytes - begin + p.prefetch_ctas - 1) / p.prefetch_ctas + 15) /
+        16 * 16;
+    const long long from = begin + blockIdx.x * share;
+    const long long to = min(p.w_bytes, from + share);
+    for (long long at = from; at + 16 <= to; at += kChunk)
+      PrefetchL2Bulk(p.w + at,
+                     static_cast<unsigned>(min(kChunk, to - at) / 16 * 16));
+  }
   // Weights do not depend on earlier kernels; activations (and y) may.
   GridLaunchDependents();
   if (p.wait)
@@ -383,8 +426,10 @@ __global__ void __launch_bounds__(kCtaGroups / kGroups * kWays * 32)
   // by every thread, all in flight at once, then one CTA barrier, which
   // measured up to 2x faster there (one-row 2048 -> 6144: 7.3 -> 3.4 us per
   // product in a stream; at 22 rows up to 1.7x slower).
-  const bool bulk_x = p.wait != 0 || p.m > 8;
-  if (bulk_x) {
+  const bool bulk_x = !kXGlobal && (p.wait != 0 || p.m > 8);
+  if (kXGlobal) {
+    // The fragments are read in place, after the wait above.
+  } else if (bulk_x) {
     if (warp == 0 && nblocks > 0) {
       if (lane == 0)
         MbarArriveExpectTx(xbar, p.m * nblocks * 64);
@@ -442,9 +487,16 @@ __global__ void __launch_bounds__(kCtaGroups / kGroups * kWays * 32)
       ++waited;
       const int st = way + i * kWays;
       const int nb = min(kStage, last - (first + st * kStage));
-      StageProduct<kFormat, kGroups, kNTiles, kStage, kHalfMath>(
-          ring + slot * kGroups * kGroupBytes, kGroupBytes, xs, p.x_stride,
-          st * kStage * 32, nb, my_groups, gid, tig, acc);
+      if constexpr (kXGlobal) {
+        StageProduct<kFormat, kGroups, kNTiles, kStage, false, true>(
+            ring + slot * kGroups * kGroupBytes, kGroupBytes,
+            reinterpret_cast<const unsigned char*>(p.x + first * 32), p.k * 2,
+            st * kStage * 32, nb, my_groups, gid, tig, acc, p.m);
+      } else {
+        StageProduct<kFormat, kGroups, kNTiles, kStage, kHalfMath>(
+            ring + slot * kGroups * kGroupBytes, kGroupBytes, xs, p.x_stride,
+            st * kStage * 32, nb, my_groups, gid, tig, acc);
+      }
       // The slot's values are in registers (consumed above); refill it.
       __syncwarp();
       if (issued < my_stages) {
@@ -585,7 +637,8 @@ constexpr KernelFn KernelFor() {
     return ProductKernel<kFormat, kVariants[kVariant].cta_groups,
                          kVariants[kVariant].ways, kVariants[kVariant].groups,
                          kNTiles, kVariants[kVariant].stage,
-                         kVariants[kVariant].depth, kVariants[kVariant].half>;
+                         kVariants[kVariant].depth, kVariants[kVariant].half,
+                         kVariants[kVariant].x_global>;
   }
 }
 
@@ -596,7 +649,7 @@ struct VariantRow {
 
 template <int kFormat, int kNTiles>
 using Row = VariantRow<kFormat, kNTiles, 0, 1, 2, 3, 4, 5, 6, 7, 8, 9, 10, 11,
-                       12, 13, 14, 15, 16, 17, 18, 19, 20, 21>;
+                       12, 13, 14, 15, 16, 17, 18, 19, 20, 21, 22, 23, 24>;
 
 /// Row classes of the measured plan tables: 1, 2..8, 9..32, 33..128.
 int RowsClass(std::size_t rows) {
@@ -626,6 +679,7 @@ KernelFn Lookup(int format, int ntiles, int variant) {
 }
 
 std::atomic<bool> g_programmatic{true};
+std::atomic<bool> g_l2_prefetch{true};
 std::atomic<bool> g_tensor_core{false};
 
 int SmCount() {
@@ -654,14 +708,17 @@ Footprint FootprintOf(int format, int variant, int ntiles,
   const int rings = warps * v.depth * v.groups * GroupStageBytes(format, v.stage);
   const int reduction = v.ways * v.cta_groups * ntiles * 32 * 16;
   f.rings_bytes = static_cast<int>(Align128(std::max(rings, reduction)));
-  f.smem = Align128(static_cast<std::size_t>(ntiles) * 8 * f.x_stride) +
-           f.rings_bytes + (warps * v.depth + 1) * 8;
+  const std::size_t x_bytes =
+      v.x_global ? 0 : static_cast<std::size_t>(ntiles) * 8 * f.x_stride;
+  f.smem = Align128(x_bytes) + f.rings_bytes + (warps * v.depth + 1) * 8;
   return f;
 }
 
 }  // namespace
 
 void SetProgrammaticLaunch(bool enabled) { g_programmatic = enabled; }
+void SetProductL2Prefetch(bool enabled) { g_l2_prefetch = enabled; }
+bool ProductL2Prefetch() { return g_l2_prefetch; }
 bool ProgrammaticLaunch() { return g_programmatic; }
 void SetTensorCoreProducts(bool enabled) { g_tensor_core = enabled; }
 bool TensorCoreProducts() { return g_tensor_core; }
@@ -690,11 +747,14 @@ struct MeasuredPlan {
   int splits;
 };
 constexpr MeasuredPlan kMeasuredPlans[] = {
-    // Whole-reduction CTAs (variants 16-21; clusters only for reductions
+    // Whole-reduction CTAs (variants 16-24; clusters only for reductions
     // beyond 2048 columns), measured on B200 in dependent chains of CUDA
     // graph launches over rotating weight copies larger than L2, at 1, 8 and
     // 22 rows for classes 0, 1 and 2; in comments the time and the cluster
-    // plan's time before them.
+    // plan's time before them (or the plan it replaced, named). Variants
+    // 22-24 (activations read in place) measured faster for bf16 rows only:
+    // for Q8_0 tiles the shared copy wins (2048 -> 6144 at 22 rows: 7.0 us
+    // with variant 16, 10.8 with 22).
     // Q8_0 tiles, one row.
     {WeightFormat::kQ8Tiles, 0, 1024, 1024, 21, 1},  // 2.24 us (3.34)
     {WeightFormat::kQ8Tiles, 0, 1024, 2560, 16, 1},  // 2.59 us (4.38)
@@ -763,7 +823,7 @@ constexpr MeasuredPlan kMeasuredPlans[] = {
     {WeightFormat::kBf16, 2, 2048, 1024, 21, 1},  // 3.99 us (6.83)
     {WeightFormat::kBf16, 2, 2048, 2048, 21, 1},  // 4.86 us (7.45)
     {WeightFormat::kBf16, 2, 2048, 2560, 20, 1},  // 6.81 us (8.39)
-    {WeightFormat::kBf16, 2, 2048, 6144, 20, 1},  // 13.65 us (14.83)
+    {WeightFormat::kBf16, 2, 2048, 6144, 22, 1},  // 9.06-9.70 us (v20: 13.65)
     {WeightFormat::kBf16, 2, 2048, 12288, 20, 1},  // 21.74 us (39.84)
     {WeightFormat::kBf16, 2, 4096, 1024, 21, 2},  // 5.86 us (12.99)
     {WeightFormat::kBf16, 2, 6144, 2048, 17, 4},  // 13.84 us (24.31)
@@ -1086,6 +1146,31 @@ int LaunchProduct(WeightFormat format, const std::uint16_t* x, const void* w,
   args.x_stride = fp.x_stride;
   args.rings_bytes = fp.rings_bytes;
   args.wait = independent ? 0 : 1;
+  // A dependent launch of more CTAs than the SMs the previous same-shaped
+  // launch leaves free: those free SMs run its first CTAs early, and they
+  // prefetch the rest's weights into L2.
+  args.prefetch_ctas = 0;
+  args.panel_bytes = 0;
+  args.w_bytes = 0;
+  {
+    const int early = SmCount() - panels;
+    if (!independent && g_programmatic && g_l2_prefetch && plan.splits == 1 &&
+        early > 0 && early < panels) {
+      const long long groups = (static_cast<long long>(out) + 15) / 16;
+      const long long group_bytes =
+          f == static_cast<int>(WeightFormat::kBf16)
+              ? 16LL * static_cast<long long>(in) * 2
+              : static_cast<long long>(k_blocks) *
+                    (f == static_cast<int>(WeightFormat::kQ8Tiles)
+                         ? kQ8TileBytes
+                         : kBf16TileBytes);
+      args.prefetch_ctas = early;
+      args.panel_bytes = v.cta_groups * group_bytes;
+      args.w_bytes = f == static_cast<int>(WeightFormat::kBf16)
+                         ? static_cast<long long>(out) * in * 2
+                         : groups * group_bytes;
+    }
+  }
 
   cudaLaunchConfig_t config = {};
   config.gridDim = dim3(static_cast<unsigned>(panels * plan.splits));

@@ -148,6 +148,10 @@ int LaunchProduct(WeightFormat format, const std::uint16_t* x, const void* w,
 
 /// Whether kernels are launched with programmatic dependent launch.
 void SetProgrammaticLaunch(bool enabled);
+/// Whether dependent product launches whose first CTAs start early have them
+/// prefetch the later CTAs' weights into L2 (default on).
+void SetProductL2Prefetch(bool enabled);
+bool ProductL2Prefetch();
 bool ProgrammaticLaunch();
 /// Whether the planner gives Q8_0 products of 9..32 rows to the
 /// tensor-core kernel or (default) to the mma.sync kernels.

@@ -152,6 +152,14 @@ __device__ inline void BulkLoad(void* smem_dst, const void* gmem_src,
       : "memory");
 }
 
+/// Asks L2 to fetch `bytes` of global memory (no copy to the SM; nothing
+/// waits for it). 16-byte aligned address, `bytes` a multiple of 16.
+__device__ inline void PrefetchL2Bulk(const void* gmem, unsigned bytes) {
+  asm volatile("cp.async.bulk.prefetch.L2.global [%0], %1;" ::"l"(gmem),
+               "r"(bytes)
+               : "memory");
+}
+
 __device__ inline std::uint64_t PolicyEvictFirst() {
   std::uint64_t policy;
   asm volatile("createpolicy.fractional.L2::evict_first.b64 %0, 1.0;"
