@@ -333,10 +333,21 @@ __global__ void __launch_bounds__(kCtaGroups / kGroups * kWays * 32)
   unsigned char* ring = rings + warp * kRingBytes;
   std::uint64_t* full = bars + warp * kDepth;
 
+  // The activation slice. After the wait on the previous kernel (dependent
+  // launches), or for more than 8 rows: one bulk copy per row, issued by
+  // lane 0 of every warp in turn (row r by warp r mod warps) onto one
+  // barrier whose byte count is set here. Independent launches of at most
+  // 8 rows (which overlap each other): asynchronous 16-byte copies by every
+  // thread, all in flight at once, then one CTA barrier, which measured up
+  // to 2x faster there (one-row 2048 -> 6144: 7.3 -> 3.4 us per product in
+  // a stream; at 22 rows up to 1.7x slower).
+  const bool bulk_x = !kXGlobal && (p.wait != 0 || p.m > 8);
   if (threadIdx.x == 0) {
     for (int i = 0; i < kWarps * kDepth + 1; ++i)
       MbarInit(&bars[i], 1);
     FenceMbarInit();
+    if (bulk_x && nblocks > 0)
+      MbarArriveExpectTx(xbar, p.m * nblocks * 64);
   }
   if constexpr (kHalfMath) {
     for (int i = threadIdx.x; i < kNTiles * 8; i += blockDim.x)
@@ -419,26 +430,14 @@ __global__ void __launch_bounds__(kCtaGroups / kGroups * kWays * 32)
   GridLaunchDependents();
   if (p.wait)
     GridDependencyWait();
-  // The activation slice. After the wait on the previous kernel (dependent
-  // launches), or for more than 8 rows: one bulk copy per row from one warp,
-  // the form the measured plans were measured with. Independent launches of
-  // at most 8 rows (which overlap each other): asynchronous 16-byte copies
-  // by every thread, all in flight at once, then one CTA barrier, which
-  // measured up to 2x faster there (one-row 2048 -> 6144: 7.3 -> 3.4 us per
-  // product in a stream; at 22 rows up to 1.7x slower).
-  const bool bulk_x = !kXGlobal && (p.wait != 0 || p.m > 8);
   if (kXGlobal) {
     // The fragments are read in place, after the wait above.
   } else if (bulk_x) {
-    if (warp == 0 && nblocks > 0) {
-      if (lane == 0)
-        MbarArriveExpectTx(xbar, p.m * nblocks * 64);
-      __syncwarp();
-      for (int row = lane; row < p.m; row += 32)
+    if (lane == 0 && nblocks > 0)
+      for (int row = warp; row < p.m; row += kWarps)
         BulkLoad(xs + row * p.x_stride,
                  p.x + static_cast<std::size_t>(row) * p.k + first * 32,
                  nblocks * 64, xbar, PolicyEvictLast());
-    }
   } else {
     CopyRowsAsync(xs, p.x_stride, p.x + first * 32, p.k, p.m, nblocks * 4);
     __syncthreads();
