@@ -142,3 +142,26 @@ def test_host_math_matches_the_oracle():
     oracle.lib().vxo_rope_table(10000.0, 128, factors.ctypes.data, 1.0, 64, ref.ctypes.data)
     assert np.array_equal(ours, ref)
     del ctypes
+
+
+def test_audio_vae_arguments_fail_without_a_gpu():
+    """The AudioVAE's C ABI rejects bad configurations and null handles
+    before any device work (vx_audio_vae_*)."""
+    import ctypes
+
+    from voxcpm_b200.vae import default_vae_config, vae_config
+
+    lib = _lib.load()
+    c = default_vae_config()
+    assert (c.latent_dim, c.decoder_dim, c.decoder_rate_count, c.out_sample_rate) == (64, 2048, 6, 48000)
+    assert list(c.decoder_rates[:6]) == [8, 6, 5, 2, 2, 2]
+    assert list(c.sr_bin_boundaries[:3]) == [20000, 30000, 40000] and c.sr_bin_boundary_count == 3
+    for bad in (vae_config(64, 2048, ()), vae_config(6, 64, (2,)), vae_config(64, 36, (2, 2))):
+        assert not lib.vx_audio_vae_create(ctypes.byref(bad), 0)
+        assert b"AudioVAE" in lib.vx_last_error()
+    assert not lib.vx_audio_vae_create(None, 0)
+    assert lib.vx_audio_vae_decode_hop(None) == 0
+    assert lib.vx_audio_vae_reset(None) == _lib.VX_INVALID
+    samples = ctypes.c_size_t(0)
+    assert lib.vx_audio_vae_collect(None, None, 0, ctypes.byref(samples)) == _lib.VX_INVALID
+    lib.vx_audio_vae_destroy(None)
