@@ -391,3 +391,43 @@ def test_global_activation_variants(cuda):
                         err = oracle.relative_error(y.cpu().numpy(), *ex)
                         assert err <= LIMIT, f"rows {rows} variant {variant} splits {splits} format {fmt}"
     assert K.DeviceError() == 0
+
+
+def test_dependent_chain_of_products(cuda):
+    """A chain where every product reads the previous one's bf16 output, on
+    one stream without synchronizing (the generator's pattern): programmatic
+    launch lets each product start before the previous ends, and the
+    config-0 shape's early CTAs prefetch the later CTAs' weights into L2
+    while it runs. Every link matches the exact sum of its own inputs."""
+    rng = np.random.default_rng(31)
+    rows = 22
+    up_blocks, up_tiles, up_dequant, _ = prepare(6144, 2048, rng)        # 2048 -> 6144
+    down_blocks, down_tiles, down_dequant, _ = prepare(2048, 6144, rng)  # 6144 -> 2048
+    gemm = Bf16Gemm()
+    for fmt, up_w, down_w, up_ref, down_ref, ref_fmt in (
+            (_lib.WEIGHTS_Q8_TILES, up_tiles, down_tiles, up_blocks, down_blocks, oracle.Q8_0),
+            (_lib.WEIGHTS_BF16, up_dequant, down_dequant, from_dev_u16(up_dequant), from_dev_u16(down_dequant),
+             oracle.BF16_ROWS)):
+        x = to_dev(make_activations(rows, 2048, rng, std=1.0)).view(torch.bfloat16)
+        links = []
+        current = x
+        for i in range(6):
+            up = i % 2 == 0
+            out, columns = (6144, 2048) if up else (2048, 6144)
+            y = torch.empty(rows, out, dtype=torch.bfloat16, device="cuda")
+            gemm.LinearEx(current, Matrix(fmt, up_w if up else down_w), y, rows, columns, out)
+            links.append((current, y, up))
+            current = y
+        torch.cuda.synchronize()
+        for i, (xi, yi, up) in enumerate(links):
+            out, columns = (6144, 2048) if up else (2048, 6144)
+            x_bits = xi.view(torch.int16).cpu().numpy().view(np.uint16)
+            exact, magnitude = oracle.product_exact(x_bits, ref_fmt, up_ref if up else down_ref, rows, columns, out)
+            y_f = yi.float().cpu().numpy().reshape(-1)
+            # One bf16 rounding of the output on top of the fp32 sum's error
+            # (as test_bf16_output bounds it).
+            err = np.abs(y_f - exact.reshape(-1))
+            bound = 2.0 ** -8 * np.abs(exact.reshape(-1)) + LIMIT * magnitude.reshape(-1)
+            assert bool(np.all(err <= bound)), f"format {fmt} link {i}"
+    assert K.DeviceError() == 0
+    gemm.close()
