@@ -214,3 +214,16 @@ def test_pending_decoding_rules(cuda):
     vae.Reset()
     np.testing.assert_array_equal(out, vae.Decode(x.cpu().numpy()))
     vae.close()
+
+
+@pytest.mark.gpu
+@pytest.mark.parametrize("rate", [16000, 44100])
+def test_other_output_rates(cuda, rate):
+    """The rate conditioning's other embedding rows (bucket 0 at 16 kHz,
+    bucket 3 at 44.1 kHz on the small decoder) against the oracle."""
+    config = dict(SMALL, out_sample_rate=rate)
+    vae = library_vae(config, seed=13)
+    x = latents(6, config["latent_dim"], seed=4)
+    expected = OracleVae(VaeConfig(**config), seed=13).decode(x)
+    assert relative(vae.Decode(x), expected) <= LIMIT
+    vae.close()
