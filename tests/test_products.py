@@ -330,6 +330,78 @@ def test_wide_rows(cuda, columns, out):
     assert K.DeviceError() == 0
 
 
+# Row-split variants: (CTA groups, ways, groups per warp, stage, depth, row split).
+ROW_SPLIT_VARIANTS = {25: (4, 2, 1, 4, 2, 2), 26: (4, 1, 1, 4, 4, 2), 27: (2, 2, 1, 4, 2, 2),
+                      28: (4, 2, 1, 4, 2, 4), 29: (2, 2, 1, 4, 2, 4), 30: (8, 1, 1, 4, 2, 2),
+                      31: (2, 1, 1, 4, 4, 4), 32: (1, 2, 1, 4, 2, 4), 33: (2, 4, 1, 4, 2, 2),
+                      34: (2, 2, 1, 8, 2, 2), 35: (1, 4, 1, 4, 2, 4)}
+
+
+def q8_footprint(shape, ntiles, blocks_per_split):
+    """Shared memory of a Q8_0 launch (the launcher's FootprintOf)."""
+    groups, ways, per_warp, stage, depth, split = shape
+    align = lambda v: (v + 127) // 128 * 128
+    row = blocks_per_split * 64
+    x_stride = row if row % 128 == 64 else align(row) + 64
+    warps = groups // per_warp * ways * split
+    rings = warps * depth * per_warp * stage * 576
+    reduction = ways * groups * ntiles * 32 * 16
+    return align(ntiles * 8 * x_stride) + align(max(rings, reduction)) + (warps * depth + 1) * 8
+
+
+def test_row_split_variants(cuda):
+    """Variants whose warps split a group's activation tiles (two or four
+    warps per group and way, 33..128 rows) against the double-precision
+    oracle: every format, plain and accumulating, one and several splits
+    (cluster reduction), a partial last panel (2560 outputs); at most 32
+    rows they are refused."""
+    variants = K.ProductVariants()
+    for v, shape in ROW_SPLIT_VARIANTS.items():
+        warps, groups, stage, depth = variants[v]
+        assert (groups, stage, depth) == (shape[0], shape[3], shape[4])
+        assert warps == shape[0] // shape[2] * shape[1] * shape[5]
+    rng = np.random.default_rng(71)
+    columns, out = 1024, 2560
+    blocks, q8_tiles, dequant, bf16_tiles = prepare(out, columns, rng)
+    host_dequant = from_dev_u16(dequant)
+    ran = {v: 0 for v in ROW_SPLIT_VARIANTS}
+    for rows in (33, 64, 65, 128):
+        x = make_activations(rows, columns, rng)
+        x_dev = to_dev(x)
+        before = rng.normal(0.0, 1.0, size=(rows, out)).astype(np.float32)
+        y = torch.empty(rows, out, dtype=torch.float32, device="cuda")
+        ntiles = 8 if rows <= 64 else 16
+        for variant, shape in ROW_SPLIT_VARIANTS.items():
+            for splits in (1, 4, 8):
+                bps = -(-(columns // 32) // splits)
+                if q8_footprint(shape, ntiles, bps) > 220 * 1024:
+                    continue  # the launcher would run its own plan instead
+                ran[variant] += 1
+                plan = _lib.WmmaPlan(splits, bps, 0, 0, variant)
+                for accumulate in (False, True):
+                    for fmt, w, ref_fmt, ref_w in (
+                        (_lib.WEIGHTS_Q8_TILES, q8_tiles, oracle.Q8_0, blocks),
+                        (_lib.WEIGHTS_BF16_TILES, bf16_tiles, oracle.BF16_ROWS, host_dequant),
+                        (_lib.WEIGHTS_BF16, dequant, oracle.BF16_ROWS, host_dequant),
+                    ):
+                        y.copy_(torch.from_numpy(before))
+                        assert K.Product(fmt, x_dev, w, y, rows, columns, out, accumulate, plan), \
+                            (variant, splits, fmt, rows)
+                        torch.cuda.synchronize()
+                        exact = oracle.product_exact(x, ref_fmt, ref_w, rows, columns, out,
+                                                     before if accumulate else None)
+                        err = oracle.relative_error(y.cpu().numpy(), *exact)
+                        assert err <= LIMIT, \
+                            f"variant {variant} splits {splits} fmt {fmt} rows {rows} acc {accumulate}: {err:.3e}"
+    assert all(count >= 4 for count in ran.values()), ran
+    x = to_dev(make_activations(32, columns, rng))
+    y = torch.empty(32, out, dtype=torch.float32, device="cuda")
+    for variant in ROW_SPLIT_VARIANTS:
+        plan = _lib.WmmaPlan(8, 4, 0, 0, variant)
+        assert not K.Product(_lib.WEIGHTS_Q8_TILES, x, q8_tiles, y, 32, columns, out, False, plan)
+    assert K.DeviceError() == 0
+
+
 @pytest.mark.parametrize("rows", [1, 22])
 def test_half_tile_math_wide_rows(cuda, rows):
     """Variant 14 on rows whose values span far more than 2^31: every

@@ -78,10 +78,12 @@ struct VariantShape {
   bool half;       // Q8_0: fp16 tile math over exactly scaled activations
   bool x_global;   // activation fragments read from global memory (L1/L2),
                    // not staged in shared memory
+  int row_split = 1;  // warps sharing a group and a stage, each taking an
+                      // equal share of the activation tiles
 };
 
 __host__ __device__ constexpr int WarpsOf(const VariantShape& v) {
-  return v.cta_groups / v.groups * v.ways;
+  return v.cta_groups / v.groups * v.ways * v.row_split;
 }
 
 constexpr VariantShape kVariants[] = {
@@ -125,6 +127,20 @@ constexpr VariantShape kVariants[] = {
     {3, 4, 1, 8, 2, false, true},  // 22: 48 rows, 12 warps (4 ways)
     {2, 4, 1, 8, 2, false, true},  // 23: 32 rows, 8 warps (4 ways)
     {4, 4, 1, 8, 2, false, true},  // 24: 64 rows, 16 warps (4 ways)
+    // 33..128 activation rows: each group's activation tiles split between
+    // two or four warps (row_split), so a warp holds 2-8 tiles of
+    // accumulators and fragments and a CTA runs 8-32 warps.
+    {4, 2, 1, 4, 2, false, false, 2},  // 25: 64 rows, 16 warps
+    {4, 1, 1, 4, 4, false, false, 2},  // 26: 64 rows, 8 warps
+    {2, 2, 1, 4, 2, false, false, 2},  // 27: 32 rows, 8 warps
+    {4, 2, 1, 4, 2, false, false, 4},  // 28: 64 rows, 32 warps
+    {2, 2, 1, 4, 2, false, false, 4},  // 29: 32 rows, 16 warps
+    {8, 1, 1, 4, 2, false, false, 2},  // 30: 128 rows, 16 warps
+    {2, 1, 1, 4, 4, false, false, 4},  // 31: 32 rows, 8 warps
+    {1, 2, 1, 4, 2, false, false, 4},  // 32: 16 rows, 8 warps
+    {2, 4, 1, 4, 2, false, false, 2},  // 33: 32 rows, 16 warps
+    {2, 2, 1, 8, 2, false, false, 2},  // 34: 32 rows, 8 warps, 8-block stages
+    {1, 4, 1, 4, 2, false, false, 4},  // 35: 16 rows, 16 warps
 };
 constexpr int kNumVariants = sizeof(kVariants) / sizeof(kVariants[0]);
 // The cost model chooses among the first eight shapes only: their plans fit
@@ -292,11 +308,15 @@ __device__ inline void CopyRowsAsync(unsigned char* dst, int dst_stride,
 }
 
 template <int kFormat, int kCtaGroups, int kWays, int kGroups, int kNTiles,
-          int kStage, int kDepth, bool kHalf, bool kXGlobal>
-__global__ void __launch_bounds__(kCtaGroups / kGroups * kWays * 32)
+          int kStage, int kDepth, bool kHalf, bool kXGlobal, int kRowSplit>
+__global__ void __launch_bounds__(kCtaGroups / kGroups * kWays * kRowSplit * 32)
     ProductKernel(const ProductArgs p) {
   static_assert(!(kHalf && kXGlobal), "fp16 tile math rescales a shared copy");
-  constexpr int kWarps = kCtaGroups / kGroups * kWays;
+  static_assert(kNTiles % kRowSplit == 0, "equal shares of activation tiles");
+  // Activation tiles of this warp: kNT from tile `tile0` (row_split warps
+  // per group and way, each loading its own copy of the group's weights).
+  constexpr int kNT = kNTiles / kRowSplit;
+  constexpr int kWarps = kCtaGroups / kGroups * kWays * kRowSplit;
   constexpr int kGroupBytes = GroupStageBytes(kFormat, kStage);
   constexpr int kRingBytes = kDepth * kGroups * kGroupBytes;
   constexpr bool kQ8 = kFormat == static_cast<int>(WeightFormat::kQ8Tiles);
@@ -313,7 +333,8 @@ __global__ void __launch_bounds__(kCtaGroups / kGroups * kWays * 32)
   const int gid = lane >> 2;
   const int tig = lane & 3;
   const int way = warp % kWays;
-  const int group_warp = warp / kWays;
+  const int tile0 = (warp / kWays) % kRowSplit * kNT;
+  const int group_warp = warp / (kWays * kRowSplit);
   const int split = static_cast<int>(blockIdx.x) % p.splits;
   const int panel = static_cast<int>(blockIdx.x) / p.splits;
   const int first = split * p.blocks_per_split;
@@ -443,11 +464,11 @@ __global__ void __launch_bounds__(kCtaGroups / kGroups * kWays * 32)
     __syncthreads();
   }
 
-  float acc[kGroups][kNTiles][4];
+  float acc[kGroups][kNT][4];
 #pragma unroll
   for (int g = 0; g < kGroups; ++g)
 #pragma unroll
-    for (int j = 0; j < kNTiles; ++j)
+    for (int j = 0; j < kNT; ++j)
 #pragma unroll
       for (int c = 0; c < 4; ++c)
         acc[g][j][c] = 0.0f;
@@ -487,14 +508,17 @@ __global__ void __launch_bounds__(kCtaGroups / kGroups * kWays * 32)
       const int st = way + i * kWays;
       const int nb = min(kStage, last - (first + st * kStage));
       if constexpr (kXGlobal) {
-        StageProduct<kFormat, kGroups, kNTiles, kStage, false, true>(
+        StageProduct<kFormat, kGroups, kNT, kStage, false, true>(
             ring + slot * kGroups * kGroupBytes, kGroupBytes,
-            reinterpret_cast<const unsigned char*>(p.x + first * 32), p.k * 2,
-            st * kStage * 32, nb, my_groups, gid, tig, acc, p.m);
+            reinterpret_cast<const unsigned char*>(
+                p.x + static_cast<std::size_t>(8 * tile0) * p.k + first * 32),
+            p.k * 2, st * kStage * 32, nb, my_groups, gid, tig, acc,
+            p.m - 8 * tile0);
       } else {
-        StageProduct<kFormat, kGroups, kNTiles, kStage, kHalfMath>(
-            ring + slot * kGroups * kGroupBytes, kGroupBytes, xs, p.x_stride,
-            st * kStage * 32, nb, my_groups, gid, tig, acc);
+        StageProduct<kFormat, kGroups, kNT, kStage, kHalfMath>(
+            ring + slot * kGroups * kGroupBytes, kGroupBytes,
+            xs + 8 * tile0 * p.x_stride, p.x_stride, st * kStage * 32, nb,
+            my_groups, gid, tig, acc);
       }
       // The slot's values are in registers (consumed above); refill it.
       __syncwarp();
@@ -517,10 +541,10 @@ __global__ void __launch_bounds__(kCtaGroups / kGroups * kWays * 32)
 #pragma unroll
     for (int g = 0; g < kGroups; ++g)
 #pragma unroll
-      for (int j = 0; j < kNTiles; ++j)
+      for (int j = 0; j < kNT; ++j)
 #pragma unroll
         for (int c = 0; c < 4; ++c)
-          acc[g][j][c] *= row_unscale[8 * j + 2 * tig + (c & 1)];
+          acc[g][j][c] *= row_unscale[8 * (tile0 + j) + 2 * tig + (c & 1)];
   }
 
   // Ways of a group add up in way order through shared memory.
@@ -533,9 +557,9 @@ __global__ void __launch_bounds__(kCtaGroups / kGroups * kWays * 32)
 #pragma unroll
       for (int g = 0; g < kGroups; ++g)
 #pragma unroll
-        for (int j = 0; j < kNTiles; ++j)
+        for (int j = 0; j < kNT; ++j)
           red[(way - 1) * kSlots +
-              ((group_warp * kGroups + g) * kNTiles + j) * 32 + lane] =
+              ((group_warp * kGroups + g) * kNTiles + tile0 + j) * 32 + lane] =
               make_float4(acc[g][j][0], acc[g][j][1], acc[g][j][2],
                           acc[g][j][3]);
     }
@@ -545,10 +569,11 @@ __global__ void __launch_bounds__(kCtaGroups / kGroups * kWays * 32)
 #pragma unroll
         for (int g = 0; g < kGroups; ++g)
 #pragma unroll
-          for (int j = 0; j < kNTiles; ++j) {
+          for (int j = 0; j < kNT; ++j) {
             const float4 v =
                 red[(w - 1) * kSlots +
-                    ((group_warp * kGroups + g) * kNTiles + j) * 32 + lane];
+                    ((group_warp * kGroups + g) * kNTiles + tile0 + j) * 32 +
+                    lane];
             acc[g][j][0] += v.x;
             acc[g][j][1] += v.y;
             acc[g][j][2] += v.z;
@@ -565,8 +590,8 @@ __global__ void __launch_bounds__(kCtaGroups / kGroups * kWays * 32)
 #pragma unroll
       for (int g = 0; g < kGroups; ++g)
 #pragma unroll
-        for (int j = 0; j < kNTiles; ++j)
-          part[((group_warp * kGroups + g) * kNTiles + j) * 32 + lane] =
+        for (int j = 0; j < kNT; ++j)
+          part[((group_warp * kGroups + g) * kNTiles + tile0 + j) * 32 + lane] =
               make_float4(acc[g][j][0], acc[g][j][1], acc[g][j][2],
                           acc[g][j][3]);
     }
@@ -576,9 +601,10 @@ __global__ void __launch_bounds__(kCtaGroups / kGroups * kWays * 32)
 #pragma unroll
         for (int g = 0; g < kGroups; ++g)
 #pragma unroll
-          for (int j = 0; j < kNTiles; ++j) {
+          for (int j = 0; j < kNT; ++j) {
             const float4 v = LoadSharedCluster4(MapShared(
-                &part[((group_warp * kGroups + g) * kNTiles + j) * 32 + lane],
+                &part[((group_warp * kGroups + g) * kNTiles + tile0 + j) * 32 +
+                      lane],
                 r));
             acc[g][j][0] += v.x;
             acc[g][j][1] += v.y;
@@ -596,11 +622,11 @@ __global__ void __launch_bounds__(kCtaGroups / kGroups * kWays * 32)
     if (g >= my_groups)
       break;
 #pragma unroll
-    for (int j = 0; j < kNTiles; ++j)
+    for (int j = 0; j < kNT; ++j)
 #pragma unroll
       for (int c = 0; c < 4; ++c) {
         const int n = (group0 + g) * 16 + gid + 8 * (c >> 1);
-        const int m = 8 * j + 2 * tig + (c & 1);
+        const int m = 8 * (tile0 + j) + 2 * tig + (c & 1);
         if (m < p.m && n < p.n) {
           const std::size_t index = static_cast<std::size_t>(m) * p.n + n;
           float value = acc[g][j][c];
@@ -624,20 +650,24 @@ using KernelFn = void (*)(const ProductArgs);
 
 // Variants that take 33..128 activation rows (8 or 16 B tiles per warp):
 // the small CTAs, whose registers and activation slices stay in bounds.
-__host__ __device__ constexpr bool WideVariant(int variant) {
-  return variant == 0 || variant == 1 || variant == 3 || variant == 15;
+constexpr bool WideVariant(int variant) {
+  return variant == 0 || variant == 1 || variant == 3 || variant == 15 ||
+         kVariants[variant].row_split > 1;
 }
 
 template <int kFormat, int kNTiles, int kVariant>
 constexpr KernelFn KernelFor() {
-  if constexpr (kNTiles > 4 && !WideVariant(kVariant)) {
+  // Row-split variants serve 33..128 rows (8 or 16 tiles) only.
+  if constexpr ((kNTiles > 4 && !WideVariant(kVariant)) ||
+                (kVariants[kVariant].row_split > 1 && kNTiles <= 4)) {
     return nullptr;
   } else {
     return ProductKernel<kFormat, kVariants[kVariant].cta_groups,
                          kVariants[kVariant].ways, kVariants[kVariant].groups,
                          kNTiles, kVariants[kVariant].stage,
                          kVariants[kVariant].depth, kVariants[kVariant].half,
-                         kVariants[kVariant].x_global>;
+                         kVariants[kVariant].x_global,
+                         kVariants[kVariant].row_split>;
   }
 }
 
@@ -648,11 +678,13 @@ struct VariantRow {
 
 template <int kFormat, int kNTiles>
 using Row = VariantRow<kFormat, kNTiles, 0, 1, 2, 3, 4, 5, 6, 7, 8, 9, 10, 11,
-                       12, 13, 14, 15, 16, 17, 18, 19, 20, 21, 22, 23, 24>;
+                       12, 13, 14, 15, 16, 17, 18, 19, 20, 21, 22, 23, 24,
+                       25, 26, 27, 28, 29, 30, 31, 32, 33, 34, 35>;
 
-/// Row classes of the measured plan tables: 1, 2..8, 9..32, 33..128.
+/// Row classes of the measured plan tables: 1, 2..8, 9..32, 33..64,
+/// 65..128.
 int RowsClass(std::size_t rows) {
-  return rows == 1 ? 0 : rows <= 8 ? 1 : rows <= 32 ? 2 : 3;
+  return rows == 1 ? 0 : rows <= 8 ? 1 : rows <= 32 ? 2 : rows <= 64 ? 3 : 4;
 }
 
 /// Index of a B-tile count (1, 2, 3, 4, 8, 16) in the tables.
@@ -841,15 +873,35 @@ constexpr MeasuredPlan kMeasuredPlans[] = {
     // Q8_0 tiles, 2..8 rows (encoder of a patch, DiT in/out).
     {WeightFormat::kQ8Tiles, 1, 64, 1024, 1, 1},
     {WeightFormat::kQ8Tiles, 1, 1024, 64, 4, 5},
-    // Q8_0 tiles, 33..128 rows (the DiT's rows of batched slots): variant
-    // 15, two ways of four warps over 64-row panels. Dependent chains, us
-    // at 48 / 128 rows against the plans before: 1024 -> 2560 7.7 / 13.5
-    // (9.2 / 14.4), 2048 -> 1024 10.1 / 14.7 (11.0 / 18.5), 4096 -> 1024
-    // 10.3 at 48 rows (11.9); at 65..128 rows its slices do not fit and the
-    // long-reduction plan runs.
-    {WeightFormat::kQ8Tiles, 3, 1024, 2560, 15, 2},
-    {WeightFormat::kQ8Tiles, 3, 2048, 1024, 15, 4},
-    {WeightFormat::kQ8Tiles, 3, 4096, 1024, 15, 6},
+    // Q8_0 tiles, 33..64 rows (the DiT's rows of batched slots, the
+    // prefill): the row-split variants 25-35. Dependent chains at 64 / 48
+    // rows, us, and in parentheses the plan before them (variant 15, the
+    // long-reduction plan or 32-row launches).
+    {WeightFormat::kQ8Tiles, 3, 1024, 1024, 35, 1},   // 4.51 / 4.46 (8.96 / 8.21)
+    {WeightFormat::kQ8Tiles, 3, 1024, 2560, 33, 1},   // 6.29 / 6.03 (8.16 / 7.84)
+    {WeightFormat::kQ8Tiles, 3, 1024, 3072, 34, 1},   // 6.25 / 6.12 (9.89 / 9.49)
+    {WeightFormat::kQ8Tiles, 3, 1024, 8192, 25, 1},   // 9.37 / 9.26 (12.20 / 12.01)
+    {WeightFormat::kQ8Tiles, 3, 2048, 1024, 32, 4},   // 6.02 / 6.03 (10.20 / 9.97)
+    {WeightFormat::kQ8Tiles, 3, 2048, 2048, 27, 4},   // 7.63 / 7.53 (11.71 / 11.29)
+    {WeightFormat::kQ8Tiles, 3, 2048, 2560, 25, 3},   // 9.54 / 9.45 (11.77 / 11.52)
+    {WeightFormat::kQ8Tiles, 3, 2048, 6144, 30, 2},   // 16.92 / 16.49 (19.17 / 15.70)
+    {WeightFormat::kQ8Tiles, 3, 2048, 12288, 15, 4},  // 31.78 / 31.33 (37.24 / 29.70)
+    {WeightFormat::kQ8Tiles, 3, 4096, 1024, 34, 4},   // 8.13 / 8.10 (10.83 / 10.41)
+    {WeightFormat::kQ8Tiles, 3, 6144, 2048, 30, 6},   // 18.71 / 18.47 (27.69 / 20.93)
+    // Q8_0 tiles, 65..128 rows, at 128 / 100 rows (before: variant 15, the
+    // wide tcgen05 kernel for 1024 -> 3072 and 8192, the long-reduction plan
+    // or 32-row launches). 4096 -> 1024 and 6144 -> 2048 have no entry: the
+    // launcher runs them as 64-row launches on the plans above (2 x 8.1 and
+    // 2 x 18.7 us against 20.3 and 55.2 at 128 rows).
+    {WeightFormat::kQ8Tiles, 4, 1024, 1024, 32, 2},   // 6.05 / 5.95 (14.58 / 13.63)
+    {WeightFormat::kQ8Tiles, 4, 1024, 2560, 26, 3},   // 10.72 / 10.51 (12.83 / 12.06)
+    {WeightFormat::kQ8Tiles, 4, 1024, 3072, 25, 2},   // 10.93 / 10.71 (22.64 / 22.55)
+    {WeightFormat::kQ8Tiles, 4, 1024, 8192, 30, 2},   // 15.88 / 15.75 (21.35 / 21.26)
+    {WeightFormat::kQ8Tiles, 4, 2048, 1024, 29, 4},   // 8.70 / 8.63 (13.86 / 13.48)
+    {WeightFormat::kQ8Tiles, 4, 2048, 2048, 25, 4},   // 12.27 / 12.10 (18.63 / 17.97)
+    {WeightFormat::kQ8Tiles, 4, 2048, 2560, 30, 4},   // 18.06 / 17.77 (18.76 / 18.30)
+    {WeightFormat::kQ8Tiles, 4, 2048, 6144, 30, 4},   // 34.18 / 33.86 (37.52 / 32.43)
+    {WeightFormat::kQ8Tiles, 4, 2048, 12288, 30, 4},  // 54.40 / 53.54 (73.26 / 63.20)
     // bf16 tiles and rows.
     {WeightFormat::kBf16Tiles, 2, 2048, 6144, 0, 2},
 };
@@ -890,6 +942,37 @@ ProductPlan StreamPlan(WeightFormat format, std::size_t rows, std::size_t in,
   return plan;
 }
 
+/// The measured plan for this shape and row class that fits these rows, or
+/// no plan (variant -1).
+ProductPlan MeasuredPlanFor(WeightFormat format, std::size_t rows,
+                            std::size_t in, std::size_t out) {
+  ProductPlan best;
+  if (rows == 0 || in == 0 || out == 0 || in % kTileColumns != 0)
+    return best;
+  const int k_blocks = static_cast<int>(in / kTileColumns);
+  const int rows_class = RowsClass(rows);
+  for (const MeasuredPlan& m : kMeasuredPlans) {
+    if (m.format != format || m.rows_class != rows_class ||
+        static_cast<std::size_t>(m.in) != in ||
+        static_cast<std::size_t>(m.out) != out)
+      continue;
+    const int bps = (k_blocks + m.splits - 1) / m.splits;
+    const int ntiles = TilesFor(rows);
+    // Measured plans were measured up to the launch limit.
+    const std::size_t limit = kMaxProductSmem;
+    if ((k_blocks + bps - 1) / bps != m.splits ||
+        bps * kTileColumns > kMaxSliceColumns ||
+        FootprintOf(static_cast<int>(format), m.variant, ntiles, bps).smem >
+            limit)
+      continue;  // does not fit these rows: a later entry, or the cost model
+    best.variant = m.variant;
+    best.splits = m.splits;
+    best.blocks_per_split = bps;
+    return best;
+  }
+  return best;
+}
+
 ProductPlan PlanProduct(WeightFormat format, std::size_t rows, std::size_t in,
                         std::size_t out, std::size_t target_ctas) {
   ProductPlan best;
@@ -906,26 +989,9 @@ ProductPlan PlanProduct(WeightFormat format, std::size_t rows, std::size_t in,
   }
   const int k_blocks = static_cast<int>(in / kTileColumns);
   if (target_ctas == 0) {
-    const int rows_class = RowsClass(rows);
-    for (const MeasuredPlan& m : kMeasuredPlans) {
-      if (m.format != format || m.rows_class != rows_class ||
-          static_cast<std::size_t>(m.in) != in ||
-          static_cast<std::size_t>(m.out) != out)
-        continue;
-      const int bps = (k_blocks + m.splits - 1) / m.splits;
-      const int ntiles = TilesFor(rows);
-      // Measured plans were measured up to the launch limit.
-      const std::size_t limit = kMaxProductSmem;
-      if ((k_blocks + bps - 1) / bps != m.splits ||
-          bps * kTileColumns > kMaxSliceColumns ||
-          FootprintOf(static_cast<int>(format), m.variant, ntiles, bps).smem >
-              limit)
-        continue;  // does not fit these rows: a later entry, or the cost model
-      best.variant = m.variant;
-      best.splits = m.splits;
-      best.blocks_per_split = bps;
-      return best;
-    }
+    const ProductPlan measured = MeasuredPlanFor(format, rows, in, out);
+    if (measured.variant >= 0)
+      return measured;
   }
   // 33..128 rows over reductions longer than 1024 columns: the cost model's
   // wide plans were compute-bound on too few CTAs there. For Q8_0 tiles into
@@ -1048,8 +1114,28 @@ int LaunchProduct(WeightFormat format, const std::uint16_t* x, const void* w,
                                accumulate, *scratch, stream, independent,
                                g_programmatic);
   }
+  // 65..128 rows of a shape measured at 33..64 rows only: launches of 64
+  // rows on that plan (4096 -> 1024 at 128 rows: 2 x 8.1 us against 20.3
+  // for the best single launch).
+  if (plan.variant < 0 && plan_in == nullptr && rows > 64 &&
+      MeasuredPlanFor(format, rows, in, out).variant < 0 &&
+      MeasuredPlanFor(format, 64, in, out).variant >= 0) {
+    for (std::size_t first = 0; first < rows; first += 64) {
+      const std::size_t count = std::min<std::size_t>(64, rows - first);
+      const int status = LaunchProduct(
+          format, x + first * in, w, y != nullptr ? y + first * out : nullptr,
+          y_bf16 != nullptr ? y_bf16 + first * out : nullptr, count, in, out,
+          accumulate, nullptr, stream, independent, scratch);
+      if (status != kOk)
+        return status;
+    }
+    return kOk;
+  }
+  // The wide tcgen05 kernel where it pays and no measured mma.sync plan
+  // exists (the row-split plans measured faster on every shape they cover).
   if (plan.variant < 0 && format == WeightFormat::kQ8Tiles &&
-      WideTensorCoreProducts() && WideProductPays(rows, in, out))
+      WideTensorCoreProducts() && WideProductPays(rows, in, out) &&
+      MeasuredPlanFor(format, rows, in, out).variant < 0)
     plan = PlanWideProduct(rows, in, out, SmCount());
   if (plan.variant < 0)
     plan = PlanProduct(format, rows, in, out, 0);
@@ -1110,6 +1196,8 @@ int LaunchProduct(WeightFormat format, const std::uint16_t* x, const void* w,
   const int panels =
       static_cast<int>((out + rows_per_cta - 1) / rows_per_cta);
   KernelFn kernel = Lookup(f, ntiles, plan.variant);
+  if (kernel == nullptr)
+    return kUnsupported;  // a row-split variant for at most 32 rows
 
   // The dynamic shared-memory limit is per function and device.
   {
