@@ -72,6 +72,8 @@ def parse():
     p.add_argument("--non-cooperative", action="store_true",
                    help="with --case: launch the persistent kernels without the cooperative attribute "
                         "(vx_set_persistent_cooperative(0)), for profilers")
+    p.add_argument("--slots", type=int, default=8,
+                   help="with --case batch: active slots of the GeneratorBatch (the bench's box_batched runs 16)")
     return p.parse_args()
 
 
@@ -1032,7 +1034,7 @@ def measure_box_batched(c, requests) -> float:
     return a.elapsed_time(b) / 1e3
 
 
-def profile_case(case: str, max_ctas: int = 0, cooperative: bool = True) -> None:
+def profile_case(case: str, max_ctas: int = 0, cooperative: bool = True, slots: int = 8) -> None:
     """A few launches of one kernel on a small case, for ncu captures:
     `product`: 8 config-0 products with the stream plan (independent), then 8
     with the planner's plan (dependent); `dit`: two eager DiT patches (the
@@ -1150,7 +1152,7 @@ def profile_case(case: str, max_ctas: int = 0, cooperative: bool = True) -> None
 
         c = released_config()
         c.max_length = 256
-        slots, rows = 8, 16
+        rows = 16
         rng = np.random.default_rng(0)
         feats = rng.normal(0, 1, (rows, c.patch_size, c.feat_dim)).astype(np.float32)
         audio = np.ones(rows, np.int32)
@@ -1186,7 +1188,7 @@ def profile_case(case: str, max_ctas: int = 0, cooperative: bool = True) -> None
 def main():
     args = parse()
     if args.case is not None:
-        profile_case(args.case, args.max_ctas, not args.non_cooperative)
+        profile_case(args.case, args.max_ctas, not args.non_cooperative, args.slots)
         return
     world, rank, local = init_dist(args.gpus)
     try:
