@@ -719,7 +719,7 @@ STREAM_MIN_LAUNCHES = 2000  # the stream line's launches at least (a few ms)
 
 BOX_REQUESTS = 64        # independent requests over the box
 BOX_PATCHES = 63         # patches per request (about 10 s of audio)
-BOX_SLOTS = 16           # requests generated together per GPU (GeneratorBatch slots, at most)
+BOX_SLOTS = 32           # requests generated together per GPU (GeneratorBatch slots, at most)
 
 
 SWEEP_ROWS = (1, 2, 8, 22, 64, 128)
