@@ -582,6 +582,69 @@ __global__ void __launch_bounds__(kCtaGroups / kGroups * kWays * kRowSplit * 32)
       }
     }
   }
+  // Row-split variants (33..128 rows) with three or more splits: every rank
+  // publishes its partial sums, the output tiles are dealt out over the
+  // ranks (tile q to rank q mod splits), and each rank adds its tiles'
+  // partials of ranks 0, 1, ... in that order and stores them, so the
+  // reduction and the stores are spread over the cluster instead of falling
+  // on rank 0 alone (the same sums in the same order as below: the same
+  // bits). Measured at 128 rows: 2048 -> 6144 34.0 -> 29.7 us, 2048 ->
+  // 12288 54.0 -> 46.0, 6144 -> 2048 in 64-row launches 37.2 -> 32.5; the
+  // other variants keep the code below (at 1..32 rows the spread measured
+  // up to 3 % slower).
+  if constexpr (kRowSplit > 1) {
+    if (p.splits > 2) {
+      float4* part = red + (kWays - 1) * kSlots;
+      if (way == 0) {
+#pragma unroll
+        for (int g = 0; g < kGroups; ++g)
+#pragma unroll
+          for (int j = 0; j < kNT; ++j)
+            part[((group_warp * kGroups + g) * kNTiles + tile0 + j) * 32 +
+                 lane] = make_float4(acc[g][j][0], acc[g][j][1],
+                                     acc[g][j][2], acc[g][j][3]);
+      }
+      ClusterSync();
+      if (way == 0) {
+        for (int g = 0; g < my_groups; ++g)
+          for (int j = 0; j < kNT; ++j) {
+            const int q = (group_warp * kGroups + g) * kNTiles + tile0 + j;
+            if (q % p.splits != split)
+              continue;
+            float4 sum = LoadSharedCluster4(MapShared(&part[q * 32 + lane], 0));
+            for (int r = 1; r < p.splits; ++r) {
+              const float4 v =
+                  LoadSharedCluster4(MapShared(&part[q * 32 + lane], r));
+              sum.x += v.x;
+              sum.y += v.y;
+              sum.z += v.z;
+              sum.w += v.w;
+            }
+            const float values[4] = {sum.x, sum.y, sum.z, sum.w};
+#pragma unroll
+            for (int c = 0; c < 4; ++c) {
+              const int n = (group0 + g) * 16 + gid + 8 * (c >> 1);
+              const int m = 8 * (tile0 + j) + 2 * tig + (c & 1);
+              if (m < p.m && n < p.n) {
+                const std::size_t index = static_cast<std::size_t>(m) * p.n + n;
+                float value = values[c];
+                if (p.y != nullptr) {
+                  if (p.accumulate)
+                    value = p.y[index] + value;
+                  p.y[index] = value;
+                } else {
+                  if (p.accumulate)
+                    value = Bf16ToFloat(p.y_bf16[index]) + value;
+                  p.y_bf16[index] = FloatToBf16(value);
+                }
+              }
+            }
+          }
+      }
+      ClusterSync();  // every rank keeps its shared memory until all read
+      return;
+    }
+  }
   // Splits of the cluster add up in rank order through distributed shared
   // memory (a region after the ways' buffers).
   if (p.splits > 1) {
@@ -887,7 +950,9 @@ constexpr MeasuredPlan kMeasuredPlans[] = {
     {WeightFormat::kQ8Tiles, 3, 2048, 6144, 30, 2},   // 16.92 / 16.49 (19.17 / 15.70)
     {WeightFormat::kQ8Tiles, 3, 2048, 12288, 15, 4},  // 31.78 / 31.33 (37.24 / 29.70)
     {WeightFormat::kQ8Tiles, 3, 4096, 1024, 34, 4},   // 8.13 / 8.10 (10.83 / 10.41)
-    {WeightFormat::kQ8Tiles, 3, 6144, 2048, 30, 6},   // 18.71 / 18.47 (27.69 / 20.93)
+    {WeightFormat::kQ8Tiles, 3, 6144, 2048, 30, 6},   // 18.71 / 18.47 (27.69 / 20.93); spread: 16.30
+    // "spread": at 64 / 128 rows with the cluster reduction spread over the
+    // ranks (row-split variants, three or more splits).
     // Q8_0 tiles, 65..128 rows, at 128 / 100 rows (before: variant 15, the
     // wide tcgen05 kernel for 1024 -> 3072 and 8192, the long-reduction plan
     // or 32-row launches). 4096 -> 1024 and 6144 -> 2048 have no entry: the
@@ -899,9 +964,9 @@ constexpr MeasuredPlan kMeasuredPlans[] = {
     {WeightFormat::kQ8Tiles, 4, 1024, 8192, 30, 2},   // 15.88 / 15.75 (21.35 / 21.26)
     {WeightFormat::kQ8Tiles, 4, 2048, 1024, 29, 4},   // 8.70 / 8.63 (13.86 / 13.48)
     {WeightFormat::kQ8Tiles, 4, 2048, 2048, 25, 4},   // 12.27 / 12.10 (18.63 / 17.97)
-    {WeightFormat::kQ8Tiles, 4, 2048, 2560, 30, 4},   // 18.06 / 17.77 (18.76 / 18.30)
-    {WeightFormat::kQ8Tiles, 4, 2048, 6144, 30, 4},   // 34.18 / 33.86 (37.52 / 32.43)
-    {WeightFormat::kQ8Tiles, 4, 2048, 12288, 30, 4},  // 54.40 / 53.54 (73.26 / 63.20)
+    {WeightFormat::kQ8Tiles, 4, 2048, 2560, 30, 4},   // 18.06 / 17.77 (18.76 / 18.30); spread: 14.85
+    {WeightFormat::kQ8Tiles, 4, 2048, 6144, 30, 4},   // 34.18 / 33.86 (37.52 / 32.43); spread: 29.85
+    {WeightFormat::kQ8Tiles, 4, 2048, 12288, 30, 4},  // 54.40 / 53.54 (73.26 / 63.20); spread: 46.26
     // bf16 tiles and rows.
     {WeightFormat::kBf16Tiles, 2, 2048, 6144, 0, 2},
 };
