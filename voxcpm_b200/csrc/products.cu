@@ -967,6 +967,29 @@ constexpr MeasuredPlan kMeasuredPlans[] = {
     {WeightFormat::kQ8Tiles, 4, 2048, 2560, 30, 4},   // 18.06 / 17.77 (18.76 / 18.30); spread: 14.85
     {WeightFormat::kQ8Tiles, 4, 2048, 6144, 30, 4},   // 34.18 / 33.86 (37.52 / 32.43); spread: 29.85
     {WeightFormat::kQ8Tiles, 4, 2048, 12288, 30, 4},  // 54.40 / 53.54 (73.26 / 63.20); spread: 46.26
+    // bf16 rows, 33..64 rows, at 64 / 48 rows (before: the cost model, the
+    // long-reduction plan or 32-row launches). 2048 -> 6144 keeps 32-row
+    // launches (17.1 / 15.7 us; the best plan measured 23.1).
+    {WeightFormat::kBf16, 3, 1024, 1024, 34, 2},   // 5.08 / 4.85 (8.27 / 7.68)
+    {WeightFormat::kBf16, 3, 1024, 2560, 27, 1},   // 7.20 / 7.13 (9.17 / 8.95)
+    {WeightFormat::kBf16, 3, 1024, 3072, 27, 1},   // 7.30 / 7.23 (15.44 / 15.07)
+    {WeightFormat::kBf16, 3, 1024, 8192, 15, 1},   // 10.66 / 10.46 (34.19 / 32.73)
+    {WeightFormat::kBf16, 3, 2048, 1024, 34, 4},   // 5.81 / 5.95 (8.64 / 8.13)
+    {WeightFormat::kBf16, 3, 2048, 2048, 27, 2},   // 8.96 / 8.90 (10.34 / 9.67)
+    {WeightFormat::kBf16, 3, 2048, 2560, 15, 3},   // 10.48 / 10.31 (14.23 / 13.18)
+    {WeightFormat::kBf16, 3, 2048, 12288, 15, 2},  // 36.05 / 35.43 (45.29 / 41.76)
+    {WeightFormat::kBf16, 3, 4096, 1024, 27, 4},   // 9.40 / 9.44 (12.41 / 11.68)
+    {WeightFormat::kBf16, 3, 6144, 2048, 15, 6},   // 24.07 / 23.79 (30.58 / 27.14)
+    // bf16 rows, 65..128 rows, at 128 / 100 rows. 4096 -> 1024, 6144 ->
+    // 2048, 1024 -> 8192, 2048 -> 2560 and 2048 -> 12288 run as 64-row
+    // launches on the plans above (2 x 9.4, 2 x 24.1, 2 x 10.7, 2 x 10.5 and
+    // 2 x 36.1 us against 24.7, 61.0, 26.7, 24.6 and 82.1 for the best
+    // single launch at 128 rows); 2048 -> 6144 keeps 32-row launches.
+    {WeightFormat::kBf16, 4, 1024, 1024, 32, 2},   // 6.67 / 6.60 (13.77 / 13.06)
+    {WeightFormat::kBf16, 4, 1024, 2560, 30, 6},   // 10.91 / 10.98 (14.02 / 13.63)
+    {WeightFormat::kBf16, 4, 1024, 3072, 15, 2},   // 13.08 / 12.75 (23.22 / 22.59)
+    {WeightFormat::kBf16, 4, 2048, 1024, 27, 4},   // 9.44 / 9.45 (17.06 / 16.53)
+    {WeightFormat::kBf16, 4, 2048, 2048, 15, 4},   // 14.85 / 14.59 (20.61 / 19.59)
     // bf16 tiles and rows.
     {WeightFormat::kBf16Tiles, 2, 2048, 6144, 0, 2},
 };
