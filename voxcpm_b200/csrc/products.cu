@@ -955,9 +955,9 @@ constexpr MeasuredPlan kMeasuredPlans[] = {
     // ranks (row-split variants, three or more splits).
     // Q8_0 tiles, 65..128 rows, at 128 / 100 rows (before: variant 15, the
     // wide tcgen05 kernel for 1024 -> 3072 and 8192, the long-reduction plan
-    // or 32-row launches). 4096 -> 1024 and 6144 -> 2048 have no entry: the
-    // launcher runs them as 64-row launches on the plans above (2 x 8.1 and
-    // 2 x 18.7 us against 20.3 and 55.2 at 128 rows).
+    // or 32-row launches). 6144 -> 2048 has no entry: the launcher runs it
+    // as 64-row launches on the plan above (2 x 16.3 us against 55.2 before
+    // and 37.2 for the best single launch at 128 rows).
     {WeightFormat::kQ8Tiles, 4, 1024, 1024, 32, 2},   // 6.05 / 5.95 (14.58 / 13.63)
     {WeightFormat::kQ8Tiles, 4, 1024, 2560, 26, 3},   // 10.72 / 10.51 (12.83 / 12.06)
     {WeightFormat::kQ8Tiles, 4, 1024, 3072, 25, 2},   // 10.93 / 10.71 (22.64 / 22.55)
@@ -967,6 +967,7 @@ constexpr MeasuredPlan kMeasuredPlans[] = {
     {WeightFormat::kQ8Tiles, 4, 2048, 2560, 30, 4},   // 18.06 / 17.77 (18.76 / 18.30); spread: 14.85
     {WeightFormat::kQ8Tiles, 4, 2048, 6144, 30, 4},   // 34.18 / 33.86 (37.52 / 32.43); spread: 29.85
     {WeightFormat::kQ8Tiles, 4, 2048, 12288, 30, 4},  // 54.40 / 53.54 (73.26 / 63.20); spread: 46.26
+    {WeightFormat::kQ8Tiles, 4, 4096, 1024, 30, 8},   // spread: 15.29 at 128 rows (64-row launches 15.82)
     // bf16 rows, 33..64 rows, at 64 / 48 rows (before: the cost model, the
     // long-reduction plan or 32-row launches). 2048 -> 6144 keeps 32-row
     // launches (17.1 / 15.7 us; the best plan measured 23.1).
