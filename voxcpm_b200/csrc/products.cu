@@ -991,6 +991,17 @@ constexpr MeasuredPlan kMeasuredPlans[] = {
     {WeightFormat::kBf16, 4, 1024, 3072, 15, 2},   // 13.08 / 12.75 (23.22 / 22.59)
     {WeightFormat::kBf16, 4, 2048, 1024, 27, 4},   // 9.44 / 9.45 (17.06 / 16.53)
     {WeightFormat::kBf16, 4, 2048, 2048, 15, 4},   // 14.85 / 14.59 (20.61 / 19.59)
+    // bf16 tiles (the DiT of bf16 checkpoints), 33..64 rows at 64 / 48 rows
+    // and 65..128 rows at 128 rows (before: the cost model or 32-row
+    // launches). 4096 -> 1024 and 1024 -> 8192 run 65..128 rows as 64-row
+    // launches (2 x 7.7 and 2 x 8.5 us against 22.1 and 22.5 for the best
+    // single launch at 128 rows).
+    {WeightFormat::kBf16Tiles, 3, 1024, 2560, 27, 1},  // 6.07 / 5.84 (9.06 / 8.66)
+    {WeightFormat::kBf16Tiles, 3, 1024, 8192, 15, 1},  // 8.53 / 8.29 (9.98 / 9.80)
+    {WeightFormat::kBf16Tiles, 3, 2048, 1024, 34, 4},  // 5.49 / 5.59 (11.85 / 11.02)
+    {WeightFormat::kBf16Tiles, 3, 4096, 1024, 27, 4},  // 7.66 / 7.68 (23.45 / 21.13)
+    {WeightFormat::kBf16Tiles, 4, 1024, 2560, 30, 6},  // 10.09 (12.97)
+    {WeightFormat::kBf16Tiles, 4, 2048, 1024, 27, 4},  // 8.11 (23.57)
     // bf16 tiles and rows.
     {WeightFormat::kBf16Tiles, 2, 2048, 6144, 0, 2},
 };
