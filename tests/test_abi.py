@@ -74,6 +74,25 @@ def test_planner():
     assert K.PlanWmma(22, 48, 16).splits == 0          # in not a multiple of 32
 
 
+def test_planner_33_to_128_rows():
+    """33..64 and 65..128 rows of VoxCPM2's Q8_0 shapes take the measured
+    row-split plans (variants 25-35: warps that share a group's activation
+    tiles), each within the reduction's limits; a row-split variant has
+    more warps than its groups and ways alone would give (host only)."""
+    variants = K.ProductVariants()
+    expected = {(48, 1024, 2560): (33, 1), (64, 2048, 1024): (32, 4), (64, 4096, 1024): (34, 4),
+                (100, 1024, 8192): (30, 2), (128, 2048, 1024): (29, 4), (128, 4096, 1024): (30, 8),
+                (128, 2048, 12288): (30, 4)}
+    for (rows, columns, out), (variant, splits) in expected.items():
+        plan = K.PlanWmma(rows, columns, out, 0)
+        assert (plan.variant, plan.splits) == (variant, splits), (rows, columns, out)
+        kb = columns // 32
+        assert plan.splits * plan.blocks_per_split >= kb
+        assert (plan.splits - 1) * plan.blocks_per_split < kb
+        warps, groups, _, _ = variants[plan.variant]
+        assert warps > groups  # two or four warps per group and way
+
+
 def test_spread_planner():
     """Spread plans (host only; without a device the SM count is B200's 148):
     one CTA per panel at least, at most one per SM, every run at most one
