@@ -1042,7 +1042,8 @@ def profile_case(case: str, max_ctas: int = 0, cooperative: bool = True, slots: 
     eager steps at context 512 (bf16 cache) with a 4-layer LM and a 2-layer
     residual LM (the persistent stack kernel at the released widths); `wide`: three
     products of 88 rows of 1024 -> 8192 (the gate/up product of four batched
-    slots' DiT rows; the planner gives it to the wide tcgen05 kernel);
+    slots' DiT rows) on the planner's row-split plan, then three on the wide
+    tcgen05 kernel;
     `batch`: two steps of a GeneratorBatch of 8 slots on the released shapes
     (the first captures the step's graph); `matmul`: three Bf16Gemm::Matmul
     calls of 4096 x 4096 x 4096 in the reduction-contiguous layout, timed
@@ -1143,9 +1144,14 @@ def profile_case(case: str, max_ctas: int = 0, cooperative: bool = True, slots: 
         K.Q8_0ToTiles(blocks, out, columns, t)
         x = torch.randn(rows, columns, device="cuda").to(torch.bfloat16)
         y = torch.empty(rows, out, dtype=torch.float32, device="cuda")
-        for _ in range(3):
-            _lib.check(lib.vx_product(_lib.WEIGHTS_Q8_TILES, x.data_ptr(), t.data_ptr(), y.data_ptr(),
-                                      _lib.OUT_F32, rows, columns, out, 0, None, None))
+        # The planner's plan (row-split variant 30), then the wide tcgen05
+        # kernel on the plan its planner makes for this shape (2 splits of
+        # 16 blocks).
+        wide = _lib.WmmaPlan(2, 16, 0, 0, K.TENSOR_CORE_WIDE_VARIANT)
+        for plan in (None, ctypes.byref(wide)):
+            for _ in range(3):
+                _lib.check(lib.vx_product(_lib.WEIGHTS_Q8_TILES, x.data_ptr(), t.data_ptr(), y.data_ptr(),
+                                          _lib.OUT_F32, rows, columns, out, 0, plan, None))
         torch.cuda.synchronize()
     elif case == "batch":
         from voxcpm_b200.generator import GeneratorBatch, released_config
